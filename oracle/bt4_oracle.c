@@ -1,0 +1,392 @@
+/*
+ * bt4_oracle.c -- CPU restatement of the reference's BT4 forward pass.
+ *
+ * TEST INFRASTRUCTURE ONLY. This file is the parity checker for the CUDA
+ * path (and the "port" CPU baseline of bench.py). It is never linked into the
+ * product library; the product fails loudly when its CUDA library is missing.
+ *
+ * It restates, for the fixed attention-body topology of BT4-family networks,
+ * the step-by-step fp32 interpretation that the reference's CPU backend runs
+ * (src/nn/cpu/cpu_network.cpp RunBatch, :580-1491) over the execution plan of
+ * src/nn/network_execution_plan.cpp:135-223. Every per-row loop keeps the
+ * reference's accumulation order and float operations (no -ffast-math), so on
+ * the same weights and inputs its outputs are bit-identical to the reference
+ * binary built from the reference sources (checked by the golden fixtures).
+ *
+ * Positions are independent, so the batch is split over pthreads; each thread
+ * runs one position at a time.
+ */
+#include <math.h>
+#include <pthread.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+
+/* Activation kinds (src/nn/cpu/cpu_network.cpp:251-324). */
+enum { ACT_NONE = 0, ACT_RELU, ACT_RELU2, ACT_TANH, ACT_SIGMOID, ACT_SWISH, ACT_MISH, ACT_SELU };
+
+/* Global tensor slots; the order is mirrored by metalfish_b200/layout.py. */
+enum {
+  G_PREPROC_W, G_PREPROC_B, G_EMB_W, G_EMB_B, G_EMB_LN_G, G_EMB_LN_B, G_MULT_GATE, G_ADD_GATE,
+  G_EFFN_W1, G_EFFN_B1, G_EFFN_W2, G_EFFN_B2, G_EFFN_LN_G, G_EFFN_LN_B, G_SMOLGEN_W,
+  G_POL_W, G_POL_B, G_POL_WQ, G_POL_BQ, G_POL_WK, G_POL_BK, G_POL_PPO,
+  G_VAL_W, G_VAL_B, G_VAL_W1, G_VAL_B1, G_VAL_W2, G_VAL_B2,
+  G_MOV_W, G_MOV_B, G_MOV_W1, G_MOV_B1, G_MOV_W2, G_MOV_B2, G_COUNT
+};
+/* Per-encoder-layer tensor slots. */
+enum {
+  L_Q_W, L_Q_B, L_K_W, L_K_B, L_V_W, L_V_B, L_O_W, L_O_B,
+  L_SG_COMPRESS, L_SG_W1, L_SG_B1, L_SG_LN1_G, L_SG_LN1_B, L_SG_W2, L_SG_B2, L_SG_LN2_G, L_SG_LN2_B,
+  L_LN1_G, L_LN1_B, L_FFN_W1, L_FFN_B1, L_FFN_W2, L_FFN_B2, L_LN2_G, L_LN2_B, L_COUNT
+};
+
+typedef struct {
+  int d, layers, heads, dff, emb_dff, pe;
+  int sg_compress, sg_hidden, sg_gen;
+  int dp, val_emb, val_hidden, mov_emb, mov_hidden;
+  int act_default, act_smolgen, act_ffn;
+} bt4o_config;
+
+int bt4o_slot_counts(int *globals, int *per_layer) {
+  *globals = G_COUNT;
+  *per_layer = L_COUNT;
+  return 0;
+}
+
+/* ActivationValue, src/nn/cpu/cpu_network.cpp:303-324. */
+static float act(float v, int kind) {
+  switch (kind) {
+  case ACT_RELU: return v > 0.0f ? v : 0.0f;
+  case ACT_RELU2: { const float r = v > 0.0f ? v : 0.0f; return r * r; }
+  case ACT_TANH: return tanhf(v);
+  case ACT_SIGMOID: return 1.0f / (1.0f + expf(-v));
+  case ACT_SWISH: return v / (1.0f + expf(-v));
+  case ACT_MISH: return v * tanhf(log1pf(expf(v)));
+  case ACT_SELU: return 1.05070098f * (v > 0.0f ? v : 1.67326324f * (expf(v) - 1.0f));
+  default: return v;
+  }
+}
+
+static void act_n(float *x, size_t n, int kind) {
+  if (kind == ACT_NONE) return;
+  for (size_t i = 0; i < n; ++i) x[i] = act(x[i], kind);
+}
+
+/* DenseAffine, src/nn/cpu/cpu_network.cpp:382-403 (sum starts at the bias). */
+static void dense(const float *in, int rows, int k, const float *w, const float *b, int n,
+                  float *out) {
+  for (int r = 0; r < rows; ++r) {
+    const float *x = in + (size_t)r * k;
+    float *y = out + (size_t)r * n;
+    for (int o = 0; o < n; ++o) {
+      const float *wr = w + (size_t)o * k;
+      float s = b ? b[o] : 0.0f;
+      for (int i = 0; i < k; ++i) s += x[i] * wr[i];
+      y[o] = s;
+    }
+  }
+}
+
+/* ApplySoftmaxRows, src/nn/cpu/cpu_network.cpp:405-422. */
+static void softmax_rows(float *v, int rows, int width) {
+  for (int r = 0; r < rows; ++r) {
+    float *x = v + (size_t)r * width;
+    float m = -INFINITY;
+    for (int c = 0; c < width; ++c) m = x[c] > m ? x[c] : m;
+    float s = 0.0f;
+    for (int c = 0; c < width; ++c) { x[c] = expf(x[c] - m); s += x[c]; }
+    if (s == 0.0f) continue;
+    const float inv = 1.0f / s;
+    for (int c = 0; c < width; ++c) x[c] *= inv;
+  }
+}
+
+/* ApplyLayerNorm, src/nn/cpu/cpu_network.cpp:424-460 (one-pass variance). */
+static void layernorm(const float *in, const float *parent, float alpha, const float *g,
+                      const float *b, float *out, int rows, int width, float eps) {
+  for (int r = 0; r < rows; ++r) {
+    const float *x = in + (size_t)r * width;
+    const float *p = parent ? parent + (size_t)r * width : NULL;
+    float *y = out + (size_t)r * width;
+    float s = 0.0f, sq = 0.0f;
+    for (int c = 0; c < width; ++c) {
+      const float v = p ? p[c] + x[c] * alpha : x[c];
+      s += v;
+      sq += v * v;
+    }
+    const float mean = s / (float)width;
+    float var = sq / (float)width - mean * mean;
+    if (var < 0.0f) var = 0.0f;
+    const float inv = 1.0f / sqrtf(var + eps);
+    for (int c = 0; c < width; ++c) {
+      const float v = p ? p[c] + x[c] * alpha : x[c];
+      y[c] = (v - mean) * inv * g[c] + b[c];
+    }
+  }
+}
+
+/* Attention-policy gather table: raw index (64*64 + 8*24) -> policy index.
+ * Generated from the move geometry of the 1858-entry policy encoding
+ * (src/nn/policy_map.cpp kMoveStrings order; table src/nn/tables/
+ * attention_policy_map.h:15): for every from-square in ascending order, every
+ * to-square in ascending order that a queen or knight reaches; then the
+ * underpromotions from the 7th rank, laid out as from_file*24 + to_file*3 +
+ * piece, for |to_file - from_file| <= 1. */
+int bt4o_build_policy_map(int16_t *table /* 4288 */) {
+  int next = 0;
+  for (int i = 0; i < 4288; ++i) table[i] = -1;
+  for (int from = 0; from < 64; ++from) {
+    const int fr = from / 8, ff = from % 8;
+    for (int to = 0; to < 64; ++to) {
+      if (to == from) continue;
+      const int tr = to / 8, tf = to % 8;
+      const int dr = tr - fr, df = tf - ff;
+      const int adr = dr < 0 ? -dr : dr, adf = df < 0 ? -df : df;
+      const int queen = dr == 0 || df == 0 || adr == adf;
+      const int knight = (adr == 1 && adf == 2) || (adr == 2 && adf == 1);
+      if (queen || knight) table[from * 64 + to] = (int16_t)next++;
+    }
+  }
+  for (int ff = 0; ff < 8; ++ff)
+    for (int tf = 0; tf < 8; ++tf)
+      for (int piece = 0; piece < 3; ++piece) {
+        const int df = tf - ff;
+        if (df >= -1 && df <= 1) table[4096 + ff * 24 + tf * 3 + piece] = (int16_t)next++;
+      }
+  return next; /* 1858 */
+}
+
+/* Attention policy map, src/nn/cpu/cpu_network.cpp:892-1025: raw[q*64+k] =
+ * (q.k) / sqrt(dq), the 8x24 promotion logits, then the 1858 gather. q and k
+ * are [64, dq] for one position, ppo is ip4_pol_w [4, dq]. */
+static int16_t g_gather[1858];
+static pthread_once_t g_gather_once = PTHREAD_ONCE_INIT;
+static void init_gather(void) {
+  int16_t t[4288];
+  bt4o_build_policy_map(t);
+  for (int i = 0; i < 1858; ++i) g_gather[i] = -1;
+  for (int r = 0; r < 4288; ++r)
+    if (t[r] >= 0) g_gather[t[r]] = (int16_t)r;
+}
+
+void bt4o_policy_map(const float *q, const float *k, const float *ppo, int dq, float *out1858) {
+  pthread_once(&g_gather_once, init_gather);
+  const int16_t *gather = g_gather;
+  float raw[4288];
+  const float scale = 1.0f / sqrtf((float)dq);
+  for (int qs = 0; qs < 64; ++qs)
+    for (int ks = 0; ks < 64; ++ks) {
+      float s = 0.0f;
+      for (int c = 0; c < dq; ++c) s += q[qs * dq + c] * k[ks * dq + c];
+      raw[qs * 64 + ks] = s * scale;
+    }
+  for (int promo = 0; promo < 192; ++promo) {
+    const int prow = promo % 3;
+    const int pks = 56 + (promo % 24) / 3;
+    const int pair = promo % 64;
+    const int qs = 48 + pair / 8;
+    const int ks = 56 + pair % 8;
+    float v = 0.0f;
+    for (int c = 0; c < dq; ++c) {
+      v += q[qs * dq + c] * k[ks * dq + c] * scale;
+      v += k[pks * dq + c] * (ppo[prow * dq + c] + ppo[3 * dq + c]);
+    }
+    raw[4096 + promo] = v;
+  }
+  for (int p = 0; p < 1858; ++p) out1858[p] = gather[p] >= 0 ? raw[gather[p]] : 0.0f;
+}
+
+/* One attention block (src/nn/cpu/cpu_network.cpp:1037-1265) for one position:
+ * x [64, d] -> out [64, d] (before the residual LN). */
+static void attention(const bt4o_config *c, const float *const *L, const float *sgw,
+                      const float *x, float *out, float *scratch) {
+  const int d = c->d, H = c->heads, dh = d / H, T = 64;
+  float *q = scratch, *k = q + T * d, *v = k + T * d;
+  float *comp = v + T * d;                         /* [64, c] */
+  float *h1 = comp + T * c->sg_compress;           /* [hidden] */
+  float *n1 = h1 + c->sg_hidden;
+  float *h2 = n1 + c->sg_hidden;                   /* [H*g] */
+  float *n2 = h2 + H * c->sg_gen;
+  float *bias = n2 + H * c->sg_gen;                /* [H, 64*64] */
+  float *scores = bias + (size_t)H * T * T;        /* [H*64, 64] */
+  float *ctx = scores + (size_t)H * T * T;         /* [64, d] */
+  dense(x, T, d, L[L_Q_W], L[L_Q_B], d, q);
+  dense(x, T, d, L[L_K_W], L[L_K_B], d, k);
+  dense(x, T, d, L[L_V_W], L[L_V_B], d, v);
+  /* smolgen (:1143-1172): dense + separate bias add, activation, LN eps 1e-3 */
+  dense(x, T, d, L[L_SG_COMPRESS], NULL, c->sg_compress, comp);
+  dense(comp, 1, T * c->sg_compress, L[L_SG_W1], NULL, c->sg_hidden, h1);
+  for (int i = 0; i < c->sg_hidden; ++i) h1[i] += L[L_SG_B1][i];
+  act_n(h1, (size_t)c->sg_hidden, c->act_smolgen);
+  layernorm(h1, NULL, 1.0f, L[L_SG_LN1_G], L[L_SG_LN1_B], n1, 1, c->sg_hidden, 1e-3f);
+  dense(n1, 1, c->sg_hidden, L[L_SG_W2], NULL, H * c->sg_gen, h2);
+  for (int i = 0; i < H * c->sg_gen; ++i) h2[i] += L[L_SG_B2][i];
+  act_n(h2, (size_t)H * c->sg_gen, c->act_smolgen);
+  layernorm(h2, NULL, 1.0f, L[L_SG_LN2_G], L[L_SG_LN2_B], n2, 1, H * c->sg_gen, 1e-3f);
+  dense(n2, H, c->sg_gen, sgw, NULL, T * T, bias);
+  /* scores + bias, softmax, context (:1175-1254) */
+  const float scale = 1.0f / sqrtf((float)dh);
+  for (int h = 0; h < H; ++h)
+    for (int qs = 0; qs < T; ++qs)
+      for (int ks = 0; ks < T; ++ks) {
+        float s = 0.0f;
+        for (int e = 0; e < dh; ++e) s += q[qs * d + h * dh + e] * k[ks * d + h * dh + e];
+        s *= scale;
+        s += bias[(size_t)h * T * T + qs * T + ks];
+        scores[((size_t)h * T + qs) * T + ks] = s;
+      }
+  softmax_rows(scores, H * T, T);
+  for (int qs = 0; qs < T; ++qs)
+    for (int h = 0; h < H; ++h) {
+      const float *p = scores + ((size_t)h * T + qs) * T;
+      for (int e = 0; e < dh; ++e) {
+        float s = 0.0f;
+        for (int ks = 0; ks < T; ++ks) s += p[ks] * v[ks * d + h * dh + e];
+        ctx[qs * d + h * dh + e] = s;
+      }
+    }
+  dense(ctx, T, d, L[L_O_W], L[L_O_B], d, out);
+}
+
+static size_t scratch_floats(const bt4o_config *c) {
+  const size_t T = 64, d = (size_t)c->d, H = (size_t)c->heads;
+  const size_t wide = (size_t)(c->dff > c->emb_dff ? c->dff : c->emb_dff);
+  size_t attn = 3 * T * d + T * (size_t)c->sg_compress + 2 * (size_t)c->sg_hidden +
+                2 * H * (size_t)c->sg_gen + 2 * H * T * T + T * d;
+  size_t ffn = T * wide;
+  size_t pol = 3 * T * (size_t)c->dp;
+  size_t m = attn > ffn ? attn : ffn;
+  return (m > pol ? m : pol) + 64;
+}
+
+/* Forward of one position, src/nn/cpu/cpu_network.cpp:580-1491 over the plan
+ * of src/nn/network_execution_plan.cpp:155-223. */
+static void forward_one(const bt4o_config *c, const float *const *G, const float *const *Ls,
+                        const uint64_t *masks, const float *values, float *policy, float *wdl,
+                        float *value, float *mlh, float *buf) {
+  const int d = c->d, T = 64, P = 112;
+  const size_t sc = scratch_floats(c);
+  float *x = buf, *y = x + T * d, *t = y + T * d, *s = t + T * d;
+  (void)sc;
+  /* dynamic PE (:691-800): square-major 12-plane input, dense, concat */
+  float pin[64 * 12];
+  for (int sq = 0; sq < T; ++sq)
+    for (int p = 0; p < 12; ++p)
+      pin[sq * 12 + p] = ((masks[p] >> sq) & 1ULL) ? values[p] : 0.0f;
+  float *pout = s;                                        /* [64*pe] */
+  dense(pin, 1, T * 12, G[G_PREPROC_W], G[G_PREPROC_B], T * c->pe, pout);
+  const int cw = P + c->pe;
+  float *cat = pout + T * c->pe;                          /* [64, 112+pe] */
+  for (int sq = 0; sq < T; ++sq) {
+    for (int p = 0; p < P; ++p) cat[sq * cw + p] = ((masks[p] >> sq) & 1ULL) ? values[p] : 0.0f;
+    for (int e = 0; e < c->pe; ++e) cat[sq * cw + P + e] = pout[sq * c->pe + e];
+  }
+  /* input embedding dense + default activation (:822-890, plan :1115-1116) */
+  dense(cat, T, cw, G[G_EMB_W], G[G_EMB_B], d, t);
+  act_n(t, (size_t)T * d, c->act_default);
+  /* LN eps 1e-3 for PE_DENSE (plan :1175-1182) */
+  layernorm(t, NULL, 1.0f, G[G_EMB_LN_G], G[G_EMB_LN_B], x, T, d, 1e-3f);
+  /* gates, channel-major [d][64] (:1268-1316): multiply, then add */
+  for (int r = 0; r < T; ++r)
+    for (int col = 0; col < d; ++col) x[r * d + col] = x[r * d + col] * G[G_MULT_GATE][col * T + r];
+  for (int r = 0; r < T; ++r)
+    for (int col = 0; col < d; ++col) x[r * d + col] = x[r * d + col] + G[G_ADD_GATE][col * T + r];
+  const float alpha = powf(2.0f * (float)c->layers, -0.25f); /* plan :1152-1162 */
+  /* input embedding FFN + LN(x + alpha*ffn) eps 1e-3 (:1318-1397, :1423-1435) */
+  {
+    float *hid = s;
+    dense(x, T, d, G[G_EFFN_W1], G[G_EFFN_B1], c->emb_dff, hid);
+    act_n(hid, (size_t)T * c->emb_dff, c->act_ffn);
+    dense(hid, T, c->emb_dff, G[G_EFFN_W2], G[G_EFFN_B2], d, t);
+    layernorm(t, x, alpha, G[G_EFFN_LN_G], G[G_EFFN_LN_B], y, T, d, 1e-3f);
+    float *sw = x; x = y; y = sw;
+  }
+  for (int l = 0; l < c->layers; ++l) {
+    const float *const *L = Ls + (size_t)l * L_COUNT;
+    attention(c, L, G[G_SMOLGEN_W], x, t, s);
+    layernorm(t, x, alpha, L[L_LN1_G], L[L_LN1_B], y, T, d, 1e-3f); /* ln1 (:1436-1447) */
+    float *hid = s;
+    dense(y, T, d, L[L_FFN_W1], L[L_FFN_B1], c->dff, hid);
+    act_n(hid, (size_t)T * c->dff, c->act_ffn);
+    dense(hid, T, c->dff, L[L_FFN_W2], L[L_FFN_B2], d, t);
+    layernorm(t, y, alpha, L[L_LN2_G], L[L_LN2_B], x, T, d, 1e-3f); /* ln2 */
+  }
+  /* attention policy head (plan :192-211; activations :1083-1096) */
+  {
+    const int dp = c->dp;
+    float *e = s, *q = e + T * dp, *k = q + T * dp;
+    dense(x, T, d, G[G_POL_W], G[G_POL_B], dp, e);
+    act_n(e, (size_t)T * dp, c->act_default);
+    dense(e, T, dp, G[G_POL_WQ], G[G_POL_BQ], dp, q);
+    dense(e, T, dp, G[G_POL_WK], G[G_POL_BK], dp, k);
+    bt4o_policy_map(q, k, G[G_POL_PPO], dp, policy);
+  }
+  /* value head (plan :213-223, :1098-1106): per square, flatten, softmax WDL */
+  {
+    float *ve = s, *v1 = ve + T * c->val_emb;
+    dense(x, T, d, G[G_VAL_W], G[G_VAL_B], c->val_emb, ve);
+    act_n(ve, (size_t)T * c->val_emb, c->act_default);
+    dense(ve, 1, T * c->val_emb, G[G_VAL_W1], G[G_VAL_B1], c->val_hidden, v1);
+    act_n(v1, (size_t)c->val_hidden, c->act_default);
+    dense(v1, 1, c->val_hidden, G[G_VAL_W2], G[G_VAL_B2], 3, wdl);
+    softmax_rows(wdl, 1, 3);
+    *value = wdl[0] - wdl[2]; /* src/nn/network_output_decoder.cpp:60-66 */
+  }
+  /* moves-left head (plan :184-190, :1108-1111) */
+  {
+    float *me = s, *m1 = me + T * c->mov_emb;
+    dense(x, T, d, G[G_MOV_W], G[G_MOV_B], c->mov_emb, me);
+    act_n(me, (size_t)T * c->mov_emb, c->act_default);
+    dense(me, 1, T * c->mov_emb, G[G_MOV_W1], G[G_MOV_B1], c->mov_hidden, m1);
+    act_n(m1, (size_t)c->mov_hidden, c->act_default);
+    dense(m1, 1, c->mov_hidden, G[G_MOV_W2], G[G_MOV_B2], 1, mlh);
+    act_n(mlh, 1, ACT_RELU);
+  }
+}
+
+typedef struct {
+  const bt4o_config *c;
+  const float *const *G, *const *L;
+  const uint64_t *masks;
+  const float *values;
+  float *policy, *wdl, *value, *mlh;
+  int lo, hi, status;
+} job_t;
+
+static void *worker(void *arg) {
+  job_t *j = (job_t *)arg;
+  const bt4o_config *c = j->c;
+  const size_t n = 3 * 64 * (size_t)c->d + scratch_floats(c) + 64 * (size_t)(112 + c->pe) +
+                   64 * (size_t)c->pe + 256;
+  float *buf = (float *)malloc(n * sizeof(float));
+  if (!buf) { j->status = -1; return NULL; }
+  for (int b = j->lo; b < j->hi; ++b)
+    forward_one(c, j->G, j->L, j->masks + (size_t)b * 112, j->values + (size_t)b * 112,
+                j->policy + (size_t)b * 1858, j->wdl + (size_t)b * 3, j->value + b, j->mlh + b,
+                buf);
+  free(buf);
+  return NULL;
+}
+
+/* Batched forward. G: G_COUNT tensor pointers; L: layers * L_COUNT pointers. */
+int bt4o_forward(const bt4o_config *c, const float *const *G, const float *const *L,
+                 const uint64_t *masks, const float *values, int batch, float *policy, float *wdl,
+                 float *value, float *mlh, int threads) {
+  if (batch <= 0) return 0;
+  if (threads < 1) threads = 1;
+  if (threads > batch) threads = batch;
+  pthread_t tid[256];
+  job_t jobs[256];
+  if (threads > 256) threads = 256;
+  for (int t = 0; t < threads; ++t) {
+    jobs[t] = (job_t){c, G, L, masks, values, policy, wdl, value, mlh,
+                      (int)((int64_t)batch * t / threads), (int)((int64_t)batch * (t + 1) / threads), 0};
+    pthread_create(&tid[t], NULL, worker, &jobs[t]);
+  }
+  int status = 0;
+  for (int t = 0; t < threads; ++t) {
+    pthread_join(tid[t], NULL);
+    if (jobs[t].status) status = jobs[t].status;
+  }
+  return status;
+}

@@ -1,0 +1,406 @@
+// Reference harness -- TEST INFRASTRUCTURE ONLY (never linked into the product).
+//
+// Drives the reference's own, unmodified CPU code (compiled from the
+// reference source tree against the protobuf shim in oracle/shim):
+//
+//   gen-inputs <seed> <count> <out.mfin>
+//       Seeded uniform-random legal playouts of 0-80 plies from the start
+//       position (per-position RNG seed = seed XOR index, std::mt19937_64),
+//       encoded with EncodePositionForNN(INPUT_112_WITH_CANONICALIZATION_V2,
+//       history <= 8, FillEmptyHistory::FEN_ONLY) -- the call the reference
+//       benchmark makes (tests/test_nn_comparison.cpp:1518-1524) -- and packed
+//       with PackInputPlanesRaw (src/nn/input_plane_packing.h:63-83).
+//
+//   eval <net.mfnt> <in.mfin> <out.mfot> [threads] [first] [count]
+//       Builds a MetalFishNN::Net in memory with FLOAT32 layers (the pattern of
+//       tests/test_mcts_module.cpp:91-103), constructs the reference
+//       Cpu::CpuNetwork through NN::CreateNetwork(weights, "cpu")
+//       (src/nn/network.cpp:188-190) and runs EvaluateBatch on contiguous
+//       chunks, one std::thread per chunk (CpuNetwork::RunBatch is const and
+//       reentrant, src/nn/cpu/cpu_network.cpp:580). Prints one JSON line with
+//       the wall time of the EvaluateBatch calls.
+//
+//   to-pb <net.mfnt> <out.pb>
+//       Serialises the same in-memory Net as a protobuf .pb weights file.
+//
+// File formats (all little-endian) are produced/consumed by
+// metalfish_b200/netfile.py.
+#include "nn/encoder.h"
+#include "nn/input_plane_packing.h"
+#include "nn/network.h"
+#include "core/bitboard.h"
+#include "core/movegen.h"
+#include "core/position.h"
+
+#include <chrono>
+#include <cstdio>
+#include <cstring>
+#include <deque>
+#include <fstream>
+#include <iostream>
+#include <map>
+#include <random>
+#include <sstream>
+#include <stdexcept>
+#include <string>
+#include <thread>
+#include <vector>
+
+using namespace MetalFish;
+namespace NN = MetalFish::NN;
+
+namespace {
+
+constexpr char kStartFen[] = "rnbqkbnr/pppppppp/8/8/8/8/PPPPPPPP/RNBQKBNR w KQkq - 0 1";
+
+std::string ReadFile(const std::string &path) {
+  std::ifstream in(path, std::ios::binary);
+  if (!in) throw std::runtime_error("cannot open " + path);
+  return std::string((std::istreambuf_iterator<char>(in)), std::istreambuf_iterator<char>());
+}
+
+struct Reader {
+  const std::string &s;
+  std::size_t off = 0;
+  template <class T> T get() {
+    if (off + sizeof(T) > s.size()) throw std::runtime_error("truncated file");
+    T v; std::memcpy(&v, s.data() + off, sizeof(T)); off += sizeof(T); return v;
+  }
+  std::string bytes(std::size_t n) {
+    if (off + n > s.size()) throw std::runtime_error("truncated file");
+    std::string r = s.substr(off, n); off += n; return r;
+  }
+};
+
+// ------------------------------------------------------------------ inputs
+struct Inputs {
+  std::vector<std::uint64_t> masks;
+  std::vector<float> values;
+  int count = 0;
+};
+
+Inputs ReadInputs(const std::string &path) {
+  const std::string s = ReadFile(path);
+  Reader r{s};
+  if (r.bytes(4) != "MFIN") throw std::runtime_error("bad input magic");
+  (void)r.get<std::uint32_t>();
+  Inputs in;
+  in.count = int(r.get<std::uint32_t>());
+  const std::uint32_t planes = r.get<std::uint32_t>();
+  if (planes != 112) throw std::runtime_error("bad plane count");
+  in.masks.resize(std::size_t(in.count) * 112);
+  in.values.resize(std::size_t(in.count) * 112);
+  std::memcpy(in.masks.data(), r.bytes(in.masks.size() * 8).data(), in.masks.size() * 8);
+  std::memcpy(in.values.data(), r.bytes(in.values.size() * 4).data(), in.values.size() * 4);
+  return in;
+}
+
+NN::InputPlanes Unpack(const Inputs &in, int b) {
+  NN::InputPlanes planes{};
+  for (int p = 0; p < 112; ++p) {
+    const std::uint64_t m = in.masks[std::size_t(b) * 112 + p];
+    const float v = in.values[std::size_t(b) * 112 + p];
+    for (int sq = 0; sq < 64; ++sq) planes[p][sq] = ((m >> sq) & 1ULL) ? v : 0.0f;
+  }
+  return planes;
+}
+
+int GenInputs(std::uint64_t seed, int count, const std::string &out_path) {
+  Bitboards::init();
+  Position::init();
+  std::vector<std::uint64_t> masks(std::size_t(count) * 112);
+  std::vector<float> values(std::size_t(count) * 112);
+  for (int i = 0; i < count; ++i) {
+    std::mt19937_64 rng(seed ^ std::uint64_t(i));
+    const int target_plies = int(rng() % 81);
+    // Play the line once to fix the moves.
+    std::vector<Move> line;
+    {
+      Position pos;
+      StateInfo root;
+      std::deque<StateInfo> states;
+      pos.set(kStartFen, false, &root);
+      for (int ply = 0; ply < target_plies; ++ply) {
+        MoveList<LEGAL> legal(pos);
+        if (legal.size() == 0) break;
+        const Move m = *(legal.begin() + (rng() % legal.size()));
+        line.push_back(m);
+        states.emplace_back();
+        pos.do_move(m, states.back());
+      }
+    }
+    // Rebuild the full game history, each position replayed from the start so
+    // that every Position keeps its own StateInfo chain (as build_history does
+    // in tests/test_nn_comparison.cpp:280-302). The whole line is needed: the
+    // canonical-v2 encoder skips non-repeating positions and may look back
+    // past the last eight plies (src/nn/encoder.cpp:371-400).
+    const int total = int(line.size());
+    const int first = 0;
+    std::vector<std::unique_ptr<Position>> positions;
+    std::vector<std::unique_ptr<StateInfo>> roots;
+    std::vector<std::deque<StateInfo>> stacks(total - first + 1);
+    std::vector<const Position *> ptrs;
+    for (int ply = first; ply <= total; ++ply) {
+      positions.push_back(std::make_unique<Position>());
+      roots.push_back(std::make_unique<StateInfo>());
+      positions.back()->set(kStartFen, false, roots.back().get());
+      auto &stack = stacks[ply - first];
+      for (int k = 0; k < ply; ++k) {
+        stack.emplace_back();
+        positions.back()->do_move(line[k], stack.back());
+      }
+      ptrs.push_back(positions.back().get());
+    }
+    int transform = 0;
+    const NN::InputPlanes planes = NN::EncodePositionForNN(
+        MetalFishNN::NetworkFormat::INPUT_112_WITH_CANONICALIZATION_V2, ptrs,
+        NN::kMoveHistory, NN::FillEmptyHistory::FEN_ONLY, &transform);
+    std::vector<std::uint64_t> m;
+    std::vector<float> v;
+    NN::PackInputPlanesRaw(planes[0].data(), 1, m, v);
+    std::memcpy(&masks[std::size_t(i) * 112], m.data(), 112 * 8);
+    std::memcpy(&values[std::size_t(i) * 112], v.data(), 112 * 4);
+  }
+  std::ofstream out(out_path, std::ios::binary);
+  const std::uint32_t hdr[3] = {1, std::uint32_t(count), 112};
+  out.write("MFIN", 4);
+  out.write(reinterpret_cast<const char *>(hdr), sizeof(hdr));
+  out.write(reinterpret_cast<const char *>(masks.data()), masks.size() * 8);
+  out.write(reinterpret_cast<const char *>(values.data()), values.size() * 4);
+  return out.good() ? 0 : 1;
+}
+
+// ------------------------------------------------------------------ network
+MetalFishNN::NetworkFormat_ActivationFunction ActivationByName(const std::string &n) {
+  using NF = MetalFishNN::NetworkFormat;
+  if (n == "mish") return NF::ACTIVATION_MISH;
+  if (n == "relu") return NF::ACTIVATION_RELU;
+  if (n == "swish") return NF::ACTIVATION_SWISH;
+  if (n == "relu_2") return NF::ACTIVATION_RELU_2;
+  if (n == "selu") return NF::ACTIVATION_SELU;
+  if (n == "tanh") return NF::ACTIVATION_TANH;
+  if (n == "sigmoid") return NF::ACTIVATION_SIGMOID;
+  if (n == "default" || n.empty()) return NF::ACTIVATION_DEFAULT;
+  throw std::runtime_error("unknown activation " + n);
+}
+
+using Layer = MetalFishNN::Weights::Layer;
+
+Layer *SmolgenLayer(MetalFishNN::Weights::Smolgen *s, const std::string &f) {
+  if (f == "compress") return s->mutable_compress();
+  if (f == "dense1_w") return s->mutable_dense1_w();
+  if (f == "dense1_b") return s->mutable_dense1_b();
+  if (f == "ln1_gammas") return s->mutable_ln1_gammas();
+  if (f == "ln1_betas") return s->mutable_ln1_betas();
+  if (f == "dense2_w") return s->mutable_dense2_w();
+  if (f == "dense2_b") return s->mutable_dense2_b();
+  if (f == "ln2_gammas") return s->mutable_ln2_gammas();
+  if (f == "ln2_betas") return s->mutable_ln2_betas();
+  return nullptr;
+}
+
+Layer *FfnLayer(MetalFishNN::Weights::FFN *f, const std::string &n) {
+  if (n == "dense1_w") return f->mutable_dense1_w();
+  if (n == "dense1_b") return f->mutable_dense1_b();
+  if (n == "dense2_w") return f->mutable_dense2_w();
+  if (n == "dense2_b") return f->mutable_dense2_b();
+  return nullptr;
+}
+
+std::vector<std::string> Split(const std::string &s) {
+  std::vector<std::string> parts;
+  std::stringstream ss(s);
+  std::string p;
+  while (std::getline(ss, p, '.')) parts.push_back(p);
+  return parts;
+}
+
+Layer *ResolveLayer(MetalFishNN::Weights *w, const std::string &name) {
+  const auto p = Split(name);
+  if (p.size() == 1) {
+    const std::string &n = p[0];
+#define TOP(x) if (n == #x) return w->mutable_##x();
+    TOP(ip_emb_preproc_w) TOP(ip_emb_preproc_b) TOP(ip_emb_w) TOP(ip_emb_b)
+    TOP(ip_emb_ln_gammas) TOP(ip_emb_ln_betas) TOP(ip_mult_gate) TOP(ip_add_gate)
+    TOP(ip_emb_ffn_ln_gammas) TOP(ip_emb_ffn_ln_betas) TOP(smolgen_w)
+    TOP(ip_mov_w) TOP(ip_mov_b) TOP(ip1_mov_w) TOP(ip1_mov_b) TOP(ip2_mov_w) TOP(ip2_mov_b)
+#undef TOP
+    return nullptr;
+  }
+  if (p[0] == "ip_emb_ffn" && p.size() == 2) return FfnLayer(w->mutable_ip_emb_ffn(), p[1]);
+  if (p[0] == "encoder" && p.size() >= 3) {
+    const int idx = std::stoi(p[1]);
+    while (w->encoder_size() <= idx) w->add_encoder();
+    auto *enc = w->mutable_encoder(idx);
+    if (p.size() == 3) {
+      if (p[2] == "ln1_gammas") return enc->mutable_ln1_gammas();
+      if (p[2] == "ln1_betas") return enc->mutable_ln1_betas();
+      if (p[2] == "ln2_gammas") return enc->mutable_ln2_gammas();
+      if (p[2] == "ln2_betas") return enc->mutable_ln2_betas();
+      return nullptr;
+    }
+    if (p[2] == "ffn" && p.size() == 4) return FfnLayer(enc->mutable_ffn(), p[3]);
+    if (p[2] == "mha" && p.size() == 4) {
+      auto *m = enc->mutable_mha();
+      const std::string &n = p[3];
+#define MHA(x) if (n == #x) return m->mutable_##x();
+      MHA(q_w) MHA(q_b) MHA(k_w) MHA(k_b) MHA(v_w) MHA(v_b) MHA(dense_w) MHA(dense_b)
+#undef MHA
+      return nullptr;
+    }
+    if (p[2] == "mha" && p.size() == 5 && p[3] == "smolgen")
+      return SmolgenLayer(enc->mutable_mha()->mutable_smolgen(), p[4]);
+    return nullptr;
+  }
+  if (p[0] == "policy_heads" && p.size() == 3 && p[1] == "vanilla") {
+    auto *h = w->mutable_policy_heads()->mutable_vanilla();
+    const std::string &n = p[2];
+#define POL(x) if (n == #x) return h->mutable_##x();
+    POL(ip_pol_w) POL(ip_pol_b) POL(ip2_pol_w) POL(ip2_pol_b) POL(ip3_pol_w) POL(ip3_pol_b)
+    POL(ip4_pol_w)
+#undef POL
+    return nullptr;
+  }
+  if (p[0] == "value_heads" && p.size() == 3 && p[1] == "winner") {
+    auto *h = w->mutable_value_heads()->mutable_winner();
+    const std::string &n = p[2];
+#define VAL(x) if (n == #x) return h->mutable_##x();
+    VAL(ip_val_w) VAL(ip_val_b) VAL(ip1_val_w) VAL(ip1_val_b) VAL(ip2_val_w) VAL(ip2_val_b)
+#undef VAL
+    return nullptr;
+  }
+  return nullptr;
+}
+
+NN::WeightsFile ReadNet(const std::string &path) {
+  const std::string s = ReadFile(path);
+  Reader r{s};
+  if (r.bytes(4) != "MFNT") throw std::runtime_error("bad net magic");
+  (void)r.get<std::uint32_t>();
+  const std::uint32_t header_len = r.get<std::uint32_t>();
+  std::map<std::string, std::string> header;
+  {
+    std::stringstream hs(r.bytes(header_len));
+    std::string line;
+    while (std::getline(hs, line)) {
+      const auto eq = line.find('=');
+      if (eq != std::string::npos) header[line.substr(0, eq)] = line.substr(eq + 1);
+    }
+  }
+  NN::WeightsFile file;
+  file.set_magic(0x1c0);
+  using NF = MetalFishNN::NetworkFormat;
+  auto *nf = file.mutable_format()->mutable_network_format();
+  nf->set_input(NF::INPUT_112_WITH_CANONICALIZATION_V2);
+  nf->set_output(NF::OUTPUT_WDL);
+  nf->set_network(NF::NETWORK_ATTENTIONBODY_WITH_MULTIHEADFORMAT);
+  nf->set_policy(NF::POLICY_ATTENTION);
+  nf->set_value(NF::VALUE_WDL);
+  nf->set_moves_left(NF::MOVES_LEFT_V1);
+  nf->set_input_embedding(NF::INPUT_EMBEDDING_PE_DENSE);
+  nf->set_default_activation(header["default_activation"] == "relu"
+                                 ? NF::DEFAULT_ACTIVATION_RELU
+                                 : NF::DEFAULT_ACTIVATION_MISH);
+  nf->set_smolgen_activation(ActivationByName(header["smolgen_activation"]));
+  nf->set_ffn_activation(ActivationByName(header["ffn_activation"]));
+  auto *w = file.mutable_weights();
+  w->set_headcount(std::uint32_t(std::stoul(header.at("heads"))));
+  const std::uint32_t count = r.get<std::uint32_t>();
+  for (std::uint32_t t = 0; t < count; ++t) {
+    const std::string name = r.bytes(r.get<std::uint32_t>());
+    const std::uint32_t ndims = r.get<std::uint32_t>();
+    std::vector<std::uint32_t> dims(ndims);
+    std::size_t elements = 1;
+    for (auto &d : dims) { d = r.get<std::uint32_t>(); elements *= d; }
+    Layer *layer = ResolveLayer(w, name);
+    if (!layer) throw std::runtime_error("unknown tensor name " + name);
+    layer->set_encoding(Layer::FLOAT32);
+    layer->set_params(r.bytes(elements * 4));
+    layer->clear_dims();
+    for (auto d : dims) layer->add_dims(d);
+  }
+  return file;
+}
+
+int Eval(const std::string &net_path, const std::string &in_path, const std::string &out_path,
+         int threads, int first, int count) {
+  const NN::WeightsFile file = ReadNet(net_path);
+  const Inputs in = ReadInputs(in_path);
+  if (count < 0) count = in.count - first;
+  if (first < 0 || count < 0 || first + count > in.count) throw std::runtime_error("bad range");
+  auto net = NN::CreateNetwork(file, "cpu");
+  std::vector<NN::InputPlanes> planes(count);
+  for (int b = 0; b < count; ++b) planes[b] = Unpack(in, first + b);
+  std::vector<NN::NetworkOutput> outputs(count);
+  threads = std::max(1, std::min(threads, std::max(count, 1)));
+  const auto t0 = std::chrono::steady_clock::now();
+  std::vector<std::thread> pool;
+  std::vector<std::string> errors(threads);
+  for (int t = 0; t < threads; ++t) {
+    pool.emplace_back([&, t] {
+      const int lo = int(std::int64_t(count) * t / threads);
+      const int hi = int(std::int64_t(count) * (t + 1) / threads);
+      if (lo >= hi) return;
+      try {
+        std::vector<NN::InputPlanes> chunk(planes.begin() + lo, planes.begin() + hi);
+        auto res = net->EvaluateBatch(chunk);
+        for (int i = lo; i < hi; ++i) outputs[i] = res[i - lo];
+      } catch (const std::exception &e) {
+        errors[t] = e.what();
+      }
+    });
+  }
+  for (auto &th : pool) th.join();
+  const double secs =
+      std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+  for (const auto &e : errors)
+    if (!e.empty()) throw std::runtime_error(e);
+  std::ofstream out(out_path, std::ios::binary);
+  out.write("MFOT", 4);
+  const std::uint32_t hdr[2] = {1, std::uint32_t(count)};
+  out.write(reinterpret_cast<const char *>(hdr), sizeof(hdr));
+  for (int b = 0; b < count; ++b)
+    out.write(reinterpret_cast<const char *>(outputs[b].policy.data()), NN::kPolicyOutputs * 4);
+  for (int b = 0; b < count; ++b)
+    out.write(reinterpret_cast<const char *>(outputs[b].wdl), 12);
+  for (int b = 0; b < count; ++b)
+    out.write(reinterpret_cast<const char *>(&outputs[b].value), 4);
+  for (int b = 0; b < count; ++b)
+    out.write(reinterpret_cast<const char *>(&outputs[b].moves_left), 4);
+  std::printf("{\"positions\": %d, \"threads\": %d, \"seconds\": %.6f, \"pos_per_s\": %.6f, "
+              "\"info\": \"%s\"}\n",
+              count, threads, secs, secs > 0 ? count / secs : 0.0,
+              net->GetBackendCapabilities().Summary().c_str());
+  return out.good() ? 0 : 1;
+}
+
+int ToPb(const std::string &net_path, const std::string &out_path) {
+  const NN::WeightsFile file = ReadNet(net_path);
+  std::string bytes;
+  file.SerializeToString(&bytes);
+  std::ofstream out(out_path, std::ios::binary);
+  out.write(bytes.data(), std::streamsize(bytes.size()));
+  return out.good() ? 0 : 1;
+}
+
+} // namespace
+
+int main(int argc, char **argv) {
+  try {
+    const std::string cmd = argc > 1 ? argv[1] : "";
+    if (cmd == "gen-inputs" && argc == 5)
+      return GenInputs(std::stoull(argv[2]), std::stoi(argv[3]), argv[4]);
+    if (cmd == "eval" && argc >= 5)
+      return Eval(argv[2], argv[3], argv[4], argc > 5 ? std::stoi(argv[5]) : 1,
+                  argc > 6 ? std::stoi(argv[6]) : 0, argc > 7 ? std::stoi(argv[7]) : -1);
+    if (cmd == "to-pb" && argc == 4) return ToPb(argv[2], argv[3]);
+    std::fprintf(stderr,
+                 "usage: ref_harness gen-inputs <seed> <count> <out.mfin>\n"
+                 "       ref_harness eval <net.mfnt> <in.mfin> <out.mfot> [threads] [first] [count]\n"
+                 "       ref_harness to-pb <net.mfnt> <out.pb>\n");
+    return 2;
+  } catch (const std::exception &e) {
+    std::fprintf(stderr, "ref_harness error: %s\n", e.what());
+    return 1;
+  }
+}

@@ -1,0 +1,95 @@
+"""Pins the C restatement oracle against the reference itself.
+
+The golden fixtures were produced by the reference's own Cpu::CpuNetwork
+(compiled unmodified from the reference sources; tests/golden/make_golden.py).
+The oracle keeps the reference's per-row accumulation order, so it must match
+those outputs bit for bit.
+"""
+import os
+
+import numpy as np
+import pytest
+
+from tests.conftest import GOLDEN, load_golden
+from metalfish_b200 import layout, netfile, synthetic
+from metalfish_b200.synthetic import CONFIGS
+from oracle import port
+from tests.golden.make_golden import weights_digest
+
+
+def test_slot_tables_match_oracle_enums():
+    assert port.slot_counts() == (len(layout.GLOBAL_SLOTS), len(layout.LAYER_SLOTS))
+
+
+def test_policy_gather_table_matches_reference():
+    ref = np.load(os.path.join(GOLDEN, "attn_policy_map.npy"))
+    ours = port.build_policy_map()
+    assert ref.shape == (4288,)
+    assert np.array_equal(ours, ref)
+    assert (ours >= 0).sum() == 1858
+
+
+def test_policy_map_known_answer():
+    """Port of the reference KAT tests/test_mcts_module.cpp:2620-2651 (fixture
+    :443-505): identity embedding and policy projection, wq = plane 0, wk =
+    plane 1, ppo = [1, 3, 5, 0]. The planes go through the input packing, which
+    keeps only the FIRST nonzero value of a plane (plane 1 = {5 @ b1, 7 @ a8}
+    packs to 5 on both squares). Expected: policy[0] (a1b1) = 2*5 = 10 and the
+    mixed promotion logit policy[1793] = 5 * (3 + 0) = 15."""
+    planes = np.zeros((1, 112, 64), np.float32)
+    planes[0, 0, 0] = 2.0
+    planes[0, 1, 1] = 5.0
+    planes[0, 0, 48] = 2.0
+    planes[0, 1, 56] = 7.0
+    packed = netfile.pack_planes(planes)
+    dense = netfile.unpack_planes(packed)[0]
+    q = np.maximum(dense[0], 0)[:, None]   # relu default activation
+    k = np.maximum(dense[1], 0)[:, None]
+    ppo = np.array([[1.0], [3.0], [5.0], [0.0]], np.float32)
+    out = port.policy_map(q, k, ppo)
+    assert abs(out[0] - 10.0) < 1e-5
+    assert abs(out[1793] - 15.0) < 1e-5
+
+
+def test_pack_unpack_matches_reference_fixture(positions):
+    """Unpacking the reference-packed positions and packing them again must
+    reproduce the reference's masks and values exactly."""
+    sub = positions.slice(0, 256)
+    again = netfile.pack_planes(netfile.unpack_planes(sub))
+    np.testing.assert_array_equal(again.masks, sub.masks)
+    np.testing.assert_array_equal(again.values, sub.values)
+
+
+@pytest.mark.parametrize("name", ["tiny", "small", "small_perturbed"])
+def test_oracle_bit_exact_vs_reference(name, positions):
+    g = load_golden(name)
+    cfg = CONFIGS[str(g["config"])]
+    tensors = synthetic.generate(cfg, int(g["weight_seed"]), bool(g["perturb_norms"]))
+    assert weights_digest(tensors) == str(g["weights_sha256"]), "weight generator drifted"
+    n = int(g["positions"])
+    out = port.forward(cfg, tensors, positions.slice(0, n))
+    np.testing.assert_array_equal(out.policy, g["policy"])
+    np.testing.assert_array_equal(out.wdl, g["wdl"])
+    np.testing.assert_array_equal(out.value, g["value"])
+    np.testing.assert_array_equal(out.moves_left, g["moves_left"])
+
+
+def test_oracle_bit_exact_vs_reference_bt4(positions):
+    g = load_golden("bt4")
+    cfg = synthetic.BT4
+    tensors = synthetic.generate(cfg, int(g["weight_seed"]), bool(g["perturb_norms"]))
+    assert weights_digest(tensors) == str(g["weights_sha256"])
+    n = 4
+    out = port.forward(cfg, tensors, positions.slice(0, n), threads=4)
+    np.testing.assert_array_equal(out.policy, g["policy"][:n])
+    np.testing.assert_array_equal(out.wdl, g["wdl"][:n])
+    np.testing.assert_array_equal(out.moves_left, g["moves_left"][:n])
+
+
+def test_golden_outputs_are_sane():
+    for name in ("tiny", "small", "small_perturbed", "bt4"):
+        g = load_golden(name)
+        assert np.isfinite(g["policy"]).all()
+        np.testing.assert_allclose(g["wdl"].sum(1), 1.0, atol=1e-5)
+        np.testing.assert_allclose(g["value"], g["wdl"][:, 0] - g["wdl"][:, 2], atol=1e-6)
+        assert (g["moves_left"] >= 0).all()
