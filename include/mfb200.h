@@ -1,0 +1,129 @@
+/* mfb200.h -- C ABI of the B200 BT4 forward library (libmfb200.so).
+ *
+ * This is the boundary a MetalFish NN backend binds: one handle owns a BT4
+ * attention-body network resident on one or more B200 GPUs and evaluates
+ * batches of packed input planes into raw policy logits, WDL probabilities
+ * and moves-left. Plain pointers and sizes only; no C++ or torch types.
+ *
+ * Reference interfaces replaced (paths in the MetalFish source tree):
+ *   mfb200_create       <- NN::CreateNetwork(const WeightsFile&, const BackendConfig&)
+ *                          (src/nn/network.h:66-75, src/nn/network.cpp:137-208) together
+ *                          with the accelerator constructor Cuda::CudaNetwork
+ *                          (src/nn/cuda/cuda_network.h:26-57, cuda_network.cpp:235-343)
+ *   mfb200_evaluate     <- NN::Network::EvaluateBatch(const std::vector<InputPlanes>&)
+ *                          (src/nn/network.h:44-45); inputs are the packed planes of
+ *                          PackInputPlanesRaw (src/nn/input_plane_packing.h:63-83) that
+ *                          Cuda::CudaNetwork::RunBatch uploads (cuda_network.cpp:393-417);
+ *                          outputs are the fields of NetworkOutput (src/nn/network_output.h:17-24)
+ *   mfb200_capabilities <- NN::Network::GetBackendCapabilities / HasWDL / HasMovesLeft /
+ *                          GetNetworkInfo (src/nn/network.h:21-51)
+ *   mfb200_last_error   <- the std::runtime_error messages the reference throws
+ *                          (src/nn/cuda/cuda_network.cpp:241-320, :457)
+ *   mfb200_destroy      <- Network::~Network (src/nn/network.h:40)
+ *
+ * Status codes: 0 = success, nonzero = error; mfb200_last_error() returns a
+ * message for the calling thread's last failure on that handle.
+ * Thread safety: calls on one handle are serialised by an internal mutex
+ * (as the reference CUDA backend's execution_mutex_, cuda_network.cpp:442).
+ */
+#ifndef MFB200_H
+#define MFB200_H
+#include <stddef.h>
+#include <stdint.h>
+#ifndef MFB200_API
+#define MFB200_API __attribute__((visibility("default")))
+#endif
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct mfb200_handle mfb200_handle;
+
+/* Activation codes (the reference's activation names, network_format.cpp:50-70). */
+enum {
+  MFB200_ACT_NONE = 0, MFB200_ACT_RELU = 1, MFB200_ACT_RELU2 = 2, MFB200_ACT_TANH = 3,
+  MFB200_ACT_SIGMOID = 4, MFB200_ACT_SWISH = 5, MFB200_ACT_MISH = 6, MFB200_ACT_SELU = 7
+};
+enum { MFB200_PRECISION_BF16 = 0, MFB200_PRECISION_FP8 = 1 };
+
+/* Shape of an attention-body network with PE_DENSE input embedding, smolgen,
+ * attention policy, WDL value and moves-left heads (the BT4 family). */
+typedef struct {
+  int32_t embedding;        /* d (multiple of 64; head depth d/heads must be 32) */
+  int32_t layers;           /* encoder layers */
+  int32_t heads;
+  int32_t dff;              /* encoder FFN hidden */
+  int32_t emb_dff;          /* input-embedding FFN hidden */
+  int32_t pe;               /* dynamic positional-encoding width per square */
+  int32_t smolgen_compress; /* per-token compress width */
+  int32_t smolgen_hidden;   /* smolgen dense1 width */
+  int32_t smolgen_gen;      /* per-head generator width */
+  int32_t policy_d;         /* attention-policy embedding width */
+  int32_t value_emb, value_hidden;
+  int32_t mlh_emb, mlh_hidden;
+  int32_t act_default, act_smolgen, act_ffn; /* MFB200_ACT_* */
+} mfb200_net_desc;
+
+typedef struct {
+  int32_t device;     /* first CUDA device ordinal */
+  int32_t num_devices;/* devices used from `device` on; the batch is sharded, weights replicated */
+  int32_t precision;  /* MFB200_PRECISION_* */
+  int32_t max_batch;  /* largest batch one evaluate call accepts */
+  int32_t use_graphs; /* capture one CUDA graph per batch size (1) or launch eagerly (0) */
+} mfb200_config;
+
+typedef struct {
+  float h2d_ms, forward_ms, d2h_ms, total_ms; /* device-timed (max over devices) */
+} mfb200_timing;
+
+typedef struct {
+  int32_t max_batch, precision, num_devices, device;
+  int32_t has_wdl, has_moves_left;
+  int64_t weight_bytes;      /* device bytes of packed weights (per device) */
+  int64_t workspace_bytes;   /* device bytes of activations (per device) */
+  char device_name[96];
+} mfb200_caps;
+
+/* Number of bytes of the fp32 weight blob mfb200_create expects for `desc`:
+ * every tensor of the network in the reference's [out, in] layout,
+ * concatenated in the slot order of metalfish_b200/layout.py. */
+MFB200_API size_t mfb200_weight_bytes(const mfb200_net_desc *desc);
+
+MFB200_API int mfb200_create(const mfb200_net_desc *desc, const void *weights_f32, size_t bytes,
+                  const mfb200_config *cfg, mfb200_handle **out);
+
+/* Host-buffer evaluation (the EvaluateBatch path): masks/values [batch,112]
+ * (packed planes), outputs policy [batch,1858] raw logits, wdl [batch,3],
+ * moves_left [batch]. Any of the output pointers may be NULL. `timing` may
+ * be NULL. Blocks until the results are in host memory. */
+MFB200_API int mfb200_evaluate(mfb200_handle *h, const uint64_t *masks, const float *values, int batch,
+                    float *policy, float *wdl, float *moves_left, mfb200_timing *timing);
+
+/* Device-buffer evaluation on device `cfg.device`, enqueued on `stream`
+ * (a cudaStream_t; NULL = the handle's stream) without synchronising. All
+ * pointers are device pointers of that device. */
+MFB200_API int mfb200_evaluate_device(mfb200_handle *h, const uint64_t *d_masks, const float *d_values,
+                           int batch, float *d_policy, float *d_wdl, float *d_moves_left,
+                           void *stream);
+
+/* FP8 handles only: set the per-tensor activation scales from the absmax of
+ * a bf16 forward over `count` calibration positions (host buffers). Must be
+ * called before the first FP8 evaluation. */
+MFB200_API int mfb200_calibrate(mfb200_handle *h, const uint64_t *masks, const float *values, int count);
+
+MFB200_API int mfb200_capabilities(mfb200_handle *h, mfb200_caps *caps);
+
+/* Per-stage device time of one eager forward at `batch` (inputs already on
+ * the device), for profiling: writes up to `max_stages` entries of ms and
+ * algorithmic FLOPs, and stage names separated by '\n' into `names`.
+ * Returns the number of stages, or a negative value on error. */
+MFB200_API int mfb200_profile(mfb200_handle *h, int batch, int iters, float *stage_ms, double *stage_flops,
+                   char *names, size_t names_len, int max_stages);
+
+MFB200_API const char *mfb200_last_error(mfb200_handle *h);
+MFB200_API void mfb200_destroy(mfb200_handle *h);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MFB200_H */

@@ -1,0 +1,72 @@
+// debug_api.cu -- self-contained kernel entry points for unit tests
+// (include/mfb200_testing.h). Each call allocates its own device buffers,
+// copies host inputs in, runs ONE kernel and copies the result back.
+#include <cuda_fp8.h>
+
+#include <cstring>
+#include <vector>
+
+#include "../../include/mfb200_testing.h"
+#include "gemm_host.h"
+
+using namespace mfb200;
+
+namespace {
+struct DevBuf {
+  void *p = nullptr;
+  ~DevBuf() {
+    if (p) cudaFree(p);
+  }
+  bool alloc(size_t n) { return cudaMalloc(&p, n ? n : 16) == cudaSuccess; }
+};
+}  // namespace
+
+extern "C" int mfb200_debug_gemm(int M, int N, int K, int bn, int fp8, const void *A,
+                                 const void *W, const float *bias, int mode, int act,
+                                 const float *resid, float alpha, const float *ln_gamma,
+                                 const float *ln_beta, float ln_eps, const float *col_scale,
+                                 float a_scale, int out_f32, void *out, unsigned *status_out) {
+  const size_t es = fp8 ? 1 : 2;
+  DevBuf dA, dW, dB, dR, dO, dG, dBe, dCs, dS;
+  if (!dA.alloc(size_t(M) * K * es) || !dW.alloc(size_t(N) * K * es) || !dB.alloc(N * 4) ||
+      !dR.alloc(size_t(M) * N * 4) || !dO.alloc(size_t(M) * N * 4) || !dG.alloc(N * 4) ||
+      !dBe.alloc(N * 4) || !dCs.alloc(N * 4) || !dS.alloc(4))
+    return 1;
+  cudaMemcpy(dA.p, A, size_t(M) * K * es, cudaMemcpyHostToDevice);
+  cudaMemcpy(dW.p, W, size_t(N) * K * es, cudaMemcpyHostToDevice);
+  if (bias) cudaMemcpy(dB.p, bias, N * 4, cudaMemcpyHostToDevice);
+  if (resid) cudaMemcpy(dR.p, resid, size_t(M) * N * 4, cudaMemcpyHostToDevice);
+  if (ln_gamma) cudaMemcpy(dG.p, ln_gamma, N * 4, cudaMemcpyHostToDevice);
+  if (ln_beta) cudaMemcpy(dBe.p, ln_beta, N * 4, cudaMemcpyHostToDevice);
+  if (col_scale) cudaMemcpy(dCs.p, col_scale, N * 4, cudaMemcpyHostToDevice);
+  cudaMemset(dO.p, 0, size_t(M) * N * 4);
+  cudaMemset(dS.p, 0, 4);
+  GemmArgs a{};
+  a.M = M;
+  a.N = N;
+  a.K = K;
+  a.mode = mode;
+  a.act = act;
+  a.bias = bias ? static_cast<float *>(dB.p) : nullptr;
+  a.out = dO.p;
+  a.ldo = N;
+  a.resid = static_cast<const float *>(dR.p);
+  a.ldr = N;
+  a.alpha = alpha;
+  a.ln_gamma = static_cast<float *>(dG.p);
+  a.ln_beta = static_cast<float *>(dBe.p);
+  a.ln_eps = ln_eps;
+  a.col_scale = col_scale ? static_cast<float *>(dCs.p) : nullptr;
+  a.a_scale = a_scale;
+  a.status = static_cast<unsigned *>(dS.p);
+  a.out_f32 = out_f32;
+  GemmLaunch g;
+  if (plan_gemm(g, dA.p, K, dW.p, K, bn, fp8 != 0, a)) return 2;
+  if (launch_gemm(g, 0) != cudaSuccess) return 3;
+  if (cudaDeviceSynchronize() != cudaSuccess) return 4;
+  cudaMemcpy(out, dO.p, size_t(M) * N * (out_f32 ? 4 : 2), cudaMemcpyDeviceToHost);
+  unsigned st = 0;
+  cudaMemcpy(&st, dS.p, 4, cudaMemcpyDeviceToHost);
+  if (status_out) *status_out = st;
+  return st ? 5 : 0;
+}

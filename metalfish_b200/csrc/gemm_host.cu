@@ -1,0 +1,118 @@
+// gemm_host.cu -- host side of the tcgen05 GEMM: TMA descriptor creation,
+// launch configuration and the template instantiations.
+#include <cstdio>
+#include <mutex>
+
+#include "gemm_host.h"
+
+namespace mfb200 {
+
+namespace {
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *,
+                                   const cuuint64_t *, const cuuint64_t *, const cuuint32_t *,
+                                   const cuuint32_t *, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+
+int g_num_sms = 0;
+}  // namespace
+
+int num_sms() {
+  if (g_num_sms == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
+    if (g_num_sms <= 0) g_num_sms = 148;
+  }
+  return g_num_sms;
+}
+
+bool make_kmajor_tmap(CUtensorMap *tm, const void *base, bool fp8, uint64_t k, uint64_t rows,
+                      uint64_t row_stride_bytes, uint32_t box_rows) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  const uint32_t elem = fp8 ? 1 : 2;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || (row_stride_bytes & 15) || k == 0 || rows == 0)
+    return false;
+  cuuint64_t dims[2] = {k, rows};
+  cuuint64_t strides[1] = {row_stride_bytes};
+  cuuint32_t box[2] = {128u / elem, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  const CUresult r =
+      fn(tm, fp8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+         const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+template <int BN, bool FP8>
+static cudaError_t launch_t(const GemmLaunch &g, cudaStream_t stream) {
+  using S = GemmShape<BN, FP8>;
+  static bool attr_done = false;
+  if (!attr_done) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_sm100_kernel<BN, FP8>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         S::SMEM_BYTES);
+    if (e != cudaSuccess) return e;
+    attr_done = true;
+  }
+  gemm_sm100_kernel<BN, FP8><<<g.grid, S::THREADS, S::SMEM_BYTES, stream>>>(g.tmA, g.tmB, g.args);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_gemm(const GemmLaunch &g, cudaStream_t stream) {
+  if (g.fp8) {
+    switch (g.bn) {
+    case 256: return launch_t<256, true>(g, stream);
+    case 128: return launch_t<128, true>(g, stream);
+    case 64: return launch_t<64, true>(g, stream);
+    }
+  } else {
+    switch (g.bn) {
+    case 256: return launch_t<256, false>(g, stream);
+    case 128: return launch_t<128, false>(g, stream);
+    case 64: return launch_t<64, false>(g, stream);
+    }
+  }
+  return cudaErrorInvalidValue;
+}
+
+const char *plan_gemm(GemmLaunch &g, const void *A, long long lda_elems, const void *W,
+                      long long ldw_elems, int bn, bool fp8, const GemmArgs &args) {
+  if (bn != 64 && bn != 128 && bn != 256) return "gemm: BN must be 64, 128 or 256";
+  if (args.M <= 0 || args.N <= 0 || args.K <= 0) return "gemm: empty problem";
+  if (args.N % 16) return "gemm: N must be a multiple of 16";
+  if (args.mode == kEpiRowLN && args.N != bn) return "gemm: row-LN epilogue needs N == BN";
+  const uint32_t elem = fp8 ? 1 : 2;
+  g = GemmLaunch{};
+  g.bn = bn;
+  g.fp8 = fp8;
+  g.args = args;
+  if (!make_kmajor_tmap(&g.tmA, A, fp8, static_cast<uint64_t>(args.K),
+                        static_cast<uint64_t>(args.M), static_cast<uint64_t>(lda_elems) * elem, 128))
+    return "gemm: cannot build TMA descriptor for A (alignment?)";
+  if (!make_kmajor_tmap(&g.tmB, W, fp8, static_cast<uint64_t>(args.K),
+                        static_cast<uint64_t>(args.N), static_cast<uint64_t>(ldw_elems) * elem, bn))
+    return "gemm: cannot build TMA descriptor for W (alignment?)";
+  const long long tiles =
+      static_cast<long long>((args.M + 127) / 128) * ((args.N + bn - 1) / bn);
+  const int sms = num_sms();
+  g.grid = dim3(static_cast<unsigned>(tiles < sms ? tiles : sms));
+  return nullptr;
+}
+
+}  // namespace mfb200

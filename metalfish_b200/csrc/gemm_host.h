@@ -1,0 +1,29 @@
+// gemm_host.h -- planning and launching of the tcgen05 GEMM.
+#pragma once
+#include "gemm_sm100.cuh"
+
+namespace mfb200 {
+
+// A fully prepared launch: both TMA descriptors and the epilogue arguments.
+// Plans are built once per (buffer set, batch size) and replayed (directly or
+// inside a CUDA graph).
+struct GemmLaunch {
+  CUtensorMap tmA, tmB;
+  GemmArgs args;
+  int bn = 256;
+  bool fp8 = false;
+  dim3 grid;
+};
+
+int num_sms();
+
+bool make_kmajor_tmap(CUtensorMap *tm, const void *base, bool fp8, uint64_t k, uint64_t rows,
+                      uint64_t row_stride_bytes, uint32_t box_rows);
+
+// Returns nullptr on success, else a static error message.
+const char *plan_gemm(GemmLaunch &g, const void *A, long long lda_elems, const void *W,
+                      long long ldw_elems, int bn, bool fp8, const GemmArgs &args);
+
+cudaError_t launch_gemm(const GemmLaunch &g, cudaStream_t stream);
+
+}  // namespace mfb200

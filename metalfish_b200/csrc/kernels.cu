@@ -1,0 +1,559 @@
+// kernels.cu -- memory-bound and small-matmul kernels of the BT4 forward.
+#include <cuda_bf16.h>
+
+#include "kernels.cuh"
+
+namespace mfb200 {
+
+// ------------------------------------------------------------------ helpers
+__device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<const uint32_t *>(&h);
+}
+__device__ __forceinline__ float2 unpack_bf16x2(uint32_t w) {
+  const __nv_bfloat162 h = *reinterpret_cast<const __nv_bfloat162 *>(&w);
+  return make_float2(__low2float(h), __high2float(h));
+}
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
+                   static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
+               "l"(src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void ldmatrix_x4(uint32_t (&r)[4], const void *p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(static_cast<uint32_t>(__cvta_generic_to_shared(p))));
+}
+__device__ __forceinline__ void ldmatrix_x4_trans(uint32_t (&r)[4], const void *p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(static_cast<uint32_t>(__cvta_generic_to_shared(p))));
+}
+// D = A(16x16 bf16, row) * B(16x8 bf16, col) + D, fp32 accumulate.
+__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                               uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// ------------------------------------------------------------------ unpack
+// One CTA per position, 128 threads. Reference semantics: an unpacked plane
+// square is `value` where the mask bit is set, else 0
+// (src/nn/cpu/cpu_network.cpp:599-605 + the inverse of
+// src/nn/input_plane_packing.h:39-61). The PE input is the first 12 planes in
+// square-major order (src/nn/cpu/cpu_network.cpp:731-747).
+__global__ void unpack_kernel(const uint64_t *__restrict__ masks, const float *__restrict__ values,
+                              __nv_bfloat16 *__restrict__ x0, __nv_bfloat16 *__restrict__ p) {
+  const int b = blockIdx.x;
+  __shared__ uint64_t sm[kPlanes];
+  __shared__ float sv[kPlanes];
+  for (int i = threadIdx.x; i < kPlanes; i += blockDim.x) {
+    sm[i] = masks[static_cast<long long>(b) * kPlanes + i];
+    sv[i] = values[static_cast<long long>(b) * kPlanes + i];
+  }
+  __syncthreads();
+  // X0 rows: 64 squares x 192 columns; each thread writes pairs of columns.
+  for (int idx = threadIdx.x; idx < kSquares * (kEmbIn / 2); idx += blockDim.x) {
+    const int sq = idx / (kEmbIn / 2);
+    const int c = 2 * (idx % (kEmbIn / 2));
+    if (c >= kPlanes && c < kEmbIn - 16) continue;  // PE columns: written by pe_concat
+    float v0 = 0.0f, v1 = 0.0f;
+    if (c < kPlanes) {
+      v0 = ((sm[c] >> sq) & 1ull) ? sv[c] : 0.0f;
+      v1 = ((sm[c + 1] >> sq) & 1ull) ? sv[c + 1] : 0.0f;
+    }
+    reinterpret_cast<uint32_t *>(x0)[((static_cast<long long>(b) * kSquares + sq) * kEmbIn + c) /
+                                     2] = pack_bf16x2(v0, v1);
+  }
+  for (int idx = threadIdx.x; idx < kPeInputs / 2; idx += blockDim.x) {
+    const int e = 2 * idx;
+    const int sq = e / 12, pl = e % 12;  // pl even, pl+1 < 12
+    const float v0 = ((sm[pl] >> sq) & 1ull) ? sv[pl] : 0.0f;
+    const float v1 = ((sm[pl + 1] >> sq) & 1ull) ? sv[pl + 1] : 0.0f;
+    reinterpret_cast<uint32_t *>(p)[(static_cast<long long>(b) * kPeInputs + e) / 2] =
+        pack_bf16x2(v0, v1);
+  }
+}
+
+void launch_unpack(const uint64_t *masks, const float *values, int batch, __nv_bfloat16 *x0,
+                   __nv_bfloat16 *p, cudaStream_t s) {
+  unpack_kernel<<<batch, 128, 0, s>>>(masks, values, x0, p);
+}
+
+// PEo[b, sq*pe + e] -> X0[b*64 + sq, 112 + e]; 8 columns (16 bytes) per thread.
+__global__ void pe_concat_kernel(const __nv_bfloat16 *__restrict__ peo, int total_rows, int pe,
+                                 __nv_bfloat16 *__restrict__ x0) {
+  const int chunks = pe / 8;
+  const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= static_cast<long long>(total_rows) * chunks) return;
+  const long long row = i / chunks;
+  const int c = static_cast<int>(i % chunks) * 8;
+  const uint4 v = *reinterpret_cast<const uint4 *>(peo + row * pe + c);
+  // X0 column 112 + c: byte offset (row*192 + 112 + c)*2 is 16-byte aligned
+  *reinterpret_cast<uint4 *>(x0 + row * kEmbIn + kPlanes + c) = v;
+}
+
+void launch_pe_concat(const __nv_bfloat16 *peo, int batch, int pe, __nv_bfloat16 *x0,
+                      cudaStream_t s) {
+  const long long n = static_cast<long long>(batch) * kSquares * (pe / 8);
+  pe_concat_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, s>>>(peo, batch * kSquares,
+                                                                          pe, x0);
+}
+
+// ------------------------------------------------------------------ layernorm
+// One warp per row. Lane l owns the 4-column groups q*128 + 4l .. +3 for
+// q < VPL/4, so every load instruction of the warp reads 256 contiguous bytes.
+template <int VPL>
+__global__ void layernorm_warp_kernel(const __nv_bfloat16 *__restrict__ in, int rows,
+                                      const float *__restrict__ gamma,
+                                      const float *__restrict__ beta, float eps,
+                                      const float *__restrict__ multT,
+                                      const float *__restrict__ addT,
+                                      __nv_bfloat16 *__restrict__ out) {
+  constexpr int W = 32 * VPL;
+  const int warps = blockDim.x >> 5;
+  const long long row = static_cast<long long>(blockIdx.x) * warps + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const __nv_bfloat16 *src = in + row * W;
+  float v[VPL];
+#pragma unroll
+  for (int q = 0; q < VPL / 4; ++q) {
+    const uint2 u = *reinterpret_cast<const uint2 *>(src + q * 128 + lane * 4);
+    const float2 f0 = unpack_bf16x2(u.x), f1 = unpack_bf16x2(u.y);
+    v[4 * q] = f0.x;
+    v[4 * q + 1] = f0.y;
+    v[4 * q + 2] = f1.x;
+    v[4 * q + 3] = f1.y;
+  }
+  float s = 0.0f;
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) s += v[i];
+#pragma unroll
+  for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  const float mean = s / static_cast<float>(W);
+  float sq = 0.0f;
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    const float t = v[i] - mean;
+    sq += t * t;
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+  const float inv = 1.0f / sqrtf(sq / static_cast<float>(W) + eps);
+  const int sqr = static_cast<int>(row % kSquares);
+  __nv_bfloat16 *dst = out + row * W;
+#pragma unroll
+  for (int q = 0; q < VPL / 4; ++q) {
+    const int c = q * 128 + lane * 4;
+    float r[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      float y = (v[4 * q + e] - mean) * inv * gamma[c + e] + beta[c + e];
+      if (multT) y = y * multT[sqr * W + c + e] + addT[sqr * W + c + e];
+      r[e] = y;
+    }
+    *reinterpret_cast<uint2 *>(dst + c) = make_uint2(pack_bf16x2(r[0], r[1]), pack_bf16x2(r[2], r[3]));
+  }
+}
+
+// One CTA (256 threads) per row for wide rows (smolgen's H*g = 8192).
+__global__ void layernorm_block_kernel(const __nv_bfloat16 *__restrict__ in, int width,
+                                       const float *__restrict__ gamma,
+                                       const float *__restrict__ beta, float eps,
+                                       __nv_bfloat16 *__restrict__ out) {
+  const long long row = blockIdx.x;
+  const __nv_bfloat16 *src = in + row * width;
+  __shared__ float red[32];
+  float s = 0.0f;
+  for (int c = threadIdx.x * 8; c < width; c += blockDim.x * 8) {
+    const uint4 u = *reinterpret_cast<const uint4 *>(src + c);
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = unpack_bf16x2(w[e]);
+      s += f.x + f.y;
+    }
+  }
+  auto block_sum = [&](float x) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = x;
+    __syncthreads();
+    float t = 0.0f;
+    for (int i = 0; i < static_cast<int>(blockDim.x >> 5); ++i) t += red[i];
+    return t;
+  };
+  const float mean = block_sum(s) / static_cast<float>(width);
+  float sq = 0.0f;
+  for (int c = threadIdx.x * 8; c < width; c += blockDim.x * 8) {
+    const uint4 u = *reinterpret_cast<const uint4 *>(src + c);
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = unpack_bf16x2(w[e]);
+      sq += (f.x - mean) * (f.x - mean) + (f.y - mean) * (f.y - mean);
+    }
+  }
+  const float inv = 1.0f / sqrtf(block_sum(sq) / static_cast<float>(width) + eps);
+  for (int c = threadIdx.x * 8; c < width; c += blockDim.x * 8) {
+    const uint4 u = *reinterpret_cast<const uint4 *>(src + c);
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = unpack_bf16x2(w[e]);
+      const int k = c + 2 * e;
+      o[e] = pack_bf16x2((f.x - mean) * inv * gamma[k] + beta[k],
+                         (f.y - mean) * inv * gamma[k + 1] + beta[k + 1]);
+    }
+    *reinterpret_cast<uint4 *>(out + row * width + c) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+void launch_layernorm(const __nv_bfloat16 *in, int rows, int width, const float *gamma,
+                      const float *beta, float eps, const float *multT, const float *addT,
+                      __nv_bfloat16 *out, cudaStream_t s) {
+  const int wpb = 8;
+  const unsigned grid = static_cast<unsigned>((rows + wpb - 1) / wpb);
+  switch (width) {
+  case 128:
+    layernorm_warp_kernel<4><<<grid, 32 * wpb, 0, s>>>(in, rows, gamma, beta, eps, multT, addT, out);
+    return;
+  case 256:
+    layernorm_warp_kernel<8><<<grid, 32 * wpb, 0, s>>>(in, rows, gamma, beta, eps, multT, addT, out);
+    return;
+  case 512:
+    layernorm_warp_kernel<16><<<grid, 32 * wpb, 0, s>>>(in, rows, gamma, beta, eps, multT, addT, out);
+    return;
+  case 1024:
+    layernorm_warp_kernel<32><<<grid, 32 * wpb, 0, s>>>(in, rows, gamma, beta, eps, multT, addT, out);
+    return;
+  default:
+    // wide rows (no gates on this path)
+    layernorm_block_kernel<<<rows, 256, 0, s>>>(in, width, gamma, beta, eps, out);
+    return;
+  }
+}
+
+// ------------------------------------------------------------------ attention
+// One CTA (4 warps) per (position, head); head depth 32. Warp w owns query
+// rows 16w..16w+15. S = Q K^T via mma.sync (2 k-steps x 8 key tiles), plus
+// scale and the smolgen bias, row softmax in registers (exp(x - max) / sum
+// as src/nn/cpu/cpu_network.cpp:405-422), then O = P V (4 k-steps x 4 tiles).
+constexpr int kDh = 32;
+constexpr int kQkvStride = 40;   // padded smem row (80 bytes): conflict-free ldmatrix
+constexpr int kBiasStride = 72;  // padded smem row (144 bytes)
+
+__global__ void __launch_bounds__(128)
+    attention_kernel(const __nv_bfloat16 *__restrict__ qkv, long long ldq,
+                     const __nv_bfloat16 *__restrict__ bias, int heads, int d,
+                     __nv_bfloat16 *__restrict__ ctx) {
+  __shared__ __align__(16) __nv_bfloat16 sQ[kSquares * kQkvStride];
+  __shared__ __align__(16) __nv_bfloat16 sK[kSquares * kQkvStride];
+  __shared__ __align__(16) __nv_bfloat16 sV[kSquares * kQkvStride];
+  __shared__ __align__(16) __nv_bfloat16 sB[kSquares * kBiasStride];
+  const int bh = blockIdx.x;
+  const int b = bh / heads, h = bh % heads;
+  const int tid = threadIdx.x;
+  const __nv_bfloat16 *base = qkv + static_cast<long long>(b) * kSquares * ldq + h * kDh;
+  // Q, K, V: 64 rows x 64 bytes = 4 chunks of 16 B each
+  for (int i = tid; i < kSquares * 4; i += 128) {
+    const int r = i >> 2, c = (i & 3) * 8;
+    const __nv_bfloat16 *g = base + r * ldq + c;
+    cp_async16(&sQ[r * kQkvStride + c], g);
+    cp_async16(&sK[r * kQkvStride + c], g + d);
+    cp_async16(&sV[r * kQkvStride + c], g + 2 * d);
+  }
+  const __nv_bfloat16 *gb = bias + static_cast<long long>(bh) * kSquares * kSquares;
+  for (int i = tid; i < kSquares * 8; i += 128) {
+    const int r = i >> 3, c = (i & 7) * 8;
+    cp_async16(&sB[r * kBiasStride + c], gb + r * kSquares + c);
+  }
+  cp_async_commit();
+  cp_async_wait<0>();
+  __syncthreads();
+
+  const int warp = tid >> 5, lane = tid & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int q0 = warp * 16;
+  // ---- S = Q K^T
+  float S[8][4];
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) S[j][e] = 0.0f;
+#pragma unroll
+  for (int ks = 0; ks < 2; ++ks) {
+    uint32_t a[4];
+    {
+      const int mat = lane >> 3;
+      const int r = q0 + (lane & 7) + 8 * (mat & 1);
+      const int c = ks * 16 + 8 * (mat >> 1);
+      ldmatrix_x4(a, &sQ[r * kQkvStride + c]);
+    }
+#pragma unroll
+    for (int j = 0; j < 8; j += 2) {
+      uint32_t bf[4];
+      const int mat = lane >> 3;
+      const int key = 8 * (j + (mat >> 1)) + (lane & 7);
+      const int c = ks * 16 + 8 * (mat & 1);
+      ldmatrix_x4(bf, &sK[key * kQkvStride + c]);
+      mma_bf16_16816(S[j], a, bf[0], bf[1]);
+      mma_bf16_16816(S[j + 1], a, bf[2], bf[3]);
+    }
+  }
+  // ---- scale + bias, softmax over 64 keys (row g and row g+8 of this warp)
+  const float scale = 1.0f / sqrtf(static_cast<float>(kDh));
+  float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int col = 8 * j + 2 * t;
+    const float2 b0 = unpack_bf16x2(
+        *reinterpret_cast<const uint32_t *>(&sB[(q0 + g) * kBiasStride + col]));
+    const float2 b1 = unpack_bf16x2(
+        *reinterpret_cast<const uint32_t *>(&sB[(q0 + g + 8) * kBiasStride + col]));
+    S[j][0] = S[j][0] * scale + b0.x;
+    S[j][1] = S[j][1] * scale + b0.y;
+    S[j][2] = S[j][2] * scale + b1.x;
+    S[j][3] = S[j][3] * scale + b1.y;
+    mx0 = fmaxf(mx0, fmaxf(S[j][0], S[j][1]));
+    mx1 = fmaxf(mx1, fmaxf(S[j][2], S[j][3]));
+  }
+#pragma unroll
+  for (int o = 1; o <= 2; o <<= 1) {
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
+  }
+  float sum0 = 0.0f, sum1 = 0.0f;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    S[j][0] = expf(S[j][0] - mx0);
+    S[j][1] = expf(S[j][1] - mx0);
+    S[j][2] = expf(S[j][2] - mx1);
+    S[j][3] = expf(S[j][3] - mx1);
+    sum0 += S[j][0] + S[j][1];
+    sum1 += S[j][2] + S[j][3];
+  }
+#pragma unroll
+  for (int o = 1; o <= 2; o <<= 1) {
+    sum0 += __shfl_xor_sync(0xffffffffu, sum0, o);
+    sum1 += __shfl_xor_sync(0xffffffffu, sum1, o);
+  }
+  const float inv0 = 1.0f / sum0, inv1 = 1.0f / sum1;
+  // ---- O = P V
+  float O[4][4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) O[j][e] = 0.0f;
+#pragma unroll
+  for (int ks = 0; ks < 4; ++ks) {
+    uint32_t a[4];
+    a[0] = pack_bf16x2(S[2 * ks][0] * inv0, S[2 * ks][1] * inv0);
+    a[1] = pack_bf16x2(S[2 * ks][2] * inv1, S[2 * ks][3] * inv1);
+    a[2] = pack_bf16x2(S[2 * ks + 1][0] * inv0, S[2 * ks + 1][1] * inv0);
+    a[3] = pack_bf16x2(S[2 * ks + 1][2] * inv1, S[2 * ks + 1][3] * inv1);
+#pragma unroll
+    for (int j = 0; j < 4; j += 2) {
+      uint32_t bf[4];
+      const int mat = lane >> 3;
+      const int key = ks * 16 + 8 * (mat & 1) + (lane & 7);
+      const int c = 8 * (j + (mat >> 1));
+      ldmatrix_x4_trans(bf, &sV[key * kQkvStride + c]);
+      mma_bf16_16816(O[j], a, bf[0], bf[1]);
+      mma_bf16_16816(O[j + 1], a, bf[2], bf[3]);
+    }
+  }
+  __nv_bfloat16 *out = ctx + (static_cast<long long>(b) * kSquares + q0) * d + h * kDh;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int col = 8 * j + 2 * t;
+    *reinterpret_cast<uint32_t *>(out + static_cast<long long>(g) * d + col) =
+        pack_bf16x2(O[j][0], O[j][1]);
+    *reinterpret_cast<uint32_t *>(out + static_cast<long long>(g + 8) * d + col) =
+        pack_bf16x2(O[j][2], O[j][3]);
+  }
+}
+
+void launch_attention(const __nv_bfloat16 *qkv, long long ldq, const __nv_bfloat16 *bias,
+                      int batch, int heads, int d, __nv_bfloat16 *ctx, cudaStream_t s) {
+  attention_kernel<<<batch * heads, 128, 0, s>>>(qkv, ldq, bias, heads, d, ctx);
+}
+
+// ------------------------------------------------------------------ policy
+// One CTA (4 warps) per position. raw[i][j] = (q_i . k_j) / sqrt(dp) by
+// mma.sync over dp in 64-wide chunks (double-buffered cp.async), then the
+// promotion logits and the 1858 gather (src/nn/cpu/cpu_network.cpp:892-1025):
+//   promo p: raw[48 + (p%64)/8][56 + p%8] + k[56 + (p%24)/3] . ppo3[p%3]
+constexpr int kPolChunk = 64;
+constexpr int kPolStride = 72;  // padded smem row (144 bytes)
+
+__global__ void __launch_bounds__(128)
+    policy_map_kernel(const __nv_bfloat16 *__restrict__ qk, int dp, const float *__restrict__ ppo3,
+                      const int16_t *__restrict__ gather, float *__restrict__ policy) {
+  // q/k double buffers; after the k-loop the same bytes hold the raw logits
+  __shared__ __align__(16) __nv_bfloat16 sQK[4][kSquares * kPolStride];
+  __nv_bfloat16(*sQ)[kSquares * kPolStride] = sQK;
+  __nv_bfloat16(*sK)[kSquares * kPolStride] = sQK + 2;
+  float *raw = reinterpret_cast<float *>(sQK);
+  static_assert(sizeof(float) * kSquares * (kSquares + 1) <= sizeof(__nv_bfloat16) * 4 * kSquares * kPolStride,
+                "raw logits must fit in the q/k buffers");
+  __shared__ float pk[8 * 3];
+  const int b = blockIdx.x;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const long long ld = 2LL * dp;
+  const __nv_bfloat16 *qbase = qk + static_cast<long long>(b) * kSquares * ld;
+  const __nv_bfloat16 *kbase = qbase + dp;
+  const int nchunks = dp / kPolChunk;
+  auto load = [&](int chunk, int buf) {
+    for (int i = tid; i < kSquares * 8; i += 128) {
+      const int r = i >> 3, c = (i & 7) * 8;
+      cp_async16(&sQ[buf][r * kPolStride + c], qbase + r * ld + chunk * kPolChunk + c);
+      cp_async16(&sK[buf][r * kPolStride + c], kbase + r * ld + chunk * kPolChunk + c);
+    }
+    cp_async_commit();
+  };
+  const int g = lane >> 2, t = lane & 3;
+  const int q0 = warp * 16;
+  float S[8][4];
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) S[j][e] = 0.0f;
+  load(0, 0);
+  for (int ch = 0; ch < nchunks; ++ch) {
+    if (ch + 1 < nchunks) {
+      load(ch + 1, (ch + 1) & 1);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    const __nv_bfloat16 *Q = sQ[ch & 1];
+    const __nv_bfloat16 *K = sK[ch & 1];
+#pragma unroll
+    for (int ks = 0; ks < kPolChunk / 16; ++ks) {
+      uint32_t a[4];
+      {
+        const int mat = lane >> 3;
+        const int r = q0 + (lane & 7) + 8 * (mat & 1);
+        const int c = ks * 16 + 8 * (mat >> 1);
+        ldmatrix_x4(a, &Q[r * kPolStride + c]);
+      }
+#pragma unroll
+      for (int j = 0; j < 8; j += 2) {
+        uint32_t bf[4];
+        const int mat = lane >> 3;
+        const int key = 8 * (j + (mat >> 1)) + (lane & 7);
+        const int c = ks * 16 + 8 * (mat & 1);
+        ldmatrix_x4(bf, &K[key * kPolStride + c]);
+        mma_bf16_16816(S[j], a, bf[0], bf[1]);
+        mma_bf16_16816(S[j + 1], a, bf[2], bf[3]);
+      }
+    }
+    __syncthreads();
+  }
+  const float scale = 1.0f / sqrtf(static_cast<float>(dp));
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int col = 8 * j + 2 * t;
+    raw[(q0 + g) * (kSquares + 1) + col] = S[j][0] * scale;
+    raw[(q0 + g) * (kSquares + 1) + col + 1] = S[j][1] * scale;
+    raw[(q0 + g + 8) * (kSquares + 1) + col] = S[j][2] * scale;
+    raw[(q0 + g + 8) * (kSquares + 1) + col + 1] = S[j][3] * scale;
+  }
+  // promotion key terms: k[56+i] . ppo3[r], 24 dot products; warp w does i = 2w, 2w+1
+  for (int pr = warp * 6; pr < warp * 6 + 6; ++pr) {
+    const int i = pr / 3, r = pr % 3;
+    const __nv_bfloat16 *krow = kbase + (56 + i) * ld;
+    float acc = 0.0f;
+    for (int c = lane * 2; c < dp; c += 64) {
+      const float2 kv = unpack_bf16x2(*reinterpret_cast<const uint32_t *>(krow + c));
+      acc += kv.x * ppo3[r * dp + c] + kv.y * ppo3[r * dp + c + 1];
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (lane == 0) pk[i * 3 + r] = acc;
+  }
+  __syncthreads();
+  float *out = policy + static_cast<long long>(b) * kPolicy;
+  for (int p = tid; p < kPolicy; p += 128) {
+    const int idx = gather[p];
+    float v;
+    if (idx < kSquares * kSquares) {
+      v = raw[(idx >> 6) * (kSquares + 1) + (idx & 63)];
+    } else {
+      const int promo = idx - kSquares * kSquares;
+      const int pair = promo % 64;
+      v = raw[(48 + pair / 8) * (kSquares + 1) + 56 + pair % 8] + pk[((promo % 24) / 3) * 3 + promo % 3];
+    }
+    out[p] = v;
+  }
+}
+
+void launch_policy_map(const __nv_bfloat16 *qk, int batch, int dp, const float *ppo3,
+                       const int16_t *gather, float *policy, cudaStream_t s) {
+  policy_map_kernel<<<batch, 128, 0, s>>>(qk, dp, ppo3, gather, policy);
+}
+
+// ------------------------------------------------------------------ heads
+// One warp per position: WDL = softmax(W2v h_v + b2v), moves_left =
+// relu(W2m h_m + b2m) (src/nn/network_execution_plan.cpp:1061-1111).
+__global__ void heads_kernel(const __nv_bfloat16 *__restrict__ h, int batch, int vh, int mh,
+                             const float *__restrict__ w2v, const float *__restrict__ b2v,
+                             const float *__restrict__ w2m, const float *__restrict__ b2m,
+                             float *__restrict__ wdl, float *__restrict__ mlh) {
+  const int warps = blockDim.x >> 5;
+  const int b = blockIdx.x * warps + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (b >= batch) return;
+  const __nv_bfloat16 *x = h + static_cast<long long>(b) * (vh + mh);
+  float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, am = 0.0f;
+  for (int i = lane; i < vh; i += 32) {
+    const float v = __bfloat162float(x[i]);
+    a0 += w2v[i] * v;
+    a1 += w2v[vh + i] * v;
+    a2 += w2v[2 * vh + i] * v;
+  }
+  for (int i = lane; i < mh; i += 32) am += w2m[i] * __bfloat162float(x[vh + i]);
+#pragma unroll
+  for (int o = 16; o; o >>= 1) {
+    a0 += __shfl_xor_sync(0xffffffffu, a0, o);
+    a1 += __shfl_xor_sync(0xffffffffu, a1, o);
+    a2 += __shfl_xor_sync(0xffffffffu, a2, o);
+    am += __shfl_xor_sync(0xffffffffu, am, o);
+  }
+  if (lane == 0) {
+    a0 += b2v[0];
+    a1 += b2v[1];
+    a2 += b2v[2];
+    const float m = fmaxf(a0, fmaxf(a1, a2));
+    const float e0 = expf(a0 - m), e1 = expf(a1 - m), e2 = expf(a2 - m);
+    const float inv = 1.0f / (e0 + e1 + e2);
+    wdl[3 * b + 0] = e0 * inv;
+    wdl[3 * b + 1] = e1 * inv;
+    wdl[3 * b + 2] = e2 * inv;
+    mlh[b] = fmaxf(am + b2m[0], 0.0f);
+  }
+}
+
+void launch_heads(const __nv_bfloat16 *h, int batch, int vh, int mh, const float *w2v,
+                  const float *b2v, const float *w2m, const float *b2m, float *wdl, float *mlh,
+                  cudaStream_t s) {
+  const int wpb = 8;
+  heads_kernel<<<(batch + wpb - 1) / wpb, 32 * wpb, 0, s>>>(h, batch, vh, mh, w2v, b2v, w2m, b2m,
+                                                           wdl, mlh);
+}
+
+}  // namespace mfb200

@@ -1,0 +1,51 @@
+// kernels.cuh -- the memory-bound / small-matmul kernels of the BT4 forward.
+// (The large projections run through the tcgen05 GEMM in gemm_sm100.cuh.)
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+namespace mfb200 {
+
+constexpr int kPlanes = 112;
+constexpr int kSquares = 64;
+constexpr int kPolicy = 1858;
+constexpr int kPeInputs = 12 * kSquares;  // 12 position planes, square-major
+constexpr int kEmbIn = 192;               // 112 planes + 64 PE, padded to 3 x 64
+
+// Input unpack: packed (mask, value) planes -> X0[M, 192] (planes in columns
+// 0..111, columns 176..191 zeroed; columns 112..175 are filled by pe_concat)
+// and the square-major PE input P[B, 768].
+void launch_unpack(const uint64_t *masks, const float *values, int batch, __nv_bfloat16 *x0,
+                   __nv_bfloat16 *p, cudaStream_t s);
+
+// X0[:, 112:112+pe] = PEo[B, 64*pe] viewed as [B*64, pe].
+void launch_pe_concat(const __nv_bfloat16 *peo, int batch, int pe, __nv_bfloat16 *x0,
+                      cudaStream_t s);
+
+// Row LayerNorm of bf16 rows (two-pass mean/variance in fp32); optional
+// square gates multT/addT [64][width] applied after the norm.
+void launch_layernorm(const __nv_bfloat16 *in, int rows, int width, const float *gamma,
+                      const float *beta, float eps, const float *multT, const float *addT,
+                      __nv_bfloat16 *out, cudaStream_t s);
+
+// 64-token attention per (position, head) with the smolgen bias added before
+// the softmax: ctx[b*64+q, h*dh:..] = softmax(Q K^T / sqrt(dh) + bias) V.
+// qkv: [B*64, ldq] with Q at column 0, K at d, V at 2d. bias: [B*H, 4096].
+void launch_attention(const __nv_bfloat16 *qkv, long long ldq, const __nv_bfloat16 *bias,
+                      int batch, int heads, int d, __nv_bfloat16 *ctx, cudaStream_t s);
+
+// Attention-policy logits: raw = q k^T / sqrt(dp) (64x64), the 8x24 promotion
+// logits, gathered onto the 1858 moves. qk: [B*64, 2*dp] (q | k);
+// ppo3: [3, dp] = ip4_pol_w[r] + ip4_pol_w[3].
+void launch_policy_map(const __nv_bfloat16 *qk, int batch, int dp, const float *ppo3,
+                       const int16_t *gather, float *policy, cudaStream_t s);
+
+// Value (WDL softmax) and moves-left (relu) output layers from the hidden
+// vector h[B, vh + mh] (value hidden first).
+void launch_heads(const __nv_bfloat16 *h, int batch, int vh, int mh, const float *w2v,
+                  const float *b2v, const float *w2m, const float *b2m, float *wdl, float *mlh,
+                  cudaStream_t s);
+
+}  // namespace mfb200

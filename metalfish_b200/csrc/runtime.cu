@@ -1,0 +1,1010 @@
+// runtime.cu -- the B200 BT4 forward behind the C ABI of include/mfb200.h.
+//
+// A handle owns, per GPU: the packed weights (one arena), an activation
+// workspace sized for max_batch, a stream, per-batch-size launch plans and
+// (optionally) one CUDA graph per batch size. A batch is sharded contiguously
+// across the handle's GPUs with one host thread per GPU; there is no
+// collective (positions are independent).
+//
+// The kernel schedule follows the reference execution plan
+// (src/nn/network_execution_plan.cpp:155-223) with the per-stage semantics of
+// the reference CPU backend (src/nn/cpu/cpu_network.cpp:580-1491):
+//   unpack -> PE dense -> concat -> embedding dense+act -> LN+gates
+//   -> embedding FFN -> LN(x + a*ffn)
+//   -> per layer: QKV(+smolgen compress) -> smolgen dense1+act+LN
+//      -> dense2+act -> LN -> global generator (bias) -> attention
+//      -> out-proj + residual -> LN -> FFN1+act -> FFN2 + residual -> LN
+//   -> policy embedding+act -> wq|wk -> policy map
+//   -> value|moves-left per-square dense+act -> flattened dense+act -> output layers.
+#include <cuda_fp8.h>
+
+#include <algorithm>
+#include <array>
+#include <chrono>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <functional>
+#include <map>
+#include <memory>
+#include <mutex>
+#include <stdexcept>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "../../include/mfb200.h"
+#include "gemm_host.h"
+#include "kernels.cuh"
+
+using namespace mfb200;
+
+namespace {
+
+thread_local std::string t_last_error;
+
+struct Fail : std::runtime_error {
+  using std::runtime_error::runtime_error;
+};
+
+void check(cudaError_t e, const char *what) {
+  if (e != cudaSuccess) throw Fail(std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+uint16_t f2bf(float f) {
+  uint32_t u;
+  std::memcpy(&u, &f, 4);
+  if ((u & 0x7fffffffu) > 0x7f800000u) return 0x7fc0;
+  u += 0x7fffu + ((u >> 16) & 1u);
+  return static_cast<uint16_t>(u >> 16);
+}
+
+// ------------------------------------------------------------ weight slots
+// Global and per-layer tensor slots, in the order of metalfish_b200/layout.py.
+enum G {
+  G_PREPROC_W, G_PREPROC_B, G_EMB_W, G_EMB_B, G_EMB_LN_G, G_EMB_LN_B, G_MULT_GATE, G_ADD_GATE,
+  G_EFFN_W1, G_EFFN_B1, G_EFFN_W2, G_EFFN_B2, G_EFFN_LN_G, G_EFFN_LN_B, G_SMOLGEN_W,
+  G_POL_W, G_POL_B, G_POL_WQ, G_POL_BQ, G_POL_WK, G_POL_BK, G_POL_PPO,
+  G_VAL_W, G_VAL_B, G_VAL_W1, G_VAL_B1, G_VAL_W2, G_VAL_B2,
+  G_MOV_W, G_MOV_B, G_MOV_W1, G_MOV_B1, G_MOV_W2, G_MOV_B2, G_COUNT
+};
+enum L {
+  L_Q_W, L_Q_B, L_K_W, L_K_B, L_V_W, L_V_B, L_O_W, L_O_B,
+  L_SG_COMPRESS, L_SG_W1, L_SG_B1, L_SG_LN1_G, L_SG_LN1_B, L_SG_W2, L_SG_B2, L_SG_LN2_G,
+  L_SG_LN2_B, L_LN1_G, L_LN1_B, L_FFN_W1, L_FFN_B1, L_FFN_W2, L_FFN_B2, L_LN2_G, L_LN2_B, L_COUNT
+};
+
+void slot_sizes(const mfb200_net_desc &n, std::vector<size_t> &g, std::vector<size_t> &l) {
+  const size_t d = n.embedding, T = 64, pe = n.pe, ed = n.emb_dff, dp = n.policy_d;
+  const size_t c = n.smolgen_compress, h1 = n.smolgen_hidden, hg = size_t(n.heads) * n.smolgen_gen;
+  g.assign(G_COUNT, 0);
+  g[G_PREPROC_W] = T * pe * 12 * T;
+  g[G_PREPROC_B] = T * pe;
+  g[G_EMB_W] = d * (112 + pe);
+  g[G_EMB_B] = d;
+  g[G_EMB_LN_G] = g[G_EMB_LN_B] = d;
+  g[G_MULT_GATE] = g[G_ADD_GATE] = d * T;
+  g[G_EFFN_W1] = ed * d;
+  g[G_EFFN_B1] = ed;
+  g[G_EFFN_W2] = d * ed;
+  g[G_EFFN_B2] = d;
+  g[G_EFFN_LN_G] = g[G_EFFN_LN_B] = d;
+  g[G_SMOLGEN_W] = T * T * size_t(n.smolgen_gen);
+  g[G_POL_W] = dp * d;
+  g[G_POL_B] = dp;
+  g[G_POL_WQ] = g[G_POL_WK] = dp * dp;
+  g[G_POL_BQ] = g[G_POL_BK] = dp;
+  g[G_POL_PPO] = 4 * dp;
+  g[G_VAL_W] = size_t(n.value_emb) * d;
+  g[G_VAL_B] = n.value_emb;
+  g[G_VAL_W1] = size_t(n.value_hidden) * T * n.value_emb;
+  g[G_VAL_B1] = n.value_hidden;
+  g[G_VAL_W2] = 3 * size_t(n.value_hidden);
+  g[G_VAL_B2] = 3;
+  g[G_MOV_W] = size_t(n.mlh_emb) * d;
+  g[G_MOV_B] = n.mlh_emb;
+  g[G_MOV_W1] = size_t(n.mlh_hidden) * T * n.mlh_emb;
+  g[G_MOV_B1] = n.mlh_hidden;
+  g[G_MOV_W2] = n.mlh_hidden;
+  g[G_MOV_B2] = 1;
+  l.assign(L_COUNT, 0);
+  l[L_Q_W] = l[L_K_W] = l[L_V_W] = l[L_O_W] = d * d;
+  l[L_Q_B] = l[L_K_B] = l[L_V_B] = l[L_O_B] = d;
+  l[L_SG_COMPRESS] = c * d;
+  l[L_SG_W1] = h1 * T * c;
+  l[L_SG_B1] = l[L_SG_LN1_G] = l[L_SG_LN1_B] = h1;
+  l[L_SG_W2] = hg * h1;
+  l[L_SG_B2] = l[L_SG_LN2_G] = l[L_SG_LN2_B] = hg;
+  l[L_LN1_G] = l[L_LN1_B] = l[L_LN2_G] = l[L_LN2_B] = d;
+  l[L_FFN_W1] = size_t(n.dff) * d;
+  l[L_FFN_B1] = n.dff;
+  l[L_FFN_W2] = d * n.dff;
+  l[L_FFN_B2] = d;
+}
+
+size_t blob_floats(const mfb200_net_desc &n) {
+  std::vector<size_t> g, l;
+  slot_sizes(n, g, l);
+  size_t t = 0;
+  for (size_t v : g) t += v;
+  size_t tl = 0;
+  for (size_t v : l) tl += v;
+  return t + tl * size_t(n.layers);
+}
+
+const char *validate(const mfb200_net_desc &n) {
+  if (n.embedding <= 0 || n.embedding % 64) return "embedding must be a positive multiple of 64";
+  if (n.layers <= 0) return "layers must be positive";
+  if (n.heads <= 0 || n.embedding / n.heads != 32 || n.embedding % n.heads)
+    return "head depth (embedding/heads) must be 32";
+  if (n.dff <= 0 || n.dff % 16 || n.emb_dff <= 0 || n.emb_dff % 16) return "dff must be a multiple of 16";
+  if (n.pe <= 0 || n.pe % 8 || 112 + n.pe > kEmbIn) return "pe must be a multiple of 8, at most 80";
+  if (n.smolgen_compress <= 0 || n.smolgen_compress % 16) return "smolgen compress must be a multiple of 16";
+  if (n.smolgen_hidden <= 0 || n.smolgen_hidden % 16) return "smolgen hidden must be a multiple of 16";
+  if (n.smolgen_gen <= 0 || n.smolgen_gen % 16) return "smolgen gen must be a multiple of 16";
+  if (n.policy_d <= 0 || n.policy_d % 64) return "policy embedding must be a multiple of 64";
+  if (n.value_emb <= 0 || n.mlh_emb <= 0 || n.value_emb + n.mlh_emb > 64)
+    return "value + moves-left embeddings must fit in 64 columns";
+  if (n.value_hidden <= 0 || n.mlh_hidden <= 0 || (n.value_hidden + n.mlh_hidden) % 16)
+    return "value + moves-left hidden widths must sum to a multiple of 16";
+  for (int a : {n.act_default, n.act_smolgen, n.act_ffn})
+    if (a < 0 || a > 7) return "unknown activation code";
+  const int w = n.embedding;
+  if (w != 128 && w != 256 && w != 512 && w != 1024) return "embedding must be 128, 256, 512 or 1024";
+  return nullptr;
+}
+
+// Policy gather table: policy index -> raw index (64*64 + 8*24 layout of
+// src/nn/tables/attention_policy_map.h:15), built from the move geometry of
+// the 1858-move encoding (src/nn/policy_map.cpp): every queen/knight move
+// from each square in ascending (from, to) order, then the 7th-rank
+// underpromotions from_file*24 + to_file*3 + piece for |df| <= 1.
+std::vector<int16_t> build_gather() {
+  std::vector<int16_t> gather(kPolicy, -1);
+  int next = 0;
+  for (int from = 0; from < 64; ++from)
+    for (int to = 0; to < 64; ++to) {
+      if (to == from) continue;
+      const int dr = to / 8 - from / 8, df = to % 8 - from % 8;
+      const int adr = dr < 0 ? -dr : dr, adf = df < 0 ? -df : df;
+      if (dr == 0 || df == 0 || adr == adf || (adr == 1 && adf == 2) || (adr == 2 && adf == 1))
+        gather[next++] = static_cast<int16_t>(from * 64 + to);
+    }
+  for (int ff = 0; ff < 8; ++ff)
+    for (int tf = 0; tf < 8; ++tf)
+      for (int piece = 0; piece < 3; ++piece)
+        if (tf - ff >= -1 && tf - ff <= 1)
+          gather[next++] = static_cast<int16_t>(4096 + ff * 24 + tf * 3 + piece);
+  if (next != kPolicy) throw Fail("internal: policy map has wrong size");
+  return gather;
+}
+
+// ------------------------------------------------------------ device state
+struct Mat {  // a weight matrix [rows, ld] on the device (bf16 or e4m3)
+  void *w = nullptr;
+  const float *scale = nullptr;  // per-row (output channel) scale for e4m3
+  int rows = 0, ld = 0;
+  bool fp8 = false;
+};
+
+struct LayerW {
+  Mat qkvc, o, f1, f2, sg1, sg2;
+  float *b_qkvc, *b_o, *ln1_g, *ln1_b, *b_f1, *b_f2, *ln2_g, *ln2_b;
+  float *b_sg1, *sg_ln1_g, *sg_ln1_b, *b_sg2, *sg_ln2_g, *sg_ln2_b;
+};
+
+struct Weights {
+  Mat pe, emb, effn1, effn2, sg_global, pol, qk, vm, vm1;
+  float *b_pe, *b_emb, *ln_emb_g, *ln_emb_b, *multT, *addT, *b_effn1, *b_effn2, *ln_effn_g,
+      *ln_effn_b, *b_pol, *b_qk, *ppo3, *b_vm, *b_vm1, *w2v, *b2v, *w2m, *b2m;
+  int16_t *gather;
+  std::vector<LayerW> layers;
+};
+
+// Builds the packed arena on the host, then one copy to the device.
+class ArenaBuilder {
+ public:
+  size_t add(size_t bytes) {
+    const size_t off = (host.size() + 255) & ~size_t(255);
+    host.resize(off + bytes);
+    return off;
+  }
+  std::vector<uint8_t> host;
+};
+
+struct Shard {  // one GPU
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  void *arena = nullptr;
+  size_t arena_bytes = 0;
+  Weights w;
+  // workspace
+  void *ws = nullptr;
+  size_t ws_bytes = 0;
+  uint64_t *masks;
+  float *values;
+  __nv_bfloat16 *x0, *p, *peo, *X, *X1, *T, *QKV, *C, *S1, *S2pre, *S2, *BIAS, *CTX, *H, *E, *QK,
+      *VM, *VH;
+  float *policy, *wdl, *mlh;
+  unsigned *status;
+  cudaEvent_t ev[4];
+  struct Step {
+    std::string name;
+    double flops = 0;
+    bool is_gemm = false;
+    GemmLaunch g;
+    std::function<void(cudaStream_t)> fn;
+  };
+  struct Plan {
+    std::vector<Step> steps;
+    cudaGraphExec_t graph = nullptr;
+  };
+  std::map<int, std::unique_ptr<Plan>> plans;
+};
+
+}  // namespace
+
+struct mfb200_handle {
+  mfb200_net_desc desc;
+  mfb200_config cfg;
+  std::vector<std::unique_ptr<Shard>> shards;
+  std::mutex mu;
+  std::string last_error;
+  size_t weight_bytes = 0, ws_bytes = 0;
+  std::string device_name;
+};
+
+namespace {
+
+// ------------------------------------------------------------ packing
+struct Packer {
+  const mfb200_net_desc &n;
+  const float *blob;
+  std::vector<const float *> gp;
+  std::vector<std::vector<const float *>> lp;
+  Packer(const mfb200_net_desc &n_, const float *b) : n(n_), blob(b) {
+    std::vector<size_t> g, l;
+    slot_sizes(n, g, l);
+    const float *p = blob;
+    gp.resize(G_COUNT);
+    for (int i = 0; i < G_COUNT; ++i) {
+      gp[i] = p;
+      p += g[i];
+    }
+    lp.resize(n.layers);
+    for (int k = 0; k < n.layers; ++k) {
+      lp[k].resize(L_COUNT);
+      for (int i = 0; i < L_COUNT; ++i) {
+        lp[k][i] = p;
+        p += l[i];
+      }
+    }
+  }
+};
+
+// Lays the packed weights out in `ab`; records host offsets in `off` for
+// pointer fix-up after the device copy.
+struct Layout {
+  std::vector<std::pair<void **, size_t>> fix;  // (pointer field, arena offset)
+};
+
+template <class T>
+void put_f32(ArenaBuilder &ab, Layout &lay, T **field, const float *src, size_t n) {
+  const size_t off = ab.add(n * 4);
+  if (src) std::memcpy(ab.host.data() + off, src, n * 4);
+  lay.fix.push_back({reinterpret_cast<void **>(field), off});
+}
+
+// bf16 matrix of `rows` x `ld` (zero padded), filled by `at(r, c)` for c < cols.
+template <class F>
+void put_mat(ArenaBuilder &ab, Layout &lay, Mat &m, int rows, int cols, int ld, F at) {
+  const size_t off = ab.add(size_t(rows) * ld * 2);
+  uint16_t *dst = reinterpret_cast<uint16_t *>(ab.host.data() + off);
+  for (int r = 0; r < rows; ++r)
+    for (int c = 0; c < ld; ++c) dst[size_t(r) * ld + c] = c < cols ? f2bf(at(r, c)) : 0;
+  m.rows = rows;
+  m.ld = ld;
+  m.fp8 = false;
+  lay.fix.push_back({&m.w, off});
+}
+
+void pack_weights(const mfb200_net_desc &n, const float *blob, ArenaBuilder &ab, Layout &lay,
+                  Weights &W) {
+  Packer P(n, blob);
+  const int d = n.embedding, T = 64, dp = n.policy_d, pe = n.pe;
+  const auto &g = P.gp;
+  auto dense = [&](Mat &m, const float *src, int rows, int cols) {
+    put_mat(ab, lay, m, rows, cols, cols, [&](int r, int c) { return src[size_t(r) * cols + c]; });
+  };
+  dense(W.pe, g[G_PREPROC_W], T * pe, 12 * T);
+  put_f32(ab, lay, &W.b_pe, g[G_PREPROC_B], size_t(T) * pe);
+  put_mat(ab, lay, W.emb, d, 112 + pe, kEmbIn,
+          [&](int r, int c) { return g[G_EMB_W][size_t(r) * (112 + pe) + c]; });
+  put_f32(ab, lay, &W.b_emb, g[G_EMB_B], d);
+  put_f32(ab, lay, &W.ln_emb_g, g[G_EMB_LN_G], d);
+  put_f32(ab, lay, &W.ln_emb_b, g[G_EMB_LN_B], d);
+  {
+    // gates: reference layout is channel-major [d][64] (cpu_network.cpp:1290-1296);
+    // stored square-major [64][d] so the LN kernel reads them contiguously.
+    std::vector<float> mt(size_t(T) * d), at(size_t(T) * d);
+    for (int c = 0; c < d; ++c)
+      for (int s = 0; s < T; ++s) {
+        mt[size_t(s) * d + c] = g[G_MULT_GATE][size_t(c) * T + s];
+        at[size_t(s) * d + c] = g[G_ADD_GATE][size_t(c) * T + s];
+      }
+    put_f32(ab, lay, &W.multT, mt.data(), mt.size());
+    put_f32(ab, lay, &W.addT, at.data(), at.size());
+  }
+  dense(W.effn1, g[G_EFFN_W1], n.emb_dff, d);
+  put_f32(ab, lay, &W.b_effn1, g[G_EFFN_B1], n.emb_dff);
+  dense(W.effn2, g[G_EFFN_W2], d, n.emb_dff);
+  put_f32(ab, lay, &W.b_effn2, g[G_EFFN_B2], d);
+  put_f32(ab, lay, &W.ln_effn_g, g[G_EFFN_LN_G], d);
+  put_f32(ab, lay, &W.ln_effn_b, g[G_EFFN_LN_B], d);
+  dense(W.sg_global, g[G_SMOLGEN_W], T * T, n.smolgen_gen);
+  dense(W.pol, g[G_POL_W], dp, d);
+  put_f32(ab, lay, &W.b_pol, g[G_POL_B], dp);
+  // wq and wk as one [2*dp, dp] matrix (q rows first)
+  put_mat(ab, lay, W.qk, 2 * dp, dp, dp, [&](int r, int c) {
+    return r < dp ? g[G_POL_WQ][size_t(r) * dp + c] : g[G_POL_WK][size_t(r - dp) * dp + c];
+  });
+  {
+    std::vector<float> b(2 * size_t(dp));
+    std::memcpy(b.data(), g[G_POL_BQ], dp * 4);
+    std::memcpy(b.data() + dp, g[G_POL_BK], dp * 4);
+    put_f32(ab, lay, &W.b_qk, b.data(), b.size());
+    std::vector<float> p3(3 * size_t(dp));
+    for (int r = 0; r < 3; ++r)
+      for (int c = 0; c < dp; ++c)
+        p3[size_t(r) * dp + c] = g[G_POL_PPO][size_t(r) * dp + c] + g[G_POL_PPO][size_t(3) * dp + c];
+    put_f32(ab, lay, &W.ppo3, p3.data(), p3.size());
+  }
+  // value | moves-left per-square embedding as one [64, d] matrix
+  const int ve = n.value_emb, me = n.mlh_emb, vh = n.value_hidden, mh = n.mlh_hidden;
+  put_mat(ab, lay, W.vm, 64, d, d, [&](int r, int c) {
+    if (r < ve) return g[G_VAL_W][size_t(r) * d + c];
+    if (r < ve + me) return g[G_MOV_W][size_t(r - ve) * d + c];
+    return 0.0f;
+  });
+  {
+    std::vector<float> b(64, 0.0f);
+    std::memcpy(b.data(), g[G_VAL_B], ve * 4);
+    std::memcpy(b.data() + ve, g[G_MOV_B], me * 4);
+    put_f32(ab, lay, &W.b_vm, b.data(), 64);
+  }
+  // flattened dense over the [64 squares x 64 columns] view of that output
+  put_mat(ab, lay, W.vm1, vh + mh, 64 * 64, 64 * 64, [&](int r, int k) {
+    const int s = k / 64, c = k % 64;
+    if (r < vh) return c < ve ? g[G_VAL_W1][size_t(r) * 64 * ve + size_t(s) * ve + c] : 0.0f;
+    if (c >= ve && c < ve + me) return g[G_MOV_W1][size_t(r - vh) * 64 * me + size_t(s) * me + (c - ve)];
+    return 0.0f;
+  });
+  {
+    std::vector<float> b(vh + mh);
+    std::memcpy(b.data(), g[G_VAL_B1], vh * 4);
+    std::memcpy(b.data() + vh, g[G_MOV_B1], mh * 4);
+    put_f32(ab, lay, &W.b_vm1, b.data(), b.size());
+  }
+  put_f32(ab, lay, &W.w2v, g[G_VAL_W2], 3 * size_t(vh));
+  put_f32(ab, lay, &W.b2v, g[G_VAL_B2], 3);
+  put_f32(ab, lay, &W.w2m, g[G_MOV_W2], mh);
+  put_f32(ab, lay, &W.b2m, g[G_MOV_B2], 1);
+  {
+    const std::vector<int16_t> gather = build_gather();
+    const size_t off = ab.add(gather.size() * 2);
+    std::memcpy(ab.host.data() + off, gather.data(), gather.size() * 2);
+    lay.fix.push_back({reinterpret_cast<void **>(&W.gather), off});
+  }
+  W.layers.resize(n.layers);
+  const int c = n.smolgen_compress, h1 = n.smolgen_hidden, hg = n.heads * n.smolgen_gen;
+  for (int k = 0; k < n.layers; ++k) {
+    const auto &l = P.lp[k];
+    LayerW &Lw = W.layers[k];
+    // Q | K | V | smolgen compress as one [3d + c, d] matrix
+    put_mat(ab, lay, Lw.qkvc, 3 * d + c, d, d, [&](int r, int col) {
+      if (r < d) return l[L_Q_W][size_t(r) * d + col];
+      if (r < 2 * d) return l[L_K_W][size_t(r - d) * d + col];
+      if (r < 3 * d) return l[L_V_W][size_t(r - 2 * d) * d + col];
+      return l[L_SG_COMPRESS][size_t(r - 3 * d) * d + col];
+    });
+    {
+      std::vector<float> b(3 * size_t(d) + c, 0.0f);
+      std::memcpy(b.data(), l[L_Q_B], d * 4);
+      std::memcpy(b.data() + d, l[L_K_B], d * 4);
+      std::memcpy(b.data() + 2 * d, l[L_V_B], d * 4);
+      put_f32(ab, lay, &Lw.b_qkvc, b.data(), b.size());
+    }
+    dense(Lw.o, l[L_O_W], d, d);
+    put_f32(ab, lay, &Lw.b_o, l[L_O_B], d);
+    put_f32(ab, lay, &Lw.ln1_g, l[L_LN1_G], d);
+    put_f32(ab, lay, &Lw.ln1_b, l[L_LN1_B], d);
+    dense(Lw.f1, l[L_FFN_W1], n.dff, d);
+    put_f32(ab, lay, &Lw.b_f1, l[L_FFN_B1], n.dff);
+    dense(Lw.f2, l[L_FFN_W2], d, n.dff);
+    put_f32(ab, lay, &Lw.b_f2, l[L_FFN_B2], d);
+    put_f32(ab, lay, &Lw.ln2_g, l[L_LN2_G], d);
+    put_f32(ab, lay, &Lw.ln2_b, l[L_LN2_B], d);
+    dense(Lw.sg1, l[L_SG_W1], h1, 64 * c);
+    put_f32(ab, lay, &Lw.b_sg1, l[L_SG_B1], h1);
+    put_f32(ab, lay, &Lw.sg_ln1_g, l[L_SG_LN1_G], h1);
+    put_f32(ab, lay, &Lw.sg_ln1_b, l[L_SG_LN1_B], h1);
+    dense(Lw.sg2, l[L_SG_W2], hg, h1);
+    put_f32(ab, lay, &Lw.b_sg2, l[L_SG_B2], hg);
+    put_f32(ab, lay, &Lw.sg_ln2_g, l[L_SG_LN2_G], hg);
+    put_f32(ab, lay, &Lw.sg_ln2_b, l[L_SG_LN2_B], hg);
+  }
+}
+
+// ------------------------------------------------------------ workspace
+void alloc_workspace(Shard &S, const mfb200_net_desc &n, int max_batch) {
+  const size_t B = max_batch, M = B * 64, d = n.embedding;
+  const size_t hg = size_t(n.heads) * n.smolgen_gen;
+  const size_t hid = std::max<size_t>(n.dff, n.emb_dff);
+  std::vector<std::pair<void **, size_t>> parts = {
+      {reinterpret_cast<void **>(&S.masks), B * kPlanes * 8},
+      {reinterpret_cast<void **>(&S.values), B * kPlanes * 4},
+      {reinterpret_cast<void **>(&S.x0), M * kEmbIn * 2},
+      {reinterpret_cast<void **>(&S.p), B * kPeInputs * 2},
+      {reinterpret_cast<void **>(&S.peo), B * 64 * n.pe * 2},
+      {reinterpret_cast<void **>(&S.X), M * d * 2},
+      {reinterpret_cast<void **>(&S.X1), M * d * 2},
+      {reinterpret_cast<void **>(&S.T), M * d * 2},
+      {reinterpret_cast<void **>(&S.QKV), M * 3 * d * 2},
+      {reinterpret_cast<void **>(&S.C), M * n.smolgen_compress * 2},
+      {reinterpret_cast<void **>(&S.S1), B * n.smolgen_hidden * 2},
+      {reinterpret_cast<void **>(&S.S2pre), B * hg * 2},
+      {reinterpret_cast<void **>(&S.S2), B * hg * 2},
+      {reinterpret_cast<void **>(&S.BIAS), B * n.heads * 4096 * 2},
+      {reinterpret_cast<void **>(&S.CTX), M * d * 2},
+      {reinterpret_cast<void **>(&S.H), M * hid * 2},
+      {reinterpret_cast<void **>(&S.E), M * n.policy_d * 2},
+      {reinterpret_cast<void **>(&S.QK), M * 2 * n.policy_d * 2},
+      {reinterpret_cast<void **>(&S.VM), M * 64 * 2},
+      {reinterpret_cast<void **>(&S.VH), B * (n.value_hidden + n.mlh_hidden) * 2},
+      {reinterpret_cast<void **>(&S.policy), B * kPolicy * 4},
+      {reinterpret_cast<void **>(&S.wdl), B * 3 * 4},
+      {reinterpret_cast<void **>(&S.mlh), B * 4},
+      {reinterpret_cast<void **>(&S.status), 256},
+  };
+  size_t total = 0;
+  std::vector<size_t> offs;
+  for (auto &p : parts) {
+    offs.push_back(total);
+    total += (p.second + 1023) & ~size_t(1023);
+  }
+  check(cudaMalloc(&S.ws, total), "workspace allocation");
+  S.ws_bytes = total;
+  check(cudaMemset(S.ws, 0, total), "workspace clear");
+  for (size_t i = 0; i < parts.size(); ++i)
+    *parts[i].first = static_cast<uint8_t *>(S.ws) + offs[i];
+}
+
+// ------------------------------------------------------------ plan
+int pick_bn(int M, int N) {
+  if (N < 128) return 64;
+  if (N < 256) return 128;
+  const long long tiles256 = static_cast<long long>((M + 127) / 128) * ((N + 255) / 256);
+  if (tiles256 >= num_sms()) return 256;
+  const long long tiles128 = static_cast<long long>((M + 127) / 128) * ((N + 127) / 128);
+  return tiles128 >= num_sms() ? 128 : (tiles128 * 2 <= num_sms() ? 64 : 128);
+}
+
+GemmArgs base_args(Shard &S, int M, int N, int K) {
+  GemmArgs a{};
+  a.M = M;
+  a.N = N;
+  a.K = K;
+  a.a_scale = 1.0f;
+  a.alpha = 1.0f;
+  a.out_inv_scale = 1.0f;
+  a.status = S.status;
+  return a;
+}
+
+void add_gemm(Shard::Plan &P, Shard &S, const char *name, const void *A, long long lda,
+              const Mat &W, GemmArgs a) {
+  Shard::Step st;
+  st.name = name;
+  st.is_gemm = true;
+  st.flops = 2.0 * a.M * double(a.N) * a.K;
+  const int bn = (a.mode == kEpiRowLN) ? a.N : pick_bn(a.M, a.N);
+  if (const char *err = plan_gemm(st.g, A, lda, W.w, W.ld, bn, W.fp8, a))
+    throw Fail(std::string(name) + ": " + err);
+  P.steps.push_back(std::move(st));
+}
+
+void add_fn(Shard::Plan &P, const char *name, double flops, std::function<void(cudaStream_t)> fn) {
+  Shard::Step st;
+  st.name = name;
+  st.flops = flops;
+  st.fn = std::move(fn);
+  P.steps.push_back(std::move(st));
+}
+
+std::unique_ptr<Shard::Plan> build_plan(Shard &S, const mfb200_net_desc &n, int B) {
+  auto P = std::make_unique<Shard::Plan>();
+  const int M = B * 64, d = n.embedding, dp = n.policy_d, H = n.heads;
+  const int hg = n.heads * n.smolgen_gen, vh = n.value_hidden, mh = n.mlh_hidden;
+  const float alpha = std::pow(2.0f * static_cast<float>(n.layers), -0.25f);  // plan :1152-1162
+  const float eps = 1e-3f;  // PE_DENSE epsilons (plan :1164-1193)
+  Weights &W = S.w;
+
+  add_fn(*P, "unpack", 0, [&S, B](cudaStream_t s) { launch_unpack(S.masks, S.values, B, S.x0, S.p, s); });
+  {
+    GemmArgs a = base_args(S, B, 64 * n.pe, kPeInputs);
+    a.bias = W.b_pe;
+    a.out = S.peo;
+    a.ldo = 64 * n.pe;
+    add_gemm(*P, S, "pe_dense", S.p, kPeInputs, W.pe, a);
+  }
+  add_fn(*P, "pe_concat", 0, [&S, B, pe = n.pe](cudaStream_t s) { launch_pe_concat(S.peo, B, pe, S.x0, s); });
+  {
+    GemmArgs a = base_args(S, M, d, kEmbIn);
+    a.bias = W.b_emb;
+    a.act = n.act_default;
+    a.out = S.T;
+    a.ldo = d;
+    add_gemm(*P, S, "emb_dense", S.x0, kEmbIn, W.emb, a);
+  }
+  add_fn(*P, "emb_ln_gates", 0, [&S, &W, M, d, eps](cudaStream_t s) {
+    launch_layernorm(S.T, M, d, W.ln_emb_g, W.ln_emb_b, eps, W.multT, W.addT, S.X, s);
+  });
+  {
+    GemmArgs a = base_args(S, M, n.emb_dff, d);
+    a.bias = W.b_effn1;
+    a.act = n.act_ffn;
+    a.out = S.H;
+    a.ldo = n.emb_dff;
+    add_gemm(*P, S, "emb_ffn1", S.X, d, W.effn1, a);
+    GemmArgs b = base_args(S, M, d, n.emb_dff);
+    b.mode = kEpiResid;
+    b.bias = W.b_effn2;
+    b.resid = S.X;
+    b.ldr = d;
+    b.alpha = alpha;
+    b.out = S.T;
+    b.ldo = d;
+    add_gemm(*P, S, "emb_ffn2", S.H, n.emb_dff, W.effn2, b);
+  }
+  add_fn(*P, "emb_ffn_ln", 0, [&S, &W, M, d, eps](cudaStream_t s) {
+    launch_layernorm(S.T, M, d, W.ln_effn_g, W.ln_effn_b, eps, nullptr, nullptr, S.X, s);
+  });
+  for (int k = 0; k < n.layers; ++k) {
+    LayerW &Lw = W.layers[k];
+    {
+      GemmArgs a = base_args(S, M, 3 * d + n.smolgen_compress, d);
+      a.bias = Lw.b_qkvc;
+      a.out = S.QKV;
+      a.ldo = 3 * d;
+      a.out2 = S.C;
+      a.ldo2 = n.smolgen_compress;
+      a.split = 3 * d;
+      add_gemm(*P, S, "qkv", S.X, d, Lw.qkvc, a);
+    }
+    {
+      // smolgen dense1 over the flattened [B, 64*c] compress output
+      GemmArgs a = base_args(S, B, n.smolgen_hidden, 64 * n.smolgen_compress);
+      a.bias = Lw.b_sg1;
+      a.act = n.act_smolgen;
+      a.out = S.S1;
+      a.ldo = n.smolgen_hidden;
+      const bool fused_ln = n.smolgen_hidden == 64 || n.smolgen_hidden == 128 || n.smolgen_hidden == 256;
+      if (fused_ln) {
+        a.mode = kEpiRowLN;
+        a.ln_gamma = Lw.sg_ln1_g;
+        a.ln_beta = Lw.sg_ln1_b;
+        a.ln_eps = eps;
+        add_gemm(*P, S, "smolgen_dense1_ln", S.C, 64 * n.smolgen_compress, Lw.sg1, a);
+      } else {
+        a.out = S.S2pre;
+        add_gemm(*P, S, "smolgen_dense1", S.C, 64 * n.smolgen_compress, Lw.sg1, a);
+        add_fn(*P, "smolgen_ln1", 0, [&S, &Lw, B, w = n.smolgen_hidden, eps](cudaStream_t s) {
+          launch_layernorm(S.S2pre, B, w, Lw.sg_ln1_g, Lw.sg_ln1_b, eps, nullptr, nullptr, S.S1, s);
+        });
+      }
+    }
+    {
+      GemmArgs a = base_args(S, B, hg, n.smolgen_hidden);
+      a.bias = Lw.b_sg2;
+      a.act = n.act_smolgen;
+      a.out = S.S2pre;
+      a.ldo = hg;
+      add_gemm(*P, S, "smolgen_dense2", S.S1, n.smolgen_hidden, Lw.sg2, a);
+    }
+    add_fn(*P, "smolgen_ln2", 0, [&S, &Lw, B, hg, eps](cudaStream_t s) {
+      launch_layernorm(S.S2pre, B, hg, Lw.sg_ln2_g, Lw.sg_ln2_b, eps, nullptr, nullptr, S.S2, s);
+    });
+    {
+      GemmArgs a = base_args(S, B * H, 4096, n.smolgen_gen);
+      a.out = S.BIAS;
+      a.ldo = 4096;
+      add_gemm(*P, S, "smolgen_global", S.S2, n.smolgen_gen, W.sg_global, a);
+    }
+    add_fn(*P, "attention", 4.0 * B * H * 64.0 * 64.0 * 32.0, [&S, B, H, d](cudaStream_t s) {
+      launch_attention(S.QKV, 3LL * d, S.BIAS, B, H, d, S.CTX, s);
+    });
+    {
+      GemmArgs a = base_args(S, M, d, d);
+      a.mode = kEpiResid;
+      a.bias = Lw.b_o;
+      a.resid = S.X;
+      a.ldr = d;
+      a.alpha = alpha;
+      a.out = S.T;
+      a.ldo = d;
+      add_gemm(*P, S, "out_proj", S.CTX, d, Lw.o, a);
+    }
+    add_fn(*P, "ln1", 0, [&S, &Lw, M, d, eps](cudaStream_t s) {
+      launch_layernorm(S.T, M, d, Lw.ln1_g, Lw.ln1_b, eps, nullptr, nullptr, S.X1, s);
+    });
+    {
+      GemmArgs a = base_args(S, M, n.dff, d);
+      a.bias = Lw.b_f1;
+      a.act = n.act_ffn;
+      a.out = S.H;
+      a.ldo = n.dff;
+      add_gemm(*P, S, "ffn1", S.X1, d, Lw.f1, a);
+      GemmArgs b = base_args(S, M, d, n.dff);
+      b.mode = kEpiResid;
+      b.bias = Lw.b_f2;
+      b.resid = S.X1;
+      b.ldr = d;
+      b.alpha = alpha;
+      b.out = S.T;
+      b.ldo = d;
+      add_gemm(*P, S, "ffn2", S.H, n.dff, Lw.f2, b);
+    }
+    add_fn(*P, "ln2", 0, [&S, &Lw, M, d, eps](cudaStream_t s) {
+      launch_layernorm(S.T, M, d, Lw.ln2_g, Lw.ln2_b, eps, nullptr, nullptr, S.X, s);
+    });
+  }
+  {
+    GemmArgs a = base_args(S, M, dp, d);
+    a.bias = W.b_pol;
+    a.act = n.act_default;
+    a.out = S.E;
+    a.ldo = dp;
+    add_gemm(*P, S, "policy_embed", S.X, d, W.pol, a);
+    GemmArgs b = base_args(S, M, 2 * dp, dp);
+    b.bias = W.b_qk;
+    b.out = S.QK;
+    b.ldo = 2 * dp;
+    add_gemm(*P, S, "policy_qk", S.E, dp, W.qk, b);
+  }
+  add_fn(*P, "policy_map", 2.0 * B * 64.0 * 64.0 * dp, [&S, &W, B, dp](cudaStream_t s) {
+    launch_policy_map(S.QK, B, dp, W.ppo3, W.gather, S.policy, s);
+  });
+  {
+    GemmArgs a = base_args(S, M, 64, d);
+    a.bias = W.b_vm;
+    a.act = n.act_default;
+    a.out = S.VM;
+    a.ldo = 64;
+    add_gemm(*P, S, "value_mlh_embed", S.X, d, W.vm, a);
+    GemmArgs b = base_args(S, B, vh + mh, 64 * 64);
+    b.bias = W.b_vm1;
+    b.act = n.act_default;
+    b.out = S.VH;
+    b.ldo = vh + mh;
+    add_gemm(*P, S, "value_mlh_dense1", S.VM, 64 * 64, W.vm1, b);
+  }
+  add_fn(*P, "heads", 0, [&S, &W, B, vh, mh](cudaStream_t s) {
+    launch_heads(S.VH, B, vh, mh, W.w2v, W.b2v, W.w2m, W.b2m, S.wdl, S.mlh, s);
+  });
+  return P;
+}
+
+void run_steps(Shard::Plan &P, cudaStream_t s) {
+  for (auto &st : P.steps) {
+    if (st.is_gemm)
+      check(launch_gemm(st.g, s), st.name.c_str());
+    else
+      st.fn(s);
+  }
+  check(cudaGetLastError(), "kernel launch");
+}
+
+Shard::Plan &get_plan(mfb200_handle *h, Shard &S, int B) {
+  auto it = S.plans.find(B);
+  if (it != S.plans.end()) return *it->second;
+  auto P = build_plan(S, h->desc, B);
+  // First run eagerly (also sets kernel attributes), then capture a graph.
+  run_steps(*P, S.stream);
+  check(cudaStreamSynchronize(S.stream), "first forward");
+  if (h->cfg.use_graphs) {
+    cudaGraph_t graph;
+    check(cudaStreamBeginCapture(S.stream, cudaStreamCaptureModeThreadLocal), "graph capture begin");
+    run_steps(*P, S.stream);
+    check(cudaStreamEndCapture(S.stream, &graph), "graph capture end");
+    check(cudaGraphInstantiate(&P->graph, graph, 0), "graph instantiate");
+    cudaGraphDestroy(graph);
+  }
+  Shard::Plan &ref = *P;
+  S.plans[B] = std::move(P);
+  return ref;
+}
+
+void forward(mfb200_handle *h, Shard &S, int B, cudaStream_t s) {
+  Shard::Plan &P = get_plan(h, S, B);
+  if (P.graph)
+    check(cudaGraphLaunch(P.graph, s), "graph launch");
+  else
+    run_steps(P, s);
+}
+
+void check_status(Shard &S) {
+  unsigned st = 0;
+  check(cudaMemcpy(&st, S.status, 4, cudaMemcpyDeviceToHost), "status read");
+  if (st) {
+    cudaMemset(S.status, 0, 4);
+    throw Fail("device wait timed out in a GEMM (code " + std::to_string(st) + ")");
+  }
+}
+
+int fail(mfb200_handle *h, const std::string &msg) {
+  t_last_error = msg;
+  if (h) h->last_error = msg;
+  return 1;
+}
+
+}  // namespace
+
+// ============================================================ C ABI
+extern "C" size_t mfb200_weight_bytes(const mfb200_net_desc *desc) {
+  return desc ? blob_floats(*desc) * sizeof(float) : 0;
+}
+
+extern "C" int mfb200_create(const mfb200_net_desc *desc, const void *weights, size_t bytes,
+                             const mfb200_config *cfg, mfb200_handle **out) {
+  if (!desc || !weights || !cfg || !out) return fail(nullptr, "mfb200_create: null argument");
+  *out = nullptr;
+  if (const char *err = validate(*desc)) return fail(nullptr, std::string("mfb200_create: ") + err);
+  if (bytes != blob_floats(*desc) * sizeof(float))
+    return fail(nullptr, "mfb200_create: weight blob has " + std::to_string(bytes) +
+                             " bytes, expected " + std::to_string(blob_floats(*desc) * 4));
+  if (cfg->precision != MFB200_PRECISION_BF16)
+    return fail(nullptr, "mfb200_create: only bf16 precision is implemented in this build");
+  if (cfg->max_batch <= 0) return fail(nullptr, "mfb200_create: max_batch must be positive");
+  auto h = std::make_unique<mfb200_handle>();
+  h->desc = *desc;
+  h->cfg = *cfg;
+  if (h->cfg.num_devices <= 0) h->cfg.num_devices = 1;
+  try {
+    int count = 0;
+    check(cudaGetDeviceCount(&count), "cudaGetDeviceCount");
+    if (cfg->device < 0 || cfg->device + h->cfg.num_devices > count)
+      throw Fail("requested devices " + std::to_string(cfg->device) + ".." +
+                 std::to_string(cfg->device + h->cfg.num_devices - 1) + " but " +
+                 std::to_string(count) + " visible");
+    ArenaBuilder ab;
+    Layout lay;
+    Weights proto;
+    pack_weights(*desc, static_cast<const float *>(weights), ab, lay, proto);
+    const int per = (cfg->max_batch + h->cfg.num_devices - 1) / h->cfg.num_devices;
+    for (int i = 0; i < h->cfg.num_devices; ++i) {
+      auto S = std::make_unique<Shard>();
+      S->device = cfg->device + i;
+      check(cudaSetDevice(S->device), "cudaSetDevice");
+      cudaDeviceProp prop;
+      check(cudaGetDeviceProperties(&prop, S->device), "cudaGetDeviceProperties");
+      if (prop.major != 10) throw Fail(std::string("device is not an sm_100 GPU: ") + prop.name);
+      h->device_name = prop.name;
+      check(cudaStreamCreateWithFlags(&S->stream, cudaStreamNonBlocking), "stream");
+      for (auto &e : S->ev) check(cudaEventCreate(&e), "event");
+      check(cudaMalloc(&S->arena, ab.host.size()), "weight allocation");
+      S->arena_bytes = ab.host.size();
+      check(cudaMemcpy(S->arena, ab.host.data(), ab.host.size(), cudaMemcpyHostToDevice),
+            "weight upload");
+      // point the weight directory at this device's arena, then copy it
+      for (auto &f : lay.fix) *f.first = static_cast<uint8_t *>(S->arena) + f.second;
+      S->w = proto;
+      alloc_workspace(*S, *desc, per);
+      h->weight_bytes = S->arena_bytes;
+      h->ws_bytes = S->ws_bytes;
+      h->shards.push_back(std::move(S));
+    }
+  } catch (const std::exception &e) {
+    for (auto &S : h->shards) {
+      cudaSetDevice(S->device);
+      if (S->arena) cudaFree(S->arena);
+      if (S->ws) cudaFree(S->ws);
+      if (S->stream) cudaStreamDestroy(S->stream);
+    }
+    return fail(nullptr, std::string("mfb200_create: ") + e.what());
+  }
+  *out = h.release();
+  return 0;
+}
+
+namespace {
+int eval_shard(mfb200_handle *h, Shard &S, const uint64_t *masks, const float *values, int B,
+               float *policy, float *wdl, float *mlh, float *ms) {
+  check(cudaSetDevice(S.device), "cudaSetDevice");
+  cudaStream_t s = S.stream;
+  check(cudaEventRecord(S.ev[0], s), "event");
+  check(cudaMemcpyAsync(S.masks, masks, size_t(B) * kPlanes * 8, cudaMemcpyHostToDevice, s), "H2D masks");
+  check(cudaMemcpyAsync(S.values, values, size_t(B) * kPlanes * 4, cudaMemcpyHostToDevice, s), "H2D values");
+  check(cudaEventRecord(S.ev[1], s), "event");
+  forward(h, S, B, s);
+  check(cudaEventRecord(S.ev[2], s), "event");
+  if (policy)
+    check(cudaMemcpyAsync(policy, S.policy, size_t(B) * kPolicy * 4, cudaMemcpyDeviceToHost, s), "D2H policy");
+  if (wdl) check(cudaMemcpyAsync(wdl, S.wdl, size_t(B) * 12, cudaMemcpyDeviceToHost, s), "D2H wdl");
+  if (mlh) check(cudaMemcpyAsync(mlh, S.mlh, size_t(B) * 4, cudaMemcpyDeviceToHost, s), "D2H mlh");
+  check(cudaEventRecord(S.ev[3], s), "event");
+  check(cudaStreamSynchronize(s), "forward");
+  check_status(S);
+  cudaEventElapsedTime(&ms[0], S.ev[0], S.ev[1]);
+  cudaEventElapsedTime(&ms[1], S.ev[1], S.ev[2]);
+  cudaEventElapsedTime(&ms[2], S.ev[2], S.ev[3]);
+  cudaEventElapsedTime(&ms[3], S.ev[0], S.ev[3]);
+  return 0;
+}
+}  // namespace
+
+extern "C" int mfb200_evaluate(mfb200_handle *h, const uint64_t *masks, const float *values,
+                               int batch, float *policy, float *wdl, float *mlh,
+                               mfb200_timing *timing) {
+  if (!h) return fail(nullptr, "mfb200_evaluate: null handle");
+  std::lock_guard<std::mutex> lock(h->mu);
+  if (batch <= 0) return 0;
+  if (batch > h->cfg.max_batch)
+    return fail(h, "mfb200_evaluate: batch " + std::to_string(batch) + " exceeds max_batch " +
+                       std::to_string(h->cfg.max_batch));
+  if (!masks || !values) return fail(h, "mfb200_evaluate: null input");
+  const int nd = static_cast<int>(h->shards.size());
+  const int per = (batch + nd - 1) / nd;
+  std::vector<std::array<float, 4>> ms(nd, {0, 0, 0, 0});
+  std::vector<std::string> errs(nd);
+  auto work = [&](int i) {
+    const int lo = i * per, hi = std::min(batch, lo + per);
+    if (lo >= hi) return;
+    try {
+      eval_shard(h, *h->shards[i], masks + size_t(lo) * kPlanes, values + size_t(lo) * kPlanes,
+                 hi - lo, policy ? policy + size_t(lo) * kPolicy : nullptr,
+                 wdl ? wdl + size_t(lo) * 3 : nullptr, mlh ? mlh + lo : nullptr, ms[i].data());
+    } catch (const std::exception &e) {
+      errs[i] = e.what();
+    }
+  };
+  if (nd == 1) {
+    work(0);
+  } else {
+    std::vector<std::thread> th;
+    for (int i = 0; i < nd; ++i) th.emplace_back(work, i);
+    for (auto &t : th) t.join();
+  }
+  for (auto &e : errs)
+    if (!e.empty()) return fail(h, "mfb200_evaluate: " + e);
+  if (timing) {
+    *timing = mfb200_timing{0, 0, 0, 0};
+    for (auto &m : ms) {
+      timing->h2d_ms = std::max(timing->h2d_ms, m[0]);
+      timing->forward_ms = std::max(timing->forward_ms, m[1]);
+      timing->d2h_ms = std::max(timing->d2h_ms, m[2]);
+      timing->total_ms = std::max(timing->total_ms, m[3]);
+    }
+  }
+  return 0;
+}
+
+extern "C" int mfb200_evaluate_device(mfb200_handle *h, const uint64_t *d_masks,
+                                      const float *d_values, int batch, float *d_policy,
+                                      float *d_wdl, float *d_mlh, void *stream) {
+  if (!h) return fail(nullptr, "mfb200_evaluate_device: null handle");
+  std::lock_guard<std::mutex> lock(h->mu);
+  if (batch <= 0) return 0;
+  Shard &S = *h->shards[0];
+  if (batch > h->cfg.max_batch / static_cast<int>(h->shards.size()) + 1 && h->shards.size() > 1)
+    return fail(h, "mfb200_evaluate_device: batch exceeds one device's share of max_batch");
+  if (batch > h->cfg.max_batch) return fail(h, "mfb200_evaluate_device: batch exceeds max_batch");
+  try {
+    check(cudaSetDevice(S.device), "cudaSetDevice");
+    cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : S.stream;
+    if (d_masks != S.masks)
+      check(cudaMemcpyAsync(S.masks, d_masks, size_t(batch) * kPlanes * 8, cudaMemcpyDeviceToDevice, s), "masks");
+    if (d_values != S.values)
+      check(cudaMemcpyAsync(S.values, d_values, size_t(batch) * kPlanes * 4, cudaMemcpyDeviceToDevice, s), "values");
+    if (stream && !S.plans.count(batch)) {
+      // build (and capture) on the handle's own stream first
+      check(cudaStreamSynchronize(s), "sync");
+      get_plan(h, S, batch);
+    }
+    forward(h, S, batch, s);
+    if (d_policy)
+      check(cudaMemcpyAsync(d_policy, S.policy, size_t(batch) * kPolicy * 4, cudaMemcpyDeviceToDevice, s), "policy");
+    if (d_wdl) check(cudaMemcpyAsync(d_wdl, S.wdl, size_t(batch) * 12, cudaMemcpyDeviceToDevice, s), "wdl");
+    if (d_mlh) check(cudaMemcpyAsync(d_mlh, S.mlh, size_t(batch) * 4, cudaMemcpyDeviceToDevice, s), "mlh");
+  } catch (const std::exception &e) {
+    return fail(h, std::string("mfb200_evaluate_device: ") + e.what());
+  }
+  return 0;
+}
+
+extern "C" int mfb200_calibrate(mfb200_handle *h, const uint64_t *, const float *, int) {
+  return fail(h, "mfb200_calibrate: FP8 is not implemented in this build");
+}
+
+extern "C" int mfb200_capabilities(mfb200_handle *h, mfb200_caps *caps) {
+  if (!h || !caps) return fail(h, "mfb200_capabilities: null argument");
+  std::memset(caps, 0, sizeof(*caps));
+  caps->max_batch = h->cfg.max_batch;
+  caps->precision = h->cfg.precision;
+  caps->num_devices = static_cast<int>(h->shards.size());
+  caps->device = h->cfg.device;
+  caps->has_wdl = 1;
+  caps->has_moves_left = 1;
+  caps->weight_bytes = static_cast<int64_t>(h->weight_bytes);
+  caps->workspace_bytes = static_cast<int64_t>(h->ws_bytes);
+  std::snprintf(caps->device_name, sizeof(caps->device_name), "%s", h->device_name.c_str());
+  return 0;
+}
+
+extern "C" int mfb200_profile(mfb200_handle *h, int batch, int iters, float *stage_ms,
+                              double *stage_flops, char *names, size_t names_len, int max_stages) {
+  if (!h) return -1;
+  std::lock_guard<std::mutex> lock(h->mu);
+  try {
+    Shard &S = *h->shards[0];
+    check(cudaSetDevice(S.device), "cudaSetDevice");
+    if (batch <= 0 || batch > h->cfg.max_batch / static_cast<int>(h->shards.size()))
+      throw Fail("profile batch out of range");
+    Shard::Plan &P = get_plan(h, S, batch);
+    const int n = static_cast<int>(P.steps.size());
+    std::vector<cudaEvent_t> ev(n + 1);
+    for (auto &e : ev) check(cudaEventCreate(&e), "event");
+    std::vector<double> acc(n, 0.0);
+    for (int it = 0; it < std::max(1, iters); ++it) {
+      check(cudaEventRecord(ev[0], S.stream), "event");
+      for (int i = 0; i < n; ++i) {
+        auto &st = P.steps[i];
+        if (st.is_gemm)
+          check(launch_gemm(st.g, S.stream), st.name.c_str());
+        else
+          st.fn(S.stream);
+        check(cudaEventRecord(ev[i + 1], S.stream), "event");
+      }
+      check(cudaStreamSynchronize(S.stream), "profile");
+      for (int i = 0; i < n; ++i) {
+        float ms = 0;
+        cudaEventElapsedTime(&ms, ev[i], ev[i + 1]);
+        acc[i] += ms;
+      }
+    }
+    check_status(S);
+    for (auto &e : ev) cudaEventDestroy(e);
+    std::string all;
+    for (int i = 0; i < n && i < max_stages; ++i) {
+      if (stage_ms) stage_ms[i] = static_cast<float>(acc[i] / std::max(1, iters));
+      if (stage_flops) stage_flops[i] = P.steps[i].flops;
+      all += P.steps[i].name + "\n";
+    }
+    if (names && names_len) {
+      std::snprintf(names, names_len, "%s", all.c_str());
+    }
+    return n;
+  } catch (const std::exception &e) {
+    fail(h, std::string("mfb200_profile: ") + e.what());
+    return -2;
+  }
+}
+
+extern "C" const char *mfb200_last_error(mfb200_handle *h) {
+  if (!t_last_error.empty()) return t_last_error.c_str();
+  return h ? h->last_error.c_str() : "";
+}
+
+extern "C" void mfb200_destroy(mfb200_handle *h) {
+  if (!h) return;
+  for (auto &S : h->shards) {
+    cudaSetDevice(S->device);
+    cudaStreamSynchronize(S->stream);
+    for (auto &kv : S->plans)
+      if (kv.second->graph) cudaGraphExecDestroy(kv.second->graph);
+    for (auto &e : S->ev) cudaEventDestroy(e);
+    if (S->arena) cudaFree(S->arena);
+    if (S->ws) cudaFree(S->ws);
+    cudaStreamDestroy(S->stream);
+  }
+  delete h;
+}

@@ -1,0 +1,239 @@
+"""Host-side mirror of the reference ``NN::Network`` interface over libmfb200.
+
+``B200Network`` follows ``src/nn/network.h:38-51`` (Evaluate, EvaluateBatch,
+GetNetworkInfo, HasWDL, HasMovesLeft, GetBackendCapabilities) and
+``create_network`` follows ``CreateNetwork(weights, BackendConfig)``
+(``src/nn/network.cpp:137-208``) for the ``"b200"`` backend. Errors raise
+``RuntimeError`` carrying the library's message, as the reference throws
+``std::runtime_error``. There is no CPU fallback: without a B200 and the built
+library every call raises.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass, field
+from typing import Dict, List, Optional, Sequence
+
+import numpy as np
+
+from . import layout
+from ._lib import lib
+from .netfile import POLICY, Outputs, PackedInputs, pack_planes
+from .synthetic import NetConfig
+
+
+class NetDesc(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int32) for n in (
+        "embedding", "layers", "heads", "dff", "emb_dff", "pe", "smolgen_compress",
+        "smolgen_hidden", "smolgen_gen", "policy_d", "value_emb", "value_hidden", "mlh_emb",
+        "mlh_hidden", "act_default", "act_smolgen", "act_ffn")]
+
+
+class Config(ctypes.Structure):
+    _fields_ = [("device", ctypes.c_int32), ("num_devices", ctypes.c_int32),
+                ("precision", ctypes.c_int32), ("max_batch", ctypes.c_int32),
+                ("use_graphs", ctypes.c_int32)]
+
+
+class Timing(ctypes.Structure):
+    _fields_ = [("h2d_ms", ctypes.c_float), ("forward_ms", ctypes.c_float),
+                ("d2h_ms", ctypes.c_float), ("total_ms", ctypes.c_float)]
+
+
+class Caps(ctypes.Structure):
+    _fields_ = [("max_batch", ctypes.c_int32), ("precision", ctypes.c_int32),
+                ("num_devices", ctypes.c_int32), ("device", ctypes.c_int32),
+                ("has_wdl", ctypes.c_int32), ("has_moves_left", ctypes.c_int32),
+                ("weight_bytes", ctypes.c_int64), ("workspace_bytes", ctypes.c_int64),
+                ("device_name", ctypes.c_char * 96)]
+
+
+PRECISIONS = {"bf16": 0, "fp8": 1}
+
+
+def _declare(L):
+    vp, c_int = ctypes.c_void_p, ctypes.c_int
+    L.mfb200_weight_bytes.restype = ctypes.c_size_t
+    L.mfb200_weight_bytes.argtypes = [ctypes.POINTER(NetDesc)]
+    L.mfb200_create.restype = c_int
+    L.mfb200_create.argtypes = [ctypes.POINTER(NetDesc), vp, ctypes.c_size_t,
+                                ctypes.POINTER(Config), ctypes.POINTER(vp)]
+    L.mfb200_evaluate.restype = c_int
+    L.mfb200_evaluate.argtypes = [vp, vp, vp, c_int, vp, vp, vp, ctypes.POINTER(Timing)]
+    L.mfb200_evaluate_device.restype = c_int
+    L.mfb200_evaluate_device.argtypes = [vp, vp, vp, c_int, vp, vp, vp, vp]
+    L.mfb200_calibrate.restype = c_int
+    L.mfb200_calibrate.argtypes = [vp, vp, vp, c_int]
+    L.mfb200_capabilities.restype = c_int
+    L.mfb200_capabilities.argtypes = [vp, ctypes.POINTER(Caps)]
+    L.mfb200_profile.restype = c_int
+    L.mfb200_profile.argtypes = [vp, c_int, c_int, vp, vp, ctypes.c_char_p, ctypes.c_size_t, c_int]
+    L.mfb200_last_error.restype = ctypes.c_char_p
+    L.mfb200_last_error.argtypes = [vp]
+    L.mfb200_destroy.restype = None
+    L.mfb200_destroy.argtypes = [vp]
+
+
+def _lib():
+    L = lib()
+    if not getattr(L, "_mfb200_declared", False):
+        _declare(L)
+        L._mfb200_declared = True
+    return L
+
+
+def net_desc(cfg: NetConfig) -> NetDesc:
+    a = layout.ACTIVATIONS
+    return NetDesc(cfg.embedding, cfg.layers, cfg.heads, cfg.dff, cfg.emb_dff, cfg.pe,
+                   cfg.smolgen_compress, cfg.smolgen_hidden, cfg.smolgen_gen, cfg.dp,
+                   cfg.value_emb, cfg.value_hidden, cfg.mlh_emb, cfg.mlh_hidden,
+                   a[cfg.default_activation], a[cfg.smolgen_activation], a[cfg.ffn_activation])
+
+
+def weight_blob(cfg: NetConfig, tensors: Dict[str, np.ndarray]) -> np.ndarray:
+    """Concatenate the fp32 tensors in the library's slot order."""
+    parts = [np.ascontiguousarray(tensors[n], np.float32).ravel() for n in layout.GLOBAL_SLOTS]
+    for i in range(cfg.layers):
+        parts += [np.ascontiguousarray(tensors[layout.layer_name(i, n)], np.float32).ravel()
+                  for n in layout.LAYER_SLOTS]
+    return np.concatenate(parts)
+
+
+@dataclass
+class NetworkOutput:
+    """``src/nn/network_output.h:17-24``."""
+    policy: np.ndarray
+    value: float
+    wdl: np.ndarray
+    has_wdl: bool = True
+    moves_left: float = 0.0
+    has_moves_left: bool = True
+
+
+@dataclass
+class BackendCapabilities:
+    """``src/nn/network.h:21-36`` (the fields this backend fills)."""
+    actual_backend: str = "b200"
+    has_wdl: bool = True
+    has_moves_left: bool = True
+    max_batch_size: int = 0
+    device_name: str = ""
+    precision: str = "bf16"
+    num_devices: int = 1
+    weight_bytes: int = 0
+    workspace_bytes: int = 0
+
+    def summary(self) -> str:
+        return (f"actual_backend={self.actual_backend} has_wdl={str(self.has_wdl).lower()} "
+                f"has_moves_left={str(self.has_moves_left).lower()} max_batch={self.max_batch_size} "
+                f'device="{self.device_name}" precision={self.precision} gpus={self.num_devices}')
+
+
+class B200Network:
+    def __init__(self, cfg: NetConfig, tensors: Dict[str, np.ndarray], *, device: int = 0,
+                 num_devices: int = 1, precision: str = "bf16", max_batch: int = 1024,
+                 use_graphs: bool = True):
+        L = _lib()
+        self.cfg = cfg
+        self.precision = precision
+        self._desc = net_desc(cfg)
+        blob = weight_blob(cfg, tensors)
+        expected = L.mfb200_weight_bytes(ctypes.byref(self._desc))
+        if blob.nbytes != expected:
+            raise RuntimeError(f"weight blob is {blob.nbytes} bytes, library expects {expected}")
+        conf = Config(device, num_devices, PRECISIONS[precision], max_batch, int(use_graphs))
+        h = ctypes.c_void_p()
+        rc = L.mfb200_create(ctypes.byref(self._desc), blob.ctypes.data, blob.nbytes,
+                             ctypes.byref(conf), ctypes.byref(h))
+        if rc != 0:
+            raise RuntimeError(L.mfb200_last_error(None).decode())
+        self._h = h
+        self.max_batch = max_batch
+
+    # -- lifecycle
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            _lib().mfb200_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def _err(self) -> RuntimeError:
+        return RuntimeError(_lib().mfb200_last_error(self._h).decode())
+
+    # -- packed-input path (what MCTS batch assembly feeds)
+    def evaluate_packed(self, inp: PackedInputs, timing: Optional[Timing] = None) -> Outputs:
+        b = inp.count
+        masks = np.ascontiguousarray(inp.masks, np.uint64)
+        values = np.ascontiguousarray(inp.values, np.float32)
+        pol = np.empty((b, POLICY), np.float32)
+        wdl = np.empty((b, 3), np.float32)
+        mlh = np.empty(b, np.float32)
+        rc = _lib().mfb200_evaluate(self._h, masks.ctypes.data, values.ctypes.data, b,
+                                    pol.ctypes.data, wdl.ctypes.data, mlh.ctypes.data,
+                                    ctypes.byref(timing) if timing is not None else None)
+        if rc != 0:
+            raise self._err()
+        return Outputs(pol, wdl, wdl[:, 0] - wdl[:, 2], mlh)
+
+    def evaluate_device(self, d_masks: int, d_values: int, batch: int, d_policy: int, d_wdl: int,
+                        d_mlh: int, stream: int = 0) -> None:
+        rc = _lib().mfb200_evaluate_device(self._h, d_masks, d_values, batch, d_policy, d_wdl,
+                                           d_mlh, stream or None)
+        if rc != 0:
+            raise self._err()
+
+    # -- the reference Network interface
+    def evaluate_batch(self, inputs: Sequence[np.ndarray]) -> List[NetworkOutput]:
+        """EvaluateBatch over InputPlanes ([112, 64] float arrays)."""
+        if len(inputs) == 0:
+            return []
+        planes = np.stack([np.asarray(x, np.float32).reshape(112, 64) for x in inputs])
+        out = self.evaluate_packed(pack_planes(planes))
+        return [NetworkOutput(out.policy[i], float(out.value[i]), out.wdl[i], True,
+                              float(out.moves_left[i]), True) for i in range(len(inputs))]
+
+    def evaluate(self, planes: np.ndarray) -> NetworkOutput:
+        return self.evaluate_batch([planes])[0]
+
+    def has_wdl(self) -> bool:
+        return True
+
+    def has_moves_left(self) -> bool:
+        return True
+
+    def get_backend_capabilities(self) -> BackendCapabilities:
+        c = Caps()
+        if _lib().mfb200_capabilities(self._h, ctypes.byref(c)) != 0:
+            raise self._err()
+        return BackendCapabilities("b200", bool(c.has_wdl), bool(c.has_moves_left), c.max_batch,
+                                   c.device_name.decode(), self.precision, c.num_devices,
+                                   c.weight_bytes, c.workspace_bytes)
+
+    def get_network_info(self) -> str:
+        c = self.cfg
+        return (f"B200 transformer backend (net={c.name} d={c.embedding} layers={c.layers} "
+                f"heads={c.heads} dff={c.dff}, {self.get_backend_capabilities().summary()})")
+
+    def profile(self, batch: int, iters: int = 3):
+        n = 512
+        ms = (ctypes.c_float * n)()
+        fl = (ctypes.c_double * n)()
+        names = ctypes.create_string_buffer(1 << 16)
+        k = _lib().mfb200_profile(self._h, batch, iters, ms, fl, names, len(names), n)
+        if k < 0:
+            raise self._err()
+        nm = names.value.decode().split("\n")
+        return [(nm[i], ms[i], fl[i]) for i in range(k)]
+
+
+def create_network(cfg: NetConfig, tensors: Dict[str, np.ndarray], backend: str = "b200",
+                   **kwargs) -> B200Network:
+    """``CreateNetwork(weights, BackendConfig)`` for the B200 backend."""
+    if backend not in ("b200", "auto"):
+        raise RuntimeError(f"Unknown NN backend: {backend}")
+    return B200Network(cfg, tensors, **kwargs)

@@ -1,0 +1,97 @@
+"""End-to-end parity of the B200 forward (through the C ABI) with the
+reference CPU backend on the committed golden fixtures.
+
+Tolerances (bf16): max |policy logit diff| <= 5e-2, |WDL diff| <= 1e-2;
+moves-left within 5e-2 absolute + 2% relative.
+"""
+import numpy as np
+import pytest
+
+from metalfish_b200 import synthetic
+from metalfish_b200.network import create_network
+from tests.conftest import load_golden
+
+pytestmark = pytest.mark.gpu
+
+POLICY_TOL = 5e-2
+WDL_TOL = 1e-2
+
+_nets = {}
+
+
+def net_for(name, max_batch=256, use_graphs=True):
+    key = (name, max_batch, use_graphs)
+    if key not in _nets:
+        g = load_golden(name)
+        cfg = synthetic.CONFIGS[str(g["config"])]
+        t = synthetic.generate(cfg, int(g["weight_seed"]), bool(g["perturb_norms"]))
+        _nets[key] = create_network(cfg, t, max_batch=max_batch, use_graphs=use_graphs)
+    return _nets[key]
+
+
+def check(out, g, n):
+    dp = np.abs(out.policy - g["policy"][:n])
+    dw = np.abs(out.wdl - g["wdl"][:n])
+    dm = np.abs(out.moves_left - g["moves_left"][:n])
+    msg = f"policy max {dp.max():.4g} wdl max {dw.max():.4g} mlh max {dm.max():.4g}"
+    print(msg)
+    assert dp.max() <= POLICY_TOL, msg
+    assert dw.max() <= WDL_TOL, msg
+    assert (dm <= 5e-2 + 2e-2 * np.abs(g["moves_left"][:n])).all(), msg
+    np.testing.assert_allclose(out.value, out.wdl[:, 0] - out.wdl[:, 2], atol=1e-6)
+
+
+@pytest.mark.parametrize("name", ["tiny", "small", "small_perturbed", "bt4"])
+def test_forward_matches_reference(name, positions):
+    g = load_golden(name)
+    n = int(g["positions"])
+    out = net_for(name).evaluate_packed(positions.slice(0, n))
+    check(out, g, n)
+
+
+@pytest.mark.parametrize("batch", [1, 3, 17])
+def test_ragged_batches(batch, positions):
+    g = load_golden("small")
+    out = net_for("small").evaluate_packed(positions.slice(0, batch))
+    check(out, g, batch)
+
+
+def test_batch_vs_single_and_graph_vs_eager(positions):
+    """Batch-vs-single parity (the reference tests the same property,
+    tests/test_nn_comparison.cpp:796-1480) and graph replay == eager launch."""
+    net = net_for("small")
+    many = net.evaluate_packed(positions.slice(0, 8))
+    for i in (0, 5):
+        one = net.evaluate_packed(positions.slice(i, i + 1))
+        np.testing.assert_allclose(one.policy[0], many.policy[i], atol=1e-2)
+    eager = net_for("small", use_graphs=False).evaluate_packed(positions.slice(0, 8))
+    np.testing.assert_array_equal(eager.policy, many.policy)
+    np.testing.assert_array_equal(eager.wdl, many.wdl)
+
+
+def test_repeated_calls_are_deterministic(positions):
+    net = net_for("tiny")
+    a = net.evaluate_packed(positions.slice(0, 32))
+    b = net.evaluate_packed(positions.slice(0, 32))
+    np.testing.assert_array_equal(a.policy, b.policy)
+
+
+def test_network_interface(positions):
+    net = net_for("tiny")
+    caps = net.get_backend_capabilities()
+    assert caps.actual_backend == "b200" and caps.has_wdl and caps.has_moves_left
+    assert "B200" in caps.device_name
+    from metalfish_b200.netfile import unpack_planes
+    planes = unpack_planes(positions.slice(0, 2))
+    outs = net.evaluate_batch(list(planes))
+    g = load_golden("tiny")
+    assert len(outs) == 2
+    assert np.abs(outs[1].policy - g["policy"][1]).max() <= POLICY_TOL
+    assert abs(outs[0].value - (g["wdl"][0, 0] - g["wdl"][0, 2])) <= 2 * WDL_TOL
+    assert net.evaluate_batch([]) == []
+
+
+def test_batch_too_large_raises(positions):
+    net = net_for("tiny", max_batch=4)
+    with pytest.raises(RuntimeError, match="exceeds max_batch"):
+        net.evaluate_packed(positions.slice(0, 5))

@@ -1,0 +1,80 @@
+"""tcgen05 GEMM kernel vs a float64 host product of the same bf16 inputs."""
+import ctypes
+
+import numpy as np
+import pytest
+
+from metalfish_b200._lib import lib
+from metalfish_b200.bf16 import from_bf16_bits, round_bf16, to_bf16_bits
+
+pytestmark = pytest.mark.gpu
+
+
+def _p(a):
+    return None if a is None else a.ctypes.data_as(ctypes.c_void_p)
+
+
+def mish(x):
+    return x * np.tanh(np.log1p(np.exp(x)))
+
+
+def run_gemm(M, N, K, bn, mode=0, act=0, bias=True, alpha=0.5, seed=0):
+    rng = np.random.default_rng(seed)
+    A = rng.standard_normal((M, K), dtype=np.float32)
+    W = rng.standard_normal((N, K), dtype=np.float32) / np.float32(np.sqrt(K))
+    b = rng.standard_normal(N, dtype=np.float32) * 0.1 if bias else None
+    R = rng.standard_normal((M, N), dtype=np.float32)
+    g = (1 + 0.1 * rng.standard_normal(N)).astype(np.float32)
+    be = (0.1 * rng.standard_normal(N)).astype(np.float32)
+    Ab, Wb, Rb = to_bf16_bits(A), to_bf16_bits(W), to_bf16_bits(R)
+    out = np.zeros((M, N), np.uint16)
+    st = ctypes.c_uint(0)
+    rc = lib().mfb200_debug_gemm(M, N, K, bn, 0, _p(Ab), _p(Wb), _p(b), mode, act, _p(Rb),
+                                 ctypes.c_float(alpha), _p(g), _p(be), ctypes.c_float(1e-3),
+                                 None, ctypes.c_float(1.0), _p(out), ctypes.byref(st))
+    assert rc == 0, f"rc={rc} status={st.value}"
+    acc = from_bf16_bits(Ab).astype(np.float64) @ from_bf16_bits(Wb).astype(np.float64).T
+    if b is not None:
+        acc = acc + b
+    if mode == 1:
+        ref = from_bf16_bits(Rb) + alpha * acc
+    else:
+        ref = {0: acc, 2: np.maximum(acc, 0) ** 2, 5: acc / (1 + np.exp(-acc)), 6: mish(acc)}[act]
+        if mode == 2:
+            mu = ref.mean(1, keepdims=True)
+            var = ref.var(1, keepdims=True)
+            ref = (ref - mu) / np.sqrt(var + 1e-3) * g + be
+    return from_bf16_bits(out), ref
+
+
+@pytest.mark.parametrize("M,N,K,bn", [
+    (128, 256, 64, 256),     # one tile, one k-block
+    (128, 64, 64, 64),
+    (256, 512, 1024, 256),
+    (300, 3104, 1024, 256),  # ragged M, N not a multiple of the tile
+    (1000, 1536, 1024, 128),
+    (64, 4096, 256, 256),    # M smaller than one tile
+    (517, 64, 192, 64),
+])
+def test_gemm_store(M, N, K, bn):
+    got, ref = run_gemm(M, N, K, bn)
+    err = np.abs(got - ref)
+    tol = 1e-2 + 1e-2 * np.abs(ref)
+    bad = err > tol
+    assert not bad.any(), f"{bad.sum()} bad of {bad.size}; max err {err.max()} first {np.argwhere(bad)[:5]}"
+
+
+@pytest.mark.parametrize("act", [2, 6])
+def test_gemm_activation(act):
+    got, ref = run_gemm(384, 1536, 1024, 256, act=act)
+    np.testing.assert_allclose(got, ref, rtol=1e-2, atol=1e-2)
+
+
+def test_gemm_residual():
+    got, ref = run_gemm(257, 1024, 1536, 256, mode=1, alpha=0.427)
+    np.testing.assert_allclose(got, ref, rtol=1e-2, atol=2e-2)
+
+
+def test_gemm_row_layernorm():
+    got, ref = run_gemm(200, 256, 2048, 256, mode=2, act=5)
+    np.testing.assert_allclose(got, ref, rtol=2e-2, atol=3e-2)
