@@ -112,28 +112,41 @@ void launch_pe_concat(const __nv_bfloat16 *peo, int batch, int pe, __nv_bfloat16
 // ------------------------------------------------------------------ layernorm
 // One warp per row. Lane l owns the 4-column groups q*128 + 4l .. +3 for
 // q < VPL/4, so every load instruction of the warp reads 256 contiguous bytes.
-template <int VPL>
-__global__ void layernorm_warp_kernel(const __nv_bfloat16 *__restrict__ in, int rows,
+template <int VPL, bool F32IN>
+__global__ void layernorm_warp_kernel(const void *__restrict__ in_, int rows,
                                       const float *__restrict__ gamma,
                                       const float *__restrict__ beta, float eps,
                                       const float *__restrict__ multT,
                                       const float *__restrict__ addT,
-                                      __nv_bfloat16 *__restrict__ out) {
+                                      __nv_bfloat16 *__restrict__ out,
+                                      float *__restrict__ out_f32) {
   constexpr int W = 32 * VPL;
   const int warps = blockDim.x >> 5;
   const long long row = static_cast<long long>(blockIdx.x) * warps + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
-  const __nv_bfloat16 *src = in + row * W;
   float v[VPL];
+  if constexpr (F32IN) {
+    const float *src = static_cast<const float *>(in_) + row * W;
 #pragma unroll
-  for (int q = 0; q < VPL / 4; ++q) {
-    const uint2 u = *reinterpret_cast<const uint2 *>(src + q * 128 + lane * 4);
-    const float2 f0 = unpack_bf16x2(u.x), f1 = unpack_bf16x2(u.y);
-    v[4 * q] = f0.x;
-    v[4 * q + 1] = f0.y;
-    v[4 * q + 2] = f1.x;
-    v[4 * q + 3] = f1.y;
+    for (int q = 0; q < VPL / 4; ++q) {
+      const float4 f = *reinterpret_cast<const float4 *>(src + q * 128 + lane * 4);
+      v[4 * q] = f.x;
+      v[4 * q + 1] = f.y;
+      v[4 * q + 2] = f.z;
+      v[4 * q + 3] = f.w;
+    }
+  } else {
+    const __nv_bfloat16 *src = static_cast<const __nv_bfloat16 *>(in_) + row * W;
+#pragma unroll
+    for (int q = 0; q < VPL / 4; ++q) {
+      const uint2 u = *reinterpret_cast<const uint2 *>(src + q * 128 + lane * 4);
+      const float2 f0 = unpack_bf16x2(u.x), f1 = unpack_bf16x2(u.y);
+      v[4 * q] = f0.x;
+      v[4 * q + 1] = f0.y;
+      v[4 * q + 2] = f1.x;
+      v[4 * q + 3] = f1.y;
+    }
   }
   float s = 0.0f;
 #pragma unroll
@@ -163,6 +176,8 @@ __global__ void layernorm_warp_kernel(const __nv_bfloat16 *__restrict__ in, int 
       r[e] = y;
     }
     *reinterpret_cast<uint2 *>(dst + c) = make_uint2(pack_bf16x2(r[0], r[1]), pack_bf16x2(r[2], r[3]));
+    if (out_f32)
+      *reinterpret_cast<float4 *>(out_f32 + row * W + c) = make_float4(r[0], r[1], r[2], r[3]);
   }
 }
 
@@ -221,27 +236,32 @@ __global__ void layernorm_block_kernel(const __nv_bfloat16 *__restrict__ in, int
   }
 }
 
-void launch_layernorm(const __nv_bfloat16 *in, int rows, int width, const float *gamma,
-                      const float *beta, float eps, const float *multT, const float *addT,
-                      __nv_bfloat16 *out, cudaStream_t s) {
+template <int VPL>
+static void ln_warp(const void *in, bool f32in, int rows, const float *gamma, const float *beta,
+                    float eps, const float *multT, const float *addT, __nv_bfloat16 *out,
+                    float *out_f32, cudaStream_t s) {
   const int wpb = 8;
   const unsigned grid = static_cast<unsigned>((rows + wpb - 1) / wpb);
+  if (f32in)
+    layernorm_warp_kernel<VPL, true><<<grid, 32 * wpb, 0, s>>>(in, rows, gamma, beta, eps, multT,
+                                                               addT, out, out_f32);
+  else
+    layernorm_warp_kernel<VPL, false><<<grid, 32 * wpb, 0, s>>>(in, rows, gamma, beta, eps, multT,
+                                                                addT, out, out_f32);
+}
+
+void launch_layernorm(const void *in, bool in_f32, int rows, int width, const float *gamma,
+                      const float *beta, float eps, const float *multT, const float *addT,
+                      __nv_bfloat16 *out, float *out_f32, cudaStream_t s) {
   switch (width) {
-  case 128:
-    layernorm_warp_kernel<4><<<grid, 32 * wpb, 0, s>>>(in, rows, gamma, beta, eps, multT, addT, out);
-    return;
-  case 256:
-    layernorm_warp_kernel<8><<<grid, 32 * wpb, 0, s>>>(in, rows, gamma, beta, eps, multT, addT, out);
-    return;
-  case 512:
-    layernorm_warp_kernel<16><<<grid, 32 * wpb, 0, s>>>(in, rows, gamma, beta, eps, multT, addT, out);
-    return;
-  case 1024:
-    layernorm_warp_kernel<32><<<grid, 32 * wpb, 0, s>>>(in, rows, gamma, beta, eps, multT, addT, out);
-    return;
+  case 128: ln_warp<4>(in, in_f32, rows, gamma, beta, eps, multT, addT, out, out_f32, s); return;
+  case 256: ln_warp<8>(in, in_f32, rows, gamma, beta, eps, multT, addT, out, out_f32, s); return;
+  case 512: ln_warp<16>(in, in_f32, rows, gamma, beta, eps, multT, addT, out, out_f32, s); return;
+  case 1024: ln_warp<32>(in, in_f32, rows, gamma, beta, eps, multT, addT, out, out_f32, s); return;
   default:
-    // wide rows (no gates on this path)
-    layernorm_block_kernel<<<rows, 256, 0, s>>>(in, width, gamma, beta, eps, out);
+    // wide bf16 rows (smolgen's H*g); no gates, no fp32 output on this path
+    layernorm_block_kernel<<<rows, 256, 0, s>>>(static_cast<const __nv_bfloat16 *>(in), width,
+                                                gamma, beta, eps, out);
     return;
   }
 }

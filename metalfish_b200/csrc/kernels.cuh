@@ -24,11 +24,14 @@ void launch_unpack(const uint64_t *masks, const float *values, int batch, __nv_b
 void launch_pe_concat(const __nv_bfloat16 *peo, int batch, int pe, __nv_bfloat16 *x0,
                       cudaStream_t s);
 
-// Row LayerNorm of bf16 rows (two-pass mean/variance in fp32); optional
-// square gates multT/addT [64][width] applied after the norm.
-void launch_layernorm(const __nv_bfloat16 *in, int rows, int width, const float *gamma,
+// Row LayerNorm (two-pass mean/variance in fp32) of bf16 or fp32 rows
+// (`in_f32`); optional square gates multT/addT [64][width] applied after the
+// norm. Writes bf16 `out` and, when `out_f32` is non-null, an fp32 copy.
+// Widths 128/256/512/1024 use one warp per row; other widths (bf16 input
+// only, no gates, no fp32 copy) one CTA per row.
+void launch_layernorm(const void *in, bool in_f32, int rows, int width, const float *gamma,
                       const float *beta, float eps, const float *multT, const float *addT,
-                      __nv_bfloat16 *out, cudaStream_t s);
+                      __nv_bfloat16 *out, float *out_f32, cudaStream_t s);
 
 // 64-token attention per (position, head) with the smolgen bias added before
 // the softmax: ctx[b*64+q, h*dh:..] = softmax(Q K^T / sqrt(dh) + bias) V.

@@ -223,8 +223,9 @@ struct Shard {  // one GPU
   size_t ws_bytes = 0;
   uint64_t *masks;
   float *values;
-  __nv_bfloat16 *x0, *p, *peo, *X, *X1, *T, *QKV, *C, *S1, *S2pre, *S2, *BIAS, *CTX, *H, *E, *QK,
+  __nv_bfloat16 *x0, *p, *peo, *X, *X1, *QKV, *C, *S1, *S2pre, *S2, *BIAS, *CTX, *H, *E, *QK,
       *VM, *VH;
+  float *Xf, *X1f, *T;  // fp32 residual stream (LN outputs) and pre-LN sums
   float *policy, *wdl, *mlh;
   unsigned *status;
   cudaEvent_t ev[4];
@@ -448,7 +449,9 @@ void alloc_workspace(Shard &S, const mfb200_net_desc &n, int max_batch) {
       {reinterpret_cast<void **>(&S.peo), B * 64 * n.pe * 2},
       {reinterpret_cast<void **>(&S.X), M * d * 2},
       {reinterpret_cast<void **>(&S.X1), M * d * 2},
-      {reinterpret_cast<void **>(&S.T), M * d * 2},
+      {reinterpret_cast<void **>(&S.T), M * d * 4},
+      {reinterpret_cast<void **>(&S.Xf), M * d * 4},
+      {reinterpret_cast<void **>(&S.X1f), M * d * 4},
       {reinterpret_cast<void **>(&S.QKV), M * 3 * d * 2},
       {reinterpret_cast<void **>(&S.C), M * n.smolgen_compress * 2},
       {reinterpret_cast<void **>(&S.S1), B * n.smolgen_hidden * 2},
@@ -543,11 +546,12 @@ std::unique_ptr<Shard::Plan> build_plan(Shard &S, const mfb200_net_desc &n, int 
     a.bias = W.b_emb;
     a.act = n.act_default;
     a.out = S.T;
+    a.out_f32 = 1;
     a.ldo = d;
     add_gemm(*P, S, "emb_dense", S.x0, kEmbIn, W.emb, a);
   }
   add_fn(*P, "emb_ln_gates", 0, [&S, &W, M, d, eps](cudaStream_t s) {
-    launch_layernorm(S.T, M, d, W.ln_emb_g, W.ln_emb_b, eps, W.multT, W.addT, S.X, s);
+    launch_layernorm(S.T, true, M, d, W.ln_emb_g, W.ln_emb_b, eps, W.multT, W.addT, S.X, S.Xf, s);
   });
   {
     GemmArgs a = base_args(S, M, n.emb_dff, d);
@@ -559,15 +563,16 @@ std::unique_ptr<Shard::Plan> build_plan(Shard &S, const mfb200_net_desc &n, int 
     GemmArgs b = base_args(S, M, d, n.emb_dff);
     b.mode = kEpiResid;
     b.bias = W.b_effn2;
-    b.resid = S.X;
+    b.resid = S.Xf;
     b.ldr = d;
     b.alpha = alpha;
     b.out = S.T;
+    b.out_f32 = 1;
     b.ldo = d;
     add_gemm(*P, S, "emb_ffn2", S.H, n.emb_dff, W.effn2, b);
   }
   add_fn(*P, "emb_ffn_ln", 0, [&S, &W, M, d, eps](cudaStream_t s) {
-    launch_layernorm(S.T, M, d, W.ln_effn_g, W.ln_effn_b, eps, nullptr, nullptr, S.X, s);
+    launch_layernorm(S.T, true, M, d, W.ln_effn_g, W.ln_effn_b, eps, nullptr, nullptr, S.X, S.Xf, s);
   });
   for (int k = 0; k < n.layers; ++k) {
     LayerW &Lw = W.layers[k];
@@ -599,7 +604,7 @@ std::unique_ptr<Shard::Plan> build_plan(Shard &S, const mfb200_net_desc &n, int 
         a.out = S.S2pre;
         add_gemm(*P, S, "smolgen_dense1", S.C, 64 * n.smolgen_compress, Lw.sg1, a);
         add_fn(*P, "smolgen_ln1", 0, [&S, &Lw, B, w = n.smolgen_hidden, eps](cudaStream_t s) {
-          launch_layernorm(S.S2pre, B, w, Lw.sg_ln1_g, Lw.sg_ln1_b, eps, nullptr, nullptr, S.S1, s);
+          launch_layernorm(S.S2pre, false, B, w, Lw.sg_ln1_g, Lw.sg_ln1_b, eps, nullptr, nullptr, S.S1, nullptr, s);
         });
       }
     }
@@ -612,7 +617,7 @@ std::unique_ptr<Shard::Plan> build_plan(Shard &S, const mfb200_net_desc &n, int 
       add_gemm(*P, S, "smolgen_dense2", S.S1, n.smolgen_hidden, Lw.sg2, a);
     }
     add_fn(*P, "smolgen_ln2", 0, [&S, &Lw, B, hg, eps](cudaStream_t s) {
-      launch_layernorm(S.S2pre, B, hg, Lw.sg_ln2_g, Lw.sg_ln2_b, eps, nullptr, nullptr, S.S2, s);
+      launch_layernorm(S.S2pre, false, B, hg, Lw.sg_ln2_g, Lw.sg_ln2_b, eps, nullptr, nullptr, S.S2, nullptr, s);
     });
     {
       GemmArgs a = base_args(S, B * H, 4096, n.smolgen_gen);
@@ -627,15 +632,16 @@ std::unique_ptr<Shard::Plan> build_plan(Shard &S, const mfb200_net_desc &n, int 
       GemmArgs a = base_args(S, M, d, d);
       a.mode = kEpiResid;
       a.bias = Lw.b_o;
-      a.resid = S.X;
+      a.resid = S.Xf;
       a.ldr = d;
       a.alpha = alpha;
       a.out = S.T;
+      a.out_f32 = 1;
       a.ldo = d;
       add_gemm(*P, S, "out_proj", S.CTX, d, Lw.o, a);
     }
     add_fn(*P, "ln1", 0, [&S, &Lw, M, d, eps](cudaStream_t s) {
-      launch_layernorm(S.T, M, d, Lw.ln1_g, Lw.ln1_b, eps, nullptr, nullptr, S.X1, s);
+      launch_layernorm(S.T, true, M, d, Lw.ln1_g, Lw.ln1_b, eps, nullptr, nullptr, S.X1, S.X1f, s);
     });
     {
       GemmArgs a = base_args(S, M, n.dff, d);
@@ -647,15 +653,16 @@ std::unique_ptr<Shard::Plan> build_plan(Shard &S, const mfb200_net_desc &n, int 
       GemmArgs b = base_args(S, M, d, n.dff);
       b.mode = kEpiResid;
       b.bias = Lw.b_f2;
-      b.resid = S.X1;
+      b.resid = S.X1f;
       b.ldr = d;
       b.alpha = alpha;
       b.out = S.T;
+      b.out_f32 = 1;
       b.ldo = d;
       add_gemm(*P, S, "ffn2", S.H, n.dff, Lw.f2, b);
     }
     add_fn(*P, "ln2", 0, [&S, &Lw, M, d, eps](cudaStream_t s) {
-      launch_layernorm(S.T, M, d, Lw.ln2_g, Lw.ln2_b, eps, nullptr, nullptr, S.X, s);
+      launch_layernorm(S.T, true, M, d, Lw.ln2_g, Lw.ln2_b, eps, nullptr, nullptr, S.X, S.Xf, s);
     });
   }
   {

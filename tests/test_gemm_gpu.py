@@ -18,7 +18,7 @@ def mish(x):
     return x * np.tanh(np.log1p(np.exp(x)))
 
 
-def run_gemm(M, N, K, bn, mode=0, act=0, bias=True, alpha=0.5, seed=0):
+def run_gemm(M, N, K, bn, mode=0, act=0, bias=True, alpha=0.5, seed=0, out_f32=False):
     rng = np.random.default_rng(seed)
     A = rng.standard_normal((M, K), dtype=np.float32)
     W = rng.standard_normal((N, K), dtype=np.float32) / np.float32(np.sqrt(K))
@@ -26,25 +26,26 @@ def run_gemm(M, N, K, bn, mode=0, act=0, bias=True, alpha=0.5, seed=0):
     R = rng.standard_normal((M, N), dtype=np.float32)
     g = (1 + 0.1 * rng.standard_normal(N)).astype(np.float32)
     be = (0.1 * rng.standard_normal(N)).astype(np.float32)
-    Ab, Wb, Rb = to_bf16_bits(A), to_bf16_bits(W), to_bf16_bits(R)
-    out = np.zeros((M, N), np.uint16)
+    Ab, Wb = to_bf16_bits(A), to_bf16_bits(W)
+    out = np.zeros((M, N), np.float32 if out_f32 else np.uint16)
     st = ctypes.c_uint(0)
-    rc = lib().mfb200_debug_gemm(M, N, K, bn, 0, _p(Ab), _p(Wb), _p(b), mode, act, _p(Rb),
+    rc = lib().mfb200_debug_gemm(M, N, K, bn, 0, _p(Ab), _p(Wb), _p(b), mode, act, _p(R),
                                  ctypes.c_float(alpha), _p(g), _p(be), ctypes.c_float(1e-3),
-                                 None, ctypes.c_float(1.0), _p(out), ctypes.byref(st))
+                                 None, ctypes.c_float(1.0), int(out_f32), _p(out),
+                                 ctypes.byref(st))
     assert rc == 0, f"rc={rc} status={st.value}"
     acc = from_bf16_bits(Ab).astype(np.float64) @ from_bf16_bits(Wb).astype(np.float64).T
     if b is not None:
         acc = acc + b
     if mode == 1:
-        ref = from_bf16_bits(Rb) + alpha * acc
+        ref = R + alpha * acc
     else:
         ref = {0: acc, 2: np.maximum(acc, 0) ** 2, 5: acc / (1 + np.exp(-acc)), 6: mish(acc)}[act]
         if mode == 2:
             mu = ref.mean(1, keepdims=True)
             var = ref.var(1, keepdims=True)
             ref = (ref - mu) / np.sqrt(var + 1e-3) * g + be
-    return from_bf16_bits(out), ref
+    return (out if out_f32 else from_bf16_bits(out)), ref
 
 
 @pytest.mark.parametrize("M,N,K,bn", [
@@ -73,6 +74,12 @@ def test_gemm_activation(act):
 def test_gemm_residual():
     got, ref = run_gemm(257, 1024, 1536, 256, mode=1, alpha=0.427)
     np.testing.assert_allclose(got, ref, rtol=1e-2, atol=2e-2)
+
+
+def test_gemm_residual_fp32_out():
+    """fp32 residual stream: accumulate error only (no output rounding)."""
+    got, ref = run_gemm(300, 1024, 1024, 256, mode=1, alpha=0.427, out_f32=True)
+    np.testing.assert_allclose(got, ref, rtol=1e-4, atol=1e-4)
 
 
 def test_gemm_row_layernorm():
