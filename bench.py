@@ -134,6 +134,17 @@ def cpu_baseline(cfg, tensors, sample_positions: int | None = None):
             "sample": f"{n} positions, C restatement oracle (fp32), {threads} threads, {dt:.1f} s"}
 
 
+def stage_summary(stages):
+    """Per stage name (summed over layers): ms and achieved TFLOP/s."""
+    agg = {}
+    for n, m, f in stages:
+        a = agg.setdefault(n, [0.0, 0.0])
+        a[0] += m
+        a[1] += f
+    return {n: {"ms": round(m, 4), "tflops": round(f / (m / 1e3) / 1e12, 1) if m > 0 and f else None}
+            for n, (m, f) in sorted(agg.items(), key=lambda kv: -kv[1][0])}
+
+
 def dist_setup(n_gpus):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -228,7 +239,9 @@ def main():
     d_pol = torch.empty((B, 1858), dtype=torch.float32, device=dev)
     d_wdl = torch.empty((B, 3), dtype=torch.float32, device=dev)
     d_mlh = torch.empty((B,), dtype=torch.float32, device=dev)
-    stream = torch.cuda.current_stream(dev)
+    # a dedicated (non-default) stream: the library enqueues on it and the
+    # CUDA events below are recorded on the same stream
+    stream = torch.cuda.Stream(dev)
 
     def step():
         net.evaluate_device(d_masks.data_ptr(), d_values.data_ptr(), B, d_pol.data_ptr(),
@@ -244,6 +257,7 @@ def main():
     barrier(world)
     torch.cuda.synchronize(dev)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    assert stream.cuda_stream != 0
     with ClockSampler(local) as clk:
         e0.record(stream)
         for _ in range(args.steps):
@@ -316,7 +330,7 @@ def main():
                          "peak_source": f"{src} bf16_tflops_sustained (kernel timed inside a long step)"},
             "flops_per_position": {"encoder_gemm": enc["encoder_gemm_flops"], "all_matmul": enc["total_flops"]},
             "model_tflops": value * enc["total_flops"] / 1e12 / world,
-            "stage_ms": {n: round(m, 4) for n, m, _ in stages[:12]},
+            "stage_ms": stage_summary(stages),
             "stage_ms_total": total_stage_ms,
             "clocks": clocks,
         }

@@ -16,13 +16,19 @@ extern "C" {
 /* out[M,N] (bf16 bits) = epilogue(A[M,K] . W[N,K]^T) through the tcgen05 GEMM.
  * A/W are bf16 bits (fp8 = 0) or e4m3 bytes (fp8 = 1); resid is fp32; out is
  * fp32 when out_f32 = 1, else bf16 bits. mode: 0 store
- * act(scale*acc+bias), 1 resid + alpha*(scale*acc+bias), 2 row LayerNorm of
- * act(scale*acc+bias) (N == bn). */
+ * act(scale*acc+bias), 1 resid + alpha*(scale*acc+bias). k_splits > 1: split-K,
+ * `out` receives k_splits fp32 partial products [k_splits, M, N] (no bias).
+ * ln_gamma/ln_beta/ln_eps are unused. */
 MFB200_API int mfb200_debug_gemm(int M, int N, int K, int bn, int fp8, const void *A, const void *W,
                       const float *bias, int mode, int act, const float *resid, float alpha,
                       const float *ln_gamma, const float *ln_beta, float ln_eps,
-                      const float *col_scale, float a_scale, int out_f32, void *out,
+                      const float *col_scale, float a_scale, int out_f32, int k_splits, void *out,
                       unsigned *status_out);
+
+/* Mean device time (ms) of `iters` back-to-back launches of one bf16 GEMM on
+ * synthetic device data (for profiling the kernel in isolation). */
+MFB200_API int mfb200_debug_gemm_bench(int M, int N, int K, int bn, int mode, int act, int out_f32,
+                                       int iters, float *ms_out);
 
 #ifdef __cplusplus
 }

@@ -29,4 +29,6 @@ def _declare(L: ctypes.CDLL) -> None:
     c_int, c_float, vp = ctypes.c_int, ctypes.c_float, ctypes.c_void_p
     L.mfb200_debug_gemm.restype = c_int
     L.mfb200_debug_gemm.argtypes = [c_int, c_int, c_int, c_int, c_int, vp, vp, vp, c_int, c_int,
-                                    vp, c_float, vp, vp, c_float, vp, c_float, c_int, vp, vp]
+                                    vp, c_float, vp, vp, c_float, vp, c_float, c_int, c_int, vp, vp]
+    L.mfb200_debug_gemm_bench.restype = c_int
+    L.mfb200_debug_gemm_bench.argtypes = [c_int] * 8 + [ctypes.POINTER(c_float)]

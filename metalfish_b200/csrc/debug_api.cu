@@ -25,21 +25,24 @@ extern "C" int mfb200_debug_gemm(int M, int N, int K, int bn, int fp8, const voi
                                  const void *W, const float *bias, int mode, int act,
                                  const float *resid, float alpha, const float *ln_gamma,
                                  const float *ln_beta, float ln_eps, const float *col_scale,
-                                 float a_scale, int out_f32, void *out, unsigned *status_out) {
+                                 float a_scale, int out_f32, int k_splits, void *out,
+                                 unsigned *status_out) {
+  (void)ln_gamma;
+  (void)ln_beta;
+  (void)ln_eps;
+  const int sp = k_splits > 1 ? k_splits : 1;
   const size_t es = fp8 ? 1 : 2;
   DevBuf dA, dW, dB, dR, dO, dG, dBe, dCs, dS;
   if (!dA.alloc(size_t(M) * K * es) || !dW.alloc(size_t(N) * K * es) || !dB.alloc(N * 4) ||
-      !dR.alloc(size_t(M) * N * 4) || !dO.alloc(size_t(M) * N * 4) || !dG.alloc(N * 4) ||
+      !dR.alloc(size_t(M) * N * 4) || !dO.alloc(size_t(sp) * M * N * 4) || !dG.alloc(N * 4) ||
       !dBe.alloc(N * 4) || !dCs.alloc(N * 4) || !dS.alloc(4))
     return 1;
   cudaMemcpy(dA.p, A, size_t(M) * K * es, cudaMemcpyHostToDevice);
   cudaMemcpy(dW.p, W, size_t(N) * K * es, cudaMemcpyHostToDevice);
   if (bias) cudaMemcpy(dB.p, bias, N * 4, cudaMemcpyHostToDevice);
   if (resid) cudaMemcpy(dR.p, resid, size_t(M) * N * 4, cudaMemcpyHostToDevice);
-  if (ln_gamma) cudaMemcpy(dG.p, ln_gamma, N * 4, cudaMemcpyHostToDevice);
-  if (ln_beta) cudaMemcpy(dBe.p, ln_beta, N * 4, cudaMemcpyHostToDevice);
   if (col_scale) cudaMemcpy(dCs.p, col_scale, N * 4, cudaMemcpyHostToDevice);
-  cudaMemset(dO.p, 0, size_t(M) * N * 4);
+  cudaMemset(dO.p, 0, size_t(sp) * M * N * 4);
   cudaMemset(dS.p, 0, 4);
   GemmArgs a{};
   a.M = M;
@@ -53,9 +56,8 @@ extern "C" int mfb200_debug_gemm(int M, int N, int K, int bn, int fp8, const voi
   a.resid = static_cast<const float *>(dR.p);
   a.ldr = N;
   a.alpha = alpha;
-  a.ln_gamma = static_cast<float *>(dG.p);
-  a.ln_beta = static_cast<float *>(dBe.p);
-  a.ln_eps = ln_eps;
+  a.k_splits = sp;
+  a.split_stride = static_cast<long long>(M) * N;
   a.col_scale = col_scale ? static_cast<float *>(dCs.p) : nullptr;
   a.a_scale = a_scale;
   a.status = static_cast<unsigned *>(dS.p);
@@ -64,9 +66,58 @@ extern "C" int mfb200_debug_gemm(int M, int N, int K, int bn, int fp8, const voi
   if (plan_gemm(g, dA.p, K, dW.p, K, bn, fp8 != 0, a)) return 2;
   if (launch_gemm(g, 0) != cudaSuccess) return 3;
   if (cudaDeviceSynchronize() != cudaSuccess) return 4;
-  cudaMemcpy(out, dO.p, size_t(M) * N * (out_f32 ? 4 : 2), cudaMemcpyDeviceToHost);
+  cudaMemcpy(out, dO.p, size_t(sp) * M * N * (sp > 1 || out_f32 ? 4 : 2), cudaMemcpyDeviceToHost);
   unsigned st = 0;
   cudaMemcpy(&st, dS.p, 4, cudaMemcpyDeviceToHost);
   if (status_out) *status_out = st;
+  return st ? 5 : 0;
+}
+
+// Times `iters` back-to-back launches of one GEMM on random device data
+// (bf16, bias, optional fp32 output); returns the mean ms per launch.
+extern "C" int mfb200_debug_gemm_bench(int M, int N, int K, int bn, int mode, int act,
+                                       int out_f32, int iters, float *ms_out) {
+  DevBuf dA, dW, dB, dR, dO, dS;
+  if (!dA.alloc(size_t(M) * K * 2) || !dW.alloc(size_t(N) * K * 2) || !dB.alloc(N * 4) ||
+      !dR.alloc(size_t(M) * N * 4) || !dO.alloc(size_t(M) * N * 4) || !dS.alloc(4))
+    return 1;
+  cudaMemset(dA.p, 0x3c, size_t(M) * K * 2);  // small finite bf16 values
+  cudaMemset(dW.p, 0x3c, size_t(N) * K * 2);
+  cudaMemset(dB.p, 0, N * 4);
+  cudaMemset(dR.p, 0, size_t(M) * N * 4);
+  cudaMemset(dS.p, 0, 4);
+  GemmArgs a{};
+  a.M = M;
+  a.N = N;
+  a.K = K;
+  a.mode = mode;
+  a.act = act;
+  a.bias = static_cast<float *>(dB.p);
+  a.out = dO.p;
+  a.ldo = N;
+  a.resid = static_cast<const float *>(dR.p);
+  a.ldr = N;
+  a.alpha = 1.0f;
+  a.a_scale = 1.0f;
+  a.out_f32 = out_f32;
+  a.status = static_cast<unsigned *>(dS.p);
+  GemmLaunch g;
+  if (plan_gemm(g, dA.p, K, dW.p, K, bn, false, a)) return 2;
+  for (int i = 0; i < 2; ++i)
+    if (launch_gemm(g, 0) != cudaSuccess) return 3;
+  cudaEvent_t e0, e1;
+  cudaEventCreate(&e0);
+  cudaEventCreate(&e1);
+  cudaEventRecord(e0, 0);
+  for (int i = 0; i < iters; ++i) launch_gemm(g, 0);
+  cudaEventRecord(e1, 0);
+  if (cudaDeviceSynchronize() != cudaSuccess) return 4;
+  float ms = 0;
+  cudaEventElapsedTime(&ms, e0, e1);
+  cudaEventDestroy(e0);
+  cudaEventDestroy(e1);
+  *ms_out = ms / iters;
+  unsigned st = 0;
+  cudaMemcpy(&st, dS.p, 4, cudaMemcpyDeviceToHost);
   return st ? 5 : 0;
 }

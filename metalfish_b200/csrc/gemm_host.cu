@@ -95,21 +95,31 @@ const char *plan_gemm(GemmLaunch &g, const void *A, long long lda_elems, const v
                       long long ldw_elems, int bn, bool fp8, const GemmArgs &args) {
   if (bn != 64 && bn != 128 && bn != 256) return "gemm: BN must be 64, 128 or 256";
   if (args.M <= 0 || args.N <= 0 || args.K <= 0) return "gemm: empty problem";
-  if (args.N % 16) return "gemm: N must be a multiple of 16";
-  if (args.mode == kEpiRowLN && args.N != bn) return "gemm: row-LN epilogue needs N == BN";
+  if (args.N % 32) return "gemm: N must be a multiple of 32";
+  if (args.out2 && args.split % 32) return "gemm: split column must be a multiple of 32";
+  if (args.k_splits > 1 && (args.bias || args.mode != kEpiStore || args.out2))
+    return "gemm: split-K writes raw fp32 partials (no bias, residual or column split)";
   const uint32_t elem = fp8 ? 1 : 2;
   g = GemmLaunch{};
   g.bn = bn;
   g.fp8 = fp8;
   g.args = args;
+  {
+    // every K slice must be non-empty
+    const int kblocks = (args.K + (fp8 ? 128 : 64) - 1) / (fp8 ? 128 : 64);
+    int splits = args.k_splits > 1 ? args.k_splits : 1;
+    if (splits > kblocks) splits = kblocks;
+    const int per = (kblocks + splits - 1) / splits;
+    g.args.k_splits = (kblocks + per - 1) / per;
+  }
   if (!make_kmajor_tmap(&g.tmA, A, fp8, static_cast<uint64_t>(args.K),
                         static_cast<uint64_t>(args.M), static_cast<uint64_t>(lda_elems) * elem, 128))
     return "gemm: cannot build TMA descriptor for A (alignment?)";
   if (!make_kmajor_tmap(&g.tmB, W, fp8, static_cast<uint64_t>(args.K),
                         static_cast<uint64_t>(args.N), static_cast<uint64_t>(ldw_elems) * elem, bn))
     return "gemm: cannot build TMA descriptor for W (alignment?)";
-  const long long tiles =
-      static_cast<long long>((args.M + 127) / 128) * ((args.N + bn - 1) / bn);
+  const long long tiles = static_cast<long long>((args.M + 127) / 128) *
+                          ((args.N + bn - 1) / bn) * g.args.k_splits;
   const int sms = num_sms();
   g.grid = dim3(static_cast<unsigned>(tiles < sms ? tiles : sms));
   return nullptr;

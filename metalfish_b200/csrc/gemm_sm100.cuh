@@ -3,17 +3,21 @@
 //   C[M,N] = epilogue( A[M,K] . W[N,K]^T )
 //
 // A (activations) and W (weights, the reference's [out, in] layout) are both
-// K-major in HBM. Each CTA owns a 128 x BN output tile at a time; the CTA is
-// persistent over tiles (grid = number of SMs) and warp-specialised:
+// K-major in HBM. Each CTA owns a 128 x BN output tile (optionally one K
+// slice of it, split-K) at a time; the CTA is persistent over work units
+// (grid = number of SMs) and warp-specialised:
 //   warp 0     TMA producer: one lane streams 128-byte-swizzled K slices of A
 //              and W into a STAGES-deep shared-memory ring (no multicast);
 //   warp 1     MMA issuer: allocates 2*BN TMEM columns (two fp32
 //              accumulators, so the epilogue of tile i overlaps the MMAs of
 //              tile i+1) and issues tcgen05.mma (M=128, N=BN, K=16 bf16 or
 //              K=32 fp8 per instruction) from one lane;
-//   warps 2-5  epilogue: tcgen05.ld the accumulator (TMEM lane = tile row),
-//              apply scale / bias / activation / residual / row-LayerNorm and
-//              store bf16 (or e4m3) to HBM.
+//   warps 2-9  epilogue: two warps per TMEM lane quarter (TMEM lane = tile
+//              row), alternating 32-column chunks; tcgen05.ld the
+//              accumulator, apply scale / bias / activation / residual, and
+//              store bf16, e4m3 or fp32 to HBM through a per-warp
+//              shared-memory staging tile so that every store instruction
+//              writes 4 rows x 128 contiguous bytes.
 // All barrier waits are bounded (sm100_ptx.cuh).
 #pragma once
 #include <cuda_fp8.h>
@@ -25,33 +29,17 @@ namespace mfb200 {
 enum EpiMode : int {
   kEpiStore = 0,  // act(scale*acc + bias)
   kEpiResid = 1,  // resid + alpha * (scale*acc + bias)
-  kEpiRowLN = 2,  // LN(act(scale*acc + bias)) over the full row (requires N == BN)
 };
 
 enum Act : int {
   kActNone = 0, kActRelu, kActRelu2, kActTanh, kActSigmoid, kActSwish, kActMish, kActSelu
 };
 
-// Activations of the reference CPU backend (src/nn/cpu/cpu_network.cpp:303-324),
-// written with CUDA's own expf/tanhf/log1pf.
-__device__ __forceinline__ float apply_act(float v, int act) {
-  switch (act) {
-  case kActRelu: return fmaxf(v, 0.0f);
-  case kActRelu2: { const float r = fmaxf(v, 0.0f); return r * r; }
-  case kActTanh: return tanhf(v);
-  case kActSigmoid: return 1.0f / (1.0f + expf(-v));
-  case kActSwish: return v / (1.0f + expf(-v));
-  case kActMish: return v * tanhf(log1pf(expf(v)));
-  case kActSelu: return 1.05070098f * (v > 0.0f ? v : 1.67326324f * (expf(v) - 1.0f));
-  default: return v;
-  }
-}
-
 struct GemmArgs {
   int M, N, K;
   int mode, act;
   const float *bias;          // [N] or nullptr
-  void *out;                  // [M, ldo] bf16 (or e4m3 when out_fp8)
+  void *out;                  // [M, ldo] bf16 (or e4m3 / fp32)
   long long ldo;
   void *out2;                 // columns n >= split go to out2[m, n - split]
   long long ldo2;
@@ -59,30 +47,219 @@ struct GemmArgs {
   const float *resid;         // kEpiResid: fp32 residual parent [M, ldr]
   long long ldr;
   float alpha;
-  const float *ln_gamma, *ln_beta;  // kEpiRowLN
-  float ln_eps;
   const float *col_scale;     // per-output-channel scale (fp8 weights) or nullptr
   float a_scale;              // activation scale (fp8) ; 1 for bf16
   int out_f32;                // store fp32 instead of bf16
   int out_fp8;                // store e4m3 instead of bf16 ...
   float out_inv_scale;        // ... after multiplying by this
+  int k_splits;               // >1: split-K; K slice s writes fp32 partials at
+  long long split_stride;     //     out + s * split_stride (raw accumulator)
   unsigned *status;           // device status word
 };
+
+// mish(x) = x * tanh(softplus(x)). With e = exp(x), tanh(log(1 + e)) =
+// ((1+e)^2 - 1) / ((1+e)^2 + 1) = n / (n + 2) where n = e * (e + 2): one
+// exponential and one division instead of exp, log1p and tanh. For x > 20 the
+// ratio is 1 to fp32 precision (and e*e would overflow), so mish(x) = x.
+__device__ __forceinline__ float mish_fast(float v) {
+  if (v > 20.0f) return v;
+  const float e = expf(v);
+  const float n = e * (e + 2.0f);
+  return v * __fdividef(n, n + 2.0f);
+}
+
+// Activations of the reference CPU backend (src/nn/cpu/cpu_network.cpp:303-324).
+template <int ACT>
+__device__ __forceinline__ float act_t(float v) {
+  if constexpr (ACT == kActRelu) return fmaxf(v, 0.0f);
+  else if constexpr (ACT == kActRelu2) { const float r = fmaxf(v, 0.0f); return r * r; }
+  else if constexpr (ACT == kActTanh) return tanhf(v);
+  else if constexpr (ACT == kActSigmoid) return 1.0f / (1.0f + expf(-v));
+  else if constexpr (ACT == kActSwish) return v / (1.0f + expf(-v));
+  else if constexpr (ACT == kActMish) return mish_fast(v);
+  else if constexpr (ACT == kActSelu) return 1.05070098f * (v > 0.0f ? v : 1.67326324f * (expf(v) - 1.0f));
+  else return v;
+}
+
+__device__ __forceinline__ float apply_act(float v, int act) {
+  switch (act) {
+  case kActRelu: return act_t<kActRelu>(v);
+  case kActRelu2: return act_t<kActRelu2>(v);
+  case kActTanh: return act_t<kActTanh>(v);
+  case kActSigmoid: return act_t<kActSigmoid>(v);
+  case kActSwish: return act_t<kActSwish>(v);
+  case kActMish: return act_t<kActMish>(v);
+  case kActSelu: return act_t<kActSelu>(v);
+  default: return v;
+  }
+}
+
+// Per-warp staging tile: 32 rows x 32 fp32, rows of 128 bytes with the 16-byte
+// column group q of row r stored at group q ^ (r & 7): conflict-free both for
+// row-per-lane writes and for the 8-lanes-per-row reads.
+constexpr int kEpiWarps = 8;
+constexpr int kStageFloats = 32 * 32;
+
+__device__ __forceinline__ float4 *stage_at(float *stage, int r, int q) {
+  return reinterpret_cast<float4 *>(stage + r * 32 + ((q ^ (r & 7)) << 2));
+}
+
+// One 32-column chunk of a 32-row slab. `v` holds the scaled accumulator
+// plus bias for tile row `lane`; phase 1 applies the activation (or alpha)
+// and writes the warp's staging tile, phase 2 re-reads it so that 8 lanes
+// cover one row: each store (and residual load) instruction moves 4 rows x
+// 32 contiguous values.
+template <int MODE, int ACT>
+__device__ __forceinline__ void epi_chunk(const GemmArgs &args, float (&v)[32], int row0, int nb,
+                                          int lane, float *stage, int ks) {
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    if constexpr (MODE == kEpiResid)
+      v[j] *= args.alpha;
+    else
+      v[j] = act_t<ACT>(v[j]);
+  }
+#pragma unroll
+  for (int q = 0; q < 8; ++q)
+    *stage_at(stage, lane, q) = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+  __syncwarp();
+  void *dst_base = args.out;
+  long long ld = args.ldo;
+  int col = nb;
+  if (ks >= 0) {
+    dst_base = static_cast<float *>(args.out) + ks * args.split_stride;
+  } else if (args.out2 && nb >= args.split) {
+    dst_base = args.out2;
+    ld = args.ldo2;
+    col = nb - args.split;
+  }
+  const int q = lane & 7;
+  const int cc = q * 4;
+  float4 rv[8];
+  if constexpr (MODE == kEpiResid) {
+    // issue all eight residual loads before using any (rows past M clamp to
+    // the last valid row; those results are discarded)
+#pragma unroll
+    for (int it = 0; it < 8; ++it) {
+      const int grow = min(row0 + it * 4 + (lane >> 3), args.M - 1);
+      rv[it] = __ldg(reinterpret_cast<const float4 *>(
+          args.resid + static_cast<long long>(grow) * args.ldr + nb + cc));
+    }
+  }
+#pragma unroll
+  for (int it = 0; it < 8; ++it) {
+    const int rr = it * 4 + (lane >> 3);
+    const int grow = row0 + rr;
+    float4 f = *stage_at(stage, rr, q);
+    if constexpr (MODE == kEpiResid) {
+      f.x += rv[it].x;
+      f.y += rv[it].y;
+      f.z += rv[it].z;
+      f.w += rv[it].w;
+    }
+    if (grow < args.M) {
+      const long long off = static_cast<long long>(grow) * ld + col + cc;
+      if (ks >= 0 || args.out_f32) {
+        *reinterpret_cast<float4 *>(static_cast<float *>(dst_base) + off) = f;
+      } else if (args.out_fp8) {
+        const float is = args.out_inv_scale;
+        const __nv_fp8_e4m3 a(f.x * is), b(f.y * is), c2(f.z * is), d(f.w * is);
+        const uint32_t w = uint32_t(a.__x) | (uint32_t(b.__x) << 8) | (uint32_t(c2.__x) << 16) |
+                           (uint32_t(d.__x) << 24);
+        *reinterpret_cast<uint32_t *>(static_cast<uint8_t *>(dst_base) + off) = w;
+      } else {
+        const __nv_bfloat162 lo = __floats2bfloat162_rn(f.x, f.y);
+        const __nv_bfloat162 hi = __floats2bfloat162_rn(f.z, f.w);
+        *reinterpret_cast<uint2 *>(static_cast<__nv_bfloat16 *>(dst_base) + off) = make_uint2(
+            *reinterpret_cast<const uint32_t *>(&lo), *reinterpret_cast<const uint32_t *>(&hi));
+      }
+    }
+  }
+  __syncwarp();
+}
+
+// The chunks of one tile owned by this warp (every other 32-column chunk,
+// starting at `group`*32), with the TMEM load of the next chunk in flight
+// while the current one is processed.
+template <int BN, int MODE, int ACT>
+__device__ __forceinline__ void epilogue_tile(const GemmArgs &args, uint32_t taddr, int row0,
+                                              int n0, int group, int lane, float *stage, int ks) {
+  uint32_t raw[32];
+  int c = group * 32;
+  tmem_ld32(taddr + c, raw);
+  for (; c < BN; c += 64) {
+    tmem_wait_ld();
+    float v[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(raw[j]);
+    if (c + 64 < BN) tmem_ld32(taddr + c + 64, raw);  // warp-collective prefetch
+    const int nb = n0 + c;
+    if (nb >= args.N) continue;
+    if (ks < 0) {
+      if (args.a_scale != 1.0f) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] *= args.a_scale;
+      }
+      if (args.col_scale) {
+        const float4 *cs = reinterpret_cast<const float4 *>(args.col_scale + nb);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const float4 f = __ldg(cs + q);
+          v[4 * q] *= f.x; v[4 * q + 1] *= f.y; v[4 * q + 2] *= f.z; v[4 * q + 3] *= f.w;
+        }
+      }
+      if (args.bias) {
+        const float4 *bp = reinterpret_cast<const float4 *>(args.bias + nb);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const float4 f = __ldg(bp + q);
+          v[4 * q] += f.x; v[4 * q + 1] += f.y; v[4 * q + 2] += f.z; v[4 * q + 3] += f.w;
+        }
+      }
+    }
+    epi_chunk<MODE, ACT>(args, v, row0, nb, lane, stage, ks);
+  }
+}
+
+template <int BN>
+__device__ __forceinline__ void epilogue_dispatch(const GemmArgs &args, uint32_t taddr, int row0,
+                                                  int n0, int group, int lane, float *stage,
+                                                  int ks) {
+#define MFB_EPI(MODE, ACT) \
+  epilogue_tile<BN, MODE, ACT>(args, taddr, row0, n0, group, lane, stage, ks)
+  if (ks >= 0 || args.mode != kEpiResid) {
+    switch (ks >= 0 ? kActNone : args.act) {
+    case kActRelu: MFB_EPI(kEpiStore, kActRelu); break;
+    case kActRelu2: MFB_EPI(kEpiStore, kActRelu2); break;
+    case kActTanh: MFB_EPI(kEpiStore, kActTanh); break;
+    case kActSigmoid: MFB_EPI(kEpiStore, kActSigmoid); break;
+    case kActSwish: MFB_EPI(kEpiStore, kActSwish); break;
+    case kActMish: MFB_EPI(kEpiStore, kActMish); break;
+    case kActSelu: MFB_EPI(kEpiStore, kActSelu); break;
+    default: MFB_EPI(kEpiStore, kActNone); break;
+    }
+  } else {
+    MFB_EPI(kEpiResid, kActNone);
+  }
+#undef MFB_EPI
+}
 
 template <int BN, bool FP8>
 struct GemmShape {
   static constexpr int BM = 128;
-  static constexpr int BK = FP8 ? 128 : 64;        // elements per 128-byte swizzled row
+  static constexpr int BK = FP8 ? 128 : 64;  // elements per 128-byte swizzled row
   static constexpr int A_BYTES = BM * 128;
   static constexpr int B_BYTES = BN * 128;
   static constexpr int STAGES = BN == 256 ? 4 : (BN == 128 ? 6 : 8);
   static constexpr int TMEM_COLS = 2 * BN;
-  static constexpr int SMEM_BYTES = STAGES * (A_BYTES + B_BYTES) + 1024 + 256;
-  static constexpr int THREADS = 192;
+  static constexpr int STAGE_BYTES = kEpiWarps * kStageFloats * 4;  // epilogue staging
+  static constexpr int SMEM_BYTES = STAGES * (A_BYTES + B_BYTES) + STAGE_BYTES + 1024 + 256;
+  static constexpr int THREADS = 64 + 32 * kEpiWarps;
+  static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 };
 
 template <int BN, bool FP8>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(64 + 32 * kEpiWarps, 1)
     gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA,
                       const __grid_constant__ CUtensorMap tmB, const GemmArgs args) {
   using S = GemmShape<BN, FP8>;
@@ -92,7 +269,8 @@ __global__ void __launch_bounds__(192, 1)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint8_t *smA = base;
   uint8_t *smB = base + STAGES * S::A_BYTES;
-  uint64_t *full = reinterpret_cast<uint64_t *>(smB + STAGES * S::B_BYTES);
+  float *stage_base = reinterpret_cast<float *>(smB + STAGES * S::B_BYTES);
+  uint64_t *full = reinterpret_cast<uint64_t *>(smB + STAGES * S::B_BYTES + S::STAGE_BYTES);
   uint64_t *empty = full + STAGES;
   uint64_t *tfull = empty + STAGES;
   uint64_t *tempty = tfull + 2;
@@ -104,8 +282,10 @@ __global__ void __launch_bounds__(192, 1)
   const int lane = threadIdx.x & 31;
   const int tiles_m = (args.M + S::BM - 1) / S::BM;
   const int tiles_n = (args.N + BN - 1) / BN;
-  const int tiles = tiles_m * tiles_n;
+  const int splits = args.k_splits > 1 ? args.k_splits : 1;
+  const int units = tiles_m * tiles_n * splits;
   const int kblocks = (args.K + S::BK - 1) / S::BK;
+  const int kb_per = (kblocks + splits - 1) / splits;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -114,7 +294,7 @@ __global__ void __launch_bounds__(192, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 128);
+      mbar_init(&tempty[a], 32 * kEpiWarps);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -138,10 +318,12 @@ __global__ void __launch_bounds__(192, 1)
       uint32_t round = 0;
       long long issued = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x) {
+      for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+        const int t = u / splits, ks = u % splits;
         const int m0 = (t / tiles_n) * S::BM;
         const int n0 = (t % tiles_n) * BN;
-        for (int kb = 0; kb < kblocks; ++kb) {
+        const int kb1 = min(kblocks, (ks + 1) * kb_per);
+        for (int kb = ks * kb_per; kb < kb1; ++kb) {
           if (!mbar_wait(&empty[stage], (round & 1) ^ 1, args.status, kErrTimeoutProducer,
                          abort_flag)) {
             ok = false;
@@ -177,7 +359,8 @@ __global__ void __launch_bounds__(192, 1)
       uint32_t round = 0;
       int local = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < tiles && ok; t += gridDim.x, ++local) {
+      for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ++local) {
+        const int ks = u % splits;
         const int acc = local & 1;
         const uint32_t aphase = (local >> 1) & 1;
         if (!mbar_wait(&tempty[acc], aphase ^ 1, args.status, kErrTimeoutMma, abort_flag)) {
@@ -186,7 +369,8 @@ __global__ void __launch_bounds__(192, 1)
         }
         tc_fence_after();
         const uint32_t d = tmem_base + static_cast<uint32_t>(acc * BN);
-        for (int kb = 0; kb < kblocks; ++kb) {
+        const int kb0 = ks * kb_per, kb1 = min(kblocks, kb0 + kb_per);
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&full[stage], round & 1, args.status, kErrTimeoutMma, abort_flag)) {
             ok = false;
             break;
@@ -197,10 +381,11 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {
             // advance 32 bytes along K inside the 128-byte swizzled row
+            const uint32_t accumulate = (kb > kb0 || kk > 0) ? 1u : 0u;
             if (FP8)
-              umma_f8(d, ad + 2 * kk, bd + 2 * kk, idesc, (kb | kk) != 0);
+              umma_f8(d, ad + 2 * kk, bd + 2 * kk, idesc, accumulate);
             else
-              umma_f16(d, ad + 2 * kk, bd + 2 * kk, idesc, (kb | kk) != 0);
+              umma_f16(d, ad + 2 * kk, bd + 2 * kk, idesc, accumulate);
           }
           umma_commit(&empty[stage]);
           if (++stage == STAGES) { stage = 0; ++round; }
@@ -222,122 +407,22 @@ __global__ void __launch_bounds__(192, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    const int quarter = warp & 3;  // TMEM lane quarter this warp may access
-    const int row_in_tile = quarter * 32 + lane;
+    const int quarter = warp & 3;        // TMEM lane quarter this warp may access
+    const int group = (warp - 2) >> 2;   // which alternate 32-column chunks
+    float *stage = stage_base + (warp - 2) * kStageFloats;
     int local = 0;
-    for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++local) {
+    for (int u = blockIdx.x; u < units; u += gridDim.x, ++local) {
+      const int t = u / splits;
+      const int ks = splits > 1 ? u % splits : -1;
       const int acc = local & 1;
       const uint32_t aphase = (local >> 1) & 1;
       if (!mbar_wait(&tfull[acc], aphase, args.status, kErrTimeoutEpilogue, abort_flag)) break;
       tc_fence_after();
       const int m0 = (t / tiles_n) * S::BM;
       const int n0 = (t % tiles_n) * BN;
-      const int row = m0 + row_in_tile;
-      const bool row_ok = row < args.M;
       const uint32_t taddr =
           tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
-      const float ascale = args.a_scale;
-
-      float mean = 0.0f, inv_std = 1.0f;
-      if (args.mode == kEpiRowLN) {
-        // pass 1: row statistics over the whole tile (N == BN)
-        float s = 0.0f, sq = 0.0f;
-        for (int c = 0; c < BN; c += 16) {
-          uint32_t r[16];
-          tmem_ld16(taddr + c, r);
-          tmem_wait_ld();
-#pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const int n = n0 + c + j;
-            float v = __uint_as_float(r[j]) * ascale;
-            if (args.col_scale) v *= args.col_scale[n];
-            if (args.bias) v += args.bias[n];
-            v = apply_act(v, args.act);
-            s += v;
-            sq += v * v;
-          }
-        }
-        mean = s / static_cast<float>(BN);
-        float var = sq / static_cast<float>(BN) - mean * mean;
-        var = var < 0.0f ? 0.0f : var;
-        inv_std = 1.0f / sqrtf(var + args.ln_eps);
-      }
-
-      for (int c = 0; c < BN; c += 16) {
-        uint32_t r[16];
-        tmem_ld16(taddr + c, r);
-        tmem_wait_ld();
-        const int nb = n0 + c;
-        if (!row_ok || nb >= args.N) continue;
-        float v[16];
-        float res[16];
-        if (args.mode == kEpiResid) {
-          const float4 *rp =
-              reinterpret_cast<const float4 *>(args.resid + static_cast<long long>(row) * args.ldr + nb);
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const float4 f = rp[q];
-            res[4 * q] = f.x;
-            res[4 * q + 1] = f.y;
-            res[4 * q + 2] = f.z;
-            res[4 * q + 3] = f.w;
-          }
-        }
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const int n = nb + j;
-          float x = __uint_as_float(r[j]) * ascale;
-          if (args.col_scale) x *= args.col_scale[n];
-          if (args.bias) x += args.bias[n];
-          if (args.mode == kEpiResid) {
-            x = res[j] + args.alpha * x;
-          } else {
-            x = apply_act(x, args.act);
-            if (args.mode == kEpiRowLN)
-              x = (x - mean) * inv_std * args.ln_gamma[n] + args.ln_beta[n];
-          }
-          v[j] = x;
-        }
-        void *dst_base = args.out;
-        long long ld = args.ldo;
-        int col = nb;
-        if (args.out2 && nb >= args.split) {
-          dst_base = args.out2;
-          ld = args.ldo2;
-          col = nb - args.split;
-        }
-        if (args.out_f32) {
-          float4 *dst = reinterpret_cast<float4 *>(static_cast<float *>(dst_base) + row * ld + col);
-#pragma unroll
-          for (int q = 0; q < 4; ++q)
-            dst[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-        } else if (args.out_fp8) {
-          __nv_fp8_e4m3 *dst = static_cast<__nv_fp8_e4m3 *>(dst_base) + row * ld + col;
-          uint32_t packed[4];
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            uint32_t w = 0;
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const __nv_fp8_e4m3 f(v[q * 4 + e] * args.out_inv_scale);
-              w |= static_cast<uint32_t>(f.__x) << (8 * e);
-            }
-            packed[q] = w;
-          }
-          *reinterpret_cast<uint4 *>(dst) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
-        } else {
-          __nv_bfloat16 *dst = static_cast<__nv_bfloat16 *>(dst_base) + row * ld + col;
-          uint32_t packed[8];
-#pragma unroll
-          for (int q = 0; q < 8; ++q) {
-            const __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * q], v[2 * q + 1]);
-            packed[q] = *reinterpret_cast<const uint32_t *>(&h);
-          }
-          uint4 *d4 = reinterpret_cast<uint4 *>(dst);
-          d4[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
-          d4[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
-        }
-      }
+      epilogue_dispatch<BN>(args, taddr, m0 + quarter * 32, n0, group, lane, stage, ks);
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
     }

@@ -1,6 +1,7 @@
 // kernels.cu -- memory-bound and small-matmul kernels of the BT4 forward.
 #include <cuda_bf16.h>
 
+#include "gemm_sm100.cuh"
 #include "kernels.cuh"
 
 namespace mfb200 {
@@ -263,6 +264,70 @@ void launch_layernorm(const void *in, bool in_f32, int rows, int width, const fl
     layernorm_block_kernel<<<rows, 256, 0, s>>>(static_cast<const __nv_bfloat16 *>(in), width,
                                                 gamma, beta, eps, out);
     return;
+  }
+}
+
+
+// ------------------------------------------------------------------ split-K reduce
+// out[r] = LN(act(sum_s part[s][r] + bias)) for rows of width 32*VPL; one warp
+// per row (the smolgen dense1 stage: dense, bias, activation, LN eps 1e-3,
+// src/nn/cpu/cpu_network.cpp:1143-1157).
+template <int VPL>
+__global__ void splitk_act_ln_kernel(const float *__restrict__ part, int splits, long long stride,
+                                     int rows, const float *__restrict__ bias, int act,
+                                     const float *__restrict__ gamma, const float *__restrict__ beta,
+                                     float eps, __nv_bfloat16 *__restrict__ out) {
+  constexpr int W = 32 * VPL;
+  const long long row = static_cast<long long>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  float v[VPL];
+#pragma unroll
+  for (int q = 0; q < VPL / 4; ++q) {
+    const int c = q * 128 + lane * 4;
+    float4 a = *reinterpret_cast<const float4 *>(bias + c);
+    for (int sidx = 0; sidx < splits; ++sidx) {
+      const float4 f = *reinterpret_cast<const float4 *>(part + sidx * stride + row * W + c);
+      a.x += f.x; a.y += f.y; a.z += f.z; a.w += f.w;
+    }
+    v[4 * q] = apply_act(a.x, act);
+    v[4 * q + 1] = apply_act(a.y, act);
+    v[4 * q + 2] = apply_act(a.z, act);
+    v[4 * q + 3] = apply_act(a.w, act);
+  }
+  float s = 0.0f;
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) s += v[i];
+#pragma unroll
+  for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  const float mean = s / static_cast<float>(W);
+  float sq = 0.0f;
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) sq += (v[i] - mean) * (v[i] - mean);
+#pragma unroll
+  for (int o = 16; o; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+  const float inv = 1.0f / sqrtf(sq / static_cast<float>(W) + eps);
+#pragma unroll
+  for (int q = 0; q < VPL / 4; ++q) {
+    const int c = q * 128 + lane * 4;
+    float r[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) r[e] = (v[4 * q + e] - mean) * inv * gamma[c + e] + beta[c + e];
+    *reinterpret_cast<uint2 *>(out + row * W + c) = make_uint2(pack_bf16x2(r[0], r[1]), pack_bf16x2(r[2], r[3]));
+  }
+}
+
+bool launch_splitk_act_ln(const float *part, int splits, long long stride, int rows, int width,
+                          const float *bias, int act, const float *gamma, const float *beta,
+                          float eps, __nv_bfloat16 *out, cudaStream_t s) {
+  const int wpb = 8;
+  const unsigned grid = static_cast<unsigned>((rows + wpb - 1) / wpb);
+  switch (width) {
+  case 128: splitk_act_ln_kernel<4><<<grid, 32 * wpb, 0, s>>>(part, splits, stride, rows, bias, act, gamma, beta, eps, out); return true;
+  case 256: splitk_act_ln_kernel<8><<<grid, 32 * wpb, 0, s>>>(part, splits, stride, rows, bias, act, gamma, beta, eps, out); return true;
+  case 512: splitk_act_ln_kernel<16><<<grid, 32 * wpb, 0, s>>>(part, splits, stride, rows, bias, act, gamma, beta, eps, out); return true;
+  case 1024: splitk_act_ln_kernel<32><<<grid, 32 * wpb, 0, s>>>(part, splits, stride, rows, bias, act, gamma, beta, eps, out); return true;
+  default: return false;
   }
 }
 

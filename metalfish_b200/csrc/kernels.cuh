@@ -33,6 +33,13 @@ void launch_layernorm(const void *in, bool in_f32, int rows, int width, const fl
                       const float *beta, float eps, const float *multT, const float *addT,
                       __nv_bfloat16 *out, float *out_f32, cudaStream_t s);
 
+// out = LN(act(sum of `splits` fp32 partials + bias)) per row (split-K
+// epilogue of a skinny GEMM); width 128/256/512/1024. Returns false for other
+// widths.
+bool launch_splitk_act_ln(const float *part, int splits, long long stride, int rows, int width,
+                          const float *bias, int act, const float *gamma, const float *beta,
+                          float eps, __nv_bfloat16 *out, cudaStream_t s);
+
 // 64-token attention per (position, head) with the smolgen bias added before
 // the softmax: ctx[b*64+q, h*dh:..] = softmax(Q K^T / sqrt(dh) + bias) V.
 // qkv: [B*64, ldq] with Q at column 0, K at d, V at 2d. bias: [B*H, 4096].

@@ -42,6 +42,7 @@ using namespace mfb200;
 namespace {
 
 thread_local std::string t_last_error;
+constexpr int kMaxSplits = 32;  // split-K slices of the smolgen dense1 GEMM
 
 struct Fail : std::runtime_error {
   using std::runtime_error::runtime_error;
@@ -140,7 +141,9 @@ const char *validate(const mfb200_net_desc &n) {
   if (n.dff <= 0 || n.dff % 16 || n.emb_dff <= 0 || n.emb_dff % 16) return "dff must be a multiple of 16";
   if (n.pe <= 0 || n.pe % 8 || 112 + n.pe > kEmbIn) return "pe must be a multiple of 8, at most 80";
   if (n.smolgen_compress <= 0 || n.smolgen_compress % 16) return "smolgen compress must be a multiple of 16";
-  if (n.smolgen_hidden <= 0 || n.smolgen_hidden % 16) return "smolgen hidden must be a multiple of 16";
+  if (n.smolgen_hidden != 128 && n.smolgen_hidden != 256 && n.smolgen_hidden != 512 &&
+      n.smolgen_hidden != 1024)
+    return "smolgen hidden must be 128, 256, 512 or 1024";
   if (n.smolgen_gen <= 0 || n.smolgen_gen % 16) return "smolgen gen must be a multiple of 16";
   if (n.policy_d <= 0 || n.policy_d % 64) return "policy embedding must be a multiple of 64";
   if (n.value_emb <= 0 || n.mlh_emb <= 0 || n.value_emb + n.mlh_emb > 64)
@@ -225,7 +228,7 @@ struct Shard {  // one GPU
   float *values;
   __nv_bfloat16 *x0, *p, *peo, *X, *X1, *QKV, *C, *S1, *S2pre, *S2, *BIAS, *CTX, *H, *E, *QK,
       *VM, *VH;
-  float *Xf, *X1f, *T;  // fp32 residual stream (LN outputs) and pre-LN sums
+  float *Xf, *X1f, *T, *SK;  // fp32 residual stream (LN outputs) and pre-LN sums
   float *policy, *wdl, *mlh;
   unsigned *status;
   cudaEvent_t ev[4];
@@ -451,6 +454,7 @@ void alloc_workspace(Shard &S, const mfb200_net_desc &n, int max_batch) {
       {reinterpret_cast<void **>(&S.X1), M * d * 2},
       {reinterpret_cast<void **>(&S.T), M * d * 4},
       {reinterpret_cast<void **>(&S.Xf), M * d * 4},
+      {reinterpret_cast<void **>(&S.SK), size_t(kMaxSplits) * B * n.smolgen_hidden * 4},
       {reinterpret_cast<void **>(&S.X1f), M * d * 4},
       {reinterpret_cast<void **>(&S.QKV), M * 3 * d * 2},
       {reinterpret_cast<void **>(&S.C), M * n.smolgen_compress * 2},
@@ -510,7 +514,7 @@ void add_gemm(Shard::Plan &P, Shard &S, const char *name, const void *A, long lo
   st.name = name;
   st.is_gemm = true;
   st.flops = 2.0 * a.M * double(a.N) * a.K;
-  const int bn = (a.mode == kEpiRowLN) ? a.N : pick_bn(a.M, a.N);
+  const int bn = pick_bn(a.M, a.N);
   if (const char *err = plan_gemm(st.g, A, lda, W.w, W.ld, bn, W.fp8, a))
     throw Fail(std::string(name) + ": " + err);
   P.steps.push_back(std::move(st));
@@ -587,26 +591,23 @@ std::unique_ptr<Shard::Plan> build_plan(Shard &S, const mfb200_net_desc &n, int 
       add_gemm(*P, S, "qkv", S.X, d, Lw.qkvc, a);
     }
     {
-      // smolgen dense1 over the flattened [B, 64*c] compress output
-      GemmArgs a = base_args(S, B, n.smolgen_hidden, 64 * n.smolgen_compress);
-      a.bias = Lw.b_sg1;
-      a.act = n.act_smolgen;
-      a.out = S.S1;
-      a.ldo = n.smolgen_hidden;
-      const bool fused_ln = n.smolgen_hidden == 64 || n.smolgen_hidden == 128 || n.smolgen_hidden == 256;
-      if (fused_ln) {
-        a.mode = kEpiRowLN;
-        a.ln_gamma = Lw.sg_ln1_g;
-        a.ln_beta = Lw.sg_ln1_b;
-        a.ln_eps = eps;
-        add_gemm(*P, S, "smolgen_dense1_ln", S.C, 64 * n.smolgen_compress, Lw.sg1, a);
-      } else {
-        a.out = S.S2pre;
-        add_gemm(*P, S, "smolgen_dense1", S.C, 64 * n.smolgen_compress, Lw.sg1, a);
-        add_fn(*P, "smolgen_ln1", 0, [&S, &Lw, B, w = n.smolgen_hidden, eps](cudaStream_t s) {
-          launch_layernorm(S.S2pre, false, B, w, Lw.sg_ln1_g, Lw.sg_ln1_b, eps, nullptr, nullptr, S.S1, nullptr, s);
-        });
-      }
+      // smolgen dense1 over the flattened [B, 64*c] compress output: M = B is
+      // skinny and K = 64*c long, so split K across CTAs, then one kernel sums
+      // the partials and applies bias, activation and LN (eps 1e-3).
+      const int h1 = n.smolgen_hidden, K1 = 64 * n.smolgen_compress;
+      GemmArgs a = base_args(S, B, h1, K1);
+      const long long tiles = static_cast<long long>((B + 127) / 128) * ((h1 + 255) / 256);
+      a.k_splits = static_cast<int>(std::max<long long>(1, std::min<long long>(kMaxSplits, num_sms() / tiles)));
+      a.out = S.SK;
+      a.ldo = h1;
+      a.out_f32 = 1;
+      a.split_stride = static_cast<long long>(B) * h1;
+      add_gemm(*P, S, "smolgen_dense1", S.C, K1, Lw.sg1, a);
+      const int splits = P->steps.back().g.args.k_splits;
+      add_fn(*P, "smolgen_dense1_reduce_ln", 0, [&S, &Lw, B, h1, splits, act = n.act_smolgen, eps](cudaStream_t s) {
+        launch_splitk_act_ln(S.SK, splits, static_cast<long long>(B) * h1, B, h1, Lw.b_sg1, act,
+                             Lw.sg_ln1_g, Lw.sg_ln1_b, eps, S.S1, s);
+      });
     }
     {
       GemmArgs a = base_args(S, B, hg, n.smolgen_hidden);

@@ -18,20 +18,23 @@ def mish(x):
     return x * np.tanh(np.log1p(np.exp(x)))
 
 
-def run_gemm(M, N, K, bn, mode=0, act=0, bias=True, alpha=0.5, seed=0, out_f32=False):
+def run_gemm(M, N, K, bn, mode=0, act=0, bias=True, alpha=0.5, seed=0, out_f32=False, k_splits=1):
     rng = np.random.default_rng(seed)
     A = rng.standard_normal((M, K), dtype=np.float32)
     W = rng.standard_normal((N, K), dtype=np.float32) / np.float32(np.sqrt(K))
-    b = rng.standard_normal(N, dtype=np.float32) * 0.1 if bias else None
+    b = rng.standard_normal(N, dtype=np.float32) * 0.1
     R = rng.standard_normal((M, N), dtype=np.float32)
     g = (1 + 0.1 * rng.standard_normal(N)).astype(np.float32)
     be = (0.1 * rng.standard_normal(N)).astype(np.float32)
     Ab, Wb = to_bf16_bits(A), to_bf16_bits(W)
-    out = np.zeros((M, N), np.float32 if out_f32 else np.uint16)
+    if k_splits > 1:
+        bias, out_f32 = False, True
+    b = b if bias else None
+    out = np.zeros((k_splits, M, N), np.float32 if out_f32 else np.uint16)
     st = ctypes.c_uint(0)
     rc = lib().mfb200_debug_gemm(M, N, K, bn, 0, _p(Ab), _p(Wb), _p(b), mode, act, _p(R),
                                  ctypes.c_float(alpha), _p(g), _p(be), ctypes.c_float(1e-3),
-                                 None, ctypes.c_float(1.0), int(out_f32), _p(out),
+                                 None, ctypes.c_float(1.0), int(out_f32), k_splits, _p(out),
                                  ctypes.byref(st))
     assert rc == 0, f"rc={rc} status={st.value}"
     acc = from_bf16_bits(Ab).astype(np.float64) @ from_bf16_bits(Wb).astype(np.float64).T
@@ -41,11 +44,8 @@ def run_gemm(M, N, K, bn, mode=0, act=0, bias=True, alpha=0.5, seed=0, out_f32=F
         ref = R + alpha * acc
     else:
         ref = {0: acc, 2: np.maximum(acc, 0) ** 2, 5: acc / (1 + np.exp(-acc)), 6: mish(acc)}[act]
-        if mode == 2:
-            mu = ref.mean(1, keepdims=True)
-            var = ref.var(1, keepdims=True)
-            ref = (ref - mu) / np.sqrt(var + 1e-3) * g + be
-    return (out if out_f32 else from_bf16_bits(out)), ref
+    got = out.sum(0) if out_f32 else from_bf16_bits(out[0])
+    return got, ref
 
 
 @pytest.mark.parametrize("M,N,K,bn", [
@@ -82,6 +82,8 @@ def test_gemm_residual_fp32_out():
     np.testing.assert_allclose(got, ref, rtol=1e-4, atol=1e-4)
 
 
-def test_gemm_row_layernorm():
-    got, ref = run_gemm(200, 256, 2048, 256, mode=2, act=5)
-    np.testing.assert_allclose(got, ref, rtol=2e-2, atol=3e-2)
+@pytest.mark.parametrize("M,K,splits", [(1024, 2048, 16), (64, 2048, 32), (300, 1024, 5)])
+def test_gemm_split_k(M, K, splits):
+    """Split-K partial products sum to the full product (smolgen dense1 path)."""
+    got, ref = run_gemm(M, 256, K, 256, k_splits=splits)
+    np.testing.assert_allclose(got, ref, rtol=1e-4, atol=1e-3)
