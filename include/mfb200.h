@@ -121,6 +121,27 @@ MFB200_API int mfb200_profile(mfb200_handle *h, int batch, int iters, float *sta
                    char *names, size_t names_len, int max_stages);
 
 MFB200_API const char *mfb200_last_error(mfb200_handle *h);
+
+/* For callers that cannot allocate GPU memory -- code running inside another
+ * framework's memory pool, or a search thread that must not take the
+ * driver's allocation locks or meet an out-of-memory error mid-game. No
+ * counterpart in the reference. Computes d_out[M,N] (fp32) = d_A[M,K] .
+ * d_W[N,K]^T + d_bias (bf16 operands, bias may be NULL) with the tcgen05 GEMM
+ * split into k_splits slices along K, enqueued on `stream` (a cudaStream_t,
+ * NULL = legacy default stream). It calls no cudaMalloc/cudaFree: the partial
+ * products live in one fixed 8 MiB device array that every GPU loading the
+ * library holds until exit, so k_splits*M*N may not exceed 2,097,088 (larger
+ * requests return an error). The first call on a device resolves that
+ * array's address (cudaGetSymbolAddress); make it before any stream capture.
+ * All calls on a device share the array: calls that overlap on the GPU (other
+ * streams, other threads) race and must be serialised by the caller. Every
+ * partial the reduction reads is written by the same call; the one word that
+ * must start at zero (a timeout status flag) is cleared by each call. Requires N % 32 == 0 and K % 8 == 0. Returns 0 on success;
+ * mfb200_noalloc_last_error() gives the calling thread's last message. */
+MFB200_API int mfb200_splitk_gemm_noalloc(const void *d_A, const void *d_W, int M, int N, int K,
+                                          int k_splits, const float *d_bias, float *d_out,
+                                          void *stream);
+MFB200_API const char *mfb200_noalloc_last_error(void);
 MFB200_API void mfb200_destroy(mfb200_handle *h);
 
 #ifdef __cplusplus
