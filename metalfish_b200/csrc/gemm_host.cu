@@ -59,6 +59,28 @@ bool make_kmajor_tmap(CUtensorMap *tm, const void *base, bool fp8, uint64_t k, u
   return r == CUDA_SUCCESS;
 }
 
+// General tiled tensor map (rank 2 or 3, innermost dimension first).
+static bool make_tmap(CUtensorMap *tm, const void *base, CUtensorMapDataType dt, int rank,
+                      const uint64_t *dims, const uint64_t *stride_bytes, const uint32_t *box,
+                      CUtensorMapSwizzle swz) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn || (reinterpret_cast<uintptr_t>(base) & 15)) return false;
+  cuuint64_t d[3], st[2];
+  cuuint32_t b[3], e[3] = {1, 1, 1};
+  for (int i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    b[i] = box[i];
+    if (dims[i] == 0) return false;
+  }
+  for (int i = 0; i + 1 < rank; ++i) {
+    st[i] = stride_bytes[i];
+    if (st[i] & 15) return false;
+  }
+  return fn(tm, dt, rank, const_cast<void *>(base), d, st, b, e, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
+         CUDA_SUCCESS;
+}
+
 template <int BN, bool FP8>
 static cudaError_t launch_t(const GemmLaunch &g, cudaStream_t stream) {
   using S = GemmShape<BN, FP8>;
@@ -70,7 +92,8 @@ static cudaError_t launch_t(const GemmLaunch &g, cudaStream_t stream) {
     if (e != cudaSuccess) return e;
     attr_done = true;
   }
-  gemm_sm100_kernel<BN, FP8><<<g.grid, S::THREADS, S::SMEM_BYTES, stream>>>(g.tmA, g.tmB, g.args);
+  gemm_sm100_kernel<BN, FP8><<<g.grid, S::THREADS, S::SMEM_BYTES, stream>>>(
+      g.tmA, g.tmB, g.tmOut, g.tmOut2, g.tmRes, g.args);
   return cudaGetLastError();
 }
 
@@ -118,6 +141,45 @@ const char *plan_gemm(GemmLaunch &g, const void *A, long long lda_elems, const v
   if (!make_kmajor_tmap(&g.tmB, W, fp8, static_cast<uint64_t>(args.K),
                         static_cast<uint64_t>(args.N), static_cast<uint64_t>(ldw_elems) * elem, bn))
     return "gemm: cannot build TMA descriptor for W (alignment?)";
+  {
+    // epilogue tensor maps: 32-row x 32-column boxes in the output format
+    const bool f32 = g.args.k_splits > 1 || args.out_f32;
+    const CUtensorMapDataType odt = f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                        : (args.out_fp8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8
+                                                        : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16);
+    const uint64_t oel = f32 ? 4 : (args.out_fp8 ? 1 : 2);
+    const CUtensorMapSwizzle oswz = f32 ? CU_TENSOR_MAP_SWIZZLE_128B
+                                        : (args.out_fp8 ? CU_TENSOR_MAP_SWIZZLE_32B
+                                                        : CU_TENSOR_MAP_SWIZZLE_64B);
+    const uint32_t box3[3] = {32, 32, 1};
+    if (g.args.k_splits > 1) {
+      if (args.split_stride != static_cast<long long>(args.M) * args.ldo)
+        return "gemm: split-K partials must be packed [splits, M, ldo]";
+      const uint64_t dims[3] = {uint64_t(args.N), uint64_t(args.M), uint64_t(g.args.k_splits)};
+      const uint64_t st[2] = {uint64_t(args.ldo) * 4, uint64_t(args.split_stride) * 4};
+      if (!make_tmap(&g.tmOut, args.out, odt, 3, dims, st, box3, oswz))
+        return "gemm: cannot build the split-K output tensor map";
+    } else {
+      const int n_main = args.out2 ? args.split : args.N;
+      const uint64_t dims[2] = {uint64_t(n_main), uint64_t(args.M)};
+      const uint64_t st[1] = {uint64_t(args.ldo) * oel};
+      if (!make_tmap(&g.tmOut, args.out, odt, 2, dims, st, box3, oswz))
+        return "gemm: cannot build the output tensor map (alignment?)";
+      if (args.out2) {
+        const uint64_t d2[2] = {uint64_t(args.N - args.split), uint64_t(args.M)};
+        const uint64_t s2[1] = {uint64_t(args.ldo2) * oel};
+        if (!make_tmap(&g.tmOut2, args.out2, odt, 2, d2, s2, box3, oswz))
+          return "gemm: cannot build the second output tensor map";
+      }
+    }
+    if (args.mode == kEpiResid) {
+      const uint64_t dims[2] = {uint64_t(args.N), uint64_t(args.M)};
+      const uint64_t st[1] = {uint64_t(args.ldr) * 4};
+      if (!make_tmap(&g.tmRes, args.resid, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, dims, st, box3,
+                     CU_TENSOR_MAP_SWIZZLE_128B))
+        return "gemm: cannot build the residual tensor map";
+    }
+  }
   const long long tiles = static_cast<long long>((args.M + 127) / 128) *
                           ((args.N + bn - 1) / bn) * g.args.k_splits;
   const int sms = num_sms();

@@ -8,7 +8,9 @@ namespace mfb200 {
 // Plans are built once per (buffer set, batch size) and replayed (directly or
 // inside a CUDA graph).
 struct GemmLaunch {
-  CUtensorMap tmA, tmB;
+  CUtensorMap tmA, tmB;        // operands (K-major, 128-byte swizzle)
+  CUtensorMap tmOut, tmOut2;   // epilogue TMA stores (32 x 32 boxes)
+  CUtensorMap tmRes;           // residual TMA loads (fp32, 32 x 32 boxes)
   GemmArgs args;
   int bn = 256;
   bool fp8 = false;

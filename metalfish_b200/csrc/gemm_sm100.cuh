@@ -14,10 +14,10 @@
 //              K=32 fp8 per instruction) from one lane;
 //   warps 2-9  epilogue: two warps per TMEM lane quarter (TMEM lane = tile
 //              row), alternating 32-column chunks; tcgen05.ld the
-//              accumulator, apply scale / bias / activation / residual, and
-//              store bf16, e4m3 or fp32 to HBM through a per-warp
-//              shared-memory staging tile so that every store instruction
-//              writes 4 rows x 128 contiguous bytes.
+//              accumulator, apply scale / bias / activation / residual
+//              (residual tiles fetched by TMA), write each 32 x 32 chunk into
+//              a per-warp swizzled shared-memory tile in the output format
+//              (bf16, e4m3 or fp32) and TMA-store it asynchronously.
 // All barrier waits are bounded (sm100_ptx.cuh).
 #pragma once
 #include <cuda_fp8.h>
@@ -94,96 +94,73 @@ __device__ __forceinline__ float apply_act(float v, int act) {
   }
 }
 
-// Per-warp staging tile: 32 rows x 32 fp32, rows of 128 bytes with the 16-byte
-// column group q of row r stored at group q ^ (r & 7): conflict-free both for
-// row-per-lane writes and for the 8-lanes-per-row reads.
+// Epilogue staging: every epilogue warp owns a 4 KB tile (1024-byte aligned)
+// that holds one 32-row x 32-column chunk in the exact byte layout the TMA
+// unit expects for the output tensor map: fp32 rows of 128 B with the 128-byte
+// swizzle, bf16 rows of 64 B with the 64-byte swizzle, e4m3 rows of 32 B with
+// the 32-byte swizzle (16-byte group q of row r stored at group q ^ f(r)). With
+// one row per lane these layouts make the shared-memory writes conflict-free,
+// and one elected lane then issues an asynchronous TMA store of the chunk.
+// Residual tiles arrive the same way, by TMA load into the staging tile.
 constexpr int kEpiWarps = 8;
-constexpr int kStageFloats = 32 * 32;
+constexpr int kStageBytes = 32 * 32 * 4;
 
-__device__ __forceinline__ float4 *stage_at(float *stage, int r, int q) {
-  return reinterpret_cast<float4 *>(stage + r * 32 + ((q ^ (r & 7)) << 2));
+struct EpiCtx {
+  const CUtensorMap *out, *out2, *res;
+  uint8_t *stage;      // this warp's staging tile
+  uint64_t *res_bar;   // this warp's mbarrier for residual tile loads
+  uint32_t res_loads;  // residual loads issued so far (phase parity)
+  int lane;
+  volatile int *abort_flag;
+};
+
+__device__ __forceinline__ uint32_t pack_bf16x2_f(float a, float b) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<const uint32_t *>(&h);
 }
 
-// One 32-column chunk of a 32-row slab. `v` holds the scaled accumulator
-// plus bias for tile row `lane`; phase 1 applies the activation (or alpha)
-// and writes the warp's staging tile, phase 2 re-reads it so that 8 lanes
-// cover one row: each store (and residual load) instruction moves 4 rows x
-// 32 contiguous values.
-template <int MODE, int ACT>
-__device__ __forceinline__ void epi_chunk(const GemmArgs &args, float (&v)[32], int row0, int nb,
-                                          int lane, float *stage, int ks) {
+__device__ __forceinline__ void stage_row(const GemmArgs &args, uint8_t *st, int r,
+                                          const float (&v)[32], bool f32) {
+  if (f32) {
 #pragma unroll
-  for (int j = 0; j < 32; ++j) {
-    if constexpr (MODE == kEpiResid)
-      v[j] *= args.alpha;
-    else
-      v[j] = act_t<ACT>(v[j]);
-  }
+    for (int q = 0; q < 8; ++q)
+      *reinterpret_cast<float4 *>(st + r * 128 + ((q ^ (r & 7)) << 4)) =
+          make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+  } else if (args.out_fp8) {
+    const float is = args.out_inv_scale;
 #pragma unroll
-  for (int q = 0; q < 8; ++q)
-    *stage_at(stage, lane, q) = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-  __syncwarp();
-  void *dst_base = args.out;
-  long long ld = args.ldo;
-  int col = nb;
-  if (ks >= 0) {
-    dst_base = static_cast<float *>(args.out) + ks * args.split_stride;
-  } else if (args.out2 && nb >= args.split) {
-    dst_base = args.out2;
-    ld = args.ldo2;
-    col = nb - args.split;
-  }
-  const int q = lane & 7;
-  const int cc = q * 4;
-  float4 rv[8];
-  if constexpr (MODE == kEpiResid) {
-    // issue all eight residual loads before using any (rows past M clamp to
-    // the last valid row; those results are discarded)
+    for (int q = 0; q < 2; ++q) {
+      uint32_t w[4];
 #pragma unroll
-    for (int it = 0; it < 8; ++it) {
-      const int grow = min(row0 + it * 4 + (lane >> 3), args.M - 1);
-      rv[it] = __ldg(reinterpret_cast<const float4 *>(
-          args.resid + static_cast<long long>(grow) * args.ldr + nb + cc));
-    }
-  }
+      for (int k = 0; k < 4; ++k) {
+        uint32_t x = 0;
 #pragma unroll
-  for (int it = 0; it < 8; ++it) {
-    const int rr = it * 4 + (lane >> 3);
-    const int grow = row0 + rr;
-    float4 f = *stage_at(stage, rr, q);
-    if constexpr (MODE == kEpiResid) {
-      f.x += rv[it].x;
-      f.y += rv[it].y;
-      f.z += rv[it].z;
-      f.w += rv[it].w;
-    }
-    if (grow < args.M) {
-      const long long off = static_cast<long long>(grow) * ld + col + cc;
-      if (ks >= 0 || args.out_f32) {
-        *reinterpret_cast<float4 *>(static_cast<float *>(dst_base) + off) = f;
-      } else if (args.out_fp8) {
-        const float is = args.out_inv_scale;
-        const __nv_fp8_e4m3 a(f.x * is), b(f.y * is), c2(f.z * is), d(f.w * is);
-        const uint32_t w = uint32_t(a.__x) | (uint32_t(b.__x) << 8) | (uint32_t(c2.__x) << 16) |
-                           (uint32_t(d.__x) << 24);
-        *reinterpret_cast<uint32_t *>(static_cast<uint8_t *>(dst_base) + off) = w;
-      } else {
-        const __nv_bfloat162 lo = __floats2bfloat162_rn(f.x, f.y);
-        const __nv_bfloat162 hi = __floats2bfloat162_rn(f.z, f.w);
-        *reinterpret_cast<uint2 *>(static_cast<__nv_bfloat16 *>(dst_base) + off) = make_uint2(
-            *reinterpret_cast<const uint32_t *>(&lo), *reinterpret_cast<const uint32_t *>(&hi));
+        for (int e = 0; e < 4; ++e) {
+          const __nv_fp8_e4m3 f(v[16 * q + 4 * k + e] * is);
+          x |= static_cast<uint32_t>(f.__x) << (8 * e);
+        }
+        w[k] = x;
       }
+      *reinterpret_cast<uint4 *>(st + r * 32 + ((q ^ ((r >> 2) & 1)) << 4)) =
+          make_uint4(w[0], w[1], w[2], w[3]);
     }
+  } else {
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      *reinterpret_cast<uint4 *>(st + r * 64 + ((q ^ ((r >> 1) & 3)) << 4)) =
+          make_uint4(pack_bf16x2_f(v[8 * q], v[8 * q + 1]), pack_bf16x2_f(v[8 * q + 2], v[8 * q + 3]),
+                     pack_bf16x2_f(v[8 * q + 4], v[8 * q + 5]), pack_bf16x2_f(v[8 * q + 6], v[8 * q + 7]));
   }
-  __syncwarp();
 }
 
 // The chunks of one tile owned by this warp (every other 32-column chunk,
 // starting at `group`*32), with the TMEM load of the next chunk in flight
-// while the current one is processed.
+// while the current one is processed. Returns false on a barrier timeout.
 template <int BN, int MODE, int ACT>
-__device__ __forceinline__ void epilogue_tile(const GemmArgs &args, uint32_t taddr, int row0,
-                                              int n0, int group, int lane, float *stage, int ks) {
+__device__ __forceinline__ bool epilogue_tile(const GemmArgs &args, EpiCtx &e, uint32_t taddr,
+                                              int row0, int n0, int group, int ks) {
+  const int lane = e.lane;
+  const bool f32 = ks >= 0 || args.out_f32;
   uint32_t raw[32];
   int c = group * 32;
   tmem_ld32(taddr + c, raw);
@@ -195,6 +172,9 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs &args, uint32_t tad
     if (c + 64 < BN) tmem_ld32(taddr + c + 64, raw);  // warp-collective prefetch
     const int nb = n0 + c;
     if (nb >= args.N) continue;
+    // the previous chunk's TMA store must have finished reading the tile
+    if (lane == 0) bulk_wait_read0();
+    __syncwarp();
     if (ks < 0) {
       if (args.a_scale != 1.0f) {
 #pragma unroll
@@ -217,29 +197,58 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs &args, uint32_t tad
         }
       }
     }
-    epi_chunk<MODE, ACT>(args, v, row0, nb, lane, stage, ks);
+    if constexpr (MODE == kEpiResid) {
+      if (lane == 0) {
+        mbar_arrive_expect_tx(e.res_bar, kStageBytes);
+        tma_load_2d(e.stage, e.res, e.res_bar, nb, row0);
+      }
+      if (!mbar_wait(e.res_bar, e.res_loads & 1, args.status, kErrTimeoutEpilogue, e.abort_flag))
+        return false;
+      ++e.res_loads;
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const float4 rv =
+            *reinterpret_cast<const float4 *>(e.stage + lane * 128 + ((q ^ (lane & 7)) << 4));
+        v[4 * q] = rv.x + args.alpha * v[4 * q];
+        v[4 * q + 1] = rv.y + args.alpha * v[4 * q + 1];
+        v[4 * q + 2] = rv.z + args.alpha * v[4 * q + 2];
+        v[4 * q + 3] = rv.w + args.alpha * v[4 * q + 3];
+      }
+      __syncwarp();  // every lane has read its residual row before the tile is overwritten
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = act_t<ACT>(v[j]);
+    }
+    stage_row(args, e.stage, lane, v, f32);
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      if (ks >= 0)
+        tma_store_3d(e.out, e.stage, nb, row0, ks);
+      else if (args.out2 && nb >= args.split)
+        tma_store_2d(e.out2, e.stage, nb - args.split, row0);
+      else
+        tma_store_2d(e.out, e.stage, nb, row0);
+      bulk_commit();
+    }
   }
+  return true;
 }
 
 template <int BN>
-__device__ __forceinline__ void epilogue_dispatch(const GemmArgs &args, uint32_t taddr, int row0,
-                                                  int n0, int group, int lane, float *stage,
-                                                  int ks) {
-#define MFB_EPI(MODE, ACT) \
-  epilogue_tile<BN, MODE, ACT>(args, taddr, row0, n0, group, lane, stage, ks)
-  if (ks >= 0 || args.mode != kEpiResid) {
-    switch (ks >= 0 ? kActNone : args.act) {
-    case kActRelu: MFB_EPI(kEpiStore, kActRelu); break;
-    case kActRelu2: MFB_EPI(kEpiStore, kActRelu2); break;
-    case kActTanh: MFB_EPI(kEpiStore, kActTanh); break;
-    case kActSigmoid: MFB_EPI(kEpiStore, kActSigmoid); break;
-    case kActSwish: MFB_EPI(kEpiStore, kActSwish); break;
-    case kActMish: MFB_EPI(kEpiStore, kActMish); break;
-    case kActSelu: MFB_EPI(kEpiStore, kActSelu); break;
-    default: MFB_EPI(kEpiStore, kActNone); break;
-    }
-  } else {
-    MFB_EPI(kEpiResid, kActNone);
+__device__ __forceinline__ bool epilogue_dispatch(const GemmArgs &args, EpiCtx &e, uint32_t taddr,
+                                                  int row0, int n0, int group, int ks) {
+#define MFB_EPI(MODE, ACT) return epilogue_tile<BN, MODE, ACT>(args, e, taddr, row0, n0, group, ks)
+  if (ks < 0 && args.mode == kEpiResid) MFB_EPI(kEpiResid, kActNone);
+  switch (ks >= 0 ? kActNone : args.act) {
+  case kActRelu: MFB_EPI(kEpiStore, kActRelu);
+  case kActRelu2: MFB_EPI(kEpiStore, kActRelu2);
+  case kActTanh: MFB_EPI(kEpiStore, kActTanh);
+  case kActSigmoid: MFB_EPI(kEpiStore, kActSigmoid);
+  case kActSwish: MFB_EPI(kEpiStore, kActSwish);
+  case kActMish: MFB_EPI(kEpiStore, kActMish);
+  case kActSelu: MFB_EPI(kEpiStore, kActSelu);
+  default: MFB_EPI(kEpiStore, kActNone);
   }
 #undef MFB_EPI
 }
@@ -252,7 +261,7 @@ struct GemmShape {
   static constexpr int B_BYTES = BN * 128;
   static constexpr int STAGES = BN == 256 ? 4 : (BN == 128 ? 6 : 8);
   static constexpr int TMEM_COLS = 2 * BN;
-  static constexpr int STAGE_BYTES = kEpiWarps * kStageFloats * 4;  // epilogue staging
+  static constexpr int STAGE_BYTES = kEpiWarps * kStageBytes;  // epilogue staging tiles
   static constexpr int SMEM_BYTES = STAGES * (A_BYTES + B_BYTES) + STAGE_BYTES + 1024 + 256;
   static constexpr int THREADS = 64 + 32 * kEpiWarps;
   static_assert(SMEM_BYTES <= 232448, "shared memory budget");
@@ -261,7 +270,10 @@ struct GemmShape {
 template <int BN, bool FP8>
 __global__ void __launch_bounds__(64 + 32 * kEpiWarps, 1)
     gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA,
-                      const __grid_constant__ CUtensorMap tmB, const GemmArgs args) {
+                      const __grid_constant__ CUtensorMap tmB,
+                      const __grid_constant__ CUtensorMap tmOut,
+                      const __grid_constant__ CUtensorMap tmOut2,
+                      const __grid_constant__ CUtensorMap tmRes, const GemmArgs args) {
   using S = GemmShape<BN, FP8>;
   constexpr int STAGES = S::STAGES;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -269,12 +281,13 @@ __global__ void __launch_bounds__(64 + 32 * kEpiWarps, 1)
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
   uint8_t *smA = base;
   uint8_t *smB = base + STAGES * S::A_BYTES;
-  float *stage_base = reinterpret_cast<float *>(smB + STAGES * S::B_BYTES);
+  uint8_t *stage_base = smB + STAGES * S::B_BYTES;
   uint64_t *full = reinterpret_cast<uint64_t *>(smB + STAGES * S::B_BYTES + S::STAGE_BYTES);
   uint64_t *empty = full + STAGES;
   uint64_t *tfull = empty + STAGES;
   uint64_t *tempty = tfull + 2;
-  uint64_t *drain = tempty + 2;
+  uint64_t *res_bars = tempty + 2;  // one per epilogue warp
+  uint64_t *drain = res_bars + kEpiWarps;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
@@ -296,6 +309,7 @@ __global__ void __launch_bounds__(64 + 32 * kEpiWarps, 1)
       mbar_init(&tfull[a], 1);
       mbar_init(&tempty[a], 32 * kEpiWarps);
     }
+    for (int w = 0; w < kEpiWarps; ++w) mbar_init(&res_bars[w], 1);
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_barrier_init();
@@ -409,7 +423,13 @@ __global__ void __launch_bounds__(64 + 32 * kEpiWarps, 1)
     // ------------------------------------------------------------ epilogue
     const int quarter = warp & 3;        // TMEM lane quarter this warp may access
     const int group = (warp - 2) >> 2;   // which alternate 32-column chunks
-    float *stage = stage_base + (warp - 2) * kStageFloats;
+    EpiCtx e{&tmOut, &tmOut2, &tmRes, stage_base + (warp - 2) * kStageBytes, &res_bars[warp - 2],
+             0u, lane, abort_flag};
+    if (lane == 0) {
+      tma_prefetch_desc(&tmOut);
+      if (args.out2) tma_prefetch_desc(&tmOut2);
+      if (args.mode == kEpiResid) tma_prefetch_desc(&tmRes);
+    }
     int local = 0;
     for (int u = blockIdx.x; u < units; u += gridDim.x, ++local) {
       const int t = u / splits;
@@ -422,10 +442,12 @@ __global__ void __launch_bounds__(64 + 32 * kEpiWarps, 1)
       const int n0 = (t % tiles_n) * BN;
       const uint32_t taddr =
           tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
-      epilogue_dispatch<BN>(args, taddr, m0 + quarter * 32, n0, group, lane, stage, ks);
+      const bool ok = epilogue_dispatch<BN>(args, e, taddr, m0 + quarter * 32, n0, group, ks);
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
+      if (!ok) break;
     }
+    if (lane == 0) bulk_wait0();  // all TMA stores of this warp have landed
   }
 
   tc_fence_before();
