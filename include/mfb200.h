@@ -70,6 +70,8 @@ typedef struct {
   int32_t precision;  /* MFB200_PRECISION_* */
   int32_t max_batch;  /* largest batch one evaluate call accepts */
   int32_t use_graphs; /* capture one CUDA graph per batch size (1) or launch eagerly (0) */
+  int32_t fp8_gemms;  /* FP8 handles: GEMM groups run in e4m3 (bit mask: 1 embedding FFN,
+                         2 QKV, 4 attention output, 8 FFN1, 16 FFN2; 0 = all) */
 } mfb200_config;
 
 typedef struct {

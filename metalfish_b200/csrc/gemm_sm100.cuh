@@ -52,6 +52,8 @@ struct GemmArgs {
   int out_f32;                // store fp32 instead of bf16
   int out_fp8;                // store e4m3 instead of bf16 ...
   float out_inv_scale;        // ... after multiplying by this
+  const float *a_scale_ptr;   // if set: activation scale multiplied by *a_scale_ptr
+  const float *out_scale_ptr; // if set (e4m3 out): stored value = v / *out_scale_ptr
   int k_splits;               // >1: split-K; K slice s writes fp32 partials at
   long long split_stride;     //     out + s * split_stride (raw accumulator)
   unsigned *status;           // device status word
@@ -120,14 +122,14 @@ __device__ __forceinline__ uint32_t pack_bf16x2_f(float a, float b) {
 }
 
 __device__ __forceinline__ void stage_row(const GemmArgs &args, uint8_t *st, int r,
-                                          const float (&v)[32], bool f32) {
+                                          const float (&v)[32], bool f32, float out_is) {
   if (f32) {
 #pragma unroll
     for (int q = 0; q < 8; ++q)
       *reinterpret_cast<float4 *>(st + r * 128 + ((q ^ (r & 7)) << 4)) =
           make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
   } else if (args.out_fp8) {
-    const float is = args.out_inv_scale;
+    const float is = out_is;
 #pragma unroll
     for (int q = 0; q < 2; ++q) {
       uint32_t w[4];
@@ -161,6 +163,8 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs &args, EpiCtx &e, u
                                               int row0, int n0, int group, int ks) {
   const int lane = e.lane;
   const bool f32 = ks >= 0 || args.out_f32;
+  const float a_scale = args.a_scale_ptr ? args.a_scale * __ldg(args.a_scale_ptr) : args.a_scale;
+  const float out_is = args.out_scale_ptr ? 1.0f / __ldg(args.out_scale_ptr) : args.out_inv_scale;
   uint32_t raw[32];
   int c = group * 32;
   tmem_ld32(taddr + c, raw);
@@ -176,9 +180,9 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs &args, EpiCtx &e, u
     if (lane == 0) bulk_wait_read0();
     __syncwarp();
     if (ks < 0) {
-      if (args.a_scale != 1.0f) {
+      if (a_scale != 1.0f) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] *= args.a_scale;
+        for (int j = 0; j < 32; ++j) v[j] *= a_scale;
       }
       if (args.col_scale) {
         const float4 *cs = reinterpret_cast<const float4 *>(args.col_scale + nb);
@@ -219,7 +223,7 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs &args, EpiCtx &e, u
 #pragma unroll
       for (int j = 0; j < 32; ++j) v[j] = act_t<ACT>(v[j]);
     }
-    stage_row(args, e.stage, lane, v, f32);
+    stage_row(args, e.stage, lane, v, f32, out_is);
     fence_proxy_async_smem();
     __syncwarp();
     if (lane == 0) {

@@ -1,5 +1,6 @@
 // kernels.cu -- memory-bound and small-matmul kernels of the BT4 forward.
 #include <cuda_bf16.h>
+#include <cuda_fp8.h>
 
 #include "gemm_sm100.cuh"
 #include "kernels.cuh"
@@ -120,7 +121,9 @@ __global__ void layernorm_warp_kernel(const void *__restrict__ in_, int rows,
                                       const float *__restrict__ multT,
                                       const float *__restrict__ addT,
                                       __nv_bfloat16 *__restrict__ out,
-                                      float *__restrict__ out_f32) {
+                                      float *__restrict__ out_f32,
+                                      uint8_t *__restrict__ out8,
+                                      const float *__restrict__ scale8) {
   constexpr int W = 32 * VPL;
   const int warps = blockDim.x >> 5;
   const long long row = static_cast<long long>(blockIdx.x) * warps + (threadIdx.x >> 5);
@@ -165,7 +168,7 @@ __global__ void layernorm_warp_kernel(const void *__restrict__ in_, int rows,
   for (int o = 16; o; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
   const float inv = 1.0f / sqrtf(sq / static_cast<float>(W) + eps);
   const int sqr = static_cast<int>(row % kSquares);
-  __nv_bfloat16 *dst = out + row * W;
+  const float inv8 = out8 ? 1.0f / __ldg(scale8) : 0.0f;
 #pragma unroll
   for (int q = 0; q < VPL / 4; ++q) {
     const int c = q * 128 + lane * 4;
@@ -176,7 +179,14 @@ __global__ void layernorm_warp_kernel(const void *__restrict__ in_, int rows,
       if (multT) y = y * multT[sqr * W + c + e] + addT[sqr * W + c + e];
       r[e] = y;
     }
-    *reinterpret_cast<uint2 *>(dst + c) = make_uint2(pack_bf16x2(r[0], r[1]), pack_bf16x2(r[2], r[3]));
+    if (out)
+      *reinterpret_cast<uint2 *>(out + row * W + c) =
+          make_uint2(pack_bf16x2(r[0], r[1]), pack_bf16x2(r[2], r[3]));
+    if (out8) {
+      const __nv_fp8_e4m3 a(r[0] * inv8), b(r[1] * inv8), c2(r[2] * inv8), d(r[3] * inv8);
+      *reinterpret_cast<uint32_t *>(out8 + row * W + c) = uint32_t(a.__x) | (uint32_t(b.__x) << 8) |
+                                                            (uint32_t(c2.__x) << 16) | (uint32_t(d.__x) << 24);
+    }
     if (out_f32)
       *reinterpret_cast<float4 *>(out_f32 + row * W + c) = make_float4(r[0], r[1], r[2], r[3]);
   }
@@ -240,25 +250,33 @@ __global__ void layernorm_block_kernel(const __nv_bfloat16 *__restrict__ in, int
 template <int VPL>
 static void ln_warp(const void *in, bool f32in, int rows, const float *gamma, const float *beta,
                     float eps, const float *multT, const float *addT, __nv_bfloat16 *out,
-                    float *out_f32, cudaStream_t s) {
+                    float *out_f32, uint8_t *out8, const float *scale8, cudaStream_t s) {
   const int wpb = 8;
   const unsigned grid = static_cast<unsigned>((rows + wpb - 1) / wpb);
   if (f32in)
     layernorm_warp_kernel<VPL, true><<<grid, 32 * wpb, 0, s>>>(in, rows, gamma, beta, eps, multT,
-                                                               addT, out, out_f32);
+                                                               addT, out, out_f32, out8, scale8);
   else
     layernorm_warp_kernel<VPL, false><<<grid, 32 * wpb, 0, s>>>(in, rows, gamma, beta, eps, multT,
-                                                                addT, out, out_f32);
+                                                                addT, out, out_f32, out8, scale8);
 }
 
 void launch_layernorm(const void *in, bool in_f32, int rows, int width, const float *gamma,
                       const float *beta, float eps, const float *multT, const float *addT,
                       __nv_bfloat16 *out, float *out_f32, cudaStream_t s) {
+  launch_layernorm_q(in, in_f32, rows, width, gamma, beta, eps, multT, addT, out, out_f32, nullptr,
+                     nullptr, s);
+}
+
+void launch_layernorm_q(const void *in, bool in_f32, int rows, int width, const float *gamma,
+                        const float *beta, float eps, const float *multT, const float *addT,
+                        __nv_bfloat16 *out, float *out_f32, uint8_t *out8, const float *scale8,
+                        cudaStream_t s) {
   switch (width) {
-  case 128: ln_warp<4>(in, in_f32, rows, gamma, beta, eps, multT, addT, out, out_f32, s); return;
-  case 256: ln_warp<8>(in, in_f32, rows, gamma, beta, eps, multT, addT, out, out_f32, s); return;
-  case 512: ln_warp<16>(in, in_f32, rows, gamma, beta, eps, multT, addT, out, out_f32, s); return;
-  case 1024: ln_warp<32>(in, in_f32, rows, gamma, beta, eps, multT, addT, out, out_f32, s); return;
+  case 128: ln_warp<4>(in, in_f32, rows, gamma, beta, eps, multT, addT, out, out_f32, out8, scale8, s); return;
+  case 256: ln_warp<8>(in, in_f32, rows, gamma, beta, eps, multT, addT, out, out_f32, out8, scale8, s); return;
+  case 512: ln_warp<16>(in, in_f32, rows, gamma, beta, eps, multT, addT, out, out_f32, out8, scale8, s); return;
+  case 1024: ln_warp<32>(in, in_f32, rows, gamma, beta, eps, multT, addT, out, out_f32, out8, scale8, s); return;
   default:
     // wide bf16 rows (smolgen's H*g); no gates, no fp32 output on this path
     layernorm_block_kernel<<<rows, 256, 0, s>>>(static_cast<const __nv_bfloat16 *>(in), width,
@@ -343,7 +361,8 @@ constexpr int kBiasStride = 72;  // padded smem row (144 bytes)
 __global__ void __launch_bounds__(128)
     attention_kernel(const __nv_bfloat16 *__restrict__ qkv, long long ldq,
                      const __nv_bfloat16 *__restrict__ bias, int heads, int d,
-                     __nv_bfloat16 *__restrict__ ctx) {
+                     __nv_bfloat16 *__restrict__ ctx, uint8_t *__restrict__ ctx8,
+                     const float *__restrict__ scale8) {
   __shared__ __align__(16) __nv_bfloat16 sQ[kSquares * kQkvStride];
   __shared__ __align__(16) __nv_bfloat16 sK[kSquares * kQkvStride];
   __shared__ __align__(16) __nv_bfloat16 sV[kSquares * kQkvStride];
@@ -460,7 +479,21 @@ __global__ void __launch_bounds__(128)
       mma_bf16_16816(O[j + 1], a, bf[2], bf[3]);
     }
   }
-  __nv_bfloat16 *out = ctx + (static_cast<long long>(b) * kSquares + q0) * d + h * kDh;
+  const long long base_off = (static_cast<long long>(b) * kSquares + q0) * d + h * kDh;
+  if (ctx8) {
+    // e4m3 context for an FP8 output projection: value / *scale8
+    const float inv = 1.0f / __ldg(scale8);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int col = 8 * j + 2 * t;
+      const __nv_fp8x2_e4m3 lo(make_float2(O[j][0] * inv, O[j][1] * inv));
+      const __nv_fp8x2_e4m3 hi(make_float2(O[j][2] * inv, O[j][3] * inv));
+      *reinterpret_cast<__nv_fp8x2_storage_t *>(ctx8 + base_off + static_cast<long long>(g) * d + col) = lo.__x;
+      *reinterpret_cast<__nv_fp8x2_storage_t *>(ctx8 + base_off + static_cast<long long>(g + 8) * d + col) = hi.__x;
+    }
+    return;
+  }
+  __nv_bfloat16 *out = ctx + base_off;
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
     const int col = 8 * j + 2 * t;
@@ -472,8 +505,43 @@ __global__ void __launch_bounds__(128)
 }
 
 void launch_attention(const __nv_bfloat16 *qkv, long long ldq, const __nv_bfloat16 *bias,
-                      int batch, int heads, int d, __nv_bfloat16 *ctx, cudaStream_t s) {
-  attention_kernel<<<batch * heads, 128, 0, s>>>(qkv, ldq, bias, heads, d, ctx);
+                      int batch, int heads, int d, __nv_bfloat16 *ctx, cudaStream_t s,
+                      uint8_t *ctx8, const float *scale8) {
+  attention_kernel<<<batch * heads, 128, 0, s>>>(qkv, ldq, bias, heads, d, ctx, ctx8, scale8);
+}
+
+// ------------------------------------------------------------------ absmax
+// slot = max(slot, max |x|) over n values (non-negative floats order like
+// their bit patterns, so an integer atomicMax suffices). FP8 calibration.
+template <typename T>
+__global__ void absmax_kernel(const T *__restrict__ x, long long n, float *__restrict__ slot) {
+  float m = 0.0f;
+  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    float v;
+    if constexpr (sizeof(T) == 2) v = __bfloat162float(x[i]); else v = x[i];
+    m = fmaxf(m, fabsf(v));
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if ((threadIdx.x & 31) == 0) atomicMax(reinterpret_cast<int *>(slot), __float_as_int(m));
+}
+
+void launch_absmax(const void *x, bool f32, long long n, float *slot, cudaStream_t s) {
+  if (f32)
+    absmax_kernel<float><<<296, 256, 0, s>>>(static_cast<const float *>(x), n, slot);
+  else
+    absmax_kernel<__nv_bfloat16><<<296, 256, 0, s>>>(static_cast<const __nv_bfloat16 *>(x), n, slot);
+}
+
+// scales[i] = max(absmax[i], tiny) / 448 (e4m3's largest finite value)
+__global__ void absmax_to_scale_kernel(const float *absmax, int n, float *scales) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) scales[i] = fmaxf(absmax[i], 1e-6f) / 448.0f;
+}
+
+void launch_absmax_to_scale(const float *absmax, int n, float *scales, cudaStream_t s) {
+  absmax_to_scale_kernel<<<(n + 127) / 128, 128, 0, s>>>(absmax, n, scales);
 }
 
 // ------------------------------------------------------------------ policy

@@ -40,11 +40,25 @@ bool launch_splitk_act_ln(const float *part, int splits, long long stride, int r
                           const float *bias, int act, const float *gamma, const float *beta,
                           float eps, __nv_bfloat16 *out, cudaStream_t s);
 
+// Same, with an optional e4m3 copy out8 = value / *scale8 (FP8 GEMM input);
+// `out` may be null when only the fp32 / e4m3 copies are needed.
+void launch_layernorm_q(const void *in, bool in_f32, int rows, int width, const float *gamma,
+                        const float *beta, float eps, const float *multT, const float *addT,
+                        __nv_bfloat16 *out, float *out_f32, uint8_t *out8, const float *scale8,
+                        cudaStream_t s);
+
 // 64-token attention per (position, head) with the smolgen bias added before
 // the softmax: ctx[b*64+q, h*dh:..] = softmax(Q K^T / sqrt(dh) + bias) V.
 // qkv: [B*64, ldq] with Q at column 0, K at d, V at 2d. bias: [B*H, 4096].
+// With ctx8 set, the context is written as e4m3 (value / *scale8) instead.
 void launch_attention(const __nv_bfloat16 *qkv, long long ldq, const __nv_bfloat16 *bias,
-                      int batch, int heads, int d, __nv_bfloat16 *ctx, cudaStream_t s);
+                      int batch, int heads, int d, __nv_bfloat16 *ctx, cudaStream_t s,
+                      uint8_t *ctx8 = nullptr, const float *scale8 = nullptr);
+
+// FP8 calibration: *slot = max(*slot, max|x|) over n bf16 or fp32 values; and
+// scales[i] = absmax[i] / 448.
+void launch_absmax(const void *x, bool f32, long long n, float *slot, cudaStream_t s);
+void launch_absmax_to_scale(const float *absmax, int n, float *scales, cudaStream_t s);
 
 // Attention-policy logits: raw = q k^T / sqrt(dp) (64x64), the 8x24 promotion
 // logits, gathered onto the 1858 moves. qk: [B*64, 2*dp] (q | k);

@@ -23,6 +23,7 @@
 #include <chrono>
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <functional>
 #include <map>
@@ -192,12 +193,14 @@ struct Mat {  // a weight matrix [rows, ld] on the device (bf16 or e4m3)
 
 struct LayerW {
   Mat qkvc, o, f1, f2, sg1, sg2;
+  Mat qkvc8, o8, f1_8, f2_8;  // e4m3 copies (FP8 handles only)
   float *b_qkvc, *b_o, *ln1_g, *ln1_b, *b_f1, *b_f2, *ln2_g, *ln2_b;
   float *b_sg1, *sg_ln1_g, *sg_ln1_b, *b_sg2, *sg_ln2_g, *sg_ln2_b;
 };
 
 struct Weights {
   Mat pe, emb, effn1, effn2, sg_global, pol, qk, vm, vm1;
+  Mat effn1_8, effn2_8;  // e4m3 copies (FP8 handles only)
   float *b_pe, *b_emb, *ln_emb_g, *ln_emb_b, *multT, *addT, *b_effn1, *b_effn2, *ln_effn_g,
       *ln_effn_b, *b_pol, *b_qk, *ppo3, *b_vm, *b_vm1, *w2v, *b2v, *w2m, *b2m;
   int16_t *gather;
@@ -229,6 +232,8 @@ struct Shard {  // one GPU
   __nv_bfloat16 *x0, *p, *peo, *X, *X1, *QKV, *C, *S1, *S2pre, *S2, *BIAS, *CTX, *H, *E, *QK,
       *VM, *VH;
   float *Xf, *X1f, *T, *SK;  // fp32 residual stream (LN outputs) and pre-LN sums
+  uint8_t *X8, *X1_8, *CTX8, *H8;  // e4m3 GEMM inputs (FP8 handles)
+  float *scales, *absmax;    // per-tensor activation scales / calibration maxima
   float *policy, *wdl, *mlh;
   unsigned *status;
   cudaEvent_t ev[4];
@@ -256,6 +261,7 @@ struct mfb200_handle {
   std::string last_error;
   size_t weight_bytes = 0, ws_bytes = 0;
   std::string device_name;
+  bool calibrated = false;  // FP8 activation scales set
 };
 
 namespace {
@@ -312,8 +318,55 @@ void put_mat(ArenaBuilder &ab, Layout &lay, Mat &m, int rows, int cols, int ld, 
   lay.fix.push_back({&m.w, off});
 }
 
+// Host float -> e4m3 (round to nearest, ties to even; saturating at +-448).
+// e4m3: 1 sign, 4 exponent bits (bias 7), 3 mantissa bits, no infinities.
+uint8_t f2e4m3(float x) {
+  static float table[127];
+  static bool init = false;
+  if (!init) {
+    for (int b = 0; b < 127; ++b) {
+      const int e = b >> 3, m = b & 7;
+      table[b] = e == 0 ? std::ldexp(m / 8.0f, -6) : std::ldexp(1.0f + m / 8.0f, e - 7);
+    }
+    init = true;
+  }
+  const uint8_t sign = std::signbit(x) ? 0x80 : 0;
+  float a = std::fabs(x);
+  if (!(a == a)) return 0x7F;
+  if (a >= table[126]) return sign | 126;
+  int lo = 0, hi = 126;  // table[lo] <= a < table[hi]
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) / 2;
+    (table[mid] <= a ? lo : hi) = mid;
+  }
+  const float dlo = a - table[lo], dhi = table[hi] - a;
+  const int idx = (dhi < dlo || (dhi == dlo && (hi % 2 == 0))) ? hi : lo;
+  return sign | static_cast<uint8_t>(idx);
+}
+
+// e4m3 matrix with a per-row (output channel) scale: row r is stored as
+// round(W[r]/scale[r]) where scale[r] = max|W[r]| / 448.
+template <class F>
+void put_mat_fp8(ArenaBuilder &ab, Layout &lay, Mat &m, int rows, int cols, int ld, F at) {
+  const size_t off = ab.add(size_t(rows) * ld);
+  std::vector<float> sc(rows);
+  for (int r = 0; r < rows; ++r) {
+    float mx = 0.0f;
+    for (int c = 0; c < cols; ++c) mx = std::max(mx, std::fabs(at(r, c)));
+    sc[r] = mx > 0.0f ? mx / 448.0f : 1.0f;
+  }
+  uint8_t *dst = ab.host.data() + off;
+  for (int r = 0; r < rows; ++r)
+    for (int c = 0; c < ld; ++c) dst[size_t(r) * ld + c] = c < cols ? f2e4m3(at(r, c) / sc[r]) : 0;
+  m.rows = rows;
+  m.ld = ld;
+  m.fp8 = true;
+  lay.fix.push_back({&m.w, off});
+  put_f32(ab, lay, const_cast<float **>(&m.scale), sc.data(), sc.size());
+}
+
 void pack_weights(const mfb200_net_desc &n, const float *blob, ArenaBuilder &ab, Layout &lay,
-                  Weights &W) {
+                  Weights &W, bool fp8) {
   Packer P(n, blob);
   const int d = n.embedding, T = 64, dp = n.policy_d, pe = n.pe;
   const auto &g = P.gp;
@@ -339,7 +392,14 @@ void pack_weights(const mfb200_net_desc &n, const float *blob, ArenaBuilder &ab,
     put_f32(ab, lay, &W.multT, mt.data(), mt.size());
     put_f32(ab, lay, &W.addT, at.data(), at.size());
   }
+  auto dense8 = [&](Mat &m, const float *src, int rows, int cols) {
+    put_mat_fp8(ab, lay, m, rows, cols, cols, [&](int r, int c) { return src[size_t(r) * cols + c]; });
+  };
   dense(W.effn1, g[G_EFFN_W1], n.emb_dff, d);
+  if (fp8) {
+    dense8(W.effn1_8, g[G_EFFN_W1], n.emb_dff, d);
+    dense8(W.effn2_8, g[G_EFFN_W2], d, n.emb_dff);
+  }
   put_f32(ab, lay, &W.b_effn1, g[G_EFFN_B1], n.emb_dff);
   dense(W.effn2, g[G_EFFN_W2], d, n.emb_dff);
   put_f32(ab, lay, &W.b_effn2, g[G_EFFN_B2], d);
@@ -405,12 +465,19 @@ void pack_weights(const mfb200_net_desc &n, const float *blob, ArenaBuilder &ab,
     const auto &l = P.lp[k];
     LayerW &Lw = W.layers[k];
     // Q | K | V | smolgen compress as one [3d + c, d] matrix
-    put_mat(ab, lay, Lw.qkvc, 3 * d + c, d, d, [&](int r, int col) {
+    auto qkvc_at = [&](int r, int col) {
       if (r < d) return l[L_Q_W][size_t(r) * d + col];
       if (r < 2 * d) return l[L_K_W][size_t(r - d) * d + col];
       if (r < 3 * d) return l[L_V_W][size_t(r - 2 * d) * d + col];
       return l[L_SG_COMPRESS][size_t(r - 3 * d) * d + col];
-    });
+    };
+    put_mat(ab, lay, Lw.qkvc, 3 * d + c, d, d, qkvc_at);
+    if (fp8) {
+      put_mat_fp8(ab, lay, Lw.qkvc8, 3 * d + c, d, d, qkvc_at);
+      dense8(Lw.o8, l[L_O_W], d, d);
+      dense8(Lw.f1_8, l[L_FFN_W1], n.dff, d);
+      dense8(Lw.f2_8, l[L_FFN_W2], d, n.dff);
+    }
     {
       std::vector<float> b(3 * size_t(d) + c, 0.0f);
       std::memcpy(b.data(), l[L_Q_B], d * 4);
@@ -440,7 +507,7 @@ void pack_weights(const mfb200_net_desc &n, const float *blob, ArenaBuilder &ab,
 }
 
 // ------------------------------------------------------------ workspace
-void alloc_workspace(Shard &S, const mfb200_net_desc &n, int max_batch) {
+void alloc_workspace(Shard &S, const mfb200_net_desc &n, int max_batch, bool fp8) {
   const size_t B = max_batch, M = B * 64, d = n.embedding;
   const size_t hg = size_t(n.heads) * n.smolgen_gen;
   const size_t hid = std::max<size_t>(n.dff, n.emb_dff);
@@ -472,6 +539,12 @@ void alloc_workspace(Shard &S, const mfb200_net_desc &n, int max_batch) {
       {reinterpret_cast<void **>(&S.wdl), B * 3 * 4},
       {reinterpret_cast<void **>(&S.mlh), B * 4},
       {reinterpret_cast<void **>(&S.status), 256},
+      {reinterpret_cast<void **>(&S.scales), size_t(2 + 4 * n.layers) * 4},
+      {reinterpret_cast<void **>(&S.absmax), size_t(2 + 4 * n.layers) * 4},
+      {reinterpret_cast<void **>(&S.X8), fp8 ? M * d : 16},
+      {reinterpret_cast<void **>(&S.X1_8), fp8 ? M * d : 16},
+      {reinterpret_cast<void **>(&S.CTX8), fp8 ? M * d : 16},
+      {reinterpret_cast<void **>(&S.H8), fp8 ? M * hid : 16},
   };
   size_t total = 0;
   std::vector<size_t> offs;
@@ -528,8 +601,35 @@ void add_fn(Shard::Plan &P, const char *name, double flops, std::function<void(c
   P.steps.push_back(std::move(st));
 }
 
-std::unique_ptr<Shard::Plan> build_plan(Shard &S, const mfb200_net_desc &n, int B) {
+// Plan modes: bf16 forward, FP8 forward (e4m3 encoder/embedding-FFN GEMMs
+// with per-tensor activation scales read from S.scales), and the bf16 forward
+// with absmax probes that calibrates those scales.
+enum PlanMode { kPlanBF16 = 0, kPlanFP8 = 1, kPlanCalibrate = 2 };
+
+// activation-scale slots: embedding LN output, embedding FFN hidden, then per
+// layer l: layer input, attention context, ln1 output, FFN hidden
+inline int slot_x(int l) { return 2 + 4 * l; }
+inline int slot_ctx(int l) { return 3 + 4 * l; }
+inline int slot_x1(int l) { return 4 + 4 * l; }
+inline int slot_h(int l) { return 5 + 4 * l; }
+
+std::unique_ptr<Shard::Plan> build_plan(Shard &S, const mfb200_net_desc &n, int B, int mode,
+                                        int fp8_gemms) {
   auto P = std::make_unique<Shard::Plan>();
+  const bool fp8_plan = mode == kPlanFP8, cal = mode == kPlanCalibrate;
+  // Which GEMM groups run in e4m3 under FP8 (mfb200_config.fp8_gemms bit
+  // mask: 1 embedding FFN, 2 QKV, 4 output projection, 8 FFN1, 16 FFN2).
+  const int fp8_mask = fp8_gemms ? fp8_gemms : 31;
+  const bool f8e = fp8_plan && (fp8_mask & 1), f8q = fp8_plan && (fp8_mask & 2),
+             f8o = fp8_plan && (fp8_mask & 4), f8f1 = fp8_plan && (fp8_mask & 8),
+             f8f2 = fp8_plan && (fp8_mask & 16);
+  const long long Md = static_cast<long long>(B) * 64 * n.embedding;
+  auto probe = [&](const char *name, const void *x, bool f32, long long cnt, int slot) {
+    if (cal)
+      add_fn(*P, name, 0, [&S, x, f32, cnt, slot](cudaStream_t s) {
+        launch_absmax(x, f32, cnt, S.absmax + slot, s);
+      });
+  };
   const int M = B * 64, d = n.embedding, dp = n.policy_d, H = n.heads;
   const int hg = n.heads * n.smolgen_gen, vh = n.value_hidden, mh = n.mlh_hidden;
   const float alpha = std::pow(2.0f * static_cast<float>(n.layers), -0.25f);  // plan :1152-1162
@@ -554,16 +654,28 @@ std::unique_ptr<Shard::Plan> build_plan(Shard &S, const mfb200_net_desc &n, int 
     a.ldo = d;
     add_gemm(*P, S, "emb_dense", S.x0, kEmbIn, W.emb, a);
   }
-  add_fn(*P, "emb_ln_gates", 0, [&S, &W, M, d, eps](cudaStream_t s) {
-    launch_layernorm(S.T, true, M, d, W.ln_emb_g, W.ln_emb_b, eps, W.multT, W.addT, S.X, S.Xf, s);
+  add_fn(*P, "emb_ln_gates", 0, [&S, &W, M, d, eps, f8e](cudaStream_t s) {
+    launch_layernorm_q(S.T, true, M, d, W.ln_emb_g, W.ln_emb_b, eps, W.multT, W.addT,
+                       f8e ? nullptr : S.X, S.Xf, f8e ? S.X8 : nullptr, S.scales + 0, s);
   });
+  probe("absmax_emb_x", S.Xf, true, Md, 0);
   {
     GemmArgs a = base_args(S, M, n.emb_dff, d);
     a.bias = W.b_effn1;
     a.act = n.act_ffn;
     a.out = S.H;
     a.ldo = n.emb_dff;
-    add_gemm(*P, S, "emb_ffn1", S.X, d, W.effn1, a);
+    if (f8e) {
+      a.a_scale_ptr = S.scales + 0;
+      a.col_scale = W.effn1_8.scale;
+      a.out = S.H8;
+      a.out_fp8 = 1;
+      a.out_scale_ptr = S.scales + 1;
+      add_gemm(*P, S, "emb_ffn1", S.X8, d, W.effn1_8, a);
+    } else {
+      add_gemm(*P, S, "emb_ffn1", S.X, d, W.effn1, a);
+    }
+    probe("absmax_emb_h", S.H, false, static_cast<long long>(M) * n.emb_dff, 1);
     GemmArgs b = base_args(S, M, d, n.emb_dff);
     b.mode = kEpiResid;
     b.bias = W.b_effn2;
@@ -573,11 +685,19 @@ std::unique_ptr<Shard::Plan> build_plan(Shard &S, const mfb200_net_desc &n, int 
     b.out = S.T;
     b.out_f32 = 1;
     b.ldo = d;
-    add_gemm(*P, S, "emb_ffn2", S.H, n.emb_dff, W.effn2, b);
+    if (f8e) {
+      b.a_scale_ptr = S.scales + 1;
+      b.col_scale = W.effn2_8.scale;
+      add_gemm(*P, S, "emb_ffn2", S.H8, n.emb_dff, W.effn2_8, b);
+    } else {
+      add_gemm(*P, S, "emb_ffn2", S.H, n.emb_dff, W.effn2, b);
+    }
   }
-  add_fn(*P, "emb_ffn_ln", 0, [&S, &W, M, d, eps](cudaStream_t s) {
-    launch_layernorm(S.T, true, M, d, W.ln_effn_g, W.ln_effn_b, eps, nullptr, nullptr, S.X, S.Xf, s);
+  add_fn(*P, "emb_ffn_ln", 0, [&S, &W, M, d, eps, f8q](cudaStream_t s) {
+    launch_layernorm_q(S.T, true, M, d, W.ln_effn_g, W.ln_effn_b, eps, nullptr, nullptr,
+                       f8q ? nullptr : S.X, S.Xf, f8q ? S.X8 : nullptr, S.scales + slot_x(0), s);
   });
+  probe("absmax_x", S.Xf, true, Md, slot_x(0));
   for (int k = 0; k < n.layers; ++k) {
     LayerW &Lw = W.layers[k];
     {
@@ -588,7 +708,13 @@ std::unique_ptr<Shard::Plan> build_plan(Shard &S, const mfb200_net_desc &n, int 
       a.out2 = S.C;
       a.ldo2 = n.smolgen_compress;
       a.split = 3 * d;
-      add_gemm(*P, S, "qkv", S.X, d, Lw.qkvc, a);
+      if (f8q) {
+        a.a_scale_ptr = S.scales + slot_x(k);
+        a.col_scale = Lw.qkvc8.scale;
+        add_gemm(*P, S, "qkv", S.X8, d, Lw.qkvc8, a);
+      } else {
+        add_gemm(*P, S, "qkv", S.X, d, Lw.qkvc, a);
+      }
     }
     {
       // smolgen dense1 over the flattened [B, 64*c] compress output: M = B is
@@ -626,9 +752,11 @@ std::unique_ptr<Shard::Plan> build_plan(Shard &S, const mfb200_net_desc &n, int 
       a.ldo = 4096;
       add_gemm(*P, S, "smolgen_global", S.S2, n.smolgen_gen, W.sg_global, a);
     }
-    add_fn(*P, "attention", 4.0 * B * H * 64.0 * 64.0 * 32.0, [&S, B, H, d](cudaStream_t s) {
-      launch_attention(S.QKV, 3LL * d, S.BIAS, B, H, d, S.CTX, s);
+    add_fn(*P, "attention", 4.0 * B * H * 64.0 * 64.0 * 32.0, [&S, B, H, d, f8o, k](cudaStream_t s) {
+      launch_attention(S.QKV, 3LL * d, S.BIAS, B, H, d, S.CTX, s, f8o ? S.CTX8 : nullptr,
+                       S.scales + slot_ctx(k));
     });
+    probe("absmax_ctx", S.CTX, false, Md, slot_ctx(k));
     {
       GemmArgs a = base_args(S, M, d, d);
       a.mode = kEpiResid;
@@ -639,18 +767,38 @@ std::unique_ptr<Shard::Plan> build_plan(Shard &S, const mfb200_net_desc &n, int 
       a.out = S.T;
       a.out_f32 = 1;
       a.ldo = d;
-      add_gemm(*P, S, "out_proj", S.CTX, d, Lw.o, a);
+      if (f8o) {
+        a.a_scale_ptr = S.scales + slot_ctx(k);
+        a.col_scale = Lw.o8.scale;
+        add_gemm(*P, S, "out_proj", S.CTX8, d, Lw.o8, a);
+      } else {
+        add_gemm(*P, S, "out_proj", S.CTX, d, Lw.o, a);
+      }
     }
-    add_fn(*P, "ln1", 0, [&S, &Lw, M, d, eps](cudaStream_t s) {
-      launch_layernorm(S.T, true, M, d, Lw.ln1_g, Lw.ln1_b, eps, nullptr, nullptr, S.X1, S.X1f, s);
+    add_fn(*P, "ln1", 0, [&S, &Lw, M, d, eps, f8f1, k](cudaStream_t s) {
+      launch_layernorm_q(S.T, true, M, d, Lw.ln1_g, Lw.ln1_b, eps, nullptr, nullptr,
+                         f8f1 ? nullptr : S.X1, S.X1f, f8f1 ? S.X1_8 : nullptr, S.scales + slot_x1(k), s);
     });
+    probe("absmax_x1", S.X1f, true, Md, slot_x1(k));
     {
       GemmArgs a = base_args(S, M, n.dff, d);
       a.bias = Lw.b_f1;
       a.act = n.act_ffn;
       a.out = S.H;
       a.ldo = n.dff;
-      add_gemm(*P, S, "ffn1", S.X1, d, Lw.f1, a);
+      if (f8f2) {  // e4m3 hidden for an FP8 FFN2
+        a.out = S.H8;
+        a.out_fp8 = 1;
+        a.out_scale_ptr = S.scales + slot_h(k);
+      }
+      if (f8f1) {
+        a.a_scale_ptr = S.scales + slot_x1(k);
+        a.col_scale = Lw.f1_8.scale;
+        add_gemm(*P, S, "ffn1", S.X1_8, d, Lw.f1_8, a);
+      } else {
+        add_gemm(*P, S, "ffn1", S.X1, d, Lw.f1, a);
+      }
+      probe("absmax_h", S.H, false, static_cast<long long>(M) * n.dff, slot_h(k));
       GemmArgs b = base_args(S, M, d, n.dff);
       b.mode = kEpiResid;
       b.bias = Lw.b_f2;
@@ -660,11 +808,25 @@ std::unique_ptr<Shard::Plan> build_plan(Shard &S, const mfb200_net_desc &n, int 
       b.out = S.T;
       b.out_f32 = 1;
       b.ldo = d;
-      add_gemm(*P, S, "ffn2", S.H, n.dff, Lw.f2, b);
+      if (f8f2) {
+        b.a_scale_ptr = S.scales + slot_h(k);
+        b.col_scale = Lw.f2_8.scale;
+        add_gemm(*P, S, "ffn2", S.H8, n.dff, Lw.f2_8, b);
+      } else {
+        add_gemm(*P, S, "ffn2", S.H, n.dff, Lw.f2, b);
+      }
     }
-    add_fn(*P, "ln2", 0, [&S, &Lw, M, d, eps](cudaStream_t s) {
-      launch_layernorm(S.T, true, M, d, Lw.ln2_g, Lw.ln2_b, eps, nullptr, nullptr, S.X, S.Xf, s);
-    });
+    {
+      // the last layer's output feeds the bf16 heads; earlier ones feed the
+      // next layer's (e4m3, under FP8) QKV projection
+      const bool last = k + 1 == n.layers;
+      const bool q8 = f8q && !last;
+      add_fn(*P, "ln2", 0, [&S, &Lw, M, d, eps, q8, k](cudaStream_t s) {
+        launch_layernorm_q(S.T, true, M, d, Lw.ln2_g, Lw.ln2_b, eps, nullptr, nullptr,
+                           q8 ? nullptr : S.X, S.Xf, q8 ? S.X8 : nullptr, S.scales + slot_x(k + 1), s);
+      });
+      if (!last) probe("absmax_x", S.Xf, true, Md, slot_x(k + 1));
+    }
   }
   {
     GemmArgs a = base_args(S, M, dp, d);
@@ -712,10 +874,19 @@ void run_steps(Shard::Plan &P, cudaStream_t s) {
   check(cudaGetLastError(), "kernel launch");
 }
 
-Shard::Plan &get_plan(mfb200_handle *h, Shard &S, int B) {
-  auto it = S.plans.find(B);
+Shard::Plan &get_plan(mfb200_handle *h, Shard &S, int B, int mode = -1) {
+  if (mode < 0) mode = h->cfg.precision == MFB200_PRECISION_FP8 ? kPlanFP8 : kPlanBF16;
+  if (mode == kPlanFP8 && !h->calibrated)
+    throw Fail("FP8 handle used before mfb200_calibrate set its activation scales");
+  const int key = B * 4 + mode;
+  auto it = S.plans.find(key);
   if (it != S.plans.end()) return *it->second;
-  auto P = build_plan(S, h->desc, B);
+  auto P = build_plan(S, h->desc, B, mode, h->cfg.fp8_gemms);
+  if (mode == kPlanCalibrate) {  // run eagerly, never captured
+    Shard::Plan &ref = *P;
+    S.plans[key] = std::move(P);
+    return ref;
+  }
   // First run eagerly (also sets kernel attributes), then capture a graph.
   run_steps(*P, S.stream);
   check(cudaStreamSynchronize(S.stream), "first forward");
@@ -728,7 +899,7 @@ Shard::Plan &get_plan(mfb200_handle *h, Shard &S, int B) {
     cudaGraphDestroy(graph);
   }
   Shard::Plan &ref = *P;
-  S.plans[B] = std::move(P);
+  S.plans[key] = std::move(P);
   return ref;
 }
 
@@ -770,8 +941,8 @@ extern "C" int mfb200_create(const mfb200_net_desc *desc, const void *weights, s
   if (bytes != blob_floats(*desc) * sizeof(float))
     return fail(nullptr, "mfb200_create: weight blob has " + std::to_string(bytes) +
                              " bytes, expected " + std::to_string(blob_floats(*desc) * 4));
-  if (cfg->precision != MFB200_PRECISION_BF16)
-    return fail(nullptr, "mfb200_create: only bf16 precision is implemented in this build");
+  if (cfg->precision != MFB200_PRECISION_BF16 && cfg->precision != MFB200_PRECISION_FP8)
+    return fail(nullptr, "mfb200_create: unknown precision");
   if (cfg->max_batch <= 0) return fail(nullptr, "mfb200_create: max_batch must be positive");
   auto h = std::make_unique<mfb200_handle>();
   h->desc = *desc;
@@ -787,7 +958,8 @@ extern "C" int mfb200_create(const mfb200_net_desc *desc, const void *weights, s
     ArenaBuilder ab;
     Layout lay;
     Weights proto;
-    pack_weights(*desc, static_cast<const float *>(weights), ab, lay, proto);
+    pack_weights(*desc, static_cast<const float *>(weights), ab, lay, proto,
+                 cfg->precision == MFB200_PRECISION_FP8);
     const int per = (cfg->max_batch + h->cfg.num_devices - 1) / h->cfg.num_devices;
     for (int i = 0; i < h->cfg.num_devices; ++i) {
       auto S = std::make_unique<Shard>();
@@ -806,7 +978,7 @@ extern "C" int mfb200_create(const mfb200_net_desc *desc, const void *weights, s
       // point the weight directory at this device's arena, then copy it
       for (auto &f : lay.fix) *f.first = static_cast<uint8_t *>(S->arena) + f.second;
       S->w = proto;
-      alloc_workspace(*S, *desc, per);
+      alloc_workspace(*S, *desc, per, cfg->precision == MFB200_PRECISION_FP8);
       h->weight_bytes = S->arena_bytes;
       h->ws_bytes = S->ws_bytes;
       h->shards.push_back(std::move(S));
@@ -913,7 +1085,7 @@ extern "C" int mfb200_evaluate_device(mfb200_handle *h, const uint64_t *d_masks,
       check(cudaMemcpyAsync(S.masks, d_masks, size_t(batch) * kPlanes * 8, cudaMemcpyDeviceToDevice, s), "masks");
     if (d_values != S.values)
       check(cudaMemcpyAsync(S.values, d_values, size_t(batch) * kPlanes * 4, cudaMemcpyDeviceToDevice, s), "values");
-    if (stream && !S.plans.count(batch)) {
+    if (stream && !S.plans.count(batch * 4 + (h->cfg.precision == MFB200_PRECISION_FP8 ? 1 : 0))) {
       // build (and capture) on the handle's own stream first
       check(cudaStreamSynchronize(s), "sync");
       get_plan(h, S, batch);
@@ -929,8 +1101,41 @@ extern "C" int mfb200_evaluate_device(mfb200_handle *h, const uint64_t *d_masks,
   return 0;
 }
 
-extern "C" int mfb200_calibrate(mfb200_handle *h, const uint64_t *, const float *, int) {
-  return fail(h, "mfb200_calibrate: FP8 is not implemented in this build");
+extern "C" int mfb200_calibrate(mfb200_handle *h, const uint64_t *masks, const float *values,
+                                int count) {
+  if (!h) return fail(nullptr, "mfb200_calibrate: null handle");
+  std::lock_guard<std::mutex> lock(h->mu);
+  if (h->cfg.precision != MFB200_PRECISION_FP8)
+    return fail(h, "mfb200_calibrate: only FP8 handles have activation scales");
+  if (!masks || !values || count <= 0) return fail(h, "mfb200_calibrate: no calibration positions");
+  try {
+    Shard &S0 = *h->shards[0];
+    check(cudaSetDevice(S0.device), "cudaSetDevice");
+    const int nscale = 2 + 4 * h->desc.layers;
+    check(cudaMemsetAsync(S0.absmax, 0, nscale * 4, S0.stream), "absmax clear");
+    const int chunk = h->cfg.max_batch / static_cast<int>(h->shards.size());
+    for (int lo = 0; lo < count; lo += chunk) {
+      const int b = std::min(chunk, count - lo);
+      check(cudaMemcpyAsync(S0.masks, masks + size_t(lo) * kPlanes, size_t(b) * kPlanes * 8,
+                            cudaMemcpyHostToDevice, S0.stream), "H2D masks");
+      check(cudaMemcpyAsync(S0.values, values + size_t(lo) * kPlanes, size_t(b) * kPlanes * 4,
+                            cudaMemcpyHostToDevice, S0.stream), "H2D values");
+      run_steps(get_plan(h, S0, b, kPlanCalibrate), S0.stream);
+    }
+    launch_absmax_to_scale(S0.absmax, nscale, S0.scales, S0.stream);
+    check(cudaStreamSynchronize(S0.stream), "calibration");
+    check_status(S0);
+    std::vector<float> sc(nscale);
+    check(cudaMemcpy(sc.data(), S0.scales, nscale * 4, cudaMemcpyDeviceToHost), "scales");
+    for (size_t i = 1; i < h->shards.size(); ++i) {
+      check(cudaSetDevice(h->shards[i]->device), "cudaSetDevice");
+      check(cudaMemcpy(h->shards[i]->scales, sc.data(), nscale * 4, cudaMemcpyHostToDevice), "scales");
+    }
+    h->calibrated = true;
+  } catch (const std::exception &e) {
+    return fail(h, std::string("mfb200_calibrate: ") + e.what());
+  }
+  return 0;
 }
 
 extern "C" int mfb200_capabilities(mfb200_handle *h, mfb200_caps *caps) {

@@ -32,7 +32,7 @@ class NetDesc(ctypes.Structure):
 class Config(ctypes.Structure):
     _fields_ = [("device", ctypes.c_int32), ("num_devices", ctypes.c_int32),
                 ("precision", ctypes.c_int32), ("max_batch", ctypes.c_int32),
-                ("use_graphs", ctypes.c_int32)]
+                ("use_graphs", ctypes.c_int32), ("fp8_gemms", ctypes.c_int32)]
 
 
 class Timing(ctypes.Structure):
@@ -132,7 +132,7 @@ class BackendCapabilities:
 class B200Network:
     def __init__(self, cfg: NetConfig, tensors: Dict[str, np.ndarray], *, device: int = 0,
                  num_devices: int = 1, precision: str = "bf16", max_batch: int = 1024,
-                 use_graphs: bool = True):
+                 use_graphs: bool = True, fp8_gemms: int = 0):
         L = _lib()
         self.cfg = cfg
         self.precision = precision
@@ -141,7 +141,8 @@ class B200Network:
         expected = L.mfb200_weight_bytes(ctypes.byref(self._desc))
         if blob.nbytes != expected:
             raise RuntimeError(f"weight blob is {blob.nbytes} bytes, library expects {expected}")
-        conf = Config(device, num_devices, PRECISIONS[precision], max_batch, int(use_graphs))
+        conf = Config(device, num_devices, PRECISIONS[precision], max_batch, int(use_graphs),
+                      fp8_gemms)
         h = ctypes.c_void_p()
         rc = L.mfb200_create(ctypes.byref(self._desc), blob.ctypes.data, blob.nbytes,
                              ctypes.byref(conf), ctypes.byref(h))
@@ -179,6 +180,14 @@ class B200Network:
         if rc != 0:
             raise self._err()
         return Outputs(pol, wdl, wdl[:, 0] - wdl[:, 2], mlh)
+
+    def calibrate(self, inp: PackedInputs) -> None:
+        """FP8 only: absmax calibration of the per-tensor activation scales
+        over the given positions (a bf16 forward with probes)."""
+        masks = np.ascontiguousarray(inp.masks, np.uint64)
+        values = np.ascontiguousarray(inp.values, np.float32)
+        if _lib().mfb200_calibrate(self._h, masks.ctypes.data, values.ctypes.data, inp.count) != 0:
+            raise self._err()
 
     def evaluate_device(self, d_masks: int, d_values: int, batch: int, d_policy: int, d_wdl: int,
                         d_mlh: int, stream: int = 0) -> None:
@@ -232,8 +241,14 @@ class B200Network:
 
 
 def create_network(cfg: NetConfig, tensors: Dict[str, np.ndarray], backend: str = "b200",
-                   **kwargs) -> B200Network:
-    """``CreateNetwork(weights, BackendConfig)`` for the B200 backend."""
+                   calibration: Optional[PackedInputs] = None, **kwargs) -> B200Network:
+    """``CreateNetwork(weights, BackendConfig)`` for the B200 backend. FP8
+    networks (precision="fp8") are calibrated on `calibration` positions."""
     if backend not in ("b200", "auto"):
         raise RuntimeError(f"Unknown NN backend: {backend}")
-    return B200Network(cfg, tensors, **kwargs)
+    net = B200Network(cfg, tensors, **kwargs)
+    if net.precision == "fp8":
+        if calibration is None:
+            raise RuntimeError("an FP8 network needs calibration positions")
+        net.calibrate(calibration)
+    return net

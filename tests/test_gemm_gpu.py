@@ -87,3 +87,26 @@ def test_gemm_split_k(M, K, splits):
     """Split-K partial products sum to the full product (smolgen dense1 path)."""
     got, ref = run_gemm(M, 256, K, 256, k_splits=splits)
     np.testing.assert_allclose(got, ref, rtol=1e-4, atol=1e-3)
+
+
+@pytest.mark.parametrize("M,N,K,bn", [(128, 256, 128, 256), (300, 1024, 1024, 256), (1000, 3104, 1024, 256),
+                                      (200, 64, 512, 64)])
+def test_gemm_fp8(M, N, K, bn):
+    """kind::f8f6f4 e4m3 operands with per-column weight scales and an
+    activation scale, vs float64 on the decoded operands."""
+    from metalfish_b200.bf16 import from_e4m3_bits, to_e4m3_bits
+    rng = np.random.default_rng(1)
+    A = rng.standard_normal((M, K)).astype(np.float32) * 3
+    W = rng.standard_normal((N, K)).astype(np.float32)
+    a8, w8 = to_e4m3_bits(A), to_e4m3_bits(W)
+    cs = (0.01 + 0.02 * rng.random(N)).astype(np.float32)
+    b = (0.1 * rng.standard_normal(N)).astype(np.float32)
+    a_scale = 0.5
+    out = np.zeros((1, M, N), np.float32)
+    st = ctypes.c_uint(0)
+    rc = lib().mfb200_debug_gemm(M, N, K, bn, 1, _p(a8), _p(w8), _p(b), 0, 0, None, ctypes.c_float(1.0),
+                                 None, None, ctypes.c_float(0.0), _p(cs), ctypes.c_float(a_scale), 1, 1,
+                                 _p(out), ctypes.byref(st))
+    assert rc == 0, f"rc={rc} status={st.value}"
+    ref = (from_e4m3_bits(a8).astype(np.float64) @ from_e4m3_bits(w8).astype(np.float64).T) * a_scale * cs + b
+    np.testing.assert_allclose(out[0], ref, rtol=1e-4, atol=1e-3)

@@ -53,7 +53,7 @@ def test_create_rejects_bad_desc_and_blob():
     d = net_desc(synthetic.TINY)
     d.heads = 3  # head depth must be 32
     h = ctypes.c_void_p()
-    conf = Config(0, 1, 0, 4, 1)
+    conf = Config(0, 1, 0, 4, 1, 0)
     blob = np.zeros(16, np.float32)
     assert L.mfb200_create(ctypes.byref(d), blob.ctypes.data, blob.nbytes, ctypes.byref(conf), ctypes.byref(h)) != 0
     assert b"head depth" in L.mfb200_last_error(None)
