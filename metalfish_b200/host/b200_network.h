@@ -1,0 +1,58 @@
+// b200_network.h -- MetalFish NN backend over libmfb200 (the B200 BT4 forward).
+//
+// Drop-in for the engine's backend factory: a Network subclass
+// (src/nn/network.h:38-51) that CreateNetwork (src/nn/network.cpp:137-208)
+// can return for backend "b200". It takes the same WeightsFile the CPU and
+// CUDA backends take, decodes it with the engine's own MultiHeadWeights
+// (src/nn/weights.h), and evaluates through the C ABI of include/mfb200.h.
+// Errors throw std::runtime_error, as the reference backends do.
+#pragma once
+
+#include <memory>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "nn/network.h"
+
+struct mfb200_handle;
+
+namespace MetalFish {
+namespace NN {
+namespace B200 {
+
+struct B200Options {
+  int device = 0;         // first CUDA device
+  int num_devices = 1;    // batch sharded over [device, device + num_devices)
+  int max_batch = 1024;   // largest EvaluateBatch size
+  bool use_graphs = true; // one CUDA graph per batch size
+};
+
+class B200Network : public Network {
+public:
+  B200Network(const WeightsFile &weights, const B200Options &options);
+  // BackendConfig mapping: cuda_device -> device, cuda_graph_execution ->
+  // use_graphs, cuda_stable_execution_batch_size (if > 0) -> max_batch.
+  B200Network(const WeightsFile &weights, const BackendConfig &config);
+  ~B200Network() override;
+
+  NetworkOutput Evaluate(const InputPlanes &input) override;
+  std::vector<NetworkOutput> EvaluateBatch(const std::vector<InputPlanes> &inputs) override;
+  std::string GetNetworkInfo() const override;
+  bool HasWDL() const override { return true; }
+  bool HasMovesLeft() const override { return true; }
+  BackendCapabilities GetBackendCapabilities() const override;
+
+private:
+  mfb200_handle *handle_ = nullptr;
+  B200Options options_;
+  std::string info_;
+  std::vector<std::uint64_t> masks_;  // packing scratch, reused across calls
+  std::vector<float> values_;
+  std::vector<float> policy_, wdl_, mlh_;
+  std::mutex mutex_;
+};
+
+}  // namespace B200
+}  // namespace NN
+}  // namespace MetalFish

@@ -1,0 +1,53 @@
+"""Small drivers for profiling the library (e.g. under ncu).
+
+  python -m metalfish_b200.profiling gemm M N K [BN MODE ACT OUT_F32 ITERS]
+      times ITERS back-to-back launches of one bf16 tcgen05 GEMM on synthetic
+      device data (mfb200_debug_gemm_bench) and prints TFLOP/s.
+  python -m metalfish_b200.profiling forward [BATCH] [bf16|fp8]
+      runs two eager forwards (no CUDA graph, so every kernel is a separate
+      launch) of the seeded BT4-shaped network on fixture positions.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import sys
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def gemm(argv) -> None:
+    from ._lib import lib
+    M, N, K = (int(x) for x in argv[:3])
+    bn, mode, act, out_f32, iters = (int(x) for x in (argv[3:8] + ["256", "0", "0", "0", "10"][len(argv) - 3:]))
+    ms = ctypes.c_float()
+    rc = lib().mfb200_debug_gemm_bench(M, N, K, bn, mode, act, out_f32, iters, ctypes.byref(ms))
+    if rc:
+        raise SystemExit(f"gemm bench failed: rc={rc}")
+    print(f"M={M} N={N} K={K} bn={bn}: {ms.value:.4f} ms  {2.0 * M * N * K / ms.value / 1e9:.1f} TFLOP/s")
+
+
+def forward(argv) -> None:
+    from .netfile import PackedInputs
+    from .network import create_network
+    from .synthetic import BT4, generate
+    batch = int(argv[0]) if argv else 512
+    precision = argv[1] if len(argv) > 1 else "bf16"
+    z = np.load(os.path.join(ROOT, "tests", "golden", "positions.npz"))
+    m, v = z["masks"], z["values"]
+    reps = (batch + 2048 + len(m) - 1) // len(m)
+    m, v = np.tile(m, (reps, 1)), np.tile(v, (reps, 1))
+    net = create_network(BT4, generate(BT4, 3), max_batch=batch, use_graphs=False, precision=precision,
+                         calibration=PackedInputs(m[1024:2048], v[1024:2048]) if precision == "fp8" else None)
+    inp = PackedInputs(m[:batch].copy(), v[:batch].copy())
+    for _ in range(2):
+        net.evaluate_packed(inp)
+    net.close()
+    print(f"forward ok: BT4 batch {batch} {precision}")
+
+
+if __name__ == "__main__":
+    cmd, rest = sys.argv[1], sys.argv[2:]
+    {"gemm": gemm, "forward": forward}[cmd](rest)

@@ -23,6 +23,10 @@
 //   to-pb <net.mfnt> <out.pb>
 //       Serialises the same in-memory Net as a protobuf .pb weights file.
 //
+//   eval-backend <cpu|b200> ...  (b200 only in the b200_harness build)
+//       As eval, through the named backend; "b200" constructs the B200
+//       Network subclass (metalfish_b200/host) from the same WeightsFile.
+//
 // File formats (all little-endian) are produced/consumed by
 // metalfish_b200/netfile.py.
 #include "nn/encoder.h"
@@ -31,6 +35,9 @@
 #include "core/bitboard.h"
 #include "core/movegen.h"
 #include "core/position.h"
+#ifdef MFB_WITH_B200
+#include "../metalfish_b200/host/b200_network.h"
+#endif
 
 #include <chrono>
 #include <cstdio>
@@ -323,12 +330,23 @@ NN::WeightsFile ReadNet(const std::string &path) {
 }
 
 int Eval(const std::string &net_path, const std::string &in_path, const std::string &out_path,
-         int threads, int first, int count) {
+         int threads, int first, int count, const std::string &backend = "cpu") {
   const NN::WeightsFile file = ReadNet(net_path);
   const Inputs in = ReadInputs(in_path);
   if (count < 0) count = in.count - first;
   if (first < 0 || count < 0 || first + count > in.count) throw std::runtime_error("bad range");
-  auto net = NN::CreateNetwork(file, "cpu");
+  std::unique_ptr<NN::Network> net;
+#ifdef MFB_WITH_B200
+  if (backend == "b200") {
+    // the integration under test: the B200 backend built from the same
+    // WeightsFile the CPU backend takes, evaluated through NN::Network
+    NN::B200::B200Options opt;
+    opt.max_batch = std::max(1, count);
+    net = std::make_unique<NN::B200::B200Network>(file, opt);
+    threads = 1;  // one handle, batched on the GPU
+  }
+#endif
+  if (!net) net = NN::CreateNetwork(file, backend);
   std::vector<NN::InputPlanes> planes(count);
   for (int b = 0; b < count; ++b) planes[b] = Unpack(in, first + b);
   std::vector<NN::NetworkOutput> outputs(count);
@@ -394,10 +412,14 @@ int main(int argc, char **argv) {
       return Eval(argv[2], argv[3], argv[4], argc > 5 ? std::stoi(argv[5]) : 1,
                   argc > 6 ? std::stoi(argv[6]) : 0, argc > 7 ? std::stoi(argv[7]) : -1);
     if (cmd == "to-pb" && argc == 4) return ToPb(argv[2], argv[3]);
+    if (cmd == "eval-backend" && argc >= 6)
+      return Eval(argv[3], argv[4], argv[5], argc > 6 ? std::stoi(argv[6]) : 1,
+                  argc > 7 ? std::stoi(argv[7]) : 0, argc > 8 ? std::stoi(argv[8]) : -1, argv[2]);
     std::fprintf(stderr,
                  "usage: ref_harness gen-inputs <seed> <count> <out.mfin>\n"
                  "       ref_harness eval <net.mfnt> <in.mfin> <out.mfot> [threads] [first] [count]\n"
-                 "       ref_harness to-pb <net.mfnt> <out.pb>\n");
+                 "       ref_harness to-pb <net.mfnt> <out.pb>\n"
+                 "       ref_harness eval-backend <cpu|b200> <net.mfnt> <in.mfin> <out.mfot> [threads] [first] [count]\n");
     return 2;
   } catch (const std::exception &e) {
     std::fprintf(stderr, "ref_harness error: %s\n", e.what());

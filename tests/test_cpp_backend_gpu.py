@@ -1,0 +1,37 @@
+"""The C++ drop-in: the reference harness (reference NN sources, compiled
+unmodified) builds a WeightsFile and evaluates it through the B200 Network
+subclass (metalfish_b200/host/b200_network.cpp) -- the path MetalFish's
+CreateNetwork takes for backend "b200". Checked against the reference CPU
+backend's golden outputs with the bf16 tolerances."""
+import os
+import subprocess
+
+import numpy as np
+import pytest
+
+from metalfish_b200 import netfile, synthetic
+from tests.conftest import load_golden
+
+pytestmark = pytest.mark.gpu
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HARNESS = os.path.join(ROOT, "oracle", "_ref", "b200_harness")
+
+
+@pytest.mark.skipif(not os.path.exists(HARNESS), reason="b200_harness not built (needs the reference tree)")
+@pytest.mark.parametrize("name", ["tiny", "small"])
+def test_cpp_network_subclass_matches_reference(name, positions, tmp_path):
+    g = load_golden(name)
+    cfg = synthetic.CONFIGS[str(g["config"])]
+    t = synthetic.generate(cfg, int(g["weight_seed"]), bool(g["perturb_norms"]))
+    n = int(g["positions"])
+    net, pos, out = tmp_path / "n.mfnt", tmp_path / "p.mfin", tmp_path / "o.mfot"
+    netfile.write_net(str(net), cfg.header(), t)
+    netfile.write_inputs(str(pos), positions.slice(0, n))
+    r = subprocess.run([HARNESS, "eval-backend", "b200", str(net), str(pos), str(out)],
+                       capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr
+    assert "b200" in r.stdout
+    o = netfile.read_outputs(str(out))
+    assert np.abs(o.policy - g["policy"][:n]).max() <= 5e-2
+    assert np.abs(o.wdl - g["wdl"][:n]).max() <= 1e-2
+    np.testing.assert_allclose(o.value, o.wdl[:, 0] - o.wdl[:, 2], atol=1e-6)
