@@ -84,13 +84,17 @@ static bool make_tmap(CUtensorMap *tm, const void *base, CUtensorMapDataType dt,
 template <int BN, bool FP8>
 static cudaError_t launch_t(const GemmLaunch &g, cudaStream_t stream) {
   using S = GemmShape<BN, FP8>;
-  static bool attr_done = false;
-  if (!attr_done) {
+  // the shared-memory opt-in is a per-device function attribute
+  static bool attr_done[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!attr_done[dev]) {
     cudaError_t e = cudaFuncSetAttribute(gemm_sm100_kernel<BN, FP8>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          S::SMEM_BYTES);
     if (e != cudaSuccess) return e;
-    attr_done = true;
+    attr_done[dev] = true;
   }
   gemm_sm100_kernel<BN, FP8><<<g.grid, S::THREADS, S::SMEM_BYTES, stream>>>(
       g.tmA, g.tmB, g.tmOut, g.tmOut2, g.tmRes, g.args);

@@ -321,15 +321,14 @@ void put_mat(ArenaBuilder &ab, Layout &lay, Mat &m, int rows, int cols, int ld, 
 // Host float -> e4m3 (round to nearest, ties to even; saturating at +-448).
 // e4m3: 1 sign, 4 exponent bits (bias 7), 3 mantissa bits, no infinities.
 uint8_t f2e4m3(float x) {
-  static float table[127];
-  static bool init = false;
-  if (!init) {
+  static const std::array<float, 127> table = [] {
+    std::array<float, 127> t{};
     for (int b = 0; b < 127; ++b) {
       const int e = b >> 3, m = b & 7;
-      table[b] = e == 0 ? std::ldexp(m / 8.0f, -6) : std::ldexp(1.0f + m / 8.0f, e - 7);
+      t[b] = e == 0 ? std::ldexp(m / 8.0f, -6) : std::ldexp(1.0f + m / 8.0f, e - 7);
     }
-    init = true;
-  }
+    return t;
+  }();
   const uint8_t sign = std::signbit(x) ? 0x80 : 0;
   float a = std::fabs(x);
   if (!(a == a)) return 0x7F;
