@@ -15,8 +15,10 @@ extern "C" {
 
 /* out[M,N] (bf16 bits) = epilogue(A[M,K] . W[N,K]^T) through the tcgen05 GEMM.
  * A/W are bf16 bits (fp8 = 0) or e4m3 bytes (fp8 = 1); resid is fp32; out is
- * fp32 when out_f32 = 1, else bf16 bits. mode: 0 store
- * act(scale*acc+bias), 1 resid + alpha*(scale*acc+bias). k_splits > 1: split-K,
+ * fp32 when out_f32 = 1, fp16 bits when out_f32 = 2, else bf16 bits. mode: 0
+ * store act(scale*acc+bias), 1 resid + alpha*(scale*acc+bias), 3 the same
+ * computed in place (the output buffer starts as resid, rounded to the output
+ * format, and the GEMM adds alpha*(scale*acc+bias) into it). k_splits > 1: split-K,
  * `out` receives k_splits fp32 partial products [k_splits, M, N] (no bias).
  * ln_gamma/ln_beta/ln_eps are unused. */
 MFB200_API int mfb200_debug_gemm(int M, int N, int K, int bn, int fp8, const void *A, const void *W,
@@ -25,8 +27,17 @@ MFB200_API int mfb200_debug_gemm(int M, int N, int K, int bn, int fp8, const voi
                       const float *col_scale, float a_scale, int out_f32, int k_splits, void *out,
                       unsigned *status_out);
 
+/* Residual + LayerNorm GEMM: y = resid + alpha*(A.W^T + bias) (A, W bf16
+ * bits, resid fp32), out_f32 = LN(y)*gamma + beta and out_bf16 = the same in
+ * bf16; N must be bn times a cluster size of 1, 2, 4 or 8. */
+MFB200_API int mfb200_debug_gemm_ln(int M, int N, int K, int bn, const void *A, const void *W,
+                                    const float *bias, const float *resid, float alpha,
+                                    const float *gamma, const float *beta, float eps,
+                                    float *out_f32, uint16_t *out_bf16, unsigned *status_out);
+
 /* Mean device time (ms) of `iters` back-to-back launches of one bf16 GEMM on
- * synthetic device data (for profiling the kernel in isolation). */
+ * synthetic device data (for profiling the kernel in isolation); mode and
+ * out_f32 as for mfb200_debug_gemm (mode 2: residual + LayerNorm). */
 MFB200_API int mfb200_debug_gemm_bench(int M, int N, int K, int bn, int mode, int act, int out_f32,
                                        int iters, float *ms_out);
 

@@ -3,6 +3,7 @@
 // copies host inputs in, runs ONE kernel and copies the result back.
 #include <cuda_fp8.h>
 
+#include <cstdio>
 #include <cstring>
 #include <vector>
 
@@ -43,6 +44,15 @@ extern "C" int mfb200_debug_gemm(int M, int N, int K, int bn, int fp8, const voi
   if (resid) cudaMemcpy(dR.p, resid, size_t(M) * N * 4, cudaMemcpyHostToDevice);
   if (col_scale) cudaMemcpy(dCs.p, col_scale, N * 4, cudaMemcpyHostToDevice);
   cudaMemset(dO.p, 0, size_t(sp) * M * N * 4);
+  if (mode == kEpiAccum && resid) {  // accumulate in place: the output starts as the residual
+    if (out_f32 == 2) {
+      std::vector<__half> h(size_t(M) * N);
+      for (size_t i = 0; i < h.size(); ++i) h[i] = __float2half_rn(resid[i]);
+      cudaMemcpy(dO.p, h.data(), h.size() * 2, cudaMemcpyHostToDevice);
+    } else {
+      cudaMemcpy(dO.p, resid, size_t(M) * N * 4, cudaMemcpyHostToDevice);
+    }
+  }
   cudaMemset(dS.p, 0, 4);
   GemmArgs a{};
   a.M = M;
@@ -61,12 +71,13 @@ extern "C" int mfb200_debug_gemm(int M, int N, int K, int bn, int fp8, const voi
   a.col_scale = col_scale ? static_cast<float *>(dCs.p) : nullptr;
   a.a_scale = a_scale;
   a.status = static_cast<unsigned *>(dS.p);
-  a.out_f32 = out_f32;
+  a.out_f32 = out_f32 == 1;
+  a.out_f16 = out_f32 == 2;  // 2: fp16 output
   GemmLaunch g;
   if (plan_gemm(g, dA.p, K, dW.p, K, bn, fp8 != 0, a)) return 2;
   if (launch_gemm(g, 0) != cudaSuccess) return 3;
   if (cudaDeviceSynchronize() != cudaSuccess) return 4;
-  cudaMemcpy(out, dO.p, size_t(sp) * M * N * (sp > 1 || out_f32 ? 4 : 2), cudaMemcpyDeviceToHost);
+  cudaMemcpy(out, dO.p, size_t(sp) * M * N * (sp > 1 || out_f32 == 1 ? 4 : 2), cudaMemcpyDeviceToHost);
   unsigned st = 0;
   cudaMemcpy(&st, dS.p, 4, cudaMemcpyDeviceToHost);
   if (status_out) *status_out = st;
@@ -77,10 +88,12 @@ extern "C" int mfb200_debug_gemm(int M, int N, int K, int bn, int fp8, const voi
 // (bf16, bias, optional fp32 output); returns the mean ms per launch.
 extern "C" int mfb200_debug_gemm_bench(int M, int N, int K, int bn, int mode, int act,
                                        int out_f32, int iters, float *ms_out) {
-  DevBuf dA, dW, dB, dR, dO, dS;
+  DevBuf dA, dW, dB, dR, dO, dS, dO2, dG, dRS;
   if (!dA.alloc(size_t(M) * K * 2) || !dW.alloc(size_t(N) * K * 2) || !dB.alloc(N * 4) ||
-      !dR.alloc(size_t(M) * N * 4) || !dO.alloc(size_t(M) * N * 4) || !dS.alloc(4))
+      !dR.alloc(size_t(M) * N * 4) || !dO.alloc(size_t(M) * N * 4) || !dS.alloc(4) ||
+      !dO2.alloc(size_t(M) * N * 2) || !dG.alloc(N * 4) || !dRS.alloc(size_t(M) * 16 * 8))
     return 1;
+  cudaMemset(dG.p, 0, N * 4);
   cudaMemset(dA.p, 0x3c, size_t(M) * K * 2);  // small finite bf16 values
   cudaMemset(dW.p, 0x3c, size_t(N) * K * 2);
   cudaMemset(dB.p, 0, N * 4);
@@ -99,8 +112,20 @@ extern "C" int mfb200_debug_gemm_bench(int M, int N, int K, int bn, int mode, in
   a.ldr = N;
   a.alpha = 1.0f;
   a.a_scale = 1.0f;
-  a.out_f32 = out_f32;
+  a.out_f32 = out_f32 == 1;
+  a.out_f16 = out_f32 == 2;  // 2: fp16 output
   a.status = static_cast<unsigned *>(dS.p);
+  if (mode == kEpiAccum && !a.out_f16) a.out_f32 = 1;
+  if (mode == kEpiResidLN) {  // fused residual + LayerNorm (N / bn CTAs per cluster)
+    a.out_f32 = 0;
+    a.out2 = dO2.p;
+    a.ldo2 = N;
+    a.ln_gamma = static_cast<float *>(dG.p);
+    a.ln_beta = static_cast<float *>(dG.p);
+    a.ln_eps = 1e-3f;
+    a.cluster_n = N / bn;
+    a.row_stats = static_cast<float2 *>(dRS.p);
+  }
   GemmLaunch g;
   if (plan_gemm(g, dA.p, K, dW.p, K, bn, false, a)) return 2;
   for (int i = 0; i < 2; ++i)
@@ -119,5 +144,61 @@ extern "C" int mfb200_debug_gemm_bench(int M, int N, int K, int bn, int mode, in
   *ms_out = ms / iters;
   unsigned st = 0;
   cudaMemcpy(&st, dS.p, 4, cudaMemcpyDeviceToHost);
+  return st ? 5 : 0;
+}
+
+// Residual + LayerNorm GEMM (kEpiResidLN): y = resid + alpha*(A.W^T + bias),
+// out_f32 = LN(y)*gamma + beta (fp32) and out_bf16 = the same in bf16. The
+// row spans N / bn CTAs of one thread-block cluster.
+extern "C" int mfb200_debug_gemm_ln(int M, int N, int K, int bn, const void *A, const void *W,
+                                    const float *bias, const float *resid, float alpha,
+                                    const float *gamma, const float *beta, float eps,
+                                    float *out_f32, uint16_t *out_bf16, unsigned *status_out) {
+  DevBuf dA, dW, dB, dR, dG, dBe, dO, dO2, dRS, dS;
+  const int C = N / bn;
+  if (!dA.alloc(size_t(M) * K * 2) || !dW.alloc(size_t(N) * K * 2) || !dB.alloc(N * 4) ||
+      !dR.alloc(size_t(M) * N * 4) || !dG.alloc(N * 4) || !dBe.alloc(N * 4) ||
+      !dO.alloc(size_t(M) * N * 4) || !dO2.alloc(size_t(M) * N * 2) ||
+      !dRS.alloc(size_t(M) * 2 * C * 8) || !dS.alloc(4))
+    return 1;
+  cudaMemcpy(dA.p, A, size_t(M) * K * 2, cudaMemcpyHostToDevice);
+  cudaMemcpy(dW.p, W, size_t(N) * K * 2, cudaMemcpyHostToDevice);
+  cudaMemcpy(dB.p, bias, N * 4, cudaMemcpyHostToDevice);
+  cudaMemcpy(dR.p, resid, size_t(M) * N * 4, cudaMemcpyHostToDevice);
+  cudaMemcpy(dG.p, gamma, N * 4, cudaMemcpyHostToDevice);
+  cudaMemcpy(dBe.p, beta, N * 4, cudaMemcpyHostToDevice);
+  cudaMemset(dS.p, 0, 4);
+  GemmArgs a{};
+  a.M = M;
+  a.N = N;
+  a.K = K;
+  a.mode = kEpiResidLN;
+  a.bias = static_cast<float *>(dB.p);
+  a.resid = static_cast<const float *>(dR.p);
+  a.ldr = N;
+  a.alpha = alpha;
+  a.a_scale = 1.0f;
+  a.out = dO.p;
+  a.ldo = N;
+  a.out2 = dO2.p;
+  a.ldo2 = N;
+  a.ln_gamma = static_cast<float *>(dG.p);
+  a.ln_beta = static_cast<float *>(dBe.p);
+  a.ln_eps = eps;
+  a.cluster_n = C;
+  a.row_stats = static_cast<float2 *>(dRS.p);
+  a.status = static_cast<unsigned *>(dS.p);
+  GemmLaunch g;
+  if (const char *e = plan_gemm(g, dA.p, K, dW.p, K, bn, false, a)) {
+    std::fprintf(stderr, "%s\n", e);
+    return 2;
+  }
+  if (launch_gemm(g, 0) != cudaSuccess) return 3;
+  if (cudaDeviceSynchronize() != cudaSuccess) return 4;
+  cudaMemcpy(out_f32, dO.p, size_t(M) * N * 4, cudaMemcpyDeviceToHost);
+  cudaMemcpy(out_bf16, dO2.p, size_t(M) * N * 2, cudaMemcpyDeviceToHost);
+  unsigned st = 0;
+  cudaMemcpy(&st, dS.p, 4, cudaMemcpyDeviceToHost);
+  if (status_out) *status_out = st;
   return st ? 5 : 0;
 }

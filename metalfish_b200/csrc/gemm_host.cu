@@ -1,6 +1,7 @@
 // gemm_host.cu -- host side of the tcgen05 GEMM: TMA descriptor creation,
 // launch configuration and the template instantiations.
 #include <cstdio>
+#include <algorithm>
 #include <mutex>
 
 #include "gemm_host.h"
@@ -81,40 +82,99 @@ static bool make_tmap(CUtensorMap *tm, const void *base, CUtensorMapDataType dt,
          CUDA_SUCCESS;
 }
 
-template <int BN, bool FP8>
+template <int BN, bool FP8, bool LN>
 static cudaError_t launch_t(const GemmLaunch &g, cudaStream_t stream) {
-  using S = GemmShape<BN, FP8>;
+  using S = GemmShape<BN, FP8, LN>;
   // the shared-memory opt-in is a per-device function attribute
   static bool attr_done[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   if (!attr_done[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_sm100_kernel<BN, FP8>,
+    cudaError_t e = cudaFuncSetAttribute(gemm_sm100_kernel<BN, FP8, LN>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          S::SMEM_BYTES);
     if (e != cudaSuccess) return e;
     attr_done[dev] = true;
   }
-  gemm_sm100_kernel<BN, FP8><<<g.grid, S::THREADS, S::SMEM_BYTES, stream>>>(
+  if (g.args.mode == kEpiResidLN && g.args.cluster_n > 1) {
+    // the CTAs covering one row block form a thread-block cluster
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = g.grid;
+    cfg.blockDim = dim3(S::THREADS);
+    cfg.dynamicSmemBytes = S::SMEM_BYTES;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = static_cast<unsigned>(g.args.cluster_n);
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, gemm_sm100_kernel<BN, FP8, LN>, g.tmA, g.tmB, g.tmOut, g.tmOut2,
+                              g.tmRes, g.args);
+  }
+  gemm_sm100_kernel<BN, FP8, LN><<<g.grid, S::THREADS, S::SMEM_BYTES, stream>>>(
       g.tmA, g.tmB, g.tmOut, g.tmOut2, g.tmRes, g.args);
   return cudaGetLastError();
 }
 
+// How many clusters of `csize` CTAs of this GEMM can be co-resident on the
+// current device (GPC boundaries make this smaller than SMs / csize).
+template <int BN, bool FP8>
+static int max_clusters_t(int csize) {
+  using S = GemmShape<BN, FP8, true>;
+  static int cache[64][9] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64 || csize < 1 || csize > 8) return 0;
+  if (cache[dev][csize]) return cache[dev][csize];
+  cudaFuncSetAttribute(gemm_sm100_kernel<BN, FP8, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       S::SMEM_BYTES);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(csize * 64));
+  cfg.blockDim = dim3(S::THREADS);
+  cfg.dynamicSmemBytes = S::SMEM_BYTES;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = static_cast<unsigned>(csize);
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, gemm_sm100_kernel<BN, FP8, true>, &cfg) != cudaSuccess || n <= 0)
+    n = num_sms() / csize;
+  cudaGetLastError();
+  cache[dev][csize] = n;
+  return n;
+}
+
+static int max_clusters(int bn, bool fp8, int csize) {
+  if (fp8) return bn == 256 ? max_clusters_t<256, true>(csize)
+                            : (bn == 128 ? max_clusters_t<128, true>(csize) : max_clusters_t<64, true>(csize));
+  return bn == 256 ? max_clusters_t<256, false>(csize)
+                   : (bn == 128 ? max_clusters_t<128, false>(csize) : max_clusters_t<64, false>(csize));
+}
+
 cudaError_t launch_gemm(const GemmLaunch &g, cudaStream_t stream) {
+  const bool ln = g.args.mode == kEpiResidLN;
+#define MFB_LAUNCH(BN, F8) \
+  return ln ? launch_t<BN, F8, true>(g, stream) : launch_t<BN, F8, false>(g, stream)
   if (g.fp8) {
     switch (g.bn) {
-    case 256: return launch_t<256, true>(g, stream);
-    case 128: return launch_t<128, true>(g, stream);
-    case 64: return launch_t<64, true>(g, stream);
+    case 256: MFB_LAUNCH(256, true);
+    case 128: MFB_LAUNCH(128, true);
+    case 64: MFB_LAUNCH(64, true);
     }
   } else {
     switch (g.bn) {
-    case 256: return launch_t<256, false>(g, stream);
-    case 128: return launch_t<128, false>(g, stream);
-    case 64: return launch_t<64, false>(g, stream);
+    case 256: MFB_LAUNCH(256, false);
+    case 128: MFB_LAUNCH(128, false);
+    case 64: MFB_LAUNCH(64, false);
     }
   }
+#undef MFB_LAUNCH
   return cudaErrorInvalidValue;
 }
 
@@ -124,6 +184,17 @@ const char *plan_gemm(GemmLaunch &g, const void *A, long long lda_elems, const v
   if (args.M <= 0 || args.N <= 0 || args.K <= 0) return "gemm: empty problem";
   if (args.N % 32) return "gemm: N must be a multiple of 32";
   if (args.out2 && args.split % 32) return "gemm: split column must be a multiple of 32";
+  if (args.mode == kEpiResidLN) {
+    const int C = args.cluster_n;
+    if (C != 1 && C != 2 && C != 4 && C != 8) return "gemm: LN epilogue cluster size must be 1, 2, 4 or 8";
+    if (args.N != C * bn) return "gemm: LN epilogue needs N == cluster_n * BN";
+    if (!args.row_stats || !args.ln_gamma || !args.ln_beta || !args.resid)
+      return "gemm: LN epilogue needs row_stats, gamma, beta and a residual";
+    if (args.k_splits > 1) return "gemm: LN epilogue cannot be split along K";
+  }
+  if (args.mode == kEpiAccum && ((!args.out_f32 && !args.out_f16) || args.out2 || args.out_fp8))
+    return "gemm: the accumulate epilogue adds into one fp32 or fp16 output";
+  if (args.out_f16 && (args.out_f32 || args.out_fp8)) return "gemm: one output format";
   if (args.k_splits > 1 && (args.bias || args.mode != kEpiStore || args.out2))
     return "gemm: split-K writes raw fp32 partials (no bias, residual or column split)";
   const uint32_t elem = fp8 ? 1 : 2;
@@ -150,7 +221,8 @@ const char *plan_gemm(GemmLaunch &g, const void *A, long long lda_elems, const v
     const bool f32 = g.args.k_splits > 1 || args.out_f32;
     const CUtensorMapDataType odt = f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
                                         : (args.out_fp8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8
-                                                        : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16);
+                                                        : (args.out_f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                                        : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16));
     const uint64_t oel = f32 ? 4 : (args.out_fp8 ? 1 : 2);
     const CUtensorMapSwizzle oswz = f32 ? CU_TENSOR_MAP_SWIZZLE_128B
                                         : (args.out_fp8 ? CU_TENSOR_MAP_SWIZZLE_32B
@@ -163,6 +235,21 @@ const char *plan_gemm(GemmLaunch &g, const void *A, long long lda_elems, const v
       const uint64_t st[2] = {uint64_t(args.ldo) * 4, uint64_t(args.split_stride) * 4};
       if (!make_tmap(&g.tmOut, args.out, odt, 3, dims, st, box3, oswz))
         return "gemm: cannot build the split-K output tensor map";
+    } else if (args.mode == kEpiResidLN) {
+      const uint64_t dims[2] = {uint64_t(args.N), uint64_t(args.M)};
+      const uint64_t st[1] = {uint64_t(args.ldo) * 4};
+      if (!make_tmap(&g.tmOut, args.out, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, dims, st, box3,
+                     CU_TENSOR_MAP_SWIZZLE_128B))
+        return "gemm: cannot build the LN fp32 output tensor map";
+      if (args.out2) {
+        const uint64_t lel = args.out_fp8 ? 1 : 2;
+        const uint64_t s2[1] = {uint64_t(args.ldo2) * lel};
+        if (!make_tmap(&g.tmOut2, args.out2,
+                       args.out_fp8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                       2, dims, s2, box3,
+                       args.out_fp8 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_64B))
+          return "gemm: cannot build the LN low-precision output tensor map";
+      }
     } else {
       const int n_main = args.out2 ? args.split : args.N;
       const uint64_t dims[2] = {uint64_t(n_main), uint64_t(args.M)};
@@ -176,7 +263,7 @@ const char *plan_gemm(GemmLaunch &g, const void *A, long long lda_elems, const v
           return "gemm: cannot build the second output tensor map";
       }
     }
-    if (args.mode == kEpiResid) {
+    if (args.mode == kEpiResid || args.mode == kEpiResidLN) {
       const uint64_t dims[2] = {uint64_t(args.N), uint64_t(args.M)};
       const uint64_t st[1] = {uint64_t(args.ldr) * 4};
       if (!make_tmap(&g.tmRes, args.resid, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, dims, st, box3,
@@ -187,6 +274,13 @@ const char *plan_gemm(GemmLaunch &g, const void *A, long long lda_elems, const v
   const long long tiles = static_cast<long long>((args.M + 127) / 128) *
                           ((args.N + bn - 1) / bn) * g.args.k_splits;
   const int sms = num_sms();
+  if (args.mode == kEpiResidLN) {
+    // whole clusters; each cluster walks row blocks
+    const long long tiles_m = (args.M + 127) / 128;
+    const long long clusters = std::min<long long>(tiles_m, max_clusters(bn, fp8, args.cluster_n));
+    g.grid = dim3(static_cast<unsigned>(clusters * args.cluster_n));
+    return nullptr;
+  }
   g.grid = dim3(static_cast<unsigned>(tiles < sms ? tiles : sms));
   return nullptr;
 }

@@ -20,6 +20,7 @@
 //              (bf16, e4m3 or fp32) and TMA-store it asynchronously.
 // All barrier waits are bounded (sm100_ptx.cuh).
 #pragma once
+#include <cuda_fp16.h>
 #include <cuda_fp8.h>
 
 #include "sm100_ptx.cuh"
@@ -27,8 +28,12 @@
 namespace mfb200 {
 
 enum EpiMode : int {
-  kEpiStore = 0,  // act(scale*acc + bias)
-  kEpiResid = 1,  // resid + alpha * (scale*acc + bias)
+  kEpiStore = 0,    // act(scale*acc + bias)
+  kEpiResid = 1,    // resid + alpha * (scale*acc + bias)
+  kEpiResidLN = 2,  // y = resid + alpha * (scale*acc + bias); LN(y) over the full row
+                    // (the row spans the cluster_n CTAs of a thread-block cluster)
+  kEpiAccum = 3,    // out (fp32 or fp16, holding the residual) += alpha * (scale*acc + bias),
+                    // added in place by TMA reduce stores: no residual reads
 };
 
 enum Act : int {
@@ -50,10 +55,15 @@ struct GemmArgs {
   const float *col_scale;     // per-output-channel scale (fp8 weights) or nullptr
   float a_scale;              // activation scale (fp8) ; 1 for bf16
   int out_f32;                // store fp32 instead of bf16
+  int out_f16;                // store fp16 instead of bf16
   int out_fp8;                // store e4m3 instead of bf16 ...
   float out_inv_scale;        // ... after multiplying by this
   const float *a_scale_ptr;   // if set: activation scale multiplied by *a_scale_ptr
   const float *out_scale_ptr; // if set (e4m3 out): stored value = v / *out_scale_ptr
+  const float *ln_gamma, *ln_beta;  // kEpiResidLN: LN affine parameters [N]
+  float ln_eps;
+  int cluster_n;              // kEpiResidLN: CTAs per row (cluster size, N = cluster_n * BN)
+  float2 *row_stats;          // kEpiResidLN: [M, 2*cluster_n] per-row partial (sum, sum of squares)
   int k_splits;               // >1: split-K; K slice s writes fp32 partials at
   long long split_stride;     //     out + s * split_stride (raw accumulator)
   unsigned *status;           // device status word
@@ -114,10 +124,19 @@ struct EpiCtx {
   uint32_t res_loads;  // residual loads issued so far (phase parity)
   int lane;
   volatile int *abort_flag;
+  uint64_t *xbar;      // row-statistics barrier (kEpiResidLN)
+  uint32_t xtiles;     // row-statistics exchanges completed (phase parity)
+  uint32_t rank;       // CTA rank in the cluster
+  uint8_t *stage2;     // second staging tile (kEpiResidLN kernels)
 };
 
 __device__ __forceinline__ uint32_t pack_bf16x2_f(float a, float b) {
   const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<const uint32_t *>(&h);
+}
+
+__device__ __forceinline__ uint32_t pack_f16x2_f(float a, float b) {
+  const __half2 h = __floats2half2_rn(a, b);
   return *reinterpret_cast<const uint32_t *>(&h);
 }
 
@@ -146,6 +165,12 @@ __device__ __forceinline__ void stage_row(const GemmArgs &args, uint8_t *st, int
       *reinterpret_cast<uint4 *>(st + r * 32 + ((q ^ ((r >> 2) & 1)) << 4)) =
           make_uint4(w[0], w[1], w[2], w[3]);
     }
+  } else if (args.out_f16) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      *reinterpret_cast<uint4 *>(st + r * 64 + ((q ^ ((r >> 1) & 3)) << 4)) =
+          make_uint4(pack_f16x2_f(v[8 * q], v[8 * q + 1]), pack_f16x2_f(v[8 * q + 2], v[8 * q + 3]),
+                     pack_f16x2_f(v[8 * q + 4], v[8 * q + 5]), pack_f16x2_f(v[8 * q + 6], v[8 * q + 7]));
   } else {
 #pragma unroll
     for (int q = 0; q < 4; ++q)
@@ -201,7 +226,10 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs &args, EpiCtx &e, u
         }
       }
     }
-    if constexpr (MODE == kEpiResid) {
+    if constexpr (MODE == kEpiAccum) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] *= args.alpha;
+    } else if constexpr (MODE == kEpiResid) {
       if (lane == 0) {
         mbar_arrive_expect_tx(e.res_bar, kStageBytes);
         tma_load_2d(e.stage, e.res, e.res_bar, nb, row0);
@@ -227,7 +255,9 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs &args, EpiCtx &e, u
     fence_proxy_async_smem();
     __syncwarp();
     if (lane == 0) {
-      if (ks >= 0)
+      if (MODE == kEpiAccum)
+        tma_reduce_add_2d(e.out, e.stage, nb, row0);
+      else if (ks >= 0)
         tma_store_3d(e.out, e.stage, nb, row0, ks);
       else if (args.out2 && nb >= args.split)
         tma_store_2d(e.out2, e.stage, nb - args.split, row0);
@@ -239,11 +269,160 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs &args, EpiCtx &e, u
   return true;
 }
 
+// Residual + LayerNorm epilogue (the reference's LN(parent + alpha*x),
+// src/nn/cpu/cpu_network.cpp:424-460, one-pass fp32 statistics).
+// In LN kernels the eight epilogue warps form two teams of four (one warp per
+// TMEM lane quarter); team t handles every other tile, in accumulator t, so
+// one team's memory traffic overlaps the other's. Each warp covers all BN
+// columns of its 32 rows.
+// Pass 1, per 32-column chunk of this lane's row: y = resid + alpha*(scale*acc
+// + bias) with the residual read once (vector loads, next chunk in flight),
+// row sum and sum of squares accumulated, and y written back over the
+// accumulator's own TMEM columns. The row statistics are then published:
+// each thread writes its row's partial to row_stats[row][rank]; after a
+// __syncwarp one lane per warp arrives (release, cluster scope) on the team's
+// barrier in every cluster CTA; once it completes (acquire) each thread sums
+// the cluster_n partials of its row. Pass 2 reads y back from TMEM, normalises
+// it and TMA-stores an fp32 copy (`out`, the next residual parent) and a
+// bf16 / e4m3 copy (`out2`, the next GEMM's input).
 template <int BN>
+__device__ __forceinline__ bool epilogue_tile_ln(const GemmArgs &args, EpiCtx &e, uint32_t taddr,
+                                                 int row0, int n0) {
+  const int lane = e.lane;
+  const int row = row0 + lane;
+  const int rrow = row < args.M ? row : args.M - 1;  // clamp loads of rows past M
+  const float a_scale = args.a_scale_ptr ? args.a_scale * __ldg(args.a_scale_ptr) : args.a_scale;
+  const float out_is = args.out_scale_ptr ? 1.0f / __ldg(args.out_scale_ptr) : args.out_inv_scale;
+  const int C = args.cluster_n;
+  const float *rbase = args.resid + static_cast<long long>(rrow) * args.ldr;
+  float s = 0.0f, sq = 0.0f;
+  float4 rv[8];
+  {
+    const float4 *rp = reinterpret_cast<const float4 *>(rbase + n0);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) rv[q] = __ldg(rp + q);
+  }
+  for (int c = 0; c < BN; c += 32) {
+    const int nb = n0 + c;
+    uint32_t raw[32];
+    tmem_ld32(taddr + c, raw);
+    float4 cur[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) cur[q] = rv[q];
+    if (c + 32 < BN) {  // next chunk's residual in flight
+      const float4 *rp = reinterpret_cast<const float4 *>(rbase + nb + 32);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) rv[q] = __ldg(rp + q);
+    }
+    tmem_wait_ld();
+    float v[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(raw[j]) * a_scale;
+    if (args.col_scale) {
+      const float4 *cs = reinterpret_cast<const float4 *>(args.col_scale + nb);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const float4 f = __ldg(cs + q);
+        v[4 * q] *= f.x; v[4 * q + 1] *= f.y; v[4 * q + 2] *= f.z; v[4 * q + 3] *= f.w;
+      }
+    }
+    const float4 *bp = reinterpret_cast<const float4 *>(args.bias + nb);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const float4 b = args.bias ? __ldg(bp + q) : make_float4(0.f, 0.f, 0.f, 0.f);
+      v[4 * q] = cur[q].x + args.alpha * (v[4 * q] + b.x);
+      v[4 * q + 1] = cur[q].y + args.alpha * (v[4 * q + 1] + b.y);
+      v[4 * q + 2] = cur[q].z + args.alpha * (v[4 * q + 2] + b.z);
+      v[4 * q + 3] = cur[q].w + args.alpha * (v[4 * q + 3] + b.w);
+    }
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      s += v[j];
+      sq += v[j] * v[j];
+      raw[j] = __float_as_uint(v[j]);
+    }
+    tmem_st32(taddr + c, raw);
+  }
+  tmem_wait_st();
+  // publish this thread's partial and signal every CTA of the cluster
+  if (row < args.M)
+    args.row_stats[static_cast<long long>(row) * C + e.rank] = make_float2(s, sq);
+  const uint32_t bar = smem_u32(e.xbar);
+  // __syncwarp orders the lanes' writes before lane 0's (cumulative) release
+  __syncwarp();
+  if (lane == 0)
+    for (int p = 0; p < C; ++p) mbar_arrive_remote(mapa_shared(bar, static_cast<uint32_t>(p)));
+  if (!mbar_wait_cluster(e.xbar, e.xtiles & 1, args.status, kErrTimeoutRowStats, e.abort_flag))
+    return false;
+  ++e.xtiles;
+  float ts = 0.0f, tq = 0.0f;
+  {
+    const float2 *rs = args.row_stats + static_cast<long long>(rrow) * C;
+    for (int k = 0; k < C; ++k) {
+      const float2 x = __ldcg(rs + k);  // L2: written by other SMs
+      ts += x.x;
+      tq += x.y;
+    }
+  }
+  const float mean = ts / static_cast<float>(args.N);
+  float var = tq / static_cast<float>(args.N) - mean * mean;
+  var = var < 0.0f ? 0.0f : var;
+  const float rstd = 1.0f / sqrtf(var + args.ln_eps);
+  uint32_t raw[32];
+  tmem_ld32(taddr, raw);
+  for (int c = 0; c < BN; c += 32) {
+    const int nb = n0 + c;
+    tmem_wait_ld();
+    float v[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(raw[j]);
+    if (c + 32 < BN) tmem_ld32(taddr + c + 32, raw);
+    const float4 *gp = reinterpret_cast<const float4 *>(args.ln_gamma + nb);
+    const float4 *bp = reinterpret_cast<const float4 *>(args.ln_beta + nb);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const float4 g = __ldg(gp + q), b = __ldg(bp + q);
+      v[4 * q] = (v[4 * q] - mean) * rstd * g.x + b.x;
+      v[4 * q + 1] = (v[4 * q + 1] - mean) * rstd * g.y + b.y;
+      v[4 * q + 2] = (v[4 * q + 2] - mean) * rstd * g.z + b.z;
+      v[4 * q + 3] = (v[4 * q + 3] - mean) * rstd * g.w + b.w;
+    }
+    // two staging tiles (LN kernels): the fp32 and the bf16/e4m3 copies go
+    // out through different tiles, so only the store two back must have
+    // finished reading before a tile is rewritten
+    if (lane == 0) bulk_wait_read1();
+    __syncwarp();
+    stage_row(args, e.stage, lane, v, true, out_is);  // fp32 copy
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      tma_store_2d(e.out, e.stage, nb, row0);
+      bulk_commit();
+    }
+    if (args.out2) {
+      if (lane == 0) bulk_wait_read1();
+      __syncwarp();
+      stage_row(args, e.stage2, lane, v, false, out_is);  // bf16 / e4m3 copy
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        tma_store_2d(e.out2, e.stage2, nb, row0);
+        bulk_commit();
+      }
+    }
+  }
+  return true;
+}
+
+template <int BN, bool LN>
 __device__ __forceinline__ bool epilogue_dispatch(const GemmArgs &args, EpiCtx &e, uint32_t taddr,
                                                   int row0, int n0, int group, int ks) {
+  if constexpr (LN) {
+    return epilogue_tile_ln<BN>(args, e, taddr, row0, n0);
+  } else {
 #define MFB_EPI(MODE, ACT) return epilogue_tile<BN, MODE, ACT>(args, e, taddr, row0, n0, group, ks)
   if (ks < 0 && args.mode == kEpiResid) MFB_EPI(kEpiResid, kActNone);
+  if (ks < 0 && args.mode == kEpiAccum) MFB_EPI(kEpiAccum, kActNone);
   switch (ks >= 0 ? kActNone : args.act) {
   case kActRelu: MFB_EPI(kEpiStore, kActRelu);
   case kActRelu2: MFB_EPI(kEpiStore, kActRelu2);
@@ -254,31 +433,34 @@ __device__ __forceinline__ bool epilogue_dispatch(const GemmArgs &args, EpiCtx &
   case kActSelu: MFB_EPI(kEpiStore, kActSelu);
   default: MFB_EPI(kEpiStore, kActNone);
   }
+  }
 #undef MFB_EPI
 }
 
-template <int BN, bool FP8>
+template <int BN, bool FP8, bool LN = false>
 struct GemmShape {
   static constexpr int BM = 128;
   static constexpr int BK = FP8 ? 128 : 64;  // elements per 128-byte swizzled row
   static constexpr int A_BYTES = BM * 128;
   static constexpr int B_BYTES = BN * 128;
-  static constexpr int STAGES = BN == 256 ? 4 : (BN == 128 ? 6 : 8);
+  // LN kernels trade one pipeline stage for a second staging tile per warp
+  static constexpr int STAGES = LN ? (BN == 256 ? 3 : (BN == 128 ? 4 : 5))
+                                   : (BN == 256 ? 4 : (BN == 128 ? 6 : 8));
   static constexpr int TMEM_COLS = 2 * BN;
-  static constexpr int STAGE_BYTES = kEpiWarps * kStageBytes;  // epilogue staging tiles
+  static constexpr int STAGE_BYTES = (LN ? 2 : 1) * kEpiWarps * kStageBytes;  // epilogue staging
   static constexpr int SMEM_BYTES = STAGES * (A_BYTES + B_BYTES) + STAGE_BYTES + 1024 + 256;
   static constexpr int THREADS = 64 + 32 * kEpiWarps;
   static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 };
 
-template <int BN, bool FP8>
+template <int BN, bool FP8, bool LN = false>
 __global__ void __launch_bounds__(64 + 32 * kEpiWarps, 1)
     gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA,
                       const __grid_constant__ CUtensorMap tmB,
                       const __grid_constant__ CUtensorMap tmOut,
                       const __grid_constant__ CUtensorMap tmOut2,
                       const __grid_constant__ CUtensorMap tmRes, const GemmArgs args) {
-  using S = GemmShape<BN, FP8>;
+  using S = GemmShape<BN, FP8, LN>;
   constexpr int STAGES = S::STAGES;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t *base = reinterpret_cast<uint8_t *>(
@@ -292,7 +474,8 @@ __global__ void __launch_bounds__(64 + 32 * kEpiWarps, 1)
   uint64_t *tempty = tfull + 2;
   uint64_t *res_bars = tempty + 2;  // one per epilogue warp
   uint64_t *drain = res_bars + kEpiWarps;
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
+  uint64_t *xbar = drain + 1;  // row-statistics exchange, one per LN team
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(xbar + 2);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -303,6 +486,15 @@ __global__ void __launch_bounds__(64 + 32 * kEpiWarps, 1)
   const int units = tiles_m * tiles_n * splits;
   const int kblocks = (args.K + S::BK - 1) / S::BK;
   const int kb_per = (kblocks + splits - 1) / splits;
+  // Work units: normally u enumerates (tile, K slice) pairs over the whole
+  // grid; with the LayerNorm epilogue the CTAs of one cluster walk the same
+  // row blocks, CTA `rank` owning column block `rank`.
+  constexpr bool ln = LN;  // launched for args.mode == kEpiResidLN
+  const int C = ln ? args.cluster_n : 1;
+  const uint32_t rank = ln ? cluster_ctarank() : 0u;
+  const int u_begin = ln ? static_cast<int>(blockIdx.x) / C : static_cast<int>(blockIdx.x);
+  const int u_step = ln ? static_cast<int>(gridDim.x) / C : static_cast<int>(gridDim.x);
+  const int u_end = ln ? tiles_m : units;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -311,10 +503,12 @@ __global__ void __launch_bounds__(64 + 32 * kEpiWarps, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 32 * kEpiWarps);
+      mbar_init(&tempty[a], LN ? 32 * kEpiWarps / 2 : 32 * kEpiWarps);
     }
     for (int w = 0; w < kEpiWarps; ++w) mbar_init(&res_bars[w], 1);
     mbar_init(drain, 1);
+    mbar_init(&xbar[0], static_cast<uint32_t>(C * kEpiWarps / 2));
+    mbar_init(&xbar[1], static_cast<uint32_t>(C * kEpiWarps / 2));
     *abort_flag = 0;
     fence_barrier_init();
     tma_prefetch_desc(&tmA);
@@ -327,6 +521,7 @@ __global__ void __launch_bounds__(64 + 32 * kEpiWarps, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  if (ln) cluster_sync();  // peers' barriers are initialised before any remote arrive
   const uint32_t tmem_base = *tmem_slot;
 
   if (warp == 0) {
@@ -336,11 +531,17 @@ __global__ void __launch_bounds__(64 + 32 * kEpiWarps, 1)
       uint32_t round = 0;
       long long issued = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
-        const int t = u / splits, ks = u % splits;
+      for (int u = u_begin; u < u_end && ok; u += u_step) {
+        const int t = ln ? u * tiles_n + static_cast<int>(rank) : u / splits;
+        const int ks = ln ? 0 : u % splits;
         const int m0 = (t / tiles_n) * S::BM;
         const int n0 = (t % tiles_n) * BN;
         const int kb1 = min(kblocks, (ks + 1) * kb_per);
+        if (ln) {
+          // pull this tile's residual into L2 while its mainloop runs
+          for (int y = m0; y < min(m0 + S::BM, args.M); y += 32)
+            for (int x = n0; x < n0 + BN; x += 32) tma_prefetch_l2_2d(&tmRes, x, y);
+        }
         for (int kb = ks * kb_per; kb < kb1; ++kb) {
           if (!mbar_wait(&empty[stage], (round & 1) ^ 1, args.status, kErrTimeoutProducer,
                          abort_flag)) {
@@ -377,8 +578,8 @@ __global__ void __launch_bounds__(64 + 32 * kEpiWarps, 1)
       uint32_t round = 0;
       int local = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ++local) {
-        const int ks = u % splits;
+      for (int u = u_begin; u < u_end && ok; u += u_step, ++local) {
+        const int ks = ln ? 0 : u % splits;
         const int acc = local & 1;
         const uint32_t aphase = (local >> 1) & 1;
         if (!mbar_wait(&tempty[acc], aphase ^ 1, args.status, kErrTimeoutMma, abort_flag)) {
@@ -428,16 +629,18 @@ __global__ void __launch_bounds__(64 + 32 * kEpiWarps, 1)
     const int quarter = warp & 3;        // TMEM lane quarter this warp may access
     const int group = (warp - 2) >> 2;   // which alternate 32-column chunks
     EpiCtx e{&tmOut, &tmOut2, &tmRes, stage_base + (warp - 2) * kStageBytes, &res_bars[warp - 2],
-             0u, lane, abort_flag};
+             0u, lane, abort_flag, &xbar[group], 0u, rank,
+             LN ? stage_base + (kEpiWarps + warp - 2) * kStageBytes : nullptr};
     if (lane == 0) {
       tma_prefetch_desc(&tmOut);
       if (args.out2) tma_prefetch_desc(&tmOut2);
       if (args.mode == kEpiResid) tma_prefetch_desc(&tmRes);
     }
     int local = 0;
-    for (int u = blockIdx.x; u < units; u += gridDim.x, ++local) {
-      const int t = u / splits;
-      const int ks = splits > 1 ? u % splits : -1;
+    for (int u = u_begin; u < u_end; u += u_step, ++local) {
+      if (ln && (local & 1) != group) continue;  // LN: team `group` takes every other tile
+      const int t = ln ? u * tiles_n + static_cast<int>(rank) : u / splits;
+      const int ks = (!ln && splits > 1) ? u % splits : -1;
       const int acc = local & 1;
       const uint32_t aphase = (local >> 1) & 1;
       if (!mbar_wait(&tfull[acc], aphase, args.status, kErrTimeoutEpilogue, abort_flag)) break;
@@ -446,7 +649,7 @@ __global__ void __launch_bounds__(64 + 32 * kEpiWarps, 1)
       const int n0 = (t % tiles_n) * BN;
       const uint32_t taddr =
           tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
-      const bool ok = epilogue_dispatch<BN>(args, e, taddr, m0 + quarter * 32, n0, group, ks);
+      const bool ok = epilogue_dispatch<BN, LN>(args, e, taddr, m0 + quarter * 32, n0, group, ks);
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
       if (!ok) break;
@@ -460,6 +663,7 @@ __global__ void __launch_bounds__(64 + 32 * kEpiWarps, 1)
     tc_fence_after();
     tmem_dealloc(tmem_base, S::TMEM_COLS);
   }
+  if (ln) cluster_sync();  // no CTA leaves while a peer may still signal it
 }
 
 }  // namespace mfb200

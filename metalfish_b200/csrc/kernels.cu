@@ -2,6 +2,8 @@
 #include <cuda_bf16.h>
 #include <cuda_fp8.h>
 
+#include <type_traits>
+
 #include "gemm_sm100.cuh"
 #include "kernels.cuh"
 
@@ -112,16 +114,33 @@ void launch_pe_concat(const __nv_bfloat16 *peo, int batch, int pe, __nv_bfloat16
 }
 
 // ------------------------------------------------------------------ layernorm
+template <Fmt F>
+__device__ __forceinline__ void load4(const void *base, long long i, float (&v)[4]) {
+  if constexpr (F == Fmt::F32) {
+    const float4 f = *reinterpret_cast<const float4 *>(static_cast<const float *>(base) + i);
+    v[0] = f.x; v[1] = f.y; v[2] = f.z; v[3] = f.w;
+  } else if constexpr (F == Fmt::F16) {
+    const uint2 u = *reinterpret_cast<const uint2 *>(static_cast<const __half *>(base) + i);
+    const float2 f0 = __half22float2(*reinterpret_cast<const __half2 *>(&u.x));
+    const float2 f1 = __half22float2(*reinterpret_cast<const __half2 *>(&u.y));
+    v[0] = f0.x; v[1] = f0.y; v[2] = f1.x; v[3] = f1.y;
+  } else {
+    const uint2 u = *reinterpret_cast<const uint2 *>(static_cast<const __nv_bfloat16 *>(base) + i);
+    const float2 f0 = unpack_bf16x2(u.x), f1 = unpack_bf16x2(u.y);
+    v[0] = f0.x; v[1] = f0.y; v[2] = f1.x; v[3] = f1.y;
+  }
+}
+
 // One warp per row. Lane l owns the 4-column groups q*128 + 4l .. +3 for
-// q < VPL/4, so every load instruction of the warp reads 256 contiguous bytes.
-template <int VPL, bool F32IN>
+// q < VPL/4, so every load instruction of the warp reads contiguous bytes.
+template <int VPL, Fmt IN, Fmt RES>
 __global__ void layernorm_warp_kernel(const void *__restrict__ in_, int rows,
                                       const float *__restrict__ gamma,
                                       const float *__restrict__ beta, float eps,
                                       const float *__restrict__ multT,
                                       const float *__restrict__ addT,
                                       __nv_bfloat16 *__restrict__ out,
-                                      float *__restrict__ out_f32,
+                                      void *__restrict__ out_res,
                                       uint8_t *__restrict__ out8,
                                       const float *__restrict__ scale8) {
   constexpr int W = 32 * VPL;
@@ -130,27 +149,14 @@ __global__ void layernorm_warp_kernel(const void *__restrict__ in_, int rows,
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
   float v[VPL];
-  if constexpr (F32IN) {
-    const float *src = static_cast<const float *>(in_) + row * W;
 #pragma unroll
-    for (int q = 0; q < VPL / 4; ++q) {
-      const float4 f = *reinterpret_cast<const float4 *>(src + q * 128 + lane * 4);
-      v[4 * q] = f.x;
-      v[4 * q + 1] = f.y;
-      v[4 * q + 2] = f.z;
-      v[4 * q + 3] = f.w;
-    }
-  } else {
-    const __nv_bfloat16 *src = static_cast<const __nv_bfloat16 *>(in_) + row * W;
-#pragma unroll
-    for (int q = 0; q < VPL / 4; ++q) {
-      const uint2 u = *reinterpret_cast<const uint2 *>(src + q * 128 + lane * 4);
-      const float2 f0 = unpack_bf16x2(u.x), f1 = unpack_bf16x2(u.y);
-      v[4 * q] = f0.x;
-      v[4 * q + 1] = f0.y;
-      v[4 * q + 2] = f1.x;
-      v[4 * q + 3] = f1.y;
-    }
+  for (int q = 0; q < VPL / 4; ++q) {
+    float f[4];
+    load4<IN>(in_, row * W + q * 128 + lane * 4, f);
+    v[4 * q] = f[0];
+    v[4 * q + 1] = f[1];
+    v[4 * q + 2] = f[2];
+    v[4 * q + 3] = f[3];
   }
   float s = 0.0f;
 #pragma unroll
@@ -187,8 +193,16 @@ __global__ void layernorm_warp_kernel(const void *__restrict__ in_, int rows,
       *reinterpret_cast<uint32_t *>(out8 + row * W + c) = uint32_t(a.__x) | (uint32_t(b.__x) << 8) |
                                                             (uint32_t(c2.__x) << 16) | (uint32_t(d.__x) << 24);
     }
-    if (out_f32)
-      *reinterpret_cast<float4 *>(out_f32 + row * W + c) = make_float4(r[0], r[1], r[2], r[3]);
+    if (out_res) {
+      if constexpr (RES == Fmt::F16) {
+        const __half2 h0 = __floats2half2_rn(r[0], r[1]), h1 = __floats2half2_rn(r[2], r[3]);
+        *reinterpret_cast<uint2 *>(static_cast<__half *>(out_res) + row * W + c) =
+            make_uint2(*reinterpret_cast<const uint32_t *>(&h0), *reinterpret_cast<const uint32_t *>(&h1));
+      } else {
+        *reinterpret_cast<float4 *>(static_cast<float *>(out_res) + row * W + c) =
+            make_float4(r[0], r[1], r[2], r[3]);
+      }
+    }
   }
 }
 
@@ -247,44 +261,64 @@ __global__ void layernorm_block_kernel(const __nv_bfloat16 *__restrict__ in, int
   }
 }
 
-template <int VPL>
-static void ln_warp(const void *in, bool f32in, int rows, const float *gamma, const float *beta,
-                    float eps, const float *multT, const float *addT, __nv_bfloat16 *out,
-                    float *out_f32, uint8_t *out8, const float *scale8, cudaStream_t s) {
+template <int VPL, Fmt IN>
+static void ln_warp_in(const void *in, int rows, const float *gamma, const float *beta, float eps,
+                       const float *multT, const float *addT, __nv_bfloat16 *out, void *out_res,
+                       Fmt res_fmt, uint8_t *out8, const float *scale8, cudaStream_t s) {
   const int wpb = 8;
   const unsigned grid = static_cast<unsigned>((rows + wpb - 1) / wpb);
-  if (f32in)
-    layernorm_warp_kernel<VPL, true><<<grid, 32 * wpb, 0, s>>>(in, rows, gamma, beta, eps, multT,
-                                                               addT, out, out_f32, out8, scale8);
+  if (res_fmt == Fmt::F16)
+    layernorm_warp_kernel<VPL, IN, Fmt::F16><<<grid, 32 * wpb, 0, s>>>(
+        in, rows, gamma, beta, eps, multT, addT, out, out_res, out8, scale8);
   else
-    layernorm_warp_kernel<VPL, false><<<grid, 32 * wpb, 0, s>>>(in, rows, gamma, beta, eps, multT,
-                                                                addT, out, out_f32, out8, scale8);
+    layernorm_warp_kernel<VPL, IN, Fmt::F32><<<grid, 32 * wpb, 0, s>>>(
+        in, rows, gamma, beta, eps, multT, addT, out, out_res, out8, scale8);
+}
+
+template <int VPL>
+static void ln_warp(const void *in, Fmt in_fmt, int rows, const float *gamma, const float *beta,
+                    float eps, const float *multT, const float *addT, __nv_bfloat16 *out,
+                    void *out_res, Fmt res_fmt, uint8_t *out8, const float *scale8, cudaStream_t s) {
+  switch (in_fmt) {
+  case Fmt::F32:
+    ln_warp_in<VPL, Fmt::F32>(in, rows, gamma, beta, eps, multT, addT, out, out_res, res_fmt, out8, scale8, s);
+    return;
+  case Fmt::F16:
+    ln_warp_in<VPL, Fmt::F16>(in, rows, gamma, beta, eps, multT, addT, out, out_res, res_fmt, out8, scale8, s);
+    return;
+  default:
+    ln_warp_in<VPL, Fmt::BF16>(in, rows, gamma, beta, eps, multT, addT, out, out_res, res_fmt, out8, scale8, s);
+    return;
+  }
+}
+
+void launch_layernorm_q(const void *in, Fmt in_fmt, int rows, int width, const float *gamma,
+                        const float *beta, float eps, const float *multT, const float *addT,
+                        __nv_bfloat16 *out, void *out_res, Fmt res_fmt, uint8_t *out8,
+                        const float *scale8, cudaStream_t s) {
+#define MFB_LN(V) ln_warp<V>(in, in_fmt, rows, gamma, beta, eps, multT, addT, out, out_res, res_fmt, out8, scale8, s)
+  switch (width) {
+  case 128: MFB_LN(4); return;
+  case 256: MFB_LN(8); return;
+  case 512: MFB_LN(16); return;
+  case 1024: MFB_LN(32); return;
+  default: return;
+  }
+#undef MFB_LN
 }
 
 void launch_layernorm(const void *in, bool in_f32, int rows, int width, const float *gamma,
                       const float *beta, float eps, const float *multT, const float *addT,
                       __nv_bfloat16 *out, float *out_f32, cudaStream_t s) {
-  launch_layernorm_q(in, in_f32, rows, width, gamma, beta, eps, multT, addT, out, out_f32, nullptr,
-                     nullptr, s);
-}
-
-void launch_layernorm_q(const void *in, bool in_f32, int rows, int width, const float *gamma,
-                        const float *beta, float eps, const float *multT, const float *addT,
-                        __nv_bfloat16 *out, float *out_f32, uint8_t *out8, const float *scale8,
-                        cudaStream_t s) {
-  switch (width) {
-  case 128: ln_warp<4>(in, in_f32, rows, gamma, beta, eps, multT, addT, out, out_f32, out8, scale8, s); return;
-  case 256: ln_warp<8>(in, in_f32, rows, gamma, beta, eps, multT, addT, out, out_f32, out8, scale8, s); return;
-  case 512: ln_warp<16>(in, in_f32, rows, gamma, beta, eps, multT, addT, out, out_f32, out8, scale8, s); return;
-  case 1024: ln_warp<32>(in, in_f32, rows, gamma, beta, eps, multT, addT, out, out_f32, out8, scale8, s); return;
-  default:
+  if (width != 128 && width != 256 && width != 512 && width != 1024) {
     // wide bf16 rows (smolgen's H*g); no gates, no fp32 output on this path
     layernorm_block_kernel<<<rows, 256, 0, s>>>(static_cast<const __nv_bfloat16 *>(in), width,
                                                 gamma, beta, eps, out);
     return;
   }
+  launch_layernorm_q(in, in_f32 ? Fmt::F32 : Fmt::BF16, rows, width, gamma, beta, eps, multT, addT,
+                     out, out_f32, Fmt::F32, nullptr, nullptr, s);
 }
-
 
 // ------------------------------------------------------------------ split-K reduce
 // out[r] = LN(act(sum_s part[s][r] + bias)) for rows of width 32*VPL; one warp
@@ -519,7 +553,9 @@ __global__ void absmax_kernel(const T *__restrict__ x, long long n, float *__res
   for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
        i += static_cast<long long>(gridDim.x) * blockDim.x) {
     float v;
-    if constexpr (sizeof(T) == 2) v = __bfloat162float(x[i]); else v = x[i];
+    if constexpr (std::is_same_v<T, __nv_bfloat16>) v = __bfloat162float(x[i]);
+    else if constexpr (std::is_same_v<T, __half>) v = __half2float(x[i]);
+    else v = x[i];
     m = fmaxf(m, fabsf(v));
   }
 #pragma unroll
@@ -527,9 +563,11 @@ __global__ void absmax_kernel(const T *__restrict__ x, long long n, float *__res
   if ((threadIdx.x & 31) == 0) atomicMax(reinterpret_cast<int *>(slot), __float_as_int(m));
 }
 
-void launch_absmax(const void *x, bool f32, long long n, float *slot, cudaStream_t s) {
-  if (f32)
+void launch_absmax(const void *x, Fmt fmt, long long n, float *slot, cudaStream_t s) {
+  if (fmt == Fmt::F32)
     absmax_kernel<float><<<296, 256, 0, s>>>(static_cast<const float *>(x), n, slot);
+  else if (fmt == Fmt::F16)
+    absmax_kernel<__half><<<296, 256, 0, s>>>(static_cast<const __half *>(x), n, slot);
   else
     absmax_kernel<__nv_bfloat16><<<296, 256, 0, s>>>(static_cast<const __nv_bfloat16 *>(x), n, slot);
 }

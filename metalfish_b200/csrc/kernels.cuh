@@ -2,6 +2,7 @@
 // (The large projections run through the tcgen05 GEMM in gemm_sm100.cuh.)
 #pragma once
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -13,6 +14,9 @@ constexpr int kSquares = 64;
 constexpr int kPolicy = 1858;
 constexpr int kPeInputs = 12 * kSquares;  // 12 position planes, square-major
 constexpr int kEmbIn = 192;               // 112 planes + 64 PE, padded to 3 x 64
+
+// Element formats of activation buffers.
+enum class Fmt : int { BF16 = 0, F32 = 1, F16 = 2 };
 
 // Input unpack: packed (mask, value) planes -> X0[M, 192] (planes in columns
 // 0..111, columns 176..191 zeroed; columns 112..175 are filled by pe_concat)
@@ -40,12 +44,14 @@ bool launch_splitk_act_ln(const float *part, int splits, long long stride, int r
                           const float *bias, int act, const float *gamma, const float *beta,
                           float eps, __nv_bfloat16 *out, cudaStream_t s);
 
-// Same, with an optional e4m3 copy out8 = value / *scale8 (FP8 GEMM input);
-// `out` may be null when only the fp32 / e4m3 copies are needed.
-void launch_layernorm_q(const void *in, bool in_f32, int rows, int width, const float *gamma,
+// Same, with the input in any Fmt, the full-precision copy `out_res` in
+// `res_fmt` (F32 or F16: the residual stream) and an optional e4m3 copy
+// out8 = value / *scale8 (FP8 GEMM input); `out` may be null when only the
+// other copies are needed. Widths 128/256/512/1024 only.
+void launch_layernorm_q(const void *in, Fmt in_fmt, int rows, int width, const float *gamma,
                         const float *beta, float eps, const float *multT, const float *addT,
-                        __nv_bfloat16 *out, float *out_f32, uint8_t *out8, const float *scale8,
-                        cudaStream_t s);
+                        __nv_bfloat16 *out, void *out_res, Fmt res_fmt, uint8_t *out8,
+                        const float *scale8, cudaStream_t s);
 
 // 64-token attention per (position, head) with the smolgen bias added before
 // the softmax: ctx[b*64+q, h*dh:..] = softmax(Q K^T / sqrt(dh) + bias) V.
@@ -55,9 +61,9 @@ void launch_attention(const __nv_bfloat16 *qkv, long long ldq, const __nv_bfloat
                       int batch, int heads, int d, __nv_bfloat16 *ctx, cudaStream_t s,
                       uint8_t *ctx8 = nullptr, const float *scale8 = nullptr);
 
-// FP8 calibration: *slot = max(*slot, max|x|) over n bf16 or fp32 values; and
-// scales[i] = absmax[i] / 448.
-void launch_absmax(const void *x, bool f32, long long n, float *slot, cudaStream_t s);
+// FP8 calibration: *slot = max(*slot, max|x|) over n values of format `fmt`;
+// and scales[i] = absmax[i] / 448.
+void launch_absmax(const void *x, Fmt fmt, long long n, float *slot, cudaStream_t s);
 void launch_absmax_to_scale(const float *absmax, int n, float *scales, cudaStream_t s);
 
 // Attention-policy logits: raw = q k^T / sqrt(dp) (64x64), the 8x24 promotion

@@ -231,7 +231,8 @@ struct Shard {  // one GPU
   float *values;
   __nv_bfloat16 *x0, *p, *peo, *X, *X1, *QKV, *C, *S1, *S2pre, *S2, *BIAS, *CTX, *H, *E, *QK,
       *VM, *VH;
-  float *Xf, *X1f, *T, *SK;  // fp32 residual stream (LN outputs) and pre-LN sums
+  __half *Xh, *X1h;  // fp16 residual stream (LN outputs; the residual GEMMs add into it in place)
+  float *T, *SK;     // fp32 embedding sum, split-K partials
   uint8_t *X8, *X1_8, *CTX8, *H8;  // e4m3 GEMM inputs (FP8 handles)
   float *scales, *absmax;    // per-tensor activation scales / calibration maxima
   float *policy, *wdl, *mlh;
@@ -519,9 +520,9 @@ void alloc_workspace(Shard &S, const mfb200_net_desc &n, int max_batch, bool fp8
       {reinterpret_cast<void **>(&S.X), M * d * 2},
       {reinterpret_cast<void **>(&S.X1), M * d * 2},
       {reinterpret_cast<void **>(&S.T), M * d * 4},
-      {reinterpret_cast<void **>(&S.Xf), M * d * 4},
+      {reinterpret_cast<void **>(&S.Xh), M * d * 2},
       {reinterpret_cast<void **>(&S.SK), size_t(kMaxSplits) * B * n.smolgen_hidden * 4},
-      {reinterpret_cast<void **>(&S.X1f), M * d * 4},
+      {reinterpret_cast<void **>(&S.X1h), M * d * 2},
       {reinterpret_cast<void **>(&S.QKV), M * 3 * d * 2},
       {reinterpret_cast<void **>(&S.C), M * n.smolgen_compress * 2},
       {reinterpret_cast<void **>(&S.S1), B * n.smolgen_hidden * 2},
@@ -623,10 +624,10 @@ std::unique_ptr<Shard::Plan> build_plan(Shard &S, const mfb200_net_desc &n, int 
              f8o = fp8_plan && (fp8_mask & 4), f8f1 = fp8_plan && (fp8_mask & 8),
              f8f2 = fp8_plan && (fp8_mask & 16);
   const long long Md = static_cast<long long>(B) * 64 * n.embedding;
-  auto probe = [&](const char *name, const void *x, bool f32, long long cnt, int slot) {
+  auto probe = [&](const char *name, const void *x, Fmt fmt, long long cnt, int slot) {
     if (cal)
-      add_fn(*P, name, 0, [&S, x, f32, cnt, slot](cudaStream_t s) {
-        launch_absmax(x, f32, cnt, S.absmax + slot, s);
+      add_fn(*P, name, 0, [&S, x, fmt, cnt, slot](cudaStream_t s) {
+        launch_absmax(x, fmt, cnt, S.absmax + slot, s);
       });
   };
   const int M = B * 64, d = n.embedding, dp = n.policy_d, H = n.heads;
@@ -654,10 +655,10 @@ std::unique_ptr<Shard::Plan> build_plan(Shard &S, const mfb200_net_desc &n, int 
     add_gemm(*P, S, "emb_dense", S.x0, kEmbIn, W.emb, a);
   }
   add_fn(*P, "emb_ln_gates", 0, [&S, &W, M, d, eps, f8e](cudaStream_t s) {
-    launch_layernorm_q(S.T, true, M, d, W.ln_emb_g, W.ln_emb_b, eps, W.multT, W.addT,
-                       f8e ? nullptr : S.X, S.Xf, f8e ? S.X8 : nullptr, S.scales + 0, s);
+    launch_layernorm_q(S.T, Fmt::F32, M, d, W.ln_emb_g, W.ln_emb_b, eps, W.multT, W.addT,
+                       f8e ? nullptr : S.X1, S.X1h, Fmt::F16, f8e ? S.X1_8 : nullptr, S.scales + 0, s);
   });
-  probe("absmax_emb_x", S.Xf, true, Md, 0);
+  probe("absmax_emb_x", S.X1h, Fmt::F16, Md, 0);
   {
     GemmArgs a = base_args(S, M, n.emb_dff, d);
     a.bias = W.b_effn1;
@@ -670,19 +671,18 @@ std::unique_ptr<Shard::Plan> build_plan(Shard &S, const mfb200_net_desc &n, int 
       a.out = S.H8;
       a.out_fp8 = 1;
       a.out_scale_ptr = S.scales + 1;
-      add_gemm(*P, S, "emb_ffn1", S.X8, d, W.effn1_8, a);
+      add_gemm(*P, S, "emb_ffn1", S.X1_8, d, W.effn1_8, a);
     } else {
-      add_gemm(*P, S, "emb_ffn1", S.X, d, W.effn1, a);
+      add_gemm(*P, S, "emb_ffn1", S.X1, d, W.effn1, a);
     }
-    probe("absmax_emb_h", S.H, false, static_cast<long long>(M) * n.emb_dff, 1);
+    probe("absmax_emb_h", S.H, Fmt::BF16, static_cast<long long>(M) * n.emb_dff, 1);
     GemmArgs b = base_args(S, M, d, n.emb_dff);
-    b.mode = kEpiResid;
+    // x1 (fp16 stream) += alpha * ffn (in place; the LN below reads the sum)
+    b.mode = kEpiAccum;
     b.bias = W.b_effn2;
-    b.resid = S.Xf;
-    b.ldr = d;
     b.alpha = alpha;
-    b.out = S.T;
-    b.out_f32 = 1;
+    b.out = S.X1h;
+    b.out_f16 = 1;
     b.ldo = d;
     if (f8e) {
       b.a_scale_ptr = S.scales + 1;
@@ -693,10 +693,10 @@ std::unique_ptr<Shard::Plan> build_plan(Shard &S, const mfb200_net_desc &n, int 
     }
   }
   add_fn(*P, "emb_ffn_ln", 0, [&S, &W, M, d, eps, f8q](cudaStream_t s) {
-    launch_layernorm_q(S.T, true, M, d, W.ln_effn_g, W.ln_effn_b, eps, nullptr, nullptr,
-                       f8q ? nullptr : S.X, S.Xf, f8q ? S.X8 : nullptr, S.scales + slot_x(0), s);
+    launch_layernorm_q(S.X1h, Fmt::F16, M, d, W.ln_effn_g, W.ln_effn_b, eps, nullptr, nullptr,
+                       f8q ? nullptr : S.X, S.Xh, Fmt::F16, f8q ? S.X8 : nullptr, S.scales + slot_x(0), s);
   });
-  probe("absmax_x", S.Xf, true, Md, slot_x(0));
+  probe("absmax_x", S.Xh, Fmt::F16, Md, slot_x(0));
   for (int k = 0; k < n.layers; ++k) {
     LayerW &Lw = W.layers[k];
     {
@@ -755,16 +755,15 @@ std::unique_ptr<Shard::Plan> build_plan(Shard &S, const mfb200_net_desc &n, int 
       launch_attention(S.QKV, 3LL * d, S.BIAS, B, H, d, S.CTX, s, f8o ? S.CTX8 : nullptr,
                        S.scales + slot_ctx(k));
     });
-    probe("absmax_ctx", S.CTX, false, Md, slot_ctx(k));
+    probe("absmax_ctx", S.CTX, Fmt::BF16, Md, slot_ctx(k));
     {
       GemmArgs a = base_args(S, M, d, d);
-      a.mode = kEpiResid;
+      // x (fp16 stream) += alpha * attention output (in place; ln1 reads the sum)
+      a.mode = kEpiAccum;
       a.bias = Lw.b_o;
-      a.resid = S.Xf;
-      a.ldr = d;
       a.alpha = alpha;
-      a.out = S.T;
-      a.out_f32 = 1;
+      a.out = S.Xh;
+      a.out_f16 = 1;
       a.ldo = d;
       if (f8o) {
         a.a_scale_ptr = S.scales + slot_ctx(k);
@@ -775,10 +774,10 @@ std::unique_ptr<Shard::Plan> build_plan(Shard &S, const mfb200_net_desc &n, int 
       }
     }
     add_fn(*P, "ln1", 0, [&S, &Lw, M, d, eps, f8f1, k](cudaStream_t s) {
-      launch_layernorm_q(S.T, true, M, d, Lw.ln1_g, Lw.ln1_b, eps, nullptr, nullptr,
-                         f8f1 ? nullptr : S.X1, S.X1f, f8f1 ? S.X1_8 : nullptr, S.scales + slot_x1(k), s);
+      launch_layernorm_q(S.Xh, Fmt::F16, M, d, Lw.ln1_g, Lw.ln1_b, eps, nullptr, nullptr,
+                         f8f1 ? nullptr : S.X1, S.X1h, Fmt::F16, f8f1 ? S.X1_8 : nullptr, S.scales + slot_x1(k), s);
     });
-    probe("absmax_x1", S.X1f, true, Md, slot_x1(k));
+    probe("absmax_x1", S.X1h, Fmt::F16, Md, slot_x1(k));
     {
       GemmArgs a = base_args(S, M, n.dff, d);
       a.bias = Lw.b_f1;
@@ -797,15 +796,14 @@ std::unique_ptr<Shard::Plan> build_plan(Shard &S, const mfb200_net_desc &n, int 
       } else {
         add_gemm(*P, S, "ffn1", S.X1, d, Lw.f1, a);
       }
-      probe("absmax_h", S.H, false, static_cast<long long>(M) * n.dff, slot_h(k));
+      probe("absmax_h", S.H, Fmt::BF16, static_cast<long long>(M) * n.dff, slot_h(k));
       GemmArgs b = base_args(S, M, d, n.dff);
-      b.mode = kEpiResid;
+      // x1 (fp16 stream) += alpha * ffn (in place; ln2 reads the sum)
+      b.mode = kEpiAccum;
       b.bias = Lw.b_f2;
-      b.resid = S.X1f;
-      b.ldr = d;
       b.alpha = alpha;
-      b.out = S.T;
-      b.out_f32 = 1;
+      b.out = S.X1h;
+      b.out_f16 = 1;
       b.ldo = d;
       if (f8f2) {
         b.a_scale_ptr = S.scales + slot_h(k);
@@ -821,10 +819,10 @@ std::unique_ptr<Shard::Plan> build_plan(Shard &S, const mfb200_net_desc &n, int 
       const bool last = k + 1 == n.layers;
       const bool q8 = f8q && !last;
       add_fn(*P, "ln2", 0, [&S, &Lw, M, d, eps, q8, k](cudaStream_t s) {
-        launch_layernorm_q(S.T, true, M, d, Lw.ln2_g, Lw.ln2_b, eps, nullptr, nullptr,
-                           q8 ? nullptr : S.X, S.Xf, q8 ? S.X8 : nullptr, S.scales + slot_x(k + 1), s);
+        launch_layernorm_q(S.X1h, Fmt::F16, M, d, Lw.ln2_g, Lw.ln2_b, eps, nullptr, nullptr,
+                           q8 ? nullptr : S.X, S.Xh, Fmt::F16, q8 ? S.X8 : nullptr, S.scales + slot_x(k + 1), s);
       });
-      if (!last) probe("absmax_x", S.Xf, true, Md, slot_x(k + 1));
+      if (!last) probe("absmax_x", S.Xh, Fmt::F16, Md, slot_x(k + 1));
     }
   }
   {

@@ -18,7 +18,8 @@ def mish(x):
     return x * np.tanh(np.log1p(np.exp(x)))
 
 
-def run_gemm(M, N, K, bn, mode=0, act=0, bias=True, alpha=0.5, seed=0, out_f32=False, k_splits=1):
+def run_gemm(M, N, K, bn, mode=0, act=0, bias=True, alpha=0.5, seed=0, out_f32=False, k_splits=1,
+             out_f16=False):
     rng = np.random.default_rng(seed)
     A = rng.standard_normal((M, K), dtype=np.float32)
     W = rng.standard_normal((N, K), dtype=np.float32) / np.float32(np.sqrt(K))
@@ -31,20 +32,23 @@ def run_gemm(M, N, K, bn, mode=0, act=0, bias=True, alpha=0.5, seed=0, out_f32=F
         bias, out_f32 = False, True
     b = b if bias else None
     out = np.zeros((k_splits, M, N), np.float32 if out_f32 else np.uint16)
+    fmt = 2 if out_f16 else int(out_f32)
     st = ctypes.c_uint(0)
     rc = lib().mfb200_debug_gemm(M, N, K, bn, 0, _p(Ab), _p(Wb), _p(b), mode, act, _p(R),
                                  ctypes.c_float(alpha), _p(g), _p(be), ctypes.c_float(1e-3),
-                                 None, ctypes.c_float(1.0), int(out_f32), k_splits, _p(out),
+                                 None, ctypes.c_float(1.0), fmt, k_splits, _p(out),
                                  ctypes.byref(st))
     assert rc == 0, f"rc={rc} status={st.value}"
     acc = from_bf16_bits(Ab).astype(np.float64) @ from_bf16_bits(Wb).astype(np.float64).T
     if b is not None:
         acc = acc + b
-    if mode == 1:
-        ref = R + alpha * acc
+    if mode in (1, 3):
+        # in place (3), the residual is first rounded to the output format
+        ref = (R.astype(np.float16).astype(np.float64) if (mode == 3 and out_f16) else R) + alpha * acc
     else:
         ref = {0: acc, 2: np.maximum(acc, 0) ** 2, 5: acc / (1 + np.exp(-acc)), 6: mish(acc)}[act]
-    got = out.sum(0) if out_f32 else from_bf16_bits(out[0])
+    got = out.sum(0) if out_f32 else (out[0].view(np.float16).astype(np.float32) if out_f16 else
+                                      from_bf16_bits(out[0]))
     return got, ref
 
 
@@ -82,6 +86,21 @@ def test_gemm_residual_fp32_out():
     np.testing.assert_allclose(got, ref, rtol=1e-4, atol=1e-4)
 
 
+@pytest.mark.parametrize("M,N,K,bn", [(300, 1024, 1024, 256), (128, 768, 1536, 128), (517, 64, 192, 64)])
+def test_gemm_accumulate_in_place(M, N, K, bn):
+    """The residual GEMM of the forward: the fp32 residual stream is the output
+    buffer and the TMA unit adds alpha*(A.W^T + bias) into it."""
+    got, ref = run_gemm(M, N, K, bn, mode=3, alpha=0.427, out_f32=True)
+    np.testing.assert_allclose(got, ref, rtol=1e-4, atol=1e-4)
+
+
+@pytest.mark.parametrize("M,N,K,bn", [(300, 1024, 1024, 256), (517, 64, 192, 64)])
+def test_gemm_accumulate_in_place_fp16(M, N, K, bn):
+    """fp16 residual stream: one fp16 rounding of the sum (2^-11 relative)."""
+    got, ref = run_gemm(M, N, K, bn, mode=3, alpha=0.427, out_f16=True)
+    np.testing.assert_allclose(got, ref, rtol=2e-3, atol=2e-3)
+
+
 @pytest.mark.parametrize("M,K,splits", [(1024, 2048, 16), (64, 2048, 32), (300, 1024, 5)])
 def test_gemm_split_k(M, K, splits):
     """Split-K partial products sum to the full product (smolgen dense1 path)."""
@@ -110,3 +129,31 @@ def test_gemm_fp8(M, N, K, bn):
     assert rc == 0, f"rc={rc} status={st.value}"
     ref = (from_e4m3_bits(a8).astype(np.float64) @ from_e4m3_bits(w8).astype(np.float64).T) * a_scale * cs + b
     np.testing.assert_allclose(out[0], ref, rtol=1e-4, atol=1e-3)
+
+
+@pytest.mark.parametrize("M,N,K,bn", [(128, 256, 256, 256), (300, 512, 1024, 256), (1000, 1024, 1536, 256),
+                                      (200, 128, 512, 128), (4096, 1024, 1024, 256)])
+def test_gemm_residual_layernorm(M, N, K, bn):
+    """Fused residual + LayerNorm epilogue; a row spans N/bn cluster CTAs that
+    exchange row statistics (the deepnorm LN(x + alpha*f) of every encoder
+    layer)."""
+    rng = np.random.default_rng(3)
+    A = rng.standard_normal((M, K), dtype=np.float32)
+    W = rng.standard_normal((N, K), dtype=np.float32) / np.float32(np.sqrt(K))
+    b = (0.1 * rng.standard_normal(N)).astype(np.float32)
+    R = (rng.standard_normal((M, N)) + 0.3).astype(np.float32)
+    g = (1 + 0.1 * rng.standard_normal(N)).astype(np.float32)
+    be = (0.1 * rng.standard_normal(N)).astype(np.float32)
+    alpha = 0.427
+    Ab, Wb = to_bf16_bits(A), to_bf16_bits(W)
+    out = np.zeros((M, N), np.float32)
+    out16 = np.zeros((M, N), np.uint16)
+    st = ctypes.c_uint(0)
+    rc = lib().mfb200_debug_gemm_ln(M, N, K, bn, _p(Ab), _p(Wb), _p(b), _p(R), ctypes.c_float(alpha),
+                                    _p(g), _p(be), ctypes.c_float(1e-3), _p(out), _p(out16), ctypes.byref(st))
+    assert rc == 0, f"rc={rc} status={st.value}"
+    y = R + alpha * (from_bf16_bits(Ab).astype(np.float64) @ from_bf16_bits(Wb).astype(np.float64).T + b)
+    mu = y.mean(1, keepdims=True)
+    ref = (y - mu) / np.sqrt(y.var(1, keepdims=True) + 1e-3) * g + be
+    np.testing.assert_allclose(out, ref, rtol=1e-3, atol=2e-3)
+    np.testing.assert_allclose(from_bf16_bits(out16), ref, rtol=1e-2, atol=2e-2)
