@@ -14,7 +14,7 @@ extern "C" {
 #endif
 
 /* out[M,N] (bf16 bits) = epilogue(A[M,K] . W[N,K]^T) through the tcgen05 GEMM.
- * A/W are bf16 bits (fp8 = 0) or e4m3 bytes (fp8 = 1); resid is fp32; out is
+ * A/W are bf16 bits (fp8 = 0), e4m3 bytes (fp8 = 1) or fp16 bits (fp8 = 2); resid is fp32; out is
  * fp32 when out_f32 = 1, fp16 bits when out_f32 = 2, else bf16 bits. mode: 0
  * store act(scale*acc+bias), 1 resid + alpha*(scale*acc+bias), 3 the same
  * computed in place (the output buffer starts as resid, rounded to the output

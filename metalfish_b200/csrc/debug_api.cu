@@ -32,7 +32,7 @@ extern "C" int mfb200_debug_gemm(int M, int N, int K, int bn, int fp8, const voi
   (void)ln_beta;
   (void)ln_eps;
   const int sp = k_splits > 1 ? k_splits : 1;
-  const size_t es = fp8 ? 1 : 2;
+  const size_t es = fp8 == 1 ? 1 : 2;  // fp8: 0 bf16, 1 e4m3, 2 fp16 operands
   DevBuf dA, dW, dB, dR, dO, dG, dBe, dCs, dS;
   if (!dA.alloc(size_t(M) * K * es) || !dW.alloc(size_t(N) * K * es) || !dB.alloc(N * 4) ||
       !dR.alloc(size_t(M) * N * 4) || !dO.alloc(size_t(sp) * M * N * 4) || !dG.alloc(N * 4) ||
@@ -74,7 +74,8 @@ extern "C" int mfb200_debug_gemm(int M, int N, int K, int bn, int fp8, const voi
   a.out_f32 = out_f32 == 1;
   a.out_f16 = out_f32 == 2;  // 2: fp16 output
   GemmLaunch g;
-  if (plan_gemm(g, dA.p, K, dW.p, K, bn, fp8 != 0, a)) return 2;
+  a.ab_f16 = fp8 == 2;
+  if (plan_gemm(g, dA.p, K, dW.p, K, bn, fp8 == 1, a)) return 2;
   if (launch_gemm(g, 0) != cudaSuccess) return 3;
   if (cudaDeviceSynchronize() != cudaSuccess) return 4;
   cudaMemcpy(out, dO.p, size_t(sp) * M * N * (sp > 1 || out_f32 == 1 ? 4 : 2), cudaMemcpyDeviceToHost);

@@ -42,6 +42,7 @@ enum Act : int {
 
 struct GemmArgs {
   int M, N, K;
+  int ab_f16;                 // 16-bit operands are fp16 (else bf16); both A and W
   int mode, act;
   const float *bias;          // [N] or nullptr
   void *out;                  // [M, ldo] bf16 (or e4m3 / fp32)
@@ -128,6 +129,7 @@ struct EpiCtx {
   uint32_t xtiles;     // row-statistics exchanges completed (phase parity)
   uint32_t rank;       // CTA rank in the cluster
   uint8_t *stage2;     // second staging tile (kEpiResidLN kernels)
+  uint32_t chunks;     // chunks staged so far (selects the half of a 2-byte-output tile)
 };
 
 __device__ __forceinline__ uint32_t pack_bf16x2_f(float a, float b) {
@@ -201,8 +203,15 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs &args, EpiCtx &e, u
     if (c + 64 < BN) tmem_ld32(taddr + c + 64, raw);  // warp-collective prefetch
     const int nb = n0 + c;
     if (nb >= args.N) continue;
-    // the previous chunk's TMA store must have finished reading the tile
-    if (lane == 0) bulk_wait_read0();
+    // A chunk of 2- or 1-byte outputs fills at most half of the 4 KB tile, so
+    // the two halves alternate and only the store before last must have
+    // finished reading; fp32 chunks (and residual tiles) use the whole tile.
+    const bool halves = !f32 && MODE != kEpiResid;
+    uint8_t *st = halves ? e.stage + (e.chunks & 1u) * (kStageBytes / 2) : e.stage;
+    ++e.chunks;
+    if (lane == 0) {
+      if (halves) bulk_wait_read1(); else bulk_wait_read0();
+    }
     __syncwarp();
     if (ks < 0) {
       if (a_scale != 1.0f) {
@@ -251,18 +260,18 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs &args, EpiCtx &e, u
 #pragma unroll
       for (int j = 0; j < 32; ++j) v[j] = act_t<ACT>(v[j]);
     }
-    stage_row(args, e.stage, lane, v, f32, out_is);
+    stage_row(args, st, lane, v, f32, out_is);
     fence_proxy_async_smem();
     __syncwarp();
     if (lane == 0) {
       if (MODE == kEpiAccum)
-        tma_reduce_add_2d(e.out, e.stage, nb, row0);
+        tma_reduce_add_2d(e.out, st, nb, row0);
       else if (ks >= 0)
-        tma_store_3d(e.out, e.stage, nb, row0, ks);
+        tma_store_3d(e.out, st, nb, row0, ks);
       else if (args.out2 && nb >= args.split)
-        tma_store_2d(e.out2, e.stage, nb - args.split, row0);
+        tma_store_2d(e.out2, st, nb - args.split, row0);
       else
-        tma_store_2d(e.out, e.stage, nb, row0);
+        tma_store_2d(e.out, st, nb, row0);
       bulk_commit();
     }
   }
@@ -572,8 +581,9 @@ __global__ void __launch_bounds__(64 + 32 * kEpiWarps, 1)
   } else if (warp == 1) {
     if (lane == 0) {
       // ---------------------------------------------------------- MMA issuer
-      constexpr uint32_t idesc =
-          FP8 ? umma_idesc(128, BN, kFmtE4M3, kFmtE4M3) : umma_idesc(128, BN, kFmtBF16, kFmtBF16);
+      const uint32_t idesc = FP8 ? umma_idesc(128, BN, kFmtE4M3, kFmtE4M3)
+                                 : (args.ab_f16 ? umma_idesc(128, BN, kFmtF16, kFmtF16)
+                                                : umma_idesc(128, BN, kFmtBF16, kFmtBF16));
       int stage = 0;
       uint32_t round = 0;
       int local = 0;
@@ -630,7 +640,7 @@ __global__ void __launch_bounds__(64 + 32 * kEpiWarps, 1)
     const int group = (warp - 2) >> 2;   // which alternate 32-column chunks
     EpiCtx e{&tmOut, &tmOut2, &tmRes, stage_base + (warp - 2) * kStageBytes, &res_bars[warp - 2],
              0u, lane, abort_flag, &xbar[group], 0u, rank,
-             LN ? stage_base + (kEpiWarps + warp - 2) * kStageBytes : nullptr};
+             LN ? stage_base + (kEpiWarps + warp - 2) * kStageBytes : nullptr, 0u};
     if (lane == 0) {
       tma_prefetch_desc(&tmOut);
       if (args.out2) tma_prefetch_desc(&tmOut2);
@@ -643,10 +653,16 @@ __global__ void __launch_bounds__(64 + 32 * kEpiWarps, 1)
       const int ks = (!ln && splits > 1) ? u % splits : -1;
       const int acc = local & 1;
       const uint32_t aphase = (local >> 1) & 1;
-      if (!mbar_wait(&tfull[acc], aphase, args.status, kErrTimeoutEpilogue, abort_flag)) break;
-      tc_fence_after();
       const int m0 = (t / tiles_n) * S::BM;
       const int n0 = (t % tiles_n) * BN;
+      if (ks < 0 && lane < BN / 32 && n0 + 32 * lane < args.N) {
+        // the tile's bias / column scales (one 128-byte line per 32 columns)
+        // reach L1 while the accumulator is still being computed
+        if (args.bias) prefetch_l1(args.bias + n0 + 32 * lane);
+        if (args.col_scale) prefetch_l1(args.col_scale + n0 + 32 * lane);
+      }
+      if (!mbar_wait(&tfull[acc], aphase, args.status, kErrTimeoutEpilogue, abort_flag)) break;
+      tc_fence_after();
       const uint32_t taddr =
           tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
       const bool ok = epilogue_dispatch<BN, LN>(args, e, taddr, m0 + quarter * 32, n0, group, ks);

@@ -114,50 +114,57 @@ void launch_pe_concat(const __nv_bfloat16 *peo, int batch, int pe, __nv_bfloat16
 }
 
 // ------------------------------------------------------------------ layernorm
-template <Fmt F>
-__device__ __forceinline__ void load4(const void *base, long long i, float (&v)[4]) {
+// Loads of G consecutive values (G = 4 or 8) as fp32.
+template <Fmt F, int G>
+__device__ __forceinline__ void load_g(const void *base, long long i, float *v) {
   if constexpr (F == Fmt::F32) {
-    const float4 f = *reinterpret_cast<const float4 *>(static_cast<const float *>(base) + i);
-    v[0] = f.x; v[1] = f.y; v[2] = f.z; v[3] = f.w;
-  } else if constexpr (F == Fmt::F16) {
-    const uint2 u = *reinterpret_cast<const uint2 *>(static_cast<const __half *>(base) + i);
-    const float2 f0 = __half22float2(*reinterpret_cast<const __half2 *>(&u.x));
-    const float2 f1 = __half22float2(*reinterpret_cast<const __half2 *>(&u.y));
-    v[0] = f0.x; v[1] = f0.y; v[2] = f1.x; v[3] = f1.y;
+    const float4 *p = reinterpret_cast<const float4 *>(static_cast<const float *>(base) + i);
+#pragma unroll
+    for (int k = 0; k < G / 4; ++k) {
+      const float4 f = p[k];
+      v[4 * k] = f.x; v[4 * k + 1] = f.y; v[4 * k + 2] = f.z; v[4 * k + 3] = f.w;
+    }
   } else {
-    const uint2 u = *reinterpret_cast<const uint2 *>(static_cast<const __nv_bfloat16 *>(base) + i);
-    const float2 f0 = unpack_bf16x2(u.x), f1 = unpack_bf16x2(u.y);
-    v[0] = f0.x; v[1] = f0.y; v[2] = f1.x; v[3] = f1.y;
+    uint32_t w[G / 2];
+    if constexpr (G == 8) {
+      const uint4 u = *reinterpret_cast<const uint4 *>(static_cast<const uint16_t *>(base) + i);
+      w[0] = u.x; w[1] = u.y; w[2] = u.z; w[3] = u.w;
+    } else {
+      const uint2 u = *reinterpret_cast<const uint2 *>(static_cast<const uint16_t *>(base) + i);
+      w[0] = u.x; w[1] = u.y;
+    }
+#pragma unroll
+    for (int k = 0; k < G / 2; ++k) {
+      const float2 f = F == Fmt::F16 ? __half22float2(*reinterpret_cast<const __half2 *>(&w[k]))
+                                     : unpack_bf16x2(w[k]);
+      v[2 * k] = f.x;
+      v[2 * k + 1] = f.y;
+    }
   }
 }
 
-// One warp per row. Lane l owns the 4-column groups q*128 + 4l .. +3 for
-// q < VPL/4, so every load instruction of the warp reads contiguous bytes.
+// One warp per row of W = 32*VPL columns. Lane l owns the G-column groups
+// starting at q*32*G + l*G (G = 8 when W is a multiple of 256, else 4), so
+// each load and store instruction of the warp moves 32*G contiguous values
+// with 16-byte (fp16/bf16) accesses.
 template <int VPL, Fmt IN, Fmt RES>
-__global__ void layernorm_warp_kernel(const void *__restrict__ in_, int rows,
-                                      const float *__restrict__ gamma,
-                                      const float *__restrict__ beta, float eps,
-                                      const float *__restrict__ multT,
-                                      const float *__restrict__ addT,
-                                      __nv_bfloat16 *__restrict__ out,
-                                      void *__restrict__ out_res,
-                                      uint8_t *__restrict__ out8,
-                                      const float *__restrict__ scale8) {
+__global__ void __launch_bounds__(256)
+    layernorm_warp_kernel(const void *__restrict__ in_, int rows,
+                          const float *__restrict__ gamma, const float *__restrict__ beta,
+                          float eps, const float *__restrict__ multT,
+                          const float *__restrict__ addT, __nv_bfloat16 *__restrict__ out,
+                          void *__restrict__ out_res, uint8_t *__restrict__ out8,
+                          const float *__restrict__ scale8) {
   constexpr int W = 32 * VPL;
+  constexpr int G = (VPL % 8 == 0) ? 8 : 4;
+  constexpr int NG = VPL / G;  // groups per lane
   const int warps = blockDim.x >> 5;
   const long long row = static_cast<long long>(blockIdx.x) * warps + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
   float v[VPL];
 #pragma unroll
-  for (int q = 0; q < VPL / 4; ++q) {
-    float f[4];
-    load4<IN>(in_, row * W + q * 128 + lane * 4, f);
-    v[4 * q] = f[0];
-    v[4 * q + 1] = f[1];
-    v[4 * q + 2] = f[2];
-    v[4 * q + 3] = f[3];
-  }
+  for (int q = 0; q < NG; ++q) load_g<IN, G>(in_, row * W + q * 32 * G + lane * G, v + q * G);
   float s = 0.0f;
 #pragma unroll
   for (int i = 0; i < VPL; ++i) s += v[i];
@@ -176,31 +183,56 @@ __global__ void layernorm_warp_kernel(const void *__restrict__ in_, int rows,
   const int sqr = static_cast<int>(row % kSquares);
   const float inv8 = out8 ? 1.0f / __ldg(scale8) : 0.0f;
 #pragma unroll
-  for (int q = 0; q < VPL / 4; ++q) {
-    const int c = q * 128 + lane * 4;
-    float r[4];
+  for (int q = 0; q < NG; ++q) {
+    const int c = q * 32 * G + lane * G;
+    float r[G], g[G], b[G];
+    load_g<Fmt::F32, G>(gamma, c, g);
+    load_g<Fmt::F32, G>(beta, c, b);
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      float y = (v[4 * q + e] - mean) * inv * gamma[c + e] + beta[c + e];
-      if (multT) y = y * multT[sqr * W + c + e] + addT[sqr * W + c + e];
-      r[e] = y;
+    for (int e = 0; e < G; ++e) r[e] = (v[q * G + e] - mean) * inv * g[e] + b[e];
+    if (multT) {
+      float mt[G], at[G];
+      load_g<Fmt::F32, G>(multT, static_cast<long long>(sqr) * W + c, mt);
+      load_g<Fmt::F32, G>(addT, static_cast<long long>(sqr) * W + c, at);
+#pragma unroll
+      for (int e = 0; e < G; ++e) r[e] = r[e] * mt[e] + at[e];
     }
-    if (out)
-      *reinterpret_cast<uint2 *>(out + row * W + c) =
-          make_uint2(pack_bf16x2(r[0], r[1]), pack_bf16x2(r[2], r[3]));
+    const long long o = row * W + c;
+    if (out) {
+      uint32_t w[G / 2];
+#pragma unroll
+      for (int k = 0; k < G / 2; ++k) w[k] = pack_bf16x2(r[2 * k], r[2 * k + 1]);
+      if constexpr (G == 8) *reinterpret_cast<uint4 *>(out + o) = make_uint4(w[0], w[1], w[2], w[3]);
+      else *reinterpret_cast<uint2 *>(out + o) = make_uint2(w[0], w[1]);
+    }
     if (out8) {
-      const __nv_fp8_e4m3 a(r[0] * inv8), b(r[1] * inv8), c2(r[2] * inv8), d(r[3] * inv8);
-      *reinterpret_cast<uint32_t *>(out8 + row * W + c) = uint32_t(a.__x) | (uint32_t(b.__x) << 8) |
-                                                            (uint32_t(c2.__x) << 16) | (uint32_t(d.__x) << 24);
+      uint32_t w[G / 4];
+#pragma unroll
+      for (int k = 0; k < G / 4; ++k) {
+        const __nv_fp8_e4m3 a(r[4 * k] * inv8), bb(r[4 * k + 1] * inv8), c2(r[4 * k + 2] * inv8),
+            d(r[4 * k + 3] * inv8);
+        w[k] = uint32_t(a.__x) | (uint32_t(bb.__x) << 8) | (uint32_t(c2.__x) << 16) |
+               (uint32_t(d.__x) << 24);
+      }
+      if constexpr (G == 8) *reinterpret_cast<uint2 *>(out8 + o) = make_uint2(w[0], w[1]);
+      else *reinterpret_cast<uint32_t *>(out8 + o) = w[0];
     }
     if (out_res) {
       if constexpr (RES == Fmt::F16) {
-        const __half2 h0 = __floats2half2_rn(r[0], r[1]), h1 = __floats2half2_rn(r[2], r[3]);
-        *reinterpret_cast<uint2 *>(static_cast<__half *>(out_res) + row * W + c) =
-            make_uint2(*reinterpret_cast<const uint32_t *>(&h0), *reinterpret_cast<const uint32_t *>(&h1));
+        uint32_t w[G / 2];
+#pragma unroll
+        for (int k = 0; k < G / 2; ++k) {
+          const __half2 h = __floats2half2_rn(r[2 * k], r[2 * k + 1]);
+          w[k] = *reinterpret_cast<const uint32_t *>(&h);
+        }
+        __half *dst = static_cast<__half *>(out_res) + o;
+        if constexpr (G == 8) *reinterpret_cast<uint4 *>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+        else *reinterpret_cast<uint2 *>(dst) = make_uint2(w[0], w[1]);
       } else {
-        *reinterpret_cast<float4 *>(static_cast<float *>(out_res) + row * W + c) =
-            make_float4(r[0], r[1], r[2], r[3]);
+        float4 *dst = reinterpret_cast<float4 *>(static_cast<float *>(out_res) + o);
+#pragma unroll
+        for (int k = 0; k < G / 4; ++k)
+          dst[k] = make_float4(r[4 * k], r[4 * k + 1], r[4 * k + 2], r[4 * k + 3]);
       }
     }
   }

@@ -16,6 +16,7 @@
 //      -> out-proj + residual -> LN -> FFN1+act -> FFN2 + residual -> LN
 //   -> policy embedding+act -> wq|wk -> policy map
 //   -> value|moves-left per-square dense+act -> flattened dense+act -> output layers.
+#include <cuda_fp16.h>
 #include <cuda_fp8.h>
 
 #include <algorithm>
@@ -184,11 +185,12 @@ std::vector<int16_t> build_gather() {
 }
 
 // ------------------------------------------------------------ device state
-struct Mat {  // a weight matrix [rows, ld] on the device (bf16 or e4m3)
+struct Mat {  // a weight matrix [rows, ld] on the device (bf16, fp16 or e4m3)
   void *w = nullptr;
   const float *scale = nullptr;  // per-row (output channel) scale for e4m3
   int rows = 0, ld = 0;
   bool fp8 = false;
+  bool f16 = false;  // fp16: multiplies the fp16 residual stream directly
 };
 
 struct LayerW {
@@ -229,7 +231,7 @@ struct Shard {  // one GPU
   size_t ws_bytes = 0;
   uint64_t *masks;
   float *values;
-  __nv_bfloat16 *x0, *p, *peo, *X, *X1, *QKV, *C, *S1, *S2pre, *S2, *BIAS, *CTX, *H, *E, *QK,
+  __nv_bfloat16 *x0, *p, *peo, *QKV, *C, *S1, *S2pre, *S2, *BIAS, *CTX, *H, *E, *QK,
       *VM, *VH;
   __half *Xh, *X1h;  // fp16 residual stream (LN outputs; the residual GEMMs add into it in place)
   float *T, *SK;     // fp32 embedding sum, split-K partials
@@ -306,16 +308,22 @@ void put_f32(ArenaBuilder &ab, Layout &lay, T **field, const float *src, size_t 
   lay.fix.push_back({reinterpret_cast<void **>(field), off});
 }
 
-// bf16 matrix of `rows` x `ld` (zero padded), filled by `at(r, c)` for c < cols.
+// bf16 (or, with f16, fp16) matrix of `rows` x `ld` (zero padded), filled by
+// `at(r, c)` for c < cols.
 template <class F>
-void put_mat(ArenaBuilder &ab, Layout &lay, Mat &m, int rows, int cols, int ld, F at) {
+void put_mat(ArenaBuilder &ab, Layout &lay, Mat &m, int rows, int cols, int ld, F at,
+             bool f16 = false) {
   const size_t off = ab.add(size_t(rows) * ld * 2);
   uint16_t *dst = reinterpret_cast<uint16_t *>(ab.host.data() + off);
   for (int r = 0; r < rows; ++r)
-    for (int c = 0; c < ld; ++c) dst[size_t(r) * ld + c] = c < cols ? f2bf(at(r, c)) : 0;
+    for (int c = 0; c < ld; ++c) {
+      const float v = c < cols ? at(r, c) : 0.0f;
+      dst[size_t(r) * ld + c] = f16 ? __half_as_ushort(__float2half_rn(v)) : f2bf(v);
+    }
   m.rows = rows;
   m.ld = ld;
   m.fp8 = false;
+  m.f16 = f16;
   lay.fix.push_back({&m.w, off});
 }
 
@@ -370,8 +378,9 @@ void pack_weights(const mfb200_net_desc &n, const float *blob, ArenaBuilder &ab,
   Packer P(n, blob);
   const int d = n.embedding, T = 64, dp = n.policy_d, pe = n.pe;
   const auto &g = P.gp;
-  auto dense = [&](Mat &m, const float *src, int rows, int cols) {
-    put_mat(ab, lay, m, rows, cols, cols, [&](int r, int c) { return src[size_t(r) * cols + c]; });
+  auto dense = [&](Mat &m, const float *src, int rows, int cols, bool f16 = false) {
+    put_mat(ab, lay, m, rows, cols, cols, [&](int r, int c) { return src[size_t(r) * cols + c]; },
+            f16);
   };
   dense(W.pe, g[G_PREPROC_W], T * pe, 12 * T);
   put_f32(ab, lay, &W.b_pe, g[G_PREPROC_B], size_t(T) * pe);
@@ -395,7 +404,8 @@ void pack_weights(const mfb200_net_desc &n, const float *blob, ArenaBuilder &ab,
   auto dense8 = [&](Mat &m, const float *src, int rows, int cols) {
     put_mat_fp8(ab, lay, m, rows, cols, cols, [&](int r, int c) { return src[size_t(r) * cols + c]; });
   };
-  dense(W.effn1, g[G_EFFN_W1], n.emb_dff, d);
+  // matrices applied to the fp16 residual stream are stored in fp16
+  dense(W.effn1, g[G_EFFN_W1], n.emb_dff, d, true);
   if (fp8) {
     dense8(W.effn1_8, g[G_EFFN_W1], n.emb_dff, d);
     dense8(W.effn2_8, g[G_EFFN_W2], d, n.emb_dff);
@@ -406,7 +416,7 @@ void pack_weights(const mfb200_net_desc &n, const float *blob, ArenaBuilder &ab,
   put_f32(ab, lay, &W.ln_effn_g, g[G_EFFN_LN_G], d);
   put_f32(ab, lay, &W.ln_effn_b, g[G_EFFN_LN_B], d);
   dense(W.sg_global, g[G_SMOLGEN_W], T * T, n.smolgen_gen);
-  dense(W.pol, g[G_POL_W], dp, d);
+  dense(W.pol, g[G_POL_W], dp, d, true);
   put_f32(ab, lay, &W.b_pol, g[G_POL_B], dp);
   // wq and wk as one [2*dp, dp] matrix (q rows first)
   put_mat(ab, lay, W.qk, 2 * dp, dp, dp, [&](int r, int c) {
@@ -429,7 +439,7 @@ void pack_weights(const mfb200_net_desc &n, const float *blob, ArenaBuilder &ab,
     if (r < ve) return g[G_VAL_W][size_t(r) * d + c];
     if (r < ve + me) return g[G_MOV_W][size_t(r - ve) * d + c];
     return 0.0f;
-  });
+  }, true);
   {
     std::vector<float> b(64, 0.0f);
     std::memcpy(b.data(), g[G_VAL_B], ve * 4);
@@ -471,7 +481,7 @@ void pack_weights(const mfb200_net_desc &n, const float *blob, ArenaBuilder &ab,
       if (r < 3 * d) return l[L_V_W][size_t(r - 2 * d) * d + col];
       return l[L_SG_COMPRESS][size_t(r - 3 * d) * d + col];
     };
-    put_mat(ab, lay, Lw.qkvc, 3 * d + c, d, d, qkvc_at);
+    put_mat(ab, lay, Lw.qkvc, 3 * d + c, d, d, qkvc_at, true);
     if (fp8) {
       put_mat_fp8(ab, lay, Lw.qkvc8, 3 * d + c, d, d, qkvc_at);
       dense8(Lw.o8, l[L_O_W], d, d);
@@ -489,7 +499,7 @@ void pack_weights(const mfb200_net_desc &n, const float *blob, ArenaBuilder &ab,
     put_f32(ab, lay, &Lw.b_o, l[L_O_B], d);
     put_f32(ab, lay, &Lw.ln1_g, l[L_LN1_G], d);
     put_f32(ab, lay, &Lw.ln1_b, l[L_LN1_B], d);
-    dense(Lw.f1, l[L_FFN_W1], n.dff, d);
+    dense(Lw.f1, l[L_FFN_W1], n.dff, d, true);
     put_f32(ab, lay, &Lw.b_f1, l[L_FFN_B1], n.dff);
     dense(Lw.f2, l[L_FFN_W2], d, n.dff);
     put_f32(ab, lay, &Lw.b_f2, l[L_FFN_B2], d);
@@ -517,8 +527,6 @@ void alloc_workspace(Shard &S, const mfb200_net_desc &n, int max_batch, bool fp8
       {reinterpret_cast<void **>(&S.x0), M * kEmbIn * 2},
       {reinterpret_cast<void **>(&S.p), B * kPeInputs * 2},
       {reinterpret_cast<void **>(&S.peo), B * 64 * n.pe * 2},
-      {reinterpret_cast<void **>(&S.X), M * d * 2},
-      {reinterpret_cast<void **>(&S.X1), M * d * 2},
       {reinterpret_cast<void **>(&S.T), M * d * 4},
       {reinterpret_cast<void **>(&S.Xh), M * d * 2},
       {reinterpret_cast<void **>(&S.SK), size_t(kMaxSplits) * B * n.smolgen_hidden * 4},
@@ -588,6 +596,7 @@ void add_gemm(Shard::Plan &P, Shard &S, const char *name, const void *A, long lo
   st.is_gemm = true;
   st.flops = 2.0 * a.M * double(a.N) * a.K;
   const int bn = pick_bn(a.M, a.N);
+  a.ab_f16 = W.f16 ? 1 : 0;
   if (const char *err = plan_gemm(st.g, A, lda, W.w, W.ld, bn, W.fp8, a))
     throw Fail(std::string(name) + ": " + err);
   P.steps.push_back(std::move(st));
@@ -656,7 +665,7 @@ std::unique_ptr<Shard::Plan> build_plan(Shard &S, const mfb200_net_desc &n, int 
   }
   add_fn(*P, "emb_ln_gates", 0, [&S, &W, M, d, eps, f8e](cudaStream_t s) {
     launch_layernorm_q(S.T, Fmt::F32, M, d, W.ln_emb_g, W.ln_emb_b, eps, W.multT, W.addT,
-                       f8e ? nullptr : S.X1, S.X1h, Fmt::F16, f8e ? S.X1_8 : nullptr, S.scales + 0, s);
+                       nullptr, S.X1h, Fmt::F16, f8e ? S.X1_8 : nullptr, S.scales + 0, s);
   });
   probe("absmax_emb_x", S.X1h, Fmt::F16, Md, 0);
   {
@@ -673,7 +682,7 @@ std::unique_ptr<Shard::Plan> build_plan(Shard &S, const mfb200_net_desc &n, int 
       a.out_scale_ptr = S.scales + 1;
       add_gemm(*P, S, "emb_ffn1", S.X1_8, d, W.effn1_8, a);
     } else {
-      add_gemm(*P, S, "emb_ffn1", S.X1, d, W.effn1, a);
+      add_gemm(*P, S, "emb_ffn1", S.X1h, d, W.effn1, a);
     }
     probe("absmax_emb_h", S.H, Fmt::BF16, static_cast<long long>(M) * n.emb_dff, 1);
     GemmArgs b = base_args(S, M, d, n.emb_dff);
@@ -694,7 +703,7 @@ std::unique_ptr<Shard::Plan> build_plan(Shard &S, const mfb200_net_desc &n, int 
   }
   add_fn(*P, "emb_ffn_ln", 0, [&S, &W, M, d, eps, f8q](cudaStream_t s) {
     launch_layernorm_q(S.X1h, Fmt::F16, M, d, W.ln_effn_g, W.ln_effn_b, eps, nullptr, nullptr,
-                       f8q ? nullptr : S.X, S.Xh, Fmt::F16, f8q ? S.X8 : nullptr, S.scales + slot_x(0), s);
+                       nullptr, S.Xh, Fmt::F16, f8q ? S.X8 : nullptr, S.scales + slot_x(0), s);
   });
   probe("absmax_x", S.Xh, Fmt::F16, Md, slot_x(0));
   for (int k = 0; k < n.layers; ++k) {
@@ -712,7 +721,7 @@ std::unique_ptr<Shard::Plan> build_plan(Shard &S, const mfb200_net_desc &n, int 
         a.col_scale = Lw.qkvc8.scale;
         add_gemm(*P, S, "qkv", S.X8, d, Lw.qkvc8, a);
       } else {
-        add_gemm(*P, S, "qkv", S.X, d, Lw.qkvc, a);
+        add_gemm(*P, S, "qkv", S.Xh, d, Lw.qkvc, a);
       }
     }
     {
@@ -775,7 +784,7 @@ std::unique_ptr<Shard::Plan> build_plan(Shard &S, const mfb200_net_desc &n, int 
     }
     add_fn(*P, "ln1", 0, [&S, &Lw, M, d, eps, f8f1, k](cudaStream_t s) {
       launch_layernorm_q(S.Xh, Fmt::F16, M, d, Lw.ln1_g, Lw.ln1_b, eps, nullptr, nullptr,
-                         f8f1 ? nullptr : S.X1, S.X1h, Fmt::F16, f8f1 ? S.X1_8 : nullptr, S.scales + slot_x1(k), s);
+                         nullptr, S.X1h, Fmt::F16, f8f1 ? S.X1_8 : nullptr, S.scales + slot_x1(k), s);
     });
     probe("absmax_x1", S.X1h, Fmt::F16, Md, slot_x1(k));
     {
@@ -794,7 +803,7 @@ std::unique_ptr<Shard::Plan> build_plan(Shard &S, const mfb200_net_desc &n, int 
         a.col_scale = Lw.f1_8.scale;
         add_gemm(*P, S, "ffn1", S.X1_8, d, Lw.f1_8, a);
       } else {
-        add_gemm(*P, S, "ffn1", S.X1, d, Lw.f1, a);
+        add_gemm(*P, S, "ffn1", S.X1h, d, Lw.f1, a);
       }
       probe("absmax_h", S.H, Fmt::BF16, static_cast<long long>(M) * n.dff, slot_h(k));
       GemmArgs b = base_args(S, M, d, n.dff);
@@ -820,7 +829,7 @@ std::unique_ptr<Shard::Plan> build_plan(Shard &S, const mfb200_net_desc &n, int 
       const bool q8 = f8q && !last;
       add_fn(*P, "ln2", 0, [&S, &Lw, M, d, eps, q8, k](cudaStream_t s) {
         launch_layernorm_q(S.X1h, Fmt::F16, M, d, Lw.ln2_g, Lw.ln2_b, eps, nullptr, nullptr,
-                           q8 ? nullptr : S.X, S.Xh, Fmt::F16, q8 ? S.X8 : nullptr, S.scales + slot_x(k + 1), s);
+                           nullptr, S.Xh, Fmt::F16, q8 ? S.X8 : nullptr, S.scales + slot_x(k + 1), s);
       });
       if (!last) probe("absmax_x", S.Xh, Fmt::F16, Md, slot_x(k + 1));
     }
@@ -831,7 +840,7 @@ std::unique_ptr<Shard::Plan> build_plan(Shard &S, const mfb200_net_desc &n, int 
     a.act = n.act_default;
     a.out = S.E;
     a.ldo = dp;
-    add_gemm(*P, S, "policy_embed", S.X, d, W.pol, a);
+    add_gemm(*P, S, "policy_embed", S.Xh, d, W.pol, a);
     GemmArgs b = base_args(S, M, 2 * dp, dp);
     b.bias = W.b_qk;
     b.out = S.QK;
@@ -847,7 +856,7 @@ std::unique_ptr<Shard::Plan> build_plan(Shard &S, const mfb200_net_desc &n, int 
     a.act = n.act_default;
     a.out = S.VM;
     a.ldo = 64;
-    add_gemm(*P, S, "value_mlh_embed", S.X, d, W.vm, a);
+    add_gemm(*P, S, "value_mlh_embed", S.Xh, d, W.vm, a);
     GemmArgs b = base_args(S, B, vh + mh, 64 * 64);
     b.bias = W.b_vm1;
     b.act = n.act_default;

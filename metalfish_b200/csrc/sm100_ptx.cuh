@@ -188,6 +188,11 @@ __device__ __forceinline__ void tma_store_3d(const CUtensorMap *tm, const void *
       "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z)
       : "memory");
 }
+// Pull one global line into L1 (and L2) ahead of its use.
+__device__ __forceinline__ void prefetch_l1(const void *p) {
+  asm volatile("prefetch.global.L1 [%0];" ::"l"(p));
+}
+
 // Element-wise fp32 add of a shared-memory tile into global memory
 // (dst += tile), performed by the TMA unit at L2.
 __device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap *tm, const void *src, int x,
@@ -333,6 +338,7 @@ __host__ __device__ constexpr uint32_t umma_idesc(int m, int n, uint32_t a_fmt, 
   return (1u << 4) | (a_fmt << 7) | (b_fmt << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
          (static_cast<uint32_t>(m >> 4) << 24);
 }
+constexpr uint32_t kFmtF16 = 0;   // kind::f16 operand format code for fp16
 constexpr uint32_t kFmtBF16 = 1;  // kind::f16 operand format code for bf16
 constexpr uint32_t kFmtE4M3 = 0;  // kind::f8f6f4 operand format code for e4m3
 

@@ -157,3 +157,20 @@ def test_gemm_residual_layernorm(M, N, K, bn):
     ref = (y - mu) / np.sqrt(y.var(1, keepdims=True) + 1e-3) * g + be
     np.testing.assert_allclose(out, ref, rtol=1e-3, atol=2e-3)
     np.testing.assert_allclose(from_bf16_bits(out16), ref, rtol=1e-2, atol=2e-2)
+
+
+@pytest.mark.parametrize("M,N,K,bn", [(300, 1024, 1024, 256), (1000, 3104, 1024, 256), (517, 64, 192, 64)])
+def test_gemm_fp16_operands(M, N, K, bn):
+    """fp16 A and W (the GEMMs that read the fp16 residual stream)."""
+    rng = np.random.default_rng(7)
+    A = rng.standard_normal((M, K)).astype(np.float16)
+    W = (rng.standard_normal((N, K)) / np.sqrt(K)).astype(np.float16)
+    b = (rng.standard_normal(N) * 0.1).astype(np.float32)
+    out = np.zeros((M, N), np.uint16)
+    st = ctypes.c_uint(0)
+    rc = lib().mfb200_debug_gemm(M, N, K, bn, 2, _p(A), _p(W), _p(b), 0, 0, None,
+                                 ctypes.c_float(1.0), None, None, ctypes.c_float(1e-3),
+                                 None, ctypes.c_float(1.0), 0, 1, _p(out), ctypes.byref(st))
+    assert rc == 0, f"rc={rc} status={st.value}"
+    ref = A.astype(np.float64) @ W.astype(np.float64).T + b
+    np.testing.assert_allclose(from_bf16_bits(out), ref, rtol=1e-2, atol=1e-2)
