@@ -13,6 +13,10 @@
 extern "C" {
 #endif
 
+/* Allow (1, the default) or forbid (0) the CTA-pair GEMM kernel in GEMMs
+ * planned afterwards (tests run both kernels). */
+MFB200_API void mfb200_debug_set_gemm_pairs(int enable);
+
 /* out[M,N] (bf16 bits) = epilogue(A[M,K] . W[N,K]^T) through the tcgen05 GEMM.
  * A/W are bf16 bits (fp8 = 0), e4m3 bytes (fp8 = 1) or fp16 bits (fp8 = 2); resid is fp32; out is
  * fp32 when out_f32 = 1, fp16 bits when out_f32 = 2, else bf16 bits. mode: 0
@@ -37,9 +41,10 @@ MFB200_API int mfb200_debug_gemm_ln(int M, int N, int K, int bn, const void *A, 
 
 /* Mean device time (ms) of `iters` back-to-back launches of one bf16 GEMM on
  * synthetic device data (for profiling the kernel in isolation); mode and
- * out_f32 as for mfb200_debug_gemm (mode 2: residual + LayerNorm). */
+ * out_f32 as for mfb200_debug_gemm (mode 2: residual + LayerNorm); dtype 0 bf16,
+ * 1 e4m3, 2 fp16 operands. */
 MFB200_API int mfb200_debug_gemm_bench(int M, int N, int K, int bn, int mode, int act, int out_f32,
-                                       int iters, float *ms_out);
+                                       int iters, int dtype, float *ms_out);
 
 #ifdef __cplusplus
 }

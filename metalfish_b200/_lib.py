@@ -30,8 +30,10 @@ def _declare(L: ctypes.CDLL) -> None:
     L.mfb200_debug_gemm.restype = c_int
     L.mfb200_debug_gemm.argtypes = [c_int, c_int, c_int, c_int, c_int, vp, vp, vp, c_int, c_int,
                                     vp, c_float, vp, vp, c_float, vp, c_float, c_int, c_int, vp, vp]
+    L.mfb200_debug_set_gemm_pairs.restype = None
+    L.mfb200_debug_set_gemm_pairs.argtypes = [c_int]
     L.mfb200_debug_gemm_bench.restype = c_int
-    L.mfb200_debug_gemm_bench.argtypes = [c_int] * 8 + [ctypes.POINTER(c_float)]
+    L.mfb200_debug_gemm_bench.argtypes = [c_int] * 9 + [ctypes.POINTER(c_float)]
     L.mfb200_debug_gemm_ln.restype = c_int
     L.mfb200_debug_gemm_ln.argtypes = [c_int, c_int, c_int, c_int, vp, vp, vp, vp, c_float, vp, vp,
                                        c_float, vp, vp, vp]

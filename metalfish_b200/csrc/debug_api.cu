@@ -22,6 +22,8 @@ struct DevBuf {
 };
 }  // namespace
 
+extern "C" void mfb200_debug_set_gemm_pairs(int enable) { set_gemm_pairs(enable != 0); }
+
 extern "C" int mfb200_debug_gemm(int M, int N, int K, int bn, int fp8, const void *A,
                                  const void *W, const float *bias, int mode, int act,
                                  const float *resid, float alpha, const float *ln_gamma,
@@ -88,7 +90,7 @@ extern "C" int mfb200_debug_gemm(int M, int N, int K, int bn, int fp8, const voi
 // Times `iters` back-to-back launches of one GEMM on random device data
 // (bf16, bias, optional fp32 output); returns the mean ms per launch.
 extern "C" int mfb200_debug_gemm_bench(int M, int N, int K, int bn, int mode, int act,
-                                       int out_f32, int iters, float *ms_out) {
+                                       int out_f32, int iters, int dtype, float *ms_out) {
   DevBuf dA, dW, dB, dR, dO, dS, dO2, dG, dRS;
   if (!dA.alloc(size_t(M) * K * 2) || !dW.alloc(size_t(N) * K * 2) || !dB.alloc(N * 4) ||
       !dR.alloc(size_t(M) * N * 4) || !dO.alloc(size_t(M) * N * 4) || !dS.alloc(4) ||
@@ -115,6 +117,7 @@ extern "C" int mfb200_debug_gemm_bench(int M, int N, int K, int bn, int mode, in
   a.a_scale = 1.0f;
   a.out_f32 = out_f32 == 1;
   a.out_f16 = out_f32 == 2;  // 2: fp16 output
+  a.ab_f16 = dtype == 2;
   a.status = static_cast<unsigned *>(dS.p);
   if (mode == kEpiAccum && !a.out_f16) a.out_f32 = 1;
   if (mode == kEpiResidLN) {  // fused residual + LayerNorm (N / bn CTAs per cluster)
@@ -128,7 +131,7 @@ extern "C" int mfb200_debug_gemm_bench(int M, int N, int K, int bn, int mode, in
     a.row_stats = static_cast<float2 *>(dRS.p);
   }
   GemmLaunch g;
-  if (plan_gemm(g, dA.p, K, dW.p, K, bn, false, a)) return 2;
+  if (plan_gemm(g, dA.p, K, dW.p, K, bn, dtype == 1, a)) return 2;
   for (int i = 0; i < 2; ++i)
     if (launch_gemm(g, 0) != cudaSuccess) return 3;
   cudaEvent_t e0, e1;

@@ -29,7 +29,10 @@ EncodeTiledFn encode_fn() {
 }
 
 int g_num_sms = 0;
+bool g_pairs = true;
 }  // namespace
+
+void set_gemm_pairs(bool enable) { g_pairs = enable; }
 
 int num_sms() {
   if (g_num_sms == 0) {
@@ -150,6 +153,65 @@ static int max_clusters_t(int csize) {
   return n;
 }
 
+// Co-resident clusters of two CTAs of the pair kernel.
+template <bool FP8>
+static int max_pairs_t() {
+  using S = PairShape<FP8>;
+  static int cache[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return 0;
+  if (cache[dev]) return cache[dev];
+  cudaFuncSetAttribute(gemm_pair_kernel<FP8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       S::SMEM_BYTES);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * 64);
+  cfg.blockDim = dim3(S::THREADS);
+  cfg.dynamicSmemBytes = S::SMEM_BYTES;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, gemm_pair_kernel<FP8>, &cfg) != cudaSuccess || n <= 0)
+    n = num_sms() / 2;
+  cudaGetLastError();
+  cache[dev] = n;
+  return n;
+}
+
+template <bool FP8>
+static cudaError_t launch_pair_t(const GemmLaunch &g, cudaStream_t stream) {
+  using S = PairShape<FP8>;
+  static bool attr_done[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!attr_done[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(gemm_pair_kernel<FP8>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM_BYTES);
+    if (e != cudaSuccess) return e;
+    attr_done[dev] = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = g.grid;
+  cfg.blockDim = dim3(S::THREADS);
+  cfg.dynamicSmemBytes = S::SMEM_BYTES;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, gemm_pair_kernel<FP8>, g.tmA, g.tmB, g.tmOut, g.tmOut2, g.tmRes,
+                            g.args);
+}
+
 static int max_clusters(int bn, bool fp8, int csize) {
   if (fp8) return bn == 256 ? max_clusters_t<256, true>(csize)
                             : (bn == 128 ? max_clusters_t<128, true>(csize) : max_clusters_t<64, true>(csize));
@@ -158,6 +220,7 @@ static int max_clusters(int bn, bool fp8, int csize) {
 }
 
 cudaError_t launch_gemm(const GemmLaunch &g, cudaStream_t stream) {
+  if (g.pair) return g.fp8 ? launch_pair_t<true>(g, stream) : launch_pair_t<false>(g, stream);
   const bool ln = g.args.mode == kEpiResidLN;
 #define MFB_LAUNCH(BN, F8) \
   return ln ? launch_t<BN, F8, true>(g, stream) : launch_t<BN, F8, false>(g, stream)
@@ -202,6 +265,15 @@ const char *plan_gemm(GemmLaunch &g, const void *A, long long lda_elems, const v
   g.bn = bn;
   g.fp8 = fp8;
   g.args = args;
+  // CTA pairs for the large store / accumulate / residual GEMMs with at
+  // least 12 K steps. With fewer, a tile is bound by its epilogue, and the
+  // pair's shared accumulator hand-off (both CTAs must drain an accumulator
+  // before it is reused) costs more than the halved W traffic saves:
+  // measured on B200 at M=65536, bf16 K=1024 (16 steps) gains 8%, e4m3
+  // K=1024 (8 steps) loses 15%, e4m3 K=1536 (12 steps) gains 9%.
+  const int ksteps = (args.K + (fp8 ? 127 : 63)) / (fp8 ? 128 : 64);
+  g.pair = g_pairs && bn == 256 && args.k_splits <= 1 && args.mode != kEpiResidLN &&
+           args.M > 128 && ksteps >= 12;
   {
     // every K slice must be non-empty
     const int kblocks = (args.K + (fp8 ? 128 : 64) - 1) / (fp8 ? 128 : 64);
@@ -214,7 +286,8 @@ const char *plan_gemm(GemmLaunch &g, const void *A, long long lda_elems, const v
                         static_cast<uint64_t>(args.M), static_cast<uint64_t>(lda_elems) * elem, 128))
     return "gemm: cannot build TMA descriptor for A (alignment?)";
   if (!make_kmajor_tmap(&g.tmB, W, fp8, static_cast<uint64_t>(args.K),
-                        static_cast<uint64_t>(args.N), static_cast<uint64_t>(ldw_elems) * elem, bn))
+                        static_cast<uint64_t>(args.N), static_cast<uint64_t>(ldw_elems) * elem,
+                        g.pair ? bn / 2 : bn))
     return "gemm: cannot build TMA descriptor for W (alignment?)";
   {
     // epilogue tensor maps: 32-row x 32-column boxes in the output format
@@ -279,6 +352,12 @@ const char *plan_gemm(GemmLaunch &g, const void *A, long long lda_elems, const v
     const long long tiles_m = (args.M + 127) / 128;
     const long long clusters = std::min<long long>(tiles_m, max_clusters(bn, fp8, args.cluster_n));
     g.grid = dim3(static_cast<unsigned>(clusters * args.cluster_n));
+    return nullptr;
+  }
+  if (g.pair) {
+    const long long units = static_cast<long long>((args.M + 255) / 256) * ((args.N + 255) / 256);
+    const long long pairs = std::min<long long>(units, fp8 ? max_pairs_t<true>() : max_pairs_t<false>());
+    g.grid = dim3(static_cast<unsigned>(2 * pairs));
     return nullptr;
   }
   g.grid = dim3(static_cast<unsigned>(tiles < sms ? tiles : sms));

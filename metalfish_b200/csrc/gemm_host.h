@@ -14,8 +14,12 @@ struct GemmLaunch {
   GemmArgs args;
   int bn = 256;
   bool fp8 = false;
+  bool pair = false;  // CTA-pair kernel (gemm_pair_kernel), clusters of 2
   dim3 grid;
 };
+
+// Whether plan_gemm may choose the CTA-pair kernel (default on).
+void set_gemm_pairs(bool enable);
 
 int num_sms();
 

@@ -682,4 +682,230 @@ __global__ void __launch_bounds__(64 + 32 * kEpiWarps, 1)
   if (ln) cluster_sync();  // no CTA leaves while a peer may still signal it
 }
 
+// ---------------------------------------------------------------------------
+// CTA-pair GEMM (tcgen05 .cta_group::2). A cluster of two CTAs owns a
+// 256 x 256 output tile: CTA r stages rows [128r, 128r+128) of the A tile and
+// rows [128r, 128r+128) of the W tile (half of the tile's N) in its shared
+// memory, rank 0 issues M=256 N=256 MMAs that read both CTAs' operands, and
+// each CTA's TMEM receives its own 128 rows x 256 columns. Per SM this halves
+// the W bytes staged and read by the tensor core (32 KB per K step instead of
+// 48 KB), which leaves room for six pipeline stages. Roles as in
+// gemm_sm100_kernel; the producer of each CTA loads its halves and counts the
+// bytes on rank 0's `full` barrier, rank 0's commits arrive on both CTAs'
+// `empty` / `tfull` barriers, and every epilogue warp of both CTAs arrives on
+// rank 0's `tempty` barrier. Store / accumulate / residual epilogues, no
+// split-K.
+template <bool FP8>
+struct PairShape {
+  static constexpr int BM = 128;                 // rows per CTA (256 per pair)
+  static constexpr int BN = 256;                 // columns per tile
+  static constexpr int BK = FP8 ? 128 : 64;
+  static constexpr int A_BYTES = BM * 128;
+  static constexpr int B_BYTES = (BN / 2) * 128; // this CTA's half of W
+  static constexpr int STAGES = 6;
+  static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int STAGE_BYTES = kEpiWarps * kStageBytes;
+  static constexpr int SMEM_BYTES = STAGES * (A_BYTES + B_BYTES) + STAGE_BYTES + 1024 + 256;
+  static constexpr int THREADS = 64 + 32 * kEpiWarps;
+  static_assert(SMEM_BYTES <= 232448, "shared memory budget");
+};
+
+template <bool FP8>
+__global__ void __launch_bounds__(64 + 32 * kEpiWarps, 1)
+    gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA,
+                     const __grid_constant__ CUtensorMap tmB,
+                     const __grid_constant__ CUtensorMap tmOut,
+                     const __grid_constant__ CUtensorMap tmOut2,
+                     const __grid_constant__ CUtensorMap tmRes, const GemmArgs args) {
+  using S = PairShape<FP8>;
+  constexpr int STAGES = S::STAGES;
+  constexpr int BN = S::BN;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t *base = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  uint8_t *smA = base;
+  uint8_t *smB = base + STAGES * S::A_BYTES;
+  uint8_t *stage_base = smB + STAGES * S::B_BYTES;
+  uint64_t *full = reinterpret_cast<uint64_t *>(stage_base + S::STAGE_BYTES);
+  uint64_t *empty = full + STAGES;
+  uint64_t *tfull = empty + STAGES;
+  uint64_t *tempty = tfull + 2;
+  uint64_t *res_bars = tempty + 2;
+  uint64_t *drain = res_bars + kEpiWarps;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const int tiles_m = (args.M + 2 * S::BM - 1) / (2 * S::BM);
+  const int tiles_n = (args.N + BN - 1) / BN;
+  const int units = tiles_m * tiles_n;
+  const int kblocks = (args.K + S::BK - 1) / S::BK;
+  const int u_begin = static_cast<int>(blockIdx.x >> 1);
+  const int u_step = static_cast<int>(gridDim.x >> 1);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 2 * kEpiWarps);  // one arrive per epilogue warp of the pair
+    }
+    for (int w = 0; w < kEpiWarps; ++w) mbar_init(&res_bars[w], 1);
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, S::TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  cluster_sync();  // both CTAs' barriers exist before any cross-CTA arrive or load
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---------------------------------------------------------- producer
+      int stage = 0;
+      uint32_t round = 0;
+      long long issued = 0;
+      bool ok = true;
+      for (int u = u_begin; u < units && ok; u += u_step) {
+        const int m0 = (u / tiles_n) * 2 * S::BM + static_cast<int>(rank) * S::BM;
+        const int nb0 = (u % tiles_n) * BN + static_cast<int>(rank) * (BN / 2);
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(&empty[stage], (round & 1) ^ 1, args.status, kErrTimeoutProducer,
+                         abort_flag)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb = mapa_shared(smem_u32(&full[stage]), 0);
+          if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * (S::A_BYTES + S::B_BYTES));
+          tma_load_2d_pair(smA + stage * S::A_BYTES, &tmA, fb, kb * S::BK, m0);
+          tma_load_2d_pair(smB + stage * S::B_BYTES, &tmB, fb, kb * S::BK, nb0);
+          ++issued;
+          if (++stage == STAGES) { stage = 0; ++round; }
+        }
+      }
+      if (!ok && rank == 0) {
+        // Drain: the loads of both CTAs complete on rank 0's barriers.
+        const long long first = issued > STAGES ? issued - STAGES : 0;
+        for (long long i = first; i < issued; ++i) {
+          const unsigned long long t0 = global_ns();
+          while (!mbar_try_wait(&full[i % STAGES], static_cast<uint32_t>((i / STAGES) & 1))) {
+            if (global_ns() - t0 > kWaitLimitNs) {
+              atomicCAS(args.status, 0u, static_cast<unsigned>(kErrTimeoutDrain));
+              break;
+            }
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && rank == 0) {
+      // ---------------------------------------------------------- MMA issuer
+      const uint32_t idesc = FP8 ? umma_idesc(256, BN, kFmtE4M3, kFmtE4M3)
+                                 : (args.ab_f16 ? umma_idesc(256, BN, kFmtF16, kFmtF16)
+                                                : umma_idesc(256, BN, kFmtBF16, kFmtBF16));
+      int stage = 0;
+      uint32_t round = 0;
+      int local = 0;
+      bool ok = true;
+      bool issued_any = false;
+      for (int u = u_begin; u < units && ok; u += u_step, ++local) {
+        const int acc = local & 1;
+        const uint32_t aphase = (local >> 1) & 1;
+        if (!mbar_wait_cluster(&tempty[acc], aphase ^ 1, args.status, kErrTimeoutMma, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem_base + static_cast<uint32_t>(acc * BN);
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(&full[stage], round & 1, args.status, kErrTimeoutMma, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t ad = sw128_kmajor_desc(smem_u32(smA + stage * S::A_BYTES));
+          const uint64_t bd = sw128_kmajor_desc(smem_u32(smB + stage * S::B_BYTES));
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            const uint32_t accumulate = (kb > 0 || kk > 0) ? 1u : 0u;
+            if (FP8)
+              umma_f8_pair(d, ad + 2 * kk, bd + 2 * kk, idesc, accumulate);
+            else
+              umma_f16_pair(d, ad + 2 * kk, bd + 2 * kk, idesc, accumulate);
+          }
+          issued_any = true;
+          umma_commit_pair_mc(&empty[stage], 0x3);
+          if (++stage == STAGES) { stage = 0; ++round; }
+        }
+        if (ok) umma_commit_pair_mc(&tfull[acc], 0x3);
+      }
+      if (!ok && issued_any) {
+        // Aborted: wait (bounded) until every MMA already issued has retired.
+        umma_commit_pair(drain);
+        const unsigned long long t0 = global_ns();
+        while (!mbar_try_wait(drain, 0)) {
+          if (global_ns() - t0 > kWaitLimitNs) {
+            atomicCAS(args.status, 0u, static_cast<unsigned>(kErrTimeoutDrain));
+            break;
+          }
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int quarter = warp & 3;
+    const int group = (warp - 2) >> 2;
+    EpiCtx e{&tmOut, &tmOut2, &tmRes, stage_base + (warp - 2) * kStageBytes, &res_bars[warp - 2],
+             0u, lane, abort_flag, nullptr, 0u, rank, nullptr, 0u};
+    if (lane == 0) {
+      tma_prefetch_desc(&tmOut);
+      if (args.out2) tma_prefetch_desc(&tmOut2);
+      if (args.mode == kEpiResid) tma_prefetch_desc(&tmRes);
+    }
+    const uint32_t tempty0 = mapa_shared(smem_u32(&tempty[0]), 0);
+    const uint32_t tempty1 = mapa_shared(smem_u32(&tempty[1]), 0);
+    int local = 0;
+    for (int u = u_begin; u < units; u += u_step, ++local) {
+      const int acc = local & 1;
+      const uint32_t aphase = (local >> 1) & 1;
+      const int m0 = (u / tiles_n) * 2 * S::BM + static_cast<int>(rank) * S::BM;
+      const int n0 = (u % tiles_n) * BN;
+      if (lane < BN / 32 && n0 + 32 * lane < args.N) {
+        if (args.bias) prefetch_l1(args.bias + n0 + 32 * lane);
+        if (args.col_scale) prefetch_l1(args.col_scale + n0 + 32 * lane);
+      }
+      if (!mbar_wait(&tfull[acc], aphase, args.status, kErrTimeoutEpilogue, abort_flag)) break;
+      tc_fence_after();
+      const uint32_t taddr =
+          tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
+      const bool ok = epilogue_dispatch<BN, false>(args, e, taddr, m0 + quarter * 32, n0, group, -1);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_remote(acc ? tempty1 : tempty0);
+      if (!ok) break;
+    }
+    if (lane == 0) bulk_wait0();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // rank 0's MMAs and both CTAs' loads are finished before release
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, S::TMEM_COLS);
+  }
+}
+
 }  // namespace mfb200

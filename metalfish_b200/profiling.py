@@ -1,8 +1,9 @@
 """Small drivers for profiling the library (e.g. under ncu).
 
-  python -m metalfish_b200.profiling gemm M N K [BN MODE ACT OUT_F32 ITERS]
-      times ITERS back-to-back launches of one bf16 tcgen05 GEMM on synthetic
-      device data (mfb200_debug_gemm_bench) and prints TFLOP/s.
+  python -m metalfish_b200.profiling gemm M N K [BN MODE ACT OUT_F32 ITERS DTYPE PAIRS]
+      times ITERS back-to-back launches of one tcgen05 GEMM on synthetic
+      device data (mfb200_debug_gemm_bench) and prints TFLOP/s. DTYPE: 0
+      bf16, 1 e4m3, 2 fp16 operands; PAIRS 0 forbids the CTA-pair kernel.
   python -m metalfish_b200.profiling forward [BATCH] [bf16|fp8]
       runs two eager forwards (no CUDA graph, so every kernel is a separate
       launch) of the seeded BT4-shaped network on fixture positions.
@@ -21,12 +22,14 @@ ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 def gemm(argv) -> None:
     from ._lib import lib
     M, N, K = (int(x) for x in argv[:3])
-    bn, mode, act, out_f32, iters = (int(x) for x in (argv[3:8] + ["256", "0", "0", "0", "10"][len(argv) - 3:]))
+    bn, mode, act, out_f32, iters, dtype, pairs = (
+        int(x) for x in (argv[3:10] + ["256", "0", "0", "0", "10", "0", "1"][len(argv) - 3:]))
     ms = ctypes.c_float()
-    rc = lib().mfb200_debug_gemm_bench(M, N, K, bn, mode, act, out_f32, iters, ctypes.byref(ms))
+    lib().mfb200_debug_set_gemm_pairs(pairs)
+    rc = lib().mfb200_debug_gemm_bench(M, N, K, bn, mode, act, out_f32, iters, dtype, ctypes.byref(ms))
     if rc:
         raise SystemExit(f"gemm bench failed: rc={rc}")
-    print(f"M={M} N={N} K={K} bn={bn}: {ms.value:.4f} ms  {2.0 * M * N * K / ms.value / 1e9:.1f} TFLOP/s")
+    print(f"M={M} N={N} K={K} bn={bn} dtype={dtype} pairs={pairs}: {ms.value:.4f} ms  {2.0 * M * N * K / ms.value / 1e9:.1f} TFLOP/s")
 
 
 def forward(argv) -> None:

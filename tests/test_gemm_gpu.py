@@ -10,6 +10,15 @@ from metalfish_b200.bf16 import from_bf16_bits, round_bf16, to_bf16_bits
 pytestmark = pytest.mark.gpu
 
 
+@pytest.fixture(autouse=True, params=[1, 0], ids=["pairs", "single"])
+def gemm_kernel(request):
+    """Every GEMM case runs through the CTA-pair kernel (where the shape
+    selects it) and through the single-CTA kernel."""
+    lib().mfb200_debug_set_gemm_pairs(request.param)
+    yield request.param
+    lib().mfb200_debug_set_gemm_pairs(1)
+
+
 def _p(a):
     return None if a is None else a.ctypes.data_as(ctypes.c_void_p)
 
