@@ -115,7 +115,10 @@ __device__ __forceinline__ float apply_act(float v, int act) {
 // one row per lane these layouts make the shared-memory writes conflict-free,
 // and one elected lane then issues an asynchronous TMA store of the chunk.
 // Residual tiles arrive the same way, by TMA load into the staging tile.
-constexpr int kEpiWarps = 8;
+// Epilogue warps: 16 (four per TMEM lane quarter, every fourth 32-column
+// chunk each) in the store / accumulate kernels, 8 in the LayerNorm kernels.
+constexpr int kEpiWarpsLN = 8;
+constexpr int kEpiWarpsMax = 16;
 constexpr int kStageBytes = 32 * 32 * 4;
 
 struct EpiCtx {
@@ -185,22 +188,29 @@ __device__ __forceinline__ void stage_row(const GemmArgs &args, uint8_t *st, int
 // The chunks of one tile owned by this warp (every other 32-column chunk,
 // starting at `group`*32), with the TMEM load of the next chunk in flight
 // while the current one is processed. Returns false on a barrier timeout.
-template <int BN, int MODE, int ACT>
+template <int BN, int MODE, int ACT, int EW>
 __device__ __forceinline__ bool epilogue_tile(const GemmArgs &args, EpiCtx &e, uint32_t taddr,
                                               int row0, int n0, int group, int ks) {
+  constexpr int STEP = 32 * (EW / 4);  // columns between this warp's chunks
   const int lane = e.lane;
   const bool f32 = ks >= 0 || args.out_f32;
   const float a_scale = args.a_scale_ptr ? args.a_scale * __ldg(args.a_scale_ptr) : args.a_scale;
   const float out_is = args.out_scale_ptr ? 1.0f / __ldg(args.out_scale_ptr) : args.out_inv_scale;
+  // With 8 epilogue warps the TMEM load of the next chunk is issued before
+  // the current one is processed; with 16 the other warps hide that latency
+  // and the registers of a second chunk are not available.
+  constexpr bool PREFETCH = EW <= 8;
   uint32_t raw[32];
   int c = group * 32;
-  tmem_ld32(taddr + c, raw);
-  for (; c < BN; c += 64) {
+  if (c >= BN) return true;
+  if (PREFETCH) tmem_ld32(taddr + c, raw);
+  for (; c < BN; c += STEP) {
+    if (!PREFETCH) tmem_ld32(taddr + c, raw);
     tmem_wait_ld();
     float v[32];
 #pragma unroll
     for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(raw[j]);
-    if (c + 64 < BN) tmem_ld32(taddr + c + 64, raw);  // warp-collective prefetch
+    if (PREFETCH && c + STEP < BN) tmem_ld32(taddr + c + STEP, raw);  // warp-collective prefetch
     const int nb = n0 + c;
     if (nb >= args.N) continue;
     // A chunk of 2- or 1-byte outputs fills at most half of the 4 KB tile, so
@@ -423,13 +433,13 @@ __device__ __forceinline__ bool epilogue_tile_ln(const GemmArgs &args, EpiCtx &e
   return true;
 }
 
-template <int BN, bool LN>
+template <int BN, bool LN, int EW>
 __device__ __forceinline__ bool epilogue_dispatch(const GemmArgs &args, EpiCtx &e, uint32_t taddr,
                                                   int row0, int n0, int group, int ks) {
   if constexpr (LN) {
     return epilogue_tile_ln<BN>(args, e, taddr, row0, n0);
   } else {
-#define MFB_EPI(MODE, ACT) return epilogue_tile<BN, MODE, ACT>(args, e, taddr, row0, n0, group, ks)
+#define MFB_EPI(MODE, ACT) return epilogue_tile<BN, MODE, ACT, EW>(args, e, taddr, row0, n0, group, ks)
   if (ks < 0 && args.mode == kEpiResid) MFB_EPI(kEpiResid, kActNone);
   if (ks < 0 && args.mode == kEpiAccum) MFB_EPI(kEpiAccum, kActNone);
   switch (ks >= 0 ? kActNone : args.act) {
@@ -452,18 +462,20 @@ struct GemmShape {
   static constexpr int BK = FP8 ? 128 : 64;  // elements per 128-byte swizzled row
   static constexpr int A_BYTES = BM * 128;
   static constexpr int B_BYTES = BN * 128;
-  // LN kernels trade one pipeline stage for a second staging tile per warp
+  static constexpr int EW = LN ? kEpiWarpsLN : kEpiWarpsMax;  // epilogue warps
+  // LN kernels trade one pipeline stage for a second staging tile per warp;
+  // the others give 64 KB to the 16 epilogue warps' staging tiles
   static constexpr int STAGES = LN ? (BN == 256 ? 3 : (BN == 128 ? 4 : 5))
-                                   : (BN == 256 ? 4 : (BN == 128 ? 6 : 8));
+                                   : (BN == 256 ? 3 : (BN == 128 ? 5 : 6));
   static constexpr int TMEM_COLS = 2 * BN;
-  static constexpr int STAGE_BYTES = (LN ? 2 : 1) * kEpiWarps * kStageBytes;  // epilogue staging
-  static constexpr int SMEM_BYTES = STAGES * (A_BYTES + B_BYTES) + STAGE_BYTES + 1024 + 256;
-  static constexpr int THREADS = 64 + 32 * kEpiWarps;
+  static constexpr int STAGE_BYTES = (LN ? 2 : 1) * EW * kStageBytes;  // epilogue staging
+  static constexpr int SMEM_BYTES = STAGES * (A_BYTES + B_BYTES) + STAGE_BYTES + 1024 + 512;
+  static constexpr int THREADS = 64 + 32 * EW;
   static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 };
 
 template <int BN, bool FP8, bool LN = false>
-__global__ void __launch_bounds__(64 + 32 * kEpiWarps, 1)
+__global__ void __launch_bounds__(64 + 32 * (LN ? kEpiWarpsLN : kEpiWarpsMax), 1)
     gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA,
                       const __grid_constant__ CUtensorMap tmB,
                       const __grid_constant__ CUtensorMap tmOut,
@@ -482,7 +494,7 @@ __global__ void __launch_bounds__(64 + 32 * kEpiWarps, 1)
   uint64_t *tfull = empty + STAGES;
   uint64_t *tempty = tfull + 2;
   uint64_t *res_bars = tempty + 2;  // one per epilogue warp
-  uint64_t *drain = res_bars + kEpiWarps;
+  uint64_t *drain = res_bars + S::EW;
   uint64_t *xbar = drain + 1;  // row-statistics exchange, one per LN team
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(xbar + 2);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
@@ -512,12 +524,12 @@ __global__ void __launch_bounds__(64 + 32 * kEpiWarps, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], LN ? 32 * kEpiWarps / 2 : 32 * kEpiWarps);
+      mbar_init(&tempty[a], LN ? 32 * S::EW / 2 : 32 * S::EW);
     }
-    for (int w = 0; w < kEpiWarps; ++w) mbar_init(&res_bars[w], 1);
+    for (int w = 0; w < S::EW; ++w) mbar_init(&res_bars[w], 1);
     mbar_init(drain, 1);
-    mbar_init(&xbar[0], static_cast<uint32_t>(C * kEpiWarps / 2));
-    mbar_init(&xbar[1], static_cast<uint32_t>(C * kEpiWarps / 2));
+    mbar_init(&xbar[0], static_cast<uint32_t>(C * S::EW / 2));
+    mbar_init(&xbar[1], static_cast<uint32_t>(C * S::EW / 2));
     *abort_flag = 0;
     fence_barrier_init();
     tma_prefetch_desc(&tmA);
@@ -640,7 +652,7 @@ __global__ void __launch_bounds__(64 + 32 * kEpiWarps, 1)
     const int group = (warp - 2) >> 2;   // which alternate 32-column chunks
     EpiCtx e{&tmOut, &tmOut2, &tmRes, stage_base + (warp - 2) * kStageBytes, &res_bars[warp - 2],
              0u, lane, abort_flag, &xbar[group], 0u, rank,
-             LN ? stage_base + (kEpiWarps + warp - 2) * kStageBytes : nullptr, 0u};
+             LN ? stage_base + (S::EW + warp - 2) * kStageBytes : nullptr, 0u};
     if (lane == 0) {
       tma_prefetch_desc(&tmOut);
       if (args.out2) tma_prefetch_desc(&tmOut2);
@@ -665,7 +677,7 @@ __global__ void __launch_bounds__(64 + 32 * kEpiWarps, 1)
       tc_fence_after();
       const uint32_t taddr =
           tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
-      const bool ok = epilogue_dispatch<BN, LN>(args, e, taddr, m0 + quarter * 32, n0, group, ks);
+      const bool ok = epilogue_dispatch<BN, LN, S::EW>(args, e, taddr, m0 + quarter * 32, n0, group, ks);
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
       if (!ok) break;
@@ -702,16 +714,17 @@ struct PairShape {
   static constexpr int BK = FP8 ? 128 : 64;
   static constexpr int A_BYTES = BM * 128;
   static constexpr int B_BYTES = (BN / 2) * 128; // this CTA's half of W
-  static constexpr int STAGES = 6;
+  static constexpr int EW = kEpiWarpsMax;         // epilogue warps
+  static constexpr int STAGES = 5;
   static constexpr int TMEM_COLS = 2 * BN;
-  static constexpr int STAGE_BYTES = kEpiWarps * kStageBytes;
+  static constexpr int STAGE_BYTES = EW * kStageBytes;
   static constexpr int SMEM_BYTES = STAGES * (A_BYTES + B_BYTES) + STAGE_BYTES + 1024 + 256;
-  static constexpr int THREADS = 64 + 32 * kEpiWarps;
+  static constexpr int THREADS = 64 + 32 * EW;
   static_assert(SMEM_BYTES <= 232448, "shared memory budget");
 };
 
 template <bool FP8>
-__global__ void __launch_bounds__(64 + 32 * kEpiWarps, 1)
+__global__ void __launch_bounds__(64 + 32 * kEpiWarpsMax, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA,
                      const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmOut,
@@ -731,7 +744,7 @@ __global__ void __launch_bounds__(64 + 32 * kEpiWarps, 1)
   uint64_t *tfull = empty + STAGES;
   uint64_t *tempty = tfull + 2;
   uint64_t *res_bars = tempty + 2;
-  uint64_t *drain = res_bars + kEpiWarps;
+  uint64_t *drain = res_bars + S::EW;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(drain + 1);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
@@ -752,9 +765,9 @@ __global__ void __launch_bounds__(64 + 32 * kEpiWarps, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 2 * kEpiWarps);  // one arrive per epilogue warp of the pair
+      mbar_init(&tempty[a], 2 * S::EW);  // one arrive per epilogue warp of the pair
     }
-    for (int w = 0; w < kEpiWarps; ++w) mbar_init(&res_bars[w], 1);
+    for (int w = 0; w < S::EW; ++w) mbar_init(&res_bars[w], 1);
     mbar_init(drain, 1);
     *abort_flag = 0;
     fence_barrier_init();
@@ -890,7 +903,7 @@ __global__ void __launch_bounds__(64 + 32 * kEpiWarps, 1)
       tc_fence_after();
       const uint32_t taddr =
           tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
-      const bool ok = epilogue_dispatch<BN, false>(args, e, taddr, m0 + quarter * 32, n0, group, -1);
+      const bool ok = epilogue_dispatch<BN, false, S::EW>(args, e, taddr, m0 + quarter * 32, n0, group, -1);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_remote(acc ? tempty1 : tempty0);
