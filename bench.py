@@ -15,8 +15,9 @@ batch is sharded, weights replicated, no collective in the forward
 * e2e        -- the same through the public host API (mfb200_evaluate) from
                 pinned host buffers: H2D of the packed planes and D2H of
                 policy/WDL/moves-left inside the timed region, wall clock.
-* roofline   -- all tcgen05 GEMM launches of one forward (the dominant
-                kernel: ~99% of the FLOPs), algorithmic FLOPs / event time.
+* roofline   -- the QKV projection GEMM (the largest stage), algorithmic
+                FLOPs / event time of its launches in this run; `gemm_all`
+                aggregates all tcgen05 GEMM launches of one forward.
 * cpu_baseline -- the reference CPU backend (oracle/_ref, built from the
                 reference sources) or, if that binary is absent, the C
                 restatement, on a bounded sample on the host cores.
@@ -132,6 +133,14 @@ def cpu_baseline(cfg, tensors, sample_positions: int | None = None):
     dt = time.perf_counter() - t0
     return {"value": n / dt, "unit": "positions/s", "cores": threads, "kind": "port",
             "sample": f"{n} positions, C restatement oracle (fp32), {threads} threads, {dt:.1f} s"}
+
+
+# DRAM bytes (read + write) of one QKV GEMM launch at batch 1024, from the
+# ncu capture named beside it (a M=16384 capture scaled by 4: traffic grows
+# with M). Part of the output is still in L2 when a launch ends.
+QKV_TRAFFIC = {
+    "bf16": (4 * (40.235e6 + 53.987e6), "profiles/gemm_pair_qkv_m16384.md (x4 to M=65536)"),
+}
 
 
 def stage_summary(stages):
@@ -302,19 +311,26 @@ def main():
     barrier(world)
     e2e_value = B * world * args.steps / e2e_s
 
-    # ---- roofline of the tcgen05 GEMM (all its launches in one forward)
-    gemm = [(n, m, f) for (n, m, f) in stages if n not in
-            ("unpack", "pe_concat", "emb_ln_gates", "emb_ffn_ln", "smolgen_ln1", "smolgen_ln2",
-             "attention", "ln1", "ln2", "policy_map", "heads")]
+    # ---- roofline. Dominant kernel: the QKV(+smolgen compress) projection
+    # GEMM, the largest single stage (15 launches per forward; the CTA-pair
+    # tcgen05 kernel in bf16, the single-CTA one in e4m3), achieved = its
+    # algorithmic FLOPs / its CUDA-event time measured in this run. `gemm_all`
+    # aggregates every GEMM launch of the forward the same way.
+    gemm = [(n, m, f) for (n, m, f) in stages if f > 0 and n not in ("attention", "policy_map")]
     g_ms = sum(m for _, m, _ in gemm)
     g_fl = sum(f for _, _, f in gemm)
+    qkv = [(m, f) for (n, m, f) in stages if n == "qkv"]
+    q_ms = sum(m for m, _ in qkv)
+    q_fl = sum(f for _, f in qkv)
     burst, sustained, src = measured_peaks()
     peak_note = f"{src} bf16_tflops_sustained (kernel timed inside a long step)"
     if args.precision == "fp8":
         # no FP8 peak was measured on this pool; e4m3 dense rate is twice bf16
         sustained *= 2.0
-        peak_note = f"2 x {src} bf16_tflops_sustained (e4m3 dense = 2x bf16); bf16 GEMMs of the forward count against it too"
-    achieved = g_fl / (g_ms / 1e3) / 1e12 if g_ms > 0 else 0.0
+        peak_note = f"2 x {src} bf16_tflops_sustained (e4m3 dense = 2x bf16)"
+    achieved = q_fl / (q_ms / 1e3) / 1e12 if q_ms > 0 else 0.0
+    g_achieved = g_fl / (g_ms / 1e3) / 1e12 if g_ms > 0 else 0.0
+    traffic, traffic_src = QKV_TRAFFIC.get(args.precision, (None, None)) if B == 1024 else (None, None)
     total_stage_ms = sum(m for _, m, _ in stages)
     enc = cfg.flops_per_position()
 
@@ -336,9 +352,15 @@ def main():
                     "d2h_bytes_per_step": int(B * (1858 + 3 + 1) * 4)},
             "gpu_launches": launches_per_step * args.steps,
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": sustained,
-                         "unit": "TFLOP/s", "frac": achieved / sustained, "traffic": None,
-                         "kernel": "gemm_sm100_kernel (tcgen05, all launches of one forward)",
-                         "peak_source": peak_note},
+                         "unit": "TFLOP/s", "frac": achieved / sustained, "traffic": traffic,
+                         "kernel": ("gemm_pair_kernel<bf16/fp16>" if args.precision == "bf16"
+                                    else "gemm_sm100_kernel<256, e4m3>")
+                                   + f": QKV+compress projection, M={B * 64} N=3104 K=1024, "
+                                     f"{len(qkv)} launches per forward",
+                         "traffic_source": traffic_src,
+                         "peak_source": peak_note,
+                         "gemm_all": {"achieved": g_achieved, "frac": g_achieved / sustained,
+                                      "launches": len(gemm)}},
             "flops_per_position": {"encoder_gemm": enc["encoder_gemm_flops"], "all_matmul": enc["total_flops"]},
             "model_tflops": value * enc["total_flops"] / 1e12 / world,
             "stage_ms": stage_summary(stages),
