@@ -238,57 +238,64 @@ __global__ void __launch_bounds__(256)
   }
 }
 
-// One CTA (256 threads) per row for wide rows (smolgen's H*g = 8192).
-__global__ void layernorm_block_kernel(const __nv_bfloat16 *__restrict__ in, int width,
-                                       const float *__restrict__ gamma,
-                                       const float *__restrict__ beta, float eps,
-                                       __nv_bfloat16 *__restrict__ out) {
+// One CTA (256 threads) per row for wide rows (smolgen's H*g = 8192): the row
+// is read once into registers (VPT values per thread in 8-value groups, each
+// warp instruction covering 512 contiguous bytes), then mean, variance and
+// the normalised output come from the registers.
+template <int VPT>
+__global__ void __launch_bounds__(256)
+    layernorm_block_kernel(const __nv_bfloat16 *__restrict__ in, int width,
+                           const float *__restrict__ gamma, const float *__restrict__ beta,
+                           float eps, __nv_bfloat16 *__restrict__ out) {
+  constexpr int NG = VPT / 8;
   const long long row = blockIdx.x;
   const __nv_bfloat16 *src = in + row * width;
-  __shared__ float red[32];
-  float s = 0.0f;
-  for (int c = threadIdx.x * 8; c < width; c += blockDim.x * 8) {
-    const uint4 u = *reinterpret_cast<const uint4 *>(src + c);
+  __shared__ float red[8];
+  float v[VPT];
+#pragma unroll
+  for (int q = 0; q < NG; ++q) {
+    const uint4 u = *reinterpret_cast<const uint4 *>(src + q * 2048 + threadIdx.x * 8);
     const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
       const float2 f = unpack_bf16x2(w[e]);
-      s += f.x + f.y;
+      v[8 * q + 2 * e] = f.x;
+      v[8 * q + 2 * e + 1] = f.y;
     }
   }
   auto block_sum = [&](float x) {
 #pragma unroll
     for (int o = 16; o; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
-    __syncthreads();
+    __syncthreads();  // red[] of the previous reduction has been read
     if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = x;
     __syncthreads();
     float t = 0.0f;
-    for (int i = 0; i < static_cast<int>(blockDim.x >> 5); ++i) t += red[i];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) t += red[i];
     return t;
   };
+  float s = 0.0f;
+#pragma unroll
+  for (int i = 0; i < VPT; ++i) s += v[i];
   const float mean = block_sum(s) / static_cast<float>(width);
   float sq = 0.0f;
-  for (int c = threadIdx.x * 8; c < width; c += blockDim.x * 8) {
-    const uint4 u = *reinterpret_cast<const uint4 *>(src + c);
-    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float2 f = unpack_bf16x2(w[e]);
-      sq += (f.x - mean) * (f.x - mean) + (f.y - mean) * (f.y - mean);
-    }
+  for (int i = 0; i < VPT; ++i) {
+    const float t = v[i] - mean;
+    sq += t * t;
   }
   const float inv = 1.0f / sqrtf(block_sum(sq) / static_cast<float>(width) + eps);
-  for (int c = threadIdx.x * 8; c < width; c += blockDim.x * 8) {
-    const uint4 u = *reinterpret_cast<const uint4 *>(src + c);
-    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int q = 0; q < NG; ++q) {
+    const int c = q * 2048 + threadIdx.x * 8;
+    float g[8], b[8];
+    load_g<Fmt::F32, 8>(gamma, c, g);
+    load_g<Fmt::F32, 8>(beta, c, b);
     uint32_t o[4];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float2 f = unpack_bf16x2(w[e]);
-      const int k = c + 2 * e;
-      o[e] = pack_bf16x2((f.x - mean) * inv * gamma[k] + beta[k],
-                         (f.y - mean) * inv * gamma[k + 1] + beta[k + 1]);
-    }
+    for (int e = 0; e < 4; ++e)
+      o[e] = pack_bf16x2((v[8 * q + 2 * e] - mean) * inv * g[2 * e] + b[2 * e],
+                         (v[8 * q + 2 * e + 1] - mean) * inv * g[2 * e + 1] + b[2 * e + 1]);
     *reinterpret_cast<uint4 *>(out + row * width + c) = make_uint4(o[0], o[1], o[2], o[3]);
   }
 }
@@ -343,10 +350,18 @@ void launch_layernorm(const void *in, bool in_f32, int rows, int width, const fl
                       const float *beta, float eps, const float *multT, const float *addT,
                       __nv_bfloat16 *out, float *out_f32, cudaStream_t s) {
   if (width != 128 && width != 256 && width != 512 && width != 1024) {
-    // wide bf16 rows (smolgen's H*g); no gates, no fp32 output on this path
-    layernorm_block_kernel<<<rows, 256, 0, s>>>(static_cast<const __nv_bfloat16 *>(in), width,
-                                                gamma, beta, eps, out);
-    return;
+    // wide bf16 rows (smolgen's H*g, a multiple of 2048 up to 16384); no
+    // gates, no fp32 output on this path
+    const __nv_bfloat16 *src = static_cast<const __nv_bfloat16 *>(in);
+    switch (width) {
+    case 2048: layernorm_block_kernel<8><<<rows, 256, 0, s>>>(src, width, gamma, beta, eps, out); return;
+    case 4096: layernorm_block_kernel<16><<<rows, 256, 0, s>>>(src, width, gamma, beta, eps, out); return;
+    case 6144: layernorm_block_kernel<24><<<rows, 256, 0, s>>>(src, width, gamma, beta, eps, out); return;
+    case 8192: layernorm_block_kernel<32><<<rows, 256, 0, s>>>(src, width, gamma, beta, eps, out); return;
+    case 12288: layernorm_block_kernel<48><<<rows, 256, 0, s>>>(src, width, gamma, beta, eps, out); return;
+    case 16384: layernorm_block_kernel<64><<<rows, 256, 0, s>>>(src, width, gamma, beta, eps, out); return;
+    default: return;
+    }
   }
   launch_layernorm_q(in, in_f32 ? Fmt::F32 : Fmt::BF16, rows, width, gamma, beta, eps, multT, addT,
                      out, out_f32, Fmt::F32, nullptr, nullptr, s);

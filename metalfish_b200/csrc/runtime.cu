@@ -147,6 +147,12 @@ const char *validate(const mfb200_net_desc &n) {
       n.smolgen_hidden != 1024)
     return "smolgen hidden must be 128, 256, 512 or 1024";
   if (n.smolgen_gen <= 0 || n.smolgen_gen % 16) return "smolgen gen must be a multiple of 16";
+  {
+    const int hg = n.heads * n.smolgen_gen;  // width of the smolgen LN rows
+    bool ok = hg == 128 || hg == 256 || hg == 512 || hg == 1024;
+    for (int k : {1, 2, 3, 4, 6, 8}) ok = ok || hg == 2048 * k;
+    if (!ok) return "heads x smolgen gen must be 128, 256, 512, 1024 or 2048 x {1,2,3,4,6,8}";
+  }
   if (n.policy_d <= 0 || n.policy_d % 64) return "policy embedding must be a multiple of 64";
   if (n.value_emb <= 0 || n.mlh_emb <= 0 || n.value_emb + n.mlh_emb > 64)
     return "value + moves-left embeddings must fit in 64 columns";
