@@ -66,6 +66,8 @@ def run_gemm(M, N, K, bn, mode=0, act=0, bias=True, alpha=0.5, seed=0, out_f32=F
     (128, 64, 64, 64),
     (256, 512, 1024, 256),
     (300, 3104, 1024, 256),  # ragged M, N not a multiple of the tile
+    (512, 416, 1024, 256),   # partial last tile of 160 columns
+    (384, 288, 1536, 256),   # partial last tile of 32 columns
     (1000, 1536, 1024, 128),
     (64, 4096, 256, 256),    # M smaller than one tile
     (517, 64, 192, 64),
