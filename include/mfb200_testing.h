@@ -39,8 +39,8 @@ MFB200_API int mfb200_debug_gemm_ln(int M, int N, int K, int bn, const void *A, 
                                     const float *gamma, const float *beta, float eps,
                                     float *out_f32, uint16_t *out_bf16, unsigned *status_out);
 
-/* Mean device time (ms) of `iters` back-to-back launches of one bf16 GEMM on
- * synthetic device data (for profiling the kernel in isolation); mode and
+/* Mean device time (ms) of `iters` back-to-back launches of one GEMM on
+ * pseudo-random device operands (for profiling the kernel in isolation); mode and
  * out_f32 as for mfb200_debug_gemm (mode 2: residual + LayerNorm); dtype 0 bf16,
  * 1 e4m3, 2 fp16 operands. */
 MFB200_API int mfb200_debug_gemm_bench(int M, int N, int K, int bn, int mode, int act, int out_f32,

@@ -1,6 +1,8 @@
 // debug_api.cu -- self-contained kernel entry points for unit tests
 // (include/mfb200_testing.h). Each call allocates its own device buffers,
 // copies host inputs in, runs ONE kernel and copies the result back.
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
 #include <cuda_fp8.h>
 
 #include <cstdio>
@@ -89,6 +91,31 @@ extern "C" int mfb200_debug_gemm(int M, int N, int K, int bn, int fp8, const voi
 
 // Times `iters` back-to-back launches of one GEMM on random device data
 // (bf16, bias, optional fp32 output); returns the mean ms per launch.
+// Pseudo-random operand fill (an integer hash of the index): values in
+// [-1, 1) for 16-bit formats, e4m3 codes of magnitude below 1 for 8-bit.
+// Random operands matter for timing: tensor-core power, and so the clock the
+// GPU holds under its power cap, depends on how many bits toggle.
+__global__ void fill_random_kernel(uint16_t *p, long long n, int dtype, uint32_t seed) {
+  const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  uint32_t h = static_cast<uint32_t>(i) * 0x9E3779B1u ^ seed;
+  h ^= h >> 15;
+  h *= 0x85EBCA77u;
+  h ^= h >> 13;
+  h *= 0xC2B2AE3Du;
+  h ^= h >> 16;
+  const float f = static_cast<float>(h & 0xFFFFu) / 32768.0f - 1.0f;
+  if (dtype == 1) {  // two e4m3 values per 16-bit word
+    const uint16_t lo = static_cast<uint16_t>((h & 0x80u) | ((h >> 8) & 0x37u));
+    const uint16_t hi = static_cast<uint16_t>(((h >> 16) & 0x80u) | ((h >> 24) & 0x37u));
+    p[i] = static_cast<uint16_t>(lo | (hi << 8));
+  } else if (dtype == 2) {
+    p[i] = __half_as_ushort(__float2half_rn(f));
+  } else {
+    p[i] = __bfloat16_as_ushort(__float2bfloat16_rn(f));
+  }
+}
+
 extern "C" int mfb200_debug_gemm_bench(int M, int N, int K, int bn, int mode, int act,
                                        int out_f32, int iters, int dtype, float *ms_out) {
   DevBuf dA, dW, dB, dR, dO, dS, dO2, dG, dRS;
@@ -97,8 +124,14 @@ extern "C" int mfb200_debug_gemm_bench(int M, int N, int K, int bn, int mode, in
       !dO2.alloc(size_t(M) * N * 2) || !dG.alloc(N * 4) || !dRS.alloc(size_t(M) * 16 * 8))
     return 1;
   cudaMemset(dG.p, 0, N * 4);
-  cudaMemset(dA.p, 0x3c, size_t(M) * K * 2);  // small finite bf16 values
-  cudaMemset(dW.p, 0x3c, size_t(N) * K * 2);
+  {
+    const long long na = static_cast<long long>(M) * K * (dtype == 1 ? 1 : 2) / 2;
+    const long long nw = static_cast<long long>(N) * K * (dtype == 1 ? 1 : 2) / 2;
+    fill_random_kernel<<<static_cast<unsigned>((na + 255) / 256), 256>>>(
+        static_cast<uint16_t *>(dA.p), na, dtype, 1u);
+    fill_random_kernel<<<static_cast<unsigned>((nw + 255) / 256), 256>>>(
+        static_cast<uint16_t *>(dW.p), nw, dtype, 2u);
+  }
   cudaMemset(dB.p, 0, N * 4);
   cudaMemset(dR.p, 0, size_t(M) * N * 4);
   cudaMemset(dS.p, 0, 4);

@@ -66,6 +66,22 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait that may suspend the thread until the phase completes, for at most
+// kSuspendNs: a waiting warp then issues nothing instead of spinning (the
+// spinning of idle warps costs power, and the GPU runs under a power cap).
+constexpr uint32_t kSuspendNs = 200000;
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t *bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendNs)
+      : "memory");
+  return ok != 0;
+}
+
 // Bounded wait on an mbarrier phase. Returns false (and records `code` in
 // *status and raises *abort_flag) on timeout or when another role already
 // aborted.
@@ -74,8 +90,8 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, unsign
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = global_ns();
   for (uint32_t it = 1;; ++it) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 255u) == 0) {
+    if (mbar_try_wait_sleep(bar, parity)) return true;
+    if ((it & 7u) == 0) {
       if (*abort_flag) return false;
       if (global_ns() - t0 > kWaitLimitNs) {
         atomicCAS(status, 0u, code);
@@ -122,13 +138,24 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t *bar, uint32_t pa
   return ok != 0;
 }
 // Bounded wait with cluster-scope acquire (see mbar_wait).
+__device__ __forceinline__ bool mbar_try_wait_cluster_sleep(uint64_t *bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendNs)
+      : "memory");
+  return ok != 0;
+}
 __device__ __forceinline__ bool mbar_wait_cluster(uint64_t *bar, uint32_t parity, unsigned *status,
                                                   unsigned code, volatile int *abort_flag) {
   if (mbar_try_wait_cluster(bar, parity)) return true;
   const unsigned long long t0 = global_ns();
   for (uint32_t it = 1;; ++it) {
-    if (mbar_try_wait_cluster(bar, parity)) return true;
-    if ((it & 255u) == 0) {
+    if (mbar_try_wait_cluster_sleep(bar, parity)) return true;
+    if ((it & 7u) == 0) {
       if (*abort_flag) return false;
       if (global_ns() - t0 > kWaitLimitNs) {
         atomicCAS(status, 0u, code);
