@@ -226,6 +226,9 @@ def main():
     ap.add_argument("--precision", default="bf16", choices=["bf16", "fp8"])
     ap.add_argument("--fp8-gemms", type=int, default=0, help="FP8 GEMM-group mask (0 = all)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--sweep", default="",
+                    help="comma-separated batch sizes: print one latency/throughput JSON line per "
+                         "batch on 1 GPU instead of the contract line")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     rank, local, world = dist_setup(args.gpus)
@@ -237,6 +240,9 @@ def main():
     from metalfish_b200 import synthetic
     from metalfish_b200.network import Timing, create_network
 
+    if args.sweep:
+        run_sweep(args, [int(x) for x in args.sweep.split(",")])
+        return
     cfg = synthetic.BT4
     B = args.batch
     tensors = synthetic.generate(cfg, WEIGHT_SEED)
@@ -311,6 +317,10 @@ def main():
     barrier(world)
     e2e_value = B * world * args.steps / e2e_s
 
+    # ---- batch-1 latency (the per-leaf MCTS case): device time of one
+    # graph-launched forward, and the host round trip through mfb200_evaluate
+    lat = batch1_latency(net, dev, stream, shard, L) if rank == 0 else None
+
     # ---- roofline. Dominant kernel: the QKV(+smolgen compress) projection
     # GEMM, the largest single stage (15 launches per forward; the CTA-pair
     # tcgen05 kernel in bf16, the single-CTA one in e4m3), achieved = its
@@ -363,6 +373,15 @@ def main():
                                       "launches": len(gemm)}},
             "flops_per_position": {"encoder_gemm": enc["encoder_gemm_flops"], "all_matmul": enc["total_flops"]},
             "model_tflops": value * enc["total_flops"] / 1e12 / world,
+            "tensor_roofline": {
+                "per_gpu_encoder_tflops": value * enc["encoder_gemm_flops"] / 1e12 / world,
+                "frac_of_measured_burst": value * enc["encoder_gemm_flops"] / 1e12 / world
+                / (burst * (2.0 if args.precision == "fp8" else 1.0)),
+                "frac_of_nominal_dense": value * enc["encoder_gemm_flops"] / 1e12 / world
+                / (4500.0 if args.precision == "fp8" else 2250.0),
+                "note": "encoder QKV/O/FFN FLOPs (14.09 GFLOP per position) per GPU against the "
+                        "measured cuBLAS bf16 burst peak (x2 for e4m3) and the nominal dense peak"},
+            "latency_batch1_ms": lat,
             "stage_ms": stage_summary(stages),
             "stage_ms_total": total_stage_ms,
             "clocks": clocks,
@@ -370,6 +389,90 @@ def main():
         if not args.no_cpu_baseline and world == 1:
             line["cpu_baseline"] = cpu_baseline(cfg, tensors)
         print(json.dumps(line), flush=True)
+    net.close()
+
+
+def batch1_latency(net, dev, stream, shard, L, iters: int = 200):
+    """p50/p99 of the batch-1 forward: device time (CUDA events around one
+    graph launch) and the host round trip through mfb200_evaluate."""
+    import torch
+    d_m = torch.from_numpy(shard.masks[:1].view(np.int64)).to(dev)
+    d_v = torch.from_numpy(shard.values[:1]).to(dev)
+    d_p = torch.empty((1, 1858), dtype=torch.float32, device=dev)
+    d_w = torch.empty((1, 3), dtype=torch.float32, device=dev)
+    d_l = torch.empty((1,), dtype=torch.float32, device=dev)
+    h_m = torch.from_numpy(shard.masks[:1].view(np.int64)).pin_memory()
+    h_v = torch.from_numpy(shard.values[:1]).pin_memory()
+    h_p = torch.empty((1, 1858), dtype=torch.float32).pin_memory()
+    h_w = torch.empty((1, 3), dtype=torch.float32).pin_memory()
+    h_l = torch.empty((1,), dtype=torch.float32).pin_memory()
+
+    def dev_step():
+        net.evaluate_device(d_m.data_ptr(), d_v.data_ptr(), 1, d_p.data_ptr(), d_w.data_ptr(),
+                            d_l.data_ptr(), stream.cuda_stream)
+
+    for _ in range(5):
+        dev_step()
+    torch.cuda.synchronize(dev)
+    dev_ms = []
+    for _ in range(iters):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        dev_step()
+        e1.record(stream)
+        e1.synchronize()
+        dev_ms.append(e0.elapsed_time(e1))
+    host_ms = []
+    for i in range(iters + 5):
+        t0 = time.perf_counter()
+        rc = L.mfb200_evaluate(net._h, h_m.data_ptr(), h_v.data_ptr(), 1, h_p.data_ptr(),
+                               h_w.data_ptr(), h_l.data_ptr(), None)
+        if rc:
+            raise RuntimeError(L.mfb200_last_error(net._h).decode())
+        if i >= 5:
+            host_ms.append((time.perf_counter() - t0) * 1e3)
+    q = lambda xs, f: float(np.percentile(np.asarray(xs), f))
+    return {"device_p50": q(dev_ms, 50), "device_p99": q(dev_ms, 99),
+            "e2e_p50": q(host_ms, 50), "e2e_p99": q(host_ms, 99), "iters": iters}
+
+
+def run_sweep(args, batches):
+    """Config 3 of the baseline: latency and positions/s per batch size on
+    one GPU (device time of graph-launched forwards, inputs resident)."""
+    import torch
+    from metalfish_b200 import synthetic
+    from metalfish_b200.network import create_network
+    cfg = synthetic.BT4
+    tensors = synthetic.generate(cfg, WEIGHT_SEED)
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    net = create_network(cfg, tensors, device=0, max_batch=max(batches), precision=args.precision,
+                         fp8_gemms=args.fp8_gemms,
+                         calibration=load_positions(2048).slice(1024, 2048) if args.precision == "fp8" else None)
+    stream = torch.cuda.Stream(dev)
+    inp = load_positions(max(batches))
+    d_m = torch.from_numpy(inp.masks.view(np.int64)).to(dev)
+    d_v = torch.from_numpy(inp.values).to(dev)
+    nb = max(batches)
+    d_p = torch.empty((nb, 1858), dtype=torch.float32, device=dev)
+    d_w = torch.empty((nb, 3), dtype=torch.float32, device=dev)
+    d_l = torch.empty((nb,), dtype=torch.float32, device=dev)
+    for B in batches:
+        def step():
+            net.evaluate_device(d_m.data_ptr(), d_v.data_ptr(), B, d_p.data_ptr(), d_w.data_ptr(),
+                                d_l.data_ptr(), stream.cuda_stream)
+        for _ in range(max(args.warmup, 3)):
+            step()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            step()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        ms = e0.elapsed_time(e1) / args.steps
+        print(json.dumps({"batch": B, "ms_per_batch": ms, "positions_per_s": B / (ms / 1e3),
+                          "precision": args.precision, "steps": args.steps}), flush=True)
     net.close()
 
 

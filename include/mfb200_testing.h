@@ -17,6 +17,10 @@ extern "C" {
  * planned afterwards (tests run both kernels). */
 MFB200_API void mfb200_debug_set_gemm_pairs(int enable);
 
+/* Launch the kernels of forwards planned afterwards with (1, the default) or
+ * without (0) programmatic dependent launch. */
+MFB200_API void mfb200_debug_set_pdl(int enable);
+
 /* out[M,N] (bf16 bits) = epilogue(A[M,K] . W[N,K]^T) through the tcgen05 GEMM.
  * A/W are bf16 bits (fp8 = 0), e4m3 bytes (fp8 = 1) or fp16 bits (fp8 = 2); resid is fp32; out is
  * fp32 when out_f32 = 1, fp16 bits when out_f32 = 2, else bf16 bits. mode: 0

@@ -30,6 +30,8 @@ def _declare(L: ctypes.CDLL) -> None:
     L.mfb200_debug_gemm.restype = c_int
     L.mfb200_debug_gemm.argtypes = [c_int, c_int, c_int, c_int, c_int, vp, vp, vp, c_int, c_int,
                                     vp, c_float, vp, vp, c_float, vp, c_float, c_int, c_int, vp, vp]
+    L.mfb200_debug_set_pdl.restype = None
+    L.mfb200_debug_set_pdl.argtypes = [c_int]
     L.mfb200_debug_set_gemm_pairs.restype = None
     L.mfb200_debug_set_gemm_pairs.argtypes = [c_int]
     L.mfb200_debug_gemm_bench.restype = c_int

@@ -26,6 +26,8 @@ struct DevBuf {
 
 extern "C" void mfb200_debug_set_gemm_pairs(int enable) { set_gemm_pairs(enable != 0); }
 
+extern "C" void mfb200_debug_set_pdl(int enable) { set_pdl(enable != 0); }
+
 extern "C" int mfb200_debug_gemm(int M, int N, int K, int bn, int fp8, const void *A,
                                  const void *W, const float *bias, int mode, int act,
                                  const float *resid, float alpha, const float *ln_gamma,

@@ -100,25 +100,12 @@ static cudaError_t launch_t(const GemmLaunch &g, cudaStream_t stream) {
     if (e != cudaSuccess) return e;
     attr_done[dev] = true;
   }
-  if (g.args.mode == kEpiResidLN && g.args.cluster_n > 1) {
-    // the CTAs covering one row block form a thread-block cluster
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = g.grid;
-    cfg.blockDim = dim3(S::THREADS);
-    cfg.dynamicSmemBytes = S::SMEM_BYTES;
-    cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = static_cast<unsigned>(g.args.cluster_n);
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, gemm_sm100_kernel<BN, FP8, LN>, g.tmA, g.tmB, g.tmOut, g.tmOut2,
-                              g.tmRes, g.args);
-  }
-  gemm_sm100_kernel<BN, FP8, LN><<<g.grid, S::THREADS, S::SMEM_BYTES, stream>>>(
-      g.tmA, g.tmB, g.tmOut, g.tmOut2, g.tmRes, g.args);
+  // the CTAs covering one row block of the LN epilogue form a cluster
+  const int cluster = (g.args.mode == kEpiResidLN && g.args.cluster_n > 1) ? g.args.cluster_n : 1;
+  const cudaError_t e = launch_k(gemm_sm100_kernel<BN, FP8, LN>, g.grid, dim3(S::THREADS),
+                                 S::SMEM_BYTES, stream, cluster, g.tmA, g.tmB, g.tmOut, g.tmOut2,
+                                 g.tmRes, g.args);
+  if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
 
@@ -196,20 +183,8 @@ static cudaError_t launch_pair_t(const GemmLaunch &g, cudaStream_t stream) {
     if (e != cudaSuccess) return e;
     attr_done[dev] = true;
   }
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = g.grid;
-  cfg.blockDim = dim3(S::THREADS);
-  cfg.dynamicSmemBytes = S::SMEM_BYTES;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 2;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, gemm_pair_kernel<FP8>, g.tmA, g.tmB, g.tmOut, g.tmOut2, g.tmRes,
-                            g.args);
+  return launch_k(gemm_pair_kernel<FP8>, g.grid, dim3(S::THREADS), S::SMEM_BYTES, stream, 2, g.tmA,
+                  g.tmB, g.tmOut, g.tmOut2, g.tmRes, g.args);
 }
 
 static int max_clusters(int bn, bool fp8, int csize) {

@@ -23,6 +23,7 @@
 #include <cuda_fp16.h>
 #include <cuda_fp8.h>
 
+#include "pdl.cuh"
 #include "sm100_ptx.cuh"
 
 namespace mfb200 {
@@ -544,6 +545,10 @@ __global__ void __launch_bounds__(64 + 32 * (LN ? kEpiWarpsLN : kEpiWarpsMax), 1
   tc_fence_after();
   if (ln) cluster_sync();  // peers' barriers are initialised before any remote arrive
   const uint32_t tmem_base = *tmem_slot;
+  // the prologue above overlaps the previous kernel; operands and outputs
+  // are touched only after it has completed
+  pdl_wait();
+  pdl_launch();
 
   if (warp == 0) {
     if (lane == 0) {
@@ -783,6 +788,8 @@ __global__ void __launch_bounds__(64 + 32 * kEpiWarpsMax, 1)
   tc_fence_after();
   cluster_sync();  // both CTAs' barriers exist before any cross-CTA arrive or load
   const uint32_t tmem_base = *tmem_slot;
+  pdl_wait();
+  pdl_launch();
 
   if (warp == 0) {
     if (lane == 0) {

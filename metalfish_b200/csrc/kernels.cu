@@ -6,8 +6,16 @@
 
 #include "gemm_sm100.cuh"
 #include "kernels.cuh"
+#include "pdl.cuh"
 
 namespace mfb200 {
+
+namespace {
+bool g_pdl = true;
+}
+bool pdl_enabled() { return g_pdl; }
+void set_pdl(bool enable) { g_pdl = enable; }
+
 
 // ------------------------------------------------------------------ helpers
 __device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
@@ -57,6 +65,8 @@ __device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint32_t (&a
 // square-major order (src/nn/cpu/cpu_network.cpp:731-747).
 __global__ void unpack_kernel(const uint64_t *__restrict__ masks, const float *__restrict__ values,
                               __nv_bfloat16 *__restrict__ x0, __nv_bfloat16 *__restrict__ p) {
+  pdl_wait();
+  pdl_launch();
   const int b = blockIdx.x;
   __shared__ uint64_t sm[kPlanes];
   __shared__ float sv[kPlanes];
@@ -90,12 +100,14 @@ __global__ void unpack_kernel(const uint64_t *__restrict__ masks, const float *_
 
 void launch_unpack(const uint64_t *masks, const float *values, int batch, __nv_bfloat16 *x0,
                    __nv_bfloat16 *p, cudaStream_t s) {
-  unpack_kernel<<<batch, 128, 0, s>>>(masks, values, x0, p);
+  launch_k(unpack_kernel, dim3(batch), dim3(128), 0, s, 1, masks, values, x0, p);
 }
 
 // PEo[b, sq*pe + e] -> X0[b*64 + sq, 112 + e]; 8 columns (16 bytes) per thread.
 __global__ void pe_concat_kernel(const __nv_bfloat16 *__restrict__ peo, int total_rows, int pe,
                                  __nv_bfloat16 *__restrict__ x0) {
+  pdl_wait();
+  pdl_launch();
   const int chunks = pe / 8;
   const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= static_cast<long long>(total_rows) * chunks) return;
@@ -109,8 +121,8 @@ __global__ void pe_concat_kernel(const __nv_bfloat16 *__restrict__ peo, int tota
 void launch_pe_concat(const __nv_bfloat16 *peo, int batch, int pe, __nv_bfloat16 *x0,
                       cudaStream_t s) {
   const long long n = static_cast<long long>(batch) * kSquares * (pe / 8);
-  pe_concat_kernel<<<static_cast<unsigned>((n + 255) / 256), 256, 0, s>>>(peo, batch * kSquares,
-                                                                          pe, x0);
+  launch_k(pe_concat_kernel, dim3(static_cast<unsigned>((n + 255) / 256)), dim3(256), 0, s, 1, peo,
+           batch * kSquares, pe, x0);
 }
 
 // ------------------------------------------------------------------ layernorm
@@ -155,6 +167,8 @@ __global__ void __launch_bounds__(256)
                           const float *__restrict__ addT, __nv_bfloat16 *__restrict__ out,
                           void *__restrict__ out_res, uint8_t *__restrict__ out8,
                           const float *__restrict__ scale8) {
+  pdl_wait();
+  pdl_launch();
   constexpr int W = 32 * VPL;
   constexpr int G = (VPL % 8 == 0) ? 8 : 4;
   constexpr int NG = VPL / G;  // groups per lane
@@ -247,6 +261,8 @@ __global__ void __launch_bounds__(256)
     layernorm_block_kernel(const __nv_bfloat16 *__restrict__ in, int width,
                            const float *__restrict__ gamma, const float *__restrict__ beta,
                            float eps, __nv_bfloat16 *__restrict__ out) {
+  pdl_wait();
+  pdl_launch();
   constexpr int NG = VPT / 8;
   const long long row = blockIdx.x;
   const __nv_bfloat16 *src = in + row * width;
@@ -307,11 +323,9 @@ static void ln_warp_in(const void *in, int rows, const float *gamma, const float
   const int wpb = 8;
   const unsigned grid = static_cast<unsigned>((rows + wpb - 1) / wpb);
   if (res_fmt == Fmt::F16)
-    layernorm_warp_kernel<VPL, IN, Fmt::F16><<<grid, 32 * wpb, 0, s>>>(
-        in, rows, gamma, beta, eps, multT, addT, out, out_res, out8, scale8);
+    launch_k(layernorm_warp_kernel<VPL, IN, Fmt::F16>, dim3(grid), dim3(32 * wpb), 0, s, 1, in, rows, gamma, beta, eps, multT, addT, out, out_res, out8, scale8);
   else
-    layernorm_warp_kernel<VPL, IN, Fmt::F32><<<grid, 32 * wpb, 0, s>>>(
-        in, rows, gamma, beta, eps, multT, addT, out, out_res, out8, scale8);
+    launch_k(layernorm_warp_kernel<VPL, IN, Fmt::F32>, dim3(grid), dim3(32 * wpb), 0, s, 1, in, rows, gamma, beta, eps, multT, addT, out, out_res, out8, scale8);
 }
 
 template <int VPL>
@@ -354,12 +368,12 @@ void launch_layernorm(const void *in, bool in_f32, int rows, int width, const fl
     // gates, no fp32 output on this path
     const __nv_bfloat16 *src = static_cast<const __nv_bfloat16 *>(in);
     switch (width) {
-    case 2048: layernorm_block_kernel<8><<<rows, 256, 0, s>>>(src, width, gamma, beta, eps, out); return;
-    case 4096: layernorm_block_kernel<16><<<rows, 256, 0, s>>>(src, width, gamma, beta, eps, out); return;
-    case 6144: layernorm_block_kernel<24><<<rows, 256, 0, s>>>(src, width, gamma, beta, eps, out); return;
-    case 8192: layernorm_block_kernel<32><<<rows, 256, 0, s>>>(src, width, gamma, beta, eps, out); return;
-    case 12288: layernorm_block_kernel<48><<<rows, 256, 0, s>>>(src, width, gamma, beta, eps, out); return;
-    case 16384: layernorm_block_kernel<64><<<rows, 256, 0, s>>>(src, width, gamma, beta, eps, out); return;
+    case 2048: launch_k(layernorm_block_kernel<8>, dim3(rows), dim3(256), 0, s, 1, src, width, gamma, beta, eps, out); return;
+    case 4096: launch_k(layernorm_block_kernel<16>, dim3(rows), dim3(256), 0, s, 1, src, width, gamma, beta, eps, out); return;
+    case 6144: launch_k(layernorm_block_kernel<24>, dim3(rows), dim3(256), 0, s, 1, src, width, gamma, beta, eps, out); return;
+    case 8192: launch_k(layernorm_block_kernel<32>, dim3(rows), dim3(256), 0, s, 1, src, width, gamma, beta, eps, out); return;
+    case 12288: launch_k(layernorm_block_kernel<48>, dim3(rows), dim3(256), 0, s, 1, src, width, gamma, beta, eps, out); return;
+    case 16384: launch_k(layernorm_block_kernel<64>, dim3(rows), dim3(256), 0, s, 1, src, width, gamma, beta, eps, out); return;
     default: return;
     }
   }
@@ -376,6 +390,8 @@ __global__ void splitk_act_ln_kernel(const float *__restrict__ part, int splits,
                                      int rows, const float *__restrict__ bias, int act,
                                      const float *__restrict__ gamma, const float *__restrict__ beta,
                                      float eps, __nv_bfloat16 *__restrict__ out) {
+  pdl_wait();
+  pdl_launch();
   constexpr int W = 32 * VPL;
   const long long row = static_cast<long long>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
@@ -422,10 +438,10 @@ bool launch_splitk_act_ln(const float *part, int splits, long long stride, int r
   const int wpb = 8;
   const unsigned grid = static_cast<unsigned>((rows + wpb - 1) / wpb);
   switch (width) {
-  case 128: splitk_act_ln_kernel<4><<<grid, 32 * wpb, 0, s>>>(part, splits, stride, rows, bias, act, gamma, beta, eps, out); return true;
-  case 256: splitk_act_ln_kernel<8><<<grid, 32 * wpb, 0, s>>>(part, splits, stride, rows, bias, act, gamma, beta, eps, out); return true;
-  case 512: splitk_act_ln_kernel<16><<<grid, 32 * wpb, 0, s>>>(part, splits, stride, rows, bias, act, gamma, beta, eps, out); return true;
-  case 1024: splitk_act_ln_kernel<32><<<grid, 32 * wpb, 0, s>>>(part, splits, stride, rows, bias, act, gamma, beta, eps, out); return true;
+  case 128: launch_k(splitk_act_ln_kernel<4>, dim3(grid), dim3(32 * wpb), 0, s, 1, part, splits, stride, rows, bias, act, gamma, beta, eps, out); return true;
+  case 256: launch_k(splitk_act_ln_kernel<8>, dim3(grid), dim3(32 * wpb), 0, s, 1, part, splits, stride, rows, bias, act, gamma, beta, eps, out); return true;
+  case 512: launch_k(splitk_act_ln_kernel<16>, dim3(grid), dim3(32 * wpb), 0, s, 1, part, splits, stride, rows, bias, act, gamma, beta, eps, out); return true;
+  case 1024: launch_k(splitk_act_ln_kernel<32>, dim3(grid), dim3(32 * wpb), 0, s, 1, part, splits, stride, rows, bias, act, gamma, beta, eps, out); return true;
   default: return false;
   }
 }
@@ -444,6 +460,8 @@ __global__ void __launch_bounds__(128)
                      const __nv_bfloat16 *__restrict__ bias, int heads, int d,
                      __nv_bfloat16 *__restrict__ ctx, uint8_t *__restrict__ ctx8,
                      const float *__restrict__ scale8) {
+  pdl_wait();
+  pdl_launch();
   __shared__ __align__(16) __nv_bfloat16 sQ[kSquares * kQkvStride];
   __shared__ __align__(16) __nv_bfloat16 sK[kSquares * kQkvStride];
   __shared__ __align__(16) __nv_bfloat16 sV[kSquares * kQkvStride];
@@ -588,7 +606,7 @@ __global__ void __launch_bounds__(128)
 void launch_attention(const __nv_bfloat16 *qkv, long long ldq, const __nv_bfloat16 *bias,
                       int batch, int heads, int d, __nv_bfloat16 *ctx, cudaStream_t s,
                       uint8_t *ctx8, const float *scale8) {
-  attention_kernel<<<batch * heads, 128, 0, s>>>(qkv, ldq, bias, heads, d, ctx, ctx8, scale8);
+  launch_k(attention_kernel, dim3(batch * heads), dim3(128), 0, s, 1, qkv, ldq, bias, heads, d, ctx, ctx8, scale8);
 }
 
 // ------------------------------------------------------------------ absmax
@@ -596,6 +614,8 @@ void launch_attention(const __nv_bfloat16 *qkv, long long ldq, const __nv_bfloat
 // their bit patterns, so an integer atomicMax suffices). FP8 calibration.
 template <typename T>
 __global__ void absmax_kernel(const T *__restrict__ x, long long n, float *__restrict__ slot) {
+  pdl_wait();
+  pdl_launch();
   float m = 0.0f;
   for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
        i += static_cast<long long>(gridDim.x) * blockDim.x) {
@@ -612,21 +632,23 @@ __global__ void absmax_kernel(const T *__restrict__ x, long long n, float *__res
 
 void launch_absmax(const void *x, Fmt fmt, long long n, float *slot, cudaStream_t s) {
   if (fmt == Fmt::F32)
-    absmax_kernel<float><<<296, 256, 0, s>>>(static_cast<const float *>(x), n, slot);
+    launch_k(absmax_kernel<float>, dim3(296), dim3(256), 0, s, 1, static_cast<const float *>(x), n, slot);
   else if (fmt == Fmt::F16)
-    absmax_kernel<__half><<<296, 256, 0, s>>>(static_cast<const __half *>(x), n, slot);
+    launch_k(absmax_kernel<__half>, dim3(296), dim3(256), 0, s, 1, static_cast<const __half *>(x), n, slot);
   else
-    absmax_kernel<__nv_bfloat16><<<296, 256, 0, s>>>(static_cast<const __nv_bfloat16 *>(x), n, slot);
+    launch_k(absmax_kernel<__nv_bfloat16>, dim3(296), dim3(256), 0, s, 1, static_cast<const __nv_bfloat16 *>(x), n, slot);
 }
 
 // scales[i] = max(absmax[i], tiny) / 448 (e4m3's largest finite value)
 __global__ void absmax_to_scale_kernel(const float *absmax, int n, float *scales) {
+  pdl_wait();
+  pdl_launch();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n) scales[i] = fmaxf(absmax[i], 1e-6f) / 448.0f;
 }
 
 void launch_absmax_to_scale(const float *absmax, int n, float *scales, cudaStream_t s) {
-  absmax_to_scale_kernel<<<(n + 127) / 128, 128, 0, s>>>(absmax, n, scales);
+  launch_k(absmax_to_scale_kernel, dim3((n + 127) / 128), dim3(128), 0, s, 1, absmax, n, scales);
 }
 
 // ------------------------------------------------------------------ policy
@@ -640,6 +662,8 @@ constexpr int kPolStride = 72;  // padded smem row (144 bytes)
 __global__ void __launch_bounds__(128)
     policy_map_kernel(const __nv_bfloat16 *__restrict__ qk, int dp, const float *__restrict__ ppo3,
                       const int16_t *__restrict__ gather, float *__restrict__ policy) {
+  pdl_wait();
+  pdl_launch();
   // q/k double buffers; after the k-loop the same bytes hold the raw logits
   __shared__ __align__(16) __nv_bfloat16 sQK[4][kSquares * kPolStride];
   __nv_bfloat16(*sQ)[kSquares * kPolStride] = sQK;
@@ -742,7 +766,7 @@ __global__ void __launch_bounds__(128)
 
 void launch_policy_map(const __nv_bfloat16 *qk, int batch, int dp, const float *ppo3,
                        const int16_t *gather, float *policy, cudaStream_t s) {
-  policy_map_kernel<<<batch, 128, 0, s>>>(qk, dp, ppo3, gather, policy);
+  launch_k(policy_map_kernel, dim3(batch), dim3(128), 0, s, 1, qk, dp, ppo3, gather, policy);
 }
 
 // ------------------------------------------------------------------ heads
@@ -752,6 +776,8 @@ __global__ void heads_kernel(const __nv_bfloat16 *__restrict__ h, int batch, int
                              const float *__restrict__ w2v, const float *__restrict__ b2v,
                              const float *__restrict__ w2m, const float *__restrict__ b2m,
                              float *__restrict__ wdl, float *__restrict__ mlh) {
+  pdl_wait();
+  pdl_launch();
   const int warps = blockDim.x >> 5;
   const int b = blockIdx.x * warps + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
@@ -790,7 +816,7 @@ void launch_heads(const __nv_bfloat16 *h, int batch, int vh, int mh, const float
                   const float *b2v, const float *w2m, const float *b2m, float *wdl, float *mlh,
                   cudaStream_t s) {
   const int wpb = 8;
-  heads_kernel<<<(batch + wpb - 1) / wpb, 32 * wpb, 0, s>>>(h, batch, vh, mh, w2v, b2v, w2m, b2m,
+  launch_k(heads_kernel, dim3((batch + wpb - 1) / wpb), dim3(32 * wpb), 0, s, 1, h, batch, vh, mh, w2v, b2v, w2m, b2m,
                                                            wdl, mlh);
 }
 
