@@ -18,6 +18,10 @@ batch is sharded, weights replicated, no collective in the forward
 * roofline   -- the QKV projection GEMM (the largest stage), algorithmic
                 FLOPs / event time of its launches in this run; `gemm_all`
                 aggregates all tcgen05 GEMM launches of one forward.
+* e2e_priors -- the MCTS leaf path through mfb200_evaluate_priors: the same
+                host round trip, returning the softmax priors of each
+                position's legal moves (computed on the GPU) instead of the
+                1858 logits.
 * cpu_baseline -- the reference CPU backend (oracle/_ref, built from the
                 reference sources) or, if that binary is absent, the C
                 restatement, on a bounded sample on the host cores.
@@ -317,6 +321,38 @@ def main():
     barrier(world)
     e2e_value = B * world * args.steps / e2e_s
 
+    # ---- the MCTS leaf path through mfb200_evaluate_priors: the same forward,
+    # then the priors of each position's legal moves computed on the GPU and
+    # copied back instead of the 1858 logits (fixture legal-move lists)
+    mv = np.load(os.path.join(ROOT, "tests", "golden", "legal_moves.npz"))
+    ids = np.arange(rank * B, (rank + 1) * B) % len(mv["offsets"][:-1])
+    counts = mv["offsets"][ids + 1] - mv["offsets"][ids]
+    m_off = np.concatenate([[0], np.cumsum(counts)]).astype(np.int32)
+    m_idx = np.concatenate([mv["index"][mv["offsets"][i]:mv["offsets"][i + 1]] for i in ids]).astype(np.int16)
+    h_pri = torch.empty(int(m_off[-1]), dtype=torch.float32).pin_memory()
+    pin_off = torch.from_numpy(m_off).pin_memory()
+    pin_idx = torch.from_numpy(m_idx).pin_memory()
+
+    def priors_step():
+        rc = L.mfb200_evaluate_priors(net._h, pin_m.data_ptr(), pin_v.data_ptr(), B, pin_off.data_ptr(),
+                                      pin_idx.data_ptr(), ctypes.c_float(1.0), h_pri.data_ptr(),
+                                      h_wdl.data_ptr(), h_mlh.data_ptr(), None)
+        if rc:
+            raise RuntimeError(L.mfb200_last_error(net._h).decode())
+
+    for _ in range(args.warmup):
+        priors_step()
+    barrier(world)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        priors_step()
+    pr_s = all_max(time.perf_counter() - t0, world)
+    barrier(world)
+    e2e_priors = {"value": B * world * args.steps / pr_s, "unit": "positions/s",
+                  "h2d_bytes_per_step": int(B * 112 * 12 + (B + 1) * 4 + len(m_idx) * 2),
+                  "d2h_bytes_per_step": int(len(m_idx) * 4 + B * 16),
+                  "legal_moves_per_step": int(len(m_idx))}
+
     # ---- batch-1 latency (the per-leaf MCTS case): device time of one
     # graph-launched forward, and the host round trip through mfb200_evaluate
     lat = batch1_latency(net, dev, stream, shard, L) if rank == 0 else None
@@ -382,6 +418,7 @@ def main():
                 "note": "encoder QKV/O/FFN FLOPs (14.09 GFLOP per position) per GPU against the "
                         "measured cuBLAS bf16 burst peak (x2 for e4m3) and the nominal dense peak"},
             "latency_batch1_ms": lat,
+            "e2e_priors": e2e_priors,
             "stage_ms": stage_summary(stages),
             "stage_ms_total": total_stage_ms,
             "clocks": clocks,

@@ -15,6 +15,11 @@
  *                          PackInputPlanesRaw (src/nn/input_plane_packing.h:63-83) that
  *                          Cuda::CudaNetwork::RunBatch uploads (cuda_network.cpp:393-417);
  *                          outputs are the fields of NetworkOutput (src/nn/network_output.h:17-24)
+ *   mfb200_evaluate_priors <- EvaluateBatch followed by the MCTS leaf step on the
+ *                          caller's legal moves: the evaluator's per-move logit gather
+ *                          (src/mcts/evaluator.cpp:182-226, NNMCTSEvaluator::Impl::BuildResult)
+ *                          and the softmax of ApplyNNPolicyToNode
+ *                          (src/mcts/search.cpp:127-197)
  *   mfb200_capabilities <- NN::Network::GetBackendCapabilities / HasWDL / HasMovesLeft /
  *                          GetNetworkInfo (src/nn/network.h:21-51)
  *   mfb200_last_error   <- the std::runtime_error messages the reference throws
@@ -100,6 +105,26 @@ MFB200_API int mfb200_create(const mfb200_net_desc *desc, const void *weights_f3
  * be NULL. Blocks until the results are in host memory. */
 MFB200_API int mfb200_evaluate(mfb200_handle *h, const uint64_t *masks, const float *values, int batch,
                     float *policy, float *wdl, float *moves_left, mfb200_timing *timing);
+
+/* Host-buffer evaluation that returns, instead of the 1858 policy logits,
+ * the normalised prior of each legal move (what MCTS needs per leaf):
+ * move_offsets [batch + 1] is a CSR over move_index (move_offsets[0] is
+ * usually 0; the slice [move_offsets[b], move_offsets[b+1]) belongs to
+ * position b) and move_index holds the policy index of each legal move as
+ * the evaluator computes it (NN::MoveToNNIndex of the move, mirrored for
+ * black, with the encoder's transform); an index outside [0, 1858) counts as
+ * logit 0. priors [move_offsets[batch] - move_offsets[0]] receives, per
+ * position, FastExp((logit - max) / softmax_temp) normalised over its first
+ * min(n, 256) moves (uniform if the sum is not positive; moves past the
+ * 256th get 0), bit-identical to the reference's float arithmetic. wdl / moves_left as
+ * in mfb200_evaluate (either may be NULL). softmax_temp must be > 0; at most
+ * 256 moves per position on average. Blocks until the results are in host
+ * memory. */
+MFB200_API int mfb200_evaluate_priors(mfb200_handle *h, const uint64_t *masks, const float *values,
+                                      int batch, const int32_t *move_offsets,
+                                      const int16_t *move_index, float softmax_temp,
+                                      float *priors, float *wdl, float *moves_left,
+                                      mfb200_timing *timing);
 
 /* Device-buffer evaluation on device `cfg.device`, enqueued on `stream`
  * (a cudaStream_t; NULL = the handle's stream) without synchronising. All

@@ -609,6 +609,76 @@ void launch_attention(const __nv_bfloat16 *qkv, long long ldq, const __nv_bfloat
   launch_k(attention_kernel, dim3(batch * heads), dim3(128), 0, s, 1, qkv, ldq, bias, heads, d, ctx, ctx8, scale8);
 }
 
+// ------------------------------------------------------------------ legal-move priors
+// The MCTS leaf step after the forward: gather each legal move's raw policy
+// logit (src/mcts/evaluator.cpp:182-226; an index outside [0, 1858) gives
+// logit 0) and normalise as ApplyNNPolicyToNode does
+// (src/mcts/search.cpp:127-197): the first n = min(moves, 256) moves, their
+// max, e = FastExp((l - max) * inv_temp), the sum in move order, uniform 1/n
+// if the sum is not positive, else e * (1/sum); moves past the 256th get 0.
+// FastExp (src/mcts/core.h:38-44) is Schraudolph's exponential: clamp to
+// [-88, 88], then the float whose bits are trunc(x * 12102203) + (127 << 23).
+// One warp per position; the sum runs on one lane so that it adds in the
+// reference's order and the priors are bit-identical to it.
+__device__ __forceinline__ float fast_exp_mcts(float x) {
+  x = x < 88.0f ? x : 88.0f;
+  x = -88.0f < x ? x : -88.0f;
+  return __int_as_float(__float2int_rz(__fmul_rn(x, 12102203.0f)) + 1065353216);
+}
+
+constexpr int kMaxEdges = 256;
+
+__global__ void __launch_bounds__(256)
+    priors_kernel(const float *__restrict__ policy, int batch, const int32_t *__restrict__ offsets,
+                  const int16_t *__restrict__ index, float inv_temp, float *__restrict__ priors) {
+  pdl_wait();
+  pdl_launch();
+  __shared__ float se[8][kMaxEdges];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int b = blockIdx.x * 8 + warp;
+  if (b >= batch) return;
+  const int lo = offsets[b] - offsets[0];
+  const int moves = offsets[b + 1] - offsets[b];
+  const int n = moves < kMaxEdges ? moves : kMaxEdges;
+  float *e = se[warp];
+  const float *pol = policy + static_cast<long long>(b) * kPolicy;
+  float mx = -INFINITY;
+  for (int i = lane; i < n; i += 32) {
+    const int idx = index[lo + i];
+    const float l = (idx >= 0 && idx < kPolicy) ? pol[idx] : 0.0f;
+    e[i] = l;
+    mx = l > mx ? l : mx;
+  }
+  for (int i = n + lane; i < moves; i += 32) priors[lo + i] = 0.0f;
+  if (n == 0) return;
+#pragma unroll
+  for (int o = 16; o; o >>= 1) {
+    const float t = __shfl_xor_sync(0xffffffffu, mx, o);
+    mx = t > mx ? t : mx;
+  }
+  __syncwarp();
+  for (int i = lane; i < n; i += 32) e[i] = fast_exp_mcts(__fmul_rn(__fsub_rn(e[i], mx), inv_temp));
+  __syncwarp();
+  float sum = 0.0f;
+  if (lane == 0)
+    for (int i = 0; i < n; ++i) sum = __fadd_rn(sum, e[i]);
+  sum = __shfl_sync(0xffffffffu, sum, 0);
+  if (sum <= 0.0f) {
+    const float u = 1.0f / static_cast<float>(n);
+    for (int i = lane; i < n; i += 32) priors[lo + i] = u;
+    return;
+  }
+  const float inv_sum = 1.0f / sum;
+  for (int i = lane; i < n; i += 32) priors[lo + i] = __fmul_rn(e[i], inv_sum);
+}
+
+void launch_priors(const float *policy, int batch, const int32_t *offsets, const int16_t *index,
+                   float softmax_temp, float *priors, cudaStream_t s) {
+  if (batch <= 0) return;
+  launch_k(priors_kernel, dim3((batch + 7) / 8), dim3(256), 0, s, 1, policy, batch, offsets, index,
+           1.0f / softmax_temp, priors);
+}
+
 // ------------------------------------------------------------------ absmax
 // slot = max(slot, max |x|) over n values (non-negative floats order like
 // their bit patterns, so an integer atomicMax suffices). FP8 calibration.

@@ -61,6 +61,13 @@ void launch_attention(const __nv_bfloat16 *qkv, long long ldq, const __nv_bfloat
                       int batch, int heads, int d, __nv_bfloat16 *ctx, cudaStream_t s,
                       uint8_t *ctx8 = nullptr, const float *scale8 = nullptr);
 
+// Legal-move priors of `batch` positions from their policy logits
+// [batch, 1858]: offsets [batch + 1] (CSR into index, offsets[0] need not be
+// 0), index = policy index of each legal move; priors has offsets[batch] -
+// offsets[0] entries (see priors_kernel).
+void launch_priors(const float *policy, int batch, const int32_t *offsets, const int16_t *index,
+                   float softmax_temp, float *priors, cudaStream_t s);
+
 // FP8 calibration: *slot = max(*slot, max|x|) over n values of format `fmt`;
 // and scales[i] = absmax[i] / 448.
 void launch_absmax(const void *x, Fmt fmt, long long n, float *slot, cudaStream_t s);

@@ -226,6 +226,10 @@ class ArenaBuilder {
   std::vector<uint8_t> host;
 };
 
+// Legal moves per position the priors buffers hold on average (the
+// reference keeps at most 256 edges per node, src/mcts/search.cpp:49).
+constexpr int kMoveCapacity = 256;
+
 struct Shard {  // one GPU
   int device = 0;
   cudaStream_t stream = nullptr;
@@ -244,6 +248,9 @@ struct Shard {  // one GPU
   uint8_t *X8, *X1_8, *CTX8, *H8;  // e4m3 GEMM inputs (FP8 handles)
   float *scales, *absmax;    // per-tensor activation scales / calibration maxima
   float *policy, *wdl, *mlh;
+  int32_t *move_off;      // legal-move priors: CSR offsets [max_batch + 1]
+  int16_t *move_idx;      //   policy index per legal move [max_batch * 256]
+  float *priors;          //   priors per legal move [max_batch * 256]
   unsigned *status;
   cudaEvent_t ev[4];
   struct Step {
@@ -552,6 +559,9 @@ void alloc_workspace(Shard &S, const mfb200_net_desc &n, int max_batch, bool fp8
       {reinterpret_cast<void **>(&S.policy), B * kPolicy * 4},
       {reinterpret_cast<void **>(&S.wdl), B * 3 * 4},
       {reinterpret_cast<void **>(&S.mlh), B * 4},
+      {reinterpret_cast<void **>(&S.move_off), (B + 1) * 4},
+      {reinterpret_cast<void **>(&S.move_idx), B * kMoveCapacity * 2},
+      {reinterpret_cast<void **>(&S.priors), B * kMoveCapacity * 4},
       {reinterpret_cast<void **>(&S.status), 256},
       {reinterpret_cast<void **>(&S.scales), size_t(2 + 4 * n.layers) * 4},
       {reinterpret_cast<void **>(&S.absmax), size_t(2 + 4 * n.layers) * 4},
@@ -1032,7 +1042,100 @@ int eval_shard(mfb200_handle *h, Shard &S, const uint64_t *masks, const float *v
   cudaEventElapsedTime(&ms[3], S.ev[0], S.ev[3]);
   return 0;
 }
+// The forward followed by the legal-move priors of the shard's positions;
+// offsets/index/priors are the shard's slices of the caller's CSR arrays.
+int eval_shard_priors(mfb200_handle *h, Shard &S, const uint64_t *masks, const float *values,
+                      int B, const int32_t *offsets, const int16_t *index, float temp,
+                      float *priors, float *wdl, float *mlh, float *ms) {
+  check(cudaSetDevice(S.device), "cudaSetDevice");
+  cudaStream_t s = S.stream;
+  const int32_t nmoves = offsets[B] - offsets[0];
+  check(cudaEventRecord(S.ev[0], s), "event");
+  check(cudaMemcpyAsync(S.masks, masks, size_t(B) * kPlanes * 8, cudaMemcpyHostToDevice, s), "H2D masks");
+  check(cudaMemcpyAsync(S.values, values, size_t(B) * kPlanes * 4, cudaMemcpyHostToDevice, s), "H2D values");
+  check(cudaMemcpyAsync(S.move_off, offsets, size_t(B + 1) * 4, cudaMemcpyHostToDevice, s), "H2D offsets");
+  if (nmoves > 0)
+    check(cudaMemcpyAsync(S.move_idx, index, size_t(nmoves) * 2, cudaMemcpyHostToDevice, s), "H2D moves");
+  check(cudaEventRecord(S.ev[1], s), "event");
+  forward(h, S, B, s);
+  launch_priors(S.policy, B, S.move_off, S.move_idx, temp, S.priors, s);
+  check(cudaGetLastError(), "priors launch");
+  check(cudaEventRecord(S.ev[2], s), "event");
+  if (priors && nmoves > 0)
+    check(cudaMemcpyAsync(priors, S.priors, size_t(nmoves) * 4, cudaMemcpyDeviceToHost, s), "D2H priors");
+  if (wdl) check(cudaMemcpyAsync(wdl, S.wdl, size_t(B) * 12, cudaMemcpyDeviceToHost, s), "D2H wdl");
+  if (mlh) check(cudaMemcpyAsync(mlh, S.mlh, size_t(B) * 4, cudaMemcpyDeviceToHost, s), "D2H mlh");
+  check(cudaEventRecord(S.ev[3], s), "event");
+  check(cudaStreamSynchronize(s), "forward");
+  check_status(S);
+  cudaEventElapsedTime(&ms[0], S.ev[0], S.ev[1]);
+  cudaEventElapsedTime(&ms[1], S.ev[1], S.ev[2]);
+  cudaEventElapsedTime(&ms[2], S.ev[2], S.ev[3]);
+  cudaEventElapsedTime(&ms[3], S.ev[0], S.ev[3]);
+  return 0;
+}
 }  // namespace
+
+extern "C" int mfb200_evaluate_priors(mfb200_handle *h, const uint64_t *masks,
+                                      const float *values, int batch,
+                                      const int32_t *move_offsets, const int16_t *move_index,
+                                      float softmax_temp, float *priors, float *wdl, float *mlh,
+                                      mfb200_timing *timing) {
+  if (!h) return fail(nullptr, "mfb200_evaluate_priors: null handle");
+  std::lock_guard<std::mutex> lock(h->mu);
+  if (batch <= 0) return 0;
+  if (batch > h->cfg.max_batch)
+    return fail(h, "mfb200_evaluate_priors: batch " + std::to_string(batch) + " exceeds max_batch " +
+                       std::to_string(h->cfg.max_batch));
+  if (!masks || !values || !move_offsets || (!move_index && move_offsets[batch] != move_offsets[0]))
+    return fail(h, "mfb200_evaluate_priors: null input");
+  if (!(softmax_temp > 0.0f)) return fail(h, "mfb200_evaluate_priors: softmax_temp must be positive");
+  for (int b = 0; b < batch; ++b)
+    if (move_offsets[b + 1] < move_offsets[b])
+      return fail(h, "mfb200_evaluate_priors: move_offsets must be non-decreasing");
+  const int nd = static_cast<int>(h->shards.size());
+  const int per = (batch + nd - 1) / nd;
+  for (int i = 0; i < nd; ++i) {
+    const int lo = i * per, hi = std::min(batch, lo + per);
+    if (lo < hi && move_offsets[hi] - move_offsets[lo] > int64_t(per) * kMoveCapacity)
+      return fail(h, "mfb200_evaluate_priors: more than " + std::to_string(kMoveCapacity) +
+                         " legal moves per position on average");
+  }
+  std::vector<std::array<float, 4>> ms(nd, {0, 0, 0, 0});
+  std::vector<std::string> errs(nd);
+  auto work = [&](int i) {
+    const int lo = i * per, hi = std::min(batch, lo + per);
+    if (lo >= hi) return;
+    const int32_t base = move_offsets[lo] - move_offsets[0];
+    try {
+      eval_shard_priors(h, *h->shards[i], masks + size_t(lo) * kPlanes, values + size_t(lo) * kPlanes,
+                        hi - lo, move_offsets + lo, move_index ? move_index + base : nullptr,
+                        softmax_temp, priors ? priors + base : nullptr,
+                        wdl ? wdl + size_t(lo) * 3 : nullptr, mlh ? mlh + lo : nullptr, ms[i].data());
+    } catch (const std::exception &e) {
+      errs[i] = e.what();
+    }
+  };
+  if (nd == 1) {
+    work(0);
+  } else {
+    std::vector<std::thread> th;
+    for (int i = 0; i < nd; ++i) th.emplace_back(work, i);
+    for (auto &t : th) t.join();
+  }
+  for (auto &e : errs)
+    if (!e.empty()) return fail(h, "mfb200_evaluate_priors: " + e);
+  if (timing) {
+    *timing = mfb200_timing{0, 0, 0, 0};
+    for (auto &m : ms) {
+      timing->h2d_ms = std::max(timing->h2d_ms, m[0]);
+      timing->forward_ms = std::max(timing->forward_ms, m[1]);
+      timing->d2h_ms = std::max(timing->d2h_ms, m[2]);
+      timing->total_ms = std::max(timing->total_ms, m[3]);
+    }
+  }
+  return 0;
+}
 
 extern "C" int mfb200_evaluate(mfb200_handle *h, const uint64_t *masks, const float *values,
                                int batch, float *policy, float *wdl, float *mlh,

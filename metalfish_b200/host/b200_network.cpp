@@ -181,6 +181,53 @@ std::vector<NetworkOutput> B200Network::EvaluateBatch(const std::vector<InputPla
   return out;
 }
 
+std::vector<B200Network::LeafResult>
+B200Network::EvaluatePriors(const std::vector<InputPlanes> &inputs,
+                            const std::vector<std::vector<std::int16_t>> &move_indices,
+                            float softmax_temp) {
+  if (move_indices.size() != inputs.size())
+    throw std::invalid_argument("legal move list count must match input count");
+  std::vector<LeafResult> out(inputs.size());
+  if (inputs.empty()) return out;
+  std::lock_guard<std::mutex> lock(mutex_);
+  const int n = static_cast<int>(inputs.size());
+  masks_.resize(size_t(n) * kPackedInputPlaneCount);
+  values_.resize(size_t(n) * kPackedInputPlaneCount);
+  for (int b = 0; b < n; ++b)
+    for (int p = 0; p < kPackedInputPlaneCount; ++p)
+      PackInputPlaneRaw(inputs[b][p].data(), p, masks_[size_t(b) * kPackedInputPlaneCount + p],
+                        values_[size_t(b) * kPackedInputPlaneCount + p]);
+  move_offsets_.assign(1, 0);
+  move_index_.clear();
+  for (const auto &m : move_indices) {
+    move_index_.insert(move_index_.end(), m.begin(), m.end());
+    move_offsets_.push_back(static_cast<std::int32_t>(move_index_.size()));
+  }
+  priors_.resize(move_index_.size());
+  wdl_.resize(size_t(n) * 3);
+  mlh_.resize(n);
+  for (int lo = 0; lo < n; lo += options_.max_batch) {
+    const int cnt = std::min(options_.max_batch, n - lo);
+    const std::int32_t base = move_offsets_[lo];
+    if (mfb200_evaluate_priors(handle_, masks_.data() + size_t(lo) * kPackedInputPlaneCount,
+                               values_.data() + size_t(lo) * kPackedInputPlaneCount, cnt,
+                               move_offsets_.data() + lo, move_index_.data() + base, softmax_temp,
+                               priors_.data() + base, wdl_.data() + size_t(lo) * 3,
+                               mlh_.data() + lo, nullptr) != 0)
+      throw std::runtime_error(std::string("B200 backend: ") + mfb200_last_error(handle_));
+  }
+  for (int b = 0; b < n; ++b) {
+    LeafResult &r = out[b];
+    r.priors.assign(priors_.begin() + move_offsets_[b], priors_.begin() + move_offsets_[b + 1]);
+    r.wdl[0] = wdl_[3 * b];
+    r.wdl[1] = wdl_[3 * b + 1];
+    r.wdl[2] = wdl_[3 * b + 2];
+    r.value = r.wdl[0] - r.wdl[2];
+    r.moves_left = mlh_[b];
+  }
+  return out;
+}
+
 std::string B200Network::GetNetworkInfo() const { return info_; }
 
 BackendCapabilities B200Network::GetBackendCapabilities() const {

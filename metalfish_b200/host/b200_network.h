@@ -8,6 +8,7 @@
 // Errors throw std::runtime_error, as the reference backends do.
 #pragma once
 
+#include <cstdint>
 #include <memory>
 #include <mutex>
 #include <string>
@@ -43,6 +44,21 @@ public:
   bool HasMovesLeft() const override { return true; }
   BackendCapabilities GetBackendCapabilities() const override;
 
+  // The MCTS leaf step on the GPU (mfb200_evaluate_priors): for each input,
+  // the normalised priors of its legal moves, given as policy indices (the
+  // evaluator's NN::MoveToNNIndex of each move, mirrored for black, with the
+  // encoder's transform: src/mcts/evaluator.cpp:195-206), with the softmax of
+  // ApplyNNPolicyToNode (src/mcts/search.cpp:127-197) at softmax_temp.
+  struct LeafResult {
+    std::vector<float> priors;  // one per legal move, in the given order
+    float wdl[3];
+    float value;                // wdl[0] - wdl[2]
+    float moves_left;
+  };
+  std::vector<LeafResult> EvaluatePriors(const std::vector<InputPlanes> &inputs,
+                                         const std::vector<std::vector<std::int16_t>> &move_indices,
+                                         float softmax_temp);
+
 private:
   mfb200_handle *handle_ = nullptr;
   B200Options options_;
@@ -50,6 +66,9 @@ private:
   std::vector<std::uint64_t> masks_;  // packing scratch, reused across calls
   std::vector<float> values_;
   std::vector<float> policy_, wdl_, mlh_;
+  std::vector<std::int32_t> move_offsets_;  // EvaluatePriors scratch
+  std::vector<std::int16_t> move_index_;
+  std::vector<float> priors_;
   std::mutex mutex_;
 };
 

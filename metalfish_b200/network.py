@@ -60,6 +60,9 @@ def _declare(L):
                                 ctypes.POINTER(Config), ctypes.POINTER(vp)]
     L.mfb200_evaluate.restype = c_int
     L.mfb200_evaluate.argtypes = [vp, vp, vp, c_int, vp, vp, vp, ctypes.POINTER(Timing)]
+    L.mfb200_evaluate_priors.restype = c_int
+    L.mfb200_evaluate_priors.argtypes = [vp, vp, vp, c_int, vp, vp, ctypes.c_float, vp, vp, vp,
+                                         ctypes.POINTER(Timing)]
     L.mfb200_evaluate_device.restype = c_int
     L.mfb200_evaluate_device.argtypes = [vp, vp, vp, c_int, vp, vp, vp, vp]
     L.mfb200_calibrate.restype = c_int
@@ -180,6 +183,31 @@ class B200Network:
         if rc != 0:
             raise self._err()
         return Outputs(pol, wdl, wdl[:, 0] - wdl[:, 2], mlh)
+
+    def evaluate_priors(self, inp: PackedInputs, move_offsets: np.ndarray, move_index: np.ndarray,
+                        softmax_temp: float = 1.0, timing: Optional[Timing] = None):
+        """Forward plus the MCTS leaf step on the GPU: the normalised prior of
+        each legal move (CSR move_offsets [B+1] over move_index, the policy
+        index of each move), instead of the 1858 logits. Returns
+        (priors [move_offsets[-1] - move_offsets[0]], wdl [B, 3], moves_left [B])."""
+        b = inp.count
+        masks = np.ascontiguousarray(inp.masks, np.uint64)
+        values = np.ascontiguousarray(inp.values, np.float32)
+        off = np.ascontiguousarray(move_offsets, np.int32)
+        idx = np.ascontiguousarray(move_index, np.int16)
+        if off.shape != (b + 1,):
+            raise ValueError("move_offsets must have batch + 1 entries")
+        pri = np.empty(int(off[-1] - off[0]), np.float32)
+        wdl = np.empty((b, 3), np.float32)
+        mlh = np.empty(b, np.float32)
+        rc = _lib().mfb200_evaluate_priors(self._h, masks.ctypes.data, values.ctypes.data, b,
+                                           off.ctypes.data, idx.ctypes.data if idx.size else None,
+                                           ctypes.c_float(softmax_temp), pri.ctypes.data,
+                                           wdl.ctypes.data, mlh.ctypes.data,
+                                           ctypes.byref(timing) if timing is not None else None)
+        if rc != 0:
+            raise self._err()
+        return pri, wdl, mlh
 
     def calibrate(self, inp: PackedInputs) -> None:
         """FP8 only: absmax calibration of the per-tensor activation scales

@@ -390,3 +390,59 @@ int bt4o_forward(const bt4o_config *c, const float *const *G, const float *const
   }
   return status;
 }
+
+/* ---------------------------------------------------------------- priors
+ * The step after the forward on the MCTS leaf path: the evaluator gathers
+ * the raw policy logit of each legal move (src/mcts/evaluator.cpp:182-226;
+ * an index outside [0, 1858) gives logit 0) and ApplyNNPolicyToNode turns
+ * them into edge priors (src/mcts/search.cpp:127-197, the non-Apple branch):
+ * n = min(moves, 256) (kMaxEdges, search.cpp:49), max over the n logits,
+ * e_i = FastExp((l_i - max) * (1/temp)), sum in move order, uniform 1/n when
+ * the sum is not positive, else e_i * (1/sum).
+ *
+ * FastExp (src/mcts/core.h:38-44) is Schraudolph's exponential (N. N.
+ * Schraudolph, "A fast, compact approximation of the exponential function",
+ * Neural Computation 11(4), 1999): clamp to [-88, 88], then the float whose
+ * bits are the integer part of x * 2^23/ln 2 (12102203) plus the exponent
+ * bias 127 << 23. */
+float bt4o_fast_exp(float x) {
+  x = x < 88.0f ? x : 88.0f;    /* std::min(88, x): a NaN x gives 88 */
+  x = -88.0f < x ? x : -88.0f;  /* std::max(-88, x) */
+  const int32_t i = (int32_t)(x * 12102203.0f) + 1065353216;
+  float r;
+  memcpy(&r, &i, sizeof r);
+  return r;
+}
+
+/* policy [batch, 1858]; offsets [batch + 1] (CSR over index); priors has
+ * offsets[batch] entries; moves past the 256th of a position get 0. */
+void bt4o_priors(const float *policy, int batch, const int32_t *offsets, const int16_t *index,
+                 float temp, float *priors) {
+  const float inv_temp = 1.0f / temp;
+  for (int b = 0; b < batch; ++b) {
+    const int32_t lo = offsets[b];
+    const int moves = offsets[b + 1] - lo;
+    const int n = moves < 256 ? moves : 256;
+    for (int i = n; i < moves; ++i) priors[lo + i] = 0.0f;
+    if (n == 0) continue;
+    float logit[256];
+    float mx = -INFINITY;
+    for (int i = 0; i < n; ++i) {
+      const int idx = index[lo + i];
+      logit[i] = (idx >= 0 && idx < 1858) ? policy[(size_t)b * 1858 + idx] : 0.0f;
+      if (logit[i] > mx) mx = logit[i];
+    }
+    float sum = 0.0f;
+    for (int i = 0; i < n; ++i) {
+      priors[lo + i] = bt4o_fast_exp((logit[i] - mx) * inv_temp);
+      sum += priors[lo + i];
+    }
+    if (sum <= 0.0f) {
+      const float u = 1.0f / (float)n;
+      for (int i = 0; i < n; ++i) priors[lo + i] = u;
+      continue;
+    }
+    const float inv_sum = 1.0f / sum;
+    for (int i = 0; i < n; ++i) priors[lo + i] *= inv_sum;
+  }
+}

@@ -103,3 +103,22 @@ def slot_counts():
     g, l = ctypes.c_int(), ctypes.c_int()
     lib().bt4o_slot_counts(ctypes.byref(g), ctypes.byref(l))
     return g.value, l.value
+
+
+def fast_exp(x: np.ndarray) -> np.ndarray:
+    """The reference FastExp (src/mcts/core.h:38-44), elementwise."""
+    L = lib()
+    L.bt4o_fast_exp.restype = ctypes.c_float
+    L.bt4o_fast_exp.argtypes = [ctypes.c_float]
+    return np.array([L.bt4o_fast_exp(float(v)) for v in np.asarray(x, np.float32)], np.float32)
+
+
+def priors(policy: np.ndarray, offsets: np.ndarray, index: np.ndarray, temp: float) -> np.ndarray:
+    """Legal-move priors of the MCTS leaf path (bt4o_priors)."""
+    policy = np.ascontiguousarray(policy, np.float32)
+    offsets = np.ascontiguousarray(offsets, np.int32)
+    index = np.ascontiguousarray(index, np.int16)
+    out = np.zeros(int(offsets[-1]), np.float32)
+    lib().bt4o_priors(_ptr(policy), ctypes.c_int(policy.shape[0]), _ptr(offsets), _ptr(index),
+                      ctypes.c_float(temp), _ptr(out))
+    return out

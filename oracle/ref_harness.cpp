@@ -35,6 +35,8 @@
 #include "core/bitboard.h"
 #include "core/movegen.h"
 #include "core/position.h"
+#include "mcts/core.h"
+#include "nn/policy_map.h"
 #ifdef MFB_WITH_B200
 #include "../metalfish_b200/host/b200_network.h"
 #endif
@@ -112,55 +114,65 @@ NN::InputPlanes Unpack(const Inputs &in, int b) {
   return planes;
 }
 
+// One seeded random-playout game: position i of a fixture is the final
+// position of a uniformly random legal line of 0..80 plies from the start
+// position (per-position seed = seed ^ i), with the whole game history kept
+// so the encoder can look back (src/nn/encoder.cpp:371-400).
+struct Game {
+  std::vector<std::unique_ptr<Position>> positions;
+  std::vector<std::unique_ptr<StateInfo>> roots;
+  std::vector<std::deque<StateInfo>> stacks;
+  std::vector<const Position *> ptrs;
+};
+
+void BuildGame(std::uint64_t seed, int i, Game &g) {
+  std::mt19937_64 rng(seed ^ std::uint64_t(i));
+  const int target_plies = int(rng() % 81);
+  // Play the line once to fix the moves.
+  std::vector<Move> line;
+  {
+    Position pos;
+    StateInfo root;
+    std::deque<StateInfo> states;
+    pos.set(kStartFen, false, &root);
+    for (int ply = 0; ply < target_plies; ++ply) {
+      MoveList<LEGAL> legal(pos);
+      if (legal.size() == 0) break;
+      const Move m = *(legal.begin() + (rng() % legal.size()));
+      line.push_back(m);
+      states.emplace_back();
+      pos.do_move(m, states.back());
+    }
+  }
+  // Rebuild the full game history, each position replayed from the start so
+  // that every Position keeps its own StateInfo chain (as build_history does
+  // in tests/test_nn_comparison.cpp:280-302).
+  const int total = int(line.size());
+  g.stacks.resize(total + 1);
+  for (int ply = 0; ply <= total; ++ply) {
+    g.positions.push_back(std::make_unique<Position>());
+    g.roots.push_back(std::make_unique<StateInfo>());
+    g.positions.back()->set(kStartFen, false, g.roots.back().get());
+    auto &stack = g.stacks[ply];
+    for (int k = 0; k < ply; ++k) {
+      stack.emplace_back();
+      g.positions.back()->do_move(line[k], stack.back());
+    }
+    g.ptrs.push_back(g.positions.back().get());
+  }
+}
+
 int GenInputs(std::uint64_t seed, int count, const std::string &out_path) {
   Bitboards::init();
   Position::init();
   std::vector<std::uint64_t> masks(std::size_t(count) * 112);
   std::vector<float> values(std::size_t(count) * 112);
   for (int i = 0; i < count; ++i) {
-    std::mt19937_64 rng(seed ^ std::uint64_t(i));
-    const int target_plies = int(rng() % 81);
-    // Play the line once to fix the moves.
-    std::vector<Move> line;
-    {
-      Position pos;
-      StateInfo root;
-      std::deque<StateInfo> states;
-      pos.set(kStartFen, false, &root);
-      for (int ply = 0; ply < target_plies; ++ply) {
-        MoveList<LEGAL> legal(pos);
-        if (legal.size() == 0) break;
-        const Move m = *(legal.begin() + (rng() % legal.size()));
-        line.push_back(m);
-        states.emplace_back();
-        pos.do_move(m, states.back());
-      }
-    }
-    // Rebuild the full game history, each position replayed from the start so
-    // that every Position keeps its own StateInfo chain (as build_history does
-    // in tests/test_nn_comparison.cpp:280-302). The whole line is needed: the
-    // canonical-v2 encoder skips non-repeating positions and may look back
-    // past the last eight plies (src/nn/encoder.cpp:371-400).
-    const int total = int(line.size());
-    const int first = 0;
-    std::vector<std::unique_ptr<Position>> positions;
-    std::vector<std::unique_ptr<StateInfo>> roots;
-    std::vector<std::deque<StateInfo>> stacks(total - first + 1);
-    std::vector<const Position *> ptrs;
-    for (int ply = first; ply <= total; ++ply) {
-      positions.push_back(std::make_unique<Position>());
-      roots.push_back(std::make_unique<StateInfo>());
-      positions.back()->set(kStartFen, false, roots.back().get());
-      auto &stack = stacks[ply - first];
-      for (int k = 0; k < ply; ++k) {
-        stack.emplace_back();
-        positions.back()->do_move(line[k], stack.back());
-      }
-      ptrs.push_back(positions.back().get());
-    }
+    Game g;
+    BuildGame(seed, i, g);
     int transform = 0;
     const NN::InputPlanes planes = NN::EncodePositionForNN(
-        MetalFishNN::NetworkFormat::INPUT_112_WITH_CANONICALIZATION_V2, ptrs,
+        MetalFishNN::NetworkFormat::INPUT_112_WITH_CANONICALIZATION_V2, g.ptrs,
         NN::kMoveHistory, NN::FillEmptyHistory::FEN_ONLY, &transform);
     std::vector<std::uint64_t> m;
     std::vector<float> v;
@@ -174,6 +186,63 @@ int GenInputs(std::uint64_t seed, int count, const std::string &out_path) {
   out.write(reinterpret_cast<const char *>(hdr), sizeof(hdr));
   out.write(reinterpret_cast<const char *>(masks.data()), masks.size() * 8);
   out.write(reinterpret_cast<const char *>(values.data()), values.size() * 4);
+  return out.good() ? 0 : 1;
+}
+
+// ------------------------------------------------------------------ legal moves
+// The evaluator's vertical mirror for black to move
+// (src/mcts/evaluator.cpp:24-36, a file-local helper there): both squares
+// mirrored; promotions keep their piece, every other move becomes a plain
+// from-to move.
+Move MirrorVertical(Move m) {
+  auto mirror = [](Square sq) { return make_square(file_of(sq), Rank(7 - rank_of(sq))); };
+  if (m.type_of() == PROMOTION)
+    return Move::make<PROMOTION>(mirror(m.from_sq()), mirror(m.to_sq()), m.promotion_type());
+  return Move(mirror(m.from_sq()), mirror(m.to_sq()));
+}
+
+// For the fixture positions of GenInputs: the policy index of every legal
+// move, in MoveList<LEGAL> order, as the evaluator maps it
+// (src/mcts/evaluator.cpp:195-206: mirror for black, then
+// NN::MoveToNNIndex(move, transform) with the encoder's transform).
+// Output "MFMV", u32 version, u32 count, i32 offsets[count+1], i16 index[total].
+int GenMoves(std::uint64_t seed, int count, const std::string &out_path) {
+  Bitboards::init();
+  Position::init();
+  NN::InitPolicyTables();
+  std::vector<std::int32_t> offsets(1, 0);
+  std::vector<std::int16_t> index;
+  for (int i = 0; i < count; ++i) {
+    Game g;
+    BuildGame(seed, i, g);
+    int transform = 0;
+    (void)NN::EncodePositionForNN(MetalFishNN::NetworkFormat::INPUT_112_WITH_CANONICALIZATION_V2,
+                                  g.ptrs, NN::kMoveHistory, NN::FillEmptyHistory::FEN_ONLY,
+                                  &transform);
+    const Position &pos = *g.ptrs.back();
+    for (Move m : MoveList<LEGAL>(pos)) {
+      const Move pm = pos.side_to_move() == BLACK ? MirrorVertical(m) : m;
+      index.push_back(std::int16_t(NN::MoveToNNIndex(pm, transform)));
+    }
+    offsets.push_back(std::int32_t(index.size()));
+  }
+  std::ofstream out(out_path, std::ios::binary);
+  const std::uint32_t hdr[2] = {1, std::uint32_t(count)};
+  out.write("MFMV", 4);
+  out.write(reinterpret_cast<const char *>(hdr), sizeof(hdr));
+  out.write(reinterpret_cast<const char *>(offsets.data()), offsets.size() * 4);
+  out.write(reinterpret_cast<const char *>(index.data()), index.size() * 2);
+  return out.good() ? 0 : 1;
+}
+
+// The reference's FastExp (src/mcts/core.h:38-44) over a raw f32 file.
+int FastExpFile(const std::string &in_path, const std::string &out_path) {
+  const std::string s = ReadFile(in_path);
+  std::vector<float> x(s.size() / 4);
+  std::memcpy(x.data(), s.data(), x.size() * 4);
+  for (float &v : x) v = MCTS::FastMath::FastExp(v);
+  std::ofstream out(out_path, std::ios::binary);
+  out.write(reinterpret_cast<const char *>(x.data()), x.size() * 4);
   return out.good() ? 0 : 1;
 }
 
@@ -401,6 +470,37 @@ int ToPb(const std::string &net_path, const std::string &out_path) {
   return out.good() ? 0 : 1;
 }
 
+#ifdef MFB_WITH_B200
+// The C++ backend's MCTS leaf step: B200Network::EvaluatePriors over the
+// fixture positions [0, count) with their legal-move index lists.
+int PriorsB200(const std::string &net_path, const std::string &in_path,
+               const std::string &moves_path, float temp, const std::string &out_path) {
+  const NN::WeightsFile file = ReadNet(net_path);
+  const Inputs in = ReadInputs(in_path);
+  const std::string s = ReadFile(moves_path);
+  Reader r{s};
+  if (r.bytes(4) != "MFMV") throw std::runtime_error("bad legal-move magic");
+  (void)r.get<std::uint32_t>();
+  const int count = int(r.get<std::uint32_t>());
+  if (count > in.count) throw std::runtime_error("more move lists than positions");
+  std::vector<std::int32_t> off(count + 1);
+  for (auto &o : off) o = r.get<std::int32_t>();
+  std::vector<std::vector<std::int16_t>> moves(count);
+  for (int b = 0; b < count; ++b)
+    for (int i = off[b]; i < off[b + 1]; ++i) moves[b].push_back(r.get<std::int16_t>());
+  NN::B200::B200Options opt;
+  opt.max_batch = std::max(1, count);
+  NN::B200::B200Network net(file, opt);
+  std::vector<NN::InputPlanes> planes(count);
+  for (int b = 0; b < count; ++b) planes[b] = Unpack(in, b);
+  const auto res = net.EvaluatePriors(planes, moves, temp);
+  std::ofstream out(out_path, std::ios::binary);
+  for (const auto &x : res)
+    out.write(reinterpret_cast<const char *>(x.priors.data()), x.priors.size() * 4);
+  return out.good() ? 0 : 1;
+}
+#endif
+
 } // namespace
 
 int main(int argc, char **argv) {
@@ -412,6 +512,13 @@ int main(int argc, char **argv) {
       return Eval(argv[2], argv[3], argv[4], argc > 5 ? std::stoi(argv[5]) : 1,
                   argc > 6 ? std::stoi(argv[6]) : 0, argc > 7 ? std::stoi(argv[7]) : -1);
     if (cmd == "to-pb" && argc == 4) return ToPb(argv[2], argv[3]);
+    if (cmd == "gen-moves" && argc == 5)
+      return GenMoves(std::stoull(argv[2]), std::stoi(argv[3]), argv[4]);
+    if (cmd == "fastexp" && argc == 4) return FastExpFile(argv[2], argv[3]);
+#ifdef MFB_WITH_B200
+    if (cmd == "priors-b200" && argc == 7)
+      return PriorsB200(argv[2], argv[3], argv[4], std::stof(argv[5]), argv[6]);
+#endif
     if (cmd == "eval-backend" && argc >= 6)
       return Eval(argv[3], argv[4], argv[5], argc > 6 ? std::stoi(argv[6]) : 1,
                   argc > 7 ? std::stoi(argv[7]) : 0, argc > 8 ? std::stoi(argv[8]) : -1, argv[2]);
@@ -419,7 +526,10 @@ int main(int argc, char **argv) {
                  "usage: ref_harness gen-inputs <seed> <count> <out.mfin>\n"
                  "       ref_harness eval <net.mfnt> <in.mfin> <out.mfot> [threads] [first] [count]\n"
                  "       ref_harness to-pb <net.mfnt> <out.pb>\n"
-                 "       ref_harness eval-backend <cpu|b200> <net.mfnt> <in.mfin> <out.mfot> [threads] [first] [count]\n");
+                 "       ref_harness gen-moves <seed> <count> <out.mfmv>\n"
+                 "       ref_harness fastexp <in.f32> <out.f32>\n"
+                 "       ref_harness eval-backend <cpu|b200> <net.mfnt> <in.mfin> <out.mfot> [threads] [first] [count]\n"
+                 "       b200_harness priors-b200 <net.mfnt> <in.mfin> <moves.mfmv> <temp> <out.f32>\n");
     return 2;
   } catch (const std::exception &e) {
     std::fprintf(stderr, "ref_harness error: %s\n", e.what());

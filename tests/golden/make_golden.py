@@ -10,6 +10,12 @@ by hand in the development container, never by the tests. Outputs:
 * ``positions.npz``        -- 4096 seeded random-playout positions (seed 20251201),
   generated and packed by the reference's own encoder (oracle/ref_harness
   gen-inputs). Used as parity inputs and as the bench's synthetic inputs.
+* ``legal_moves.npz``     -- for the same positions, the policy index of every
+  legal move as the reference evaluator maps it (oracle/ref_harness gen-moves:
+  MoveList<LEGAL>, the black-side mirror, NN::MoveToNNIndex with the encoder's
+  transform), CSR ``offsets`` / ``index``.
+* ``fastexp.npz``         -- inputs and outputs of the reference's FastExp
+  (src/mcts/core.h:38-44), the exponential of the MCTS policy softmax.
 * ``ref_<config>.npz``     -- outputs of the reference ``Cpu::CpuNetwork`` on the
   first N of those positions, for seeded synthetic weights; plus a SHA-256 of
   the weights so a numpy change that alters the generator is caught.
@@ -49,7 +55,41 @@ def weights_digest(tensors) -> str:
     return h.hexdigest()
 
 
+def read_moves(path):
+    b = open(path, "rb").read()
+    assert b[:4] == b"MFMV", "bad legal-move file"
+    count = int(np.frombuffer(b[8:12], np.uint32)[0])
+    offsets = np.frombuffer(b[12:12 + 4 * (count + 1)], np.int32).copy()
+    index = np.frombuffer(b[12 + 4 * (count + 1):], np.int16).copy()
+    assert len(index) == offsets[-1]
+    return offsets, index
+
+
+def make_moves_and_fastexp(tmp) -> None:
+    mv = os.path.join(tmp, "moves.mfmv")
+    subprocess.run([HARNESS, "gen-moves", str(POSITION_SEED), str(POSITIONS), mv], check=True)
+    offsets, index = read_moves(mv)
+    np.savez_compressed(os.path.join(HERE, "legal_moves.npz"), offsets=offsets, index=index,
+                        seed=POSITION_SEED)
+    rng = np.random.default_rng(5)
+    x = np.concatenate([
+        np.linspace(-100.0, 100.0, 20001, dtype=np.float32),
+        (rng.standard_normal(20000) * 8.0).astype(np.float32),
+        np.array([-88.0, 88.0, -88.00001, 88.00001, 0.0, -0.0, 1e-30, -1e-30, np.inf, -np.inf,
+                  np.nan], np.float32)])
+    xin, yout = os.path.join(tmp, "fx.f32"), os.path.join(tmp, "fy.f32")
+    x.tofile(xin)
+    subprocess.run([HARNESS, "fastexp", xin, yout], check=True)
+    np.savez_compressed(os.path.join(HERE, "fastexp.npz"), x=x, y=np.fromfile(yout, np.float32))
+
+
 def main() -> None:
+    if sys.argv[1:] == ["--moves-only"]:
+        subprocess.run(["make", "-s", "-C", os.path.join(ROOT, "oracle"), f"REF={REF}", "ref"],
+                       check=True)
+        with tempfile.TemporaryDirectory() as tmp:
+            make_moves_and_fastexp(tmp)
+        return
     subprocess.run(["make", "-s", "-C", os.path.join(ROOT, "oracle"), f"REF={REF}", "ref"],
                    check=True)
     with tempfile.TemporaryDirectory() as tmp:
@@ -62,6 +102,7 @@ def main() -> None:
         inp = netfile.read_inputs(pos)
         np.savez_compressed(os.path.join(HERE, "positions.npz"), masks=inp.masks,
                             values=inp.values, seed=POSITION_SEED)
+        make_moves_and_fastexp(tmp)
 
         threads = os.cpu_count() or 1
         for name, cfg, seed, perturb, n in CASES:

@@ -93,3 +93,64 @@ def test_golden_outputs_are_sane():
         np.testing.assert_allclose(g["wdl"].sum(1), 1.0, atol=1e-5)
         np.testing.assert_allclose(g["value"], g["wdl"][:, 0] - g["wdl"][:, 2], atol=1e-6)
         assert (g["moves_left"] >= 0).all()
+
+
+# ---------------------------------------------------------------- MCTS leaf priors
+def test_fast_exp_matches_reference():
+    """The oracle's FastExp is bit-identical to the reference's
+    (src/mcts/core.h:38-44) on a grid, random values and the clamp/NaN/inf edges."""
+    z = np.load(os.path.join(GOLDEN, "fastexp.npz"))
+    got = port.fast_exp(z["x"])
+    np.testing.assert_array_equal(got.view(np.uint32), z["y"].view(np.uint32))
+
+
+def test_legal_move_fixture_is_consistent():
+    z = np.load(os.path.join(GOLDEN, "legal_moves.npz"))
+    off, idx = z["offsets"], z["index"]
+    assert off[0] == 0 and off[-1] == len(idx) and len(off) == 4097
+    n = np.diff(off)
+    assert n.min() == 0 and n.max() <= 218  # mates/stalemates have no moves
+    assert idx.min() >= 0 and idx.max() < 1858
+    for b in range(0, 4096, 97):  # each move maps to its own policy entry
+        s = idx[off[b]:off[b + 1]]
+        assert len(set(s.tolist())) == len(s)
+
+
+def _priors_py(pol, off, idx, temp):
+    """Float32 restatement in numpy of the same loop, for the oracle's own check."""
+    out = np.zeros(off[-1] - off[0], np.float32)
+    inv_t = np.float32(1.0) / np.float32(temp)
+    for b in range(len(off) - 1):
+        lo, moves = off[b] - off[0], off[b + 1] - off[b]
+        n = min(moves, 256)
+        if n == 0:
+            continue
+        l = np.array([pol[b, i] if 0 <= i < 1858 else 0.0 for i in idx[lo:lo + n]], np.float32)
+        e = port.fast_exp((l - l.max()) * inv_t)
+        s = np.float32(0)
+        for v in e:
+            s = np.float32(s + v)
+        out[lo:lo + n] = e * (np.float32(1) / s) if s > 0 else np.float32(1) / np.float32(n)
+    return out
+
+
+def test_oracle_priors_semantics():
+    rng = np.random.default_rng(4)
+    B = 6
+    pol = rng.standard_normal((B, 1858)).astype(np.float32) * 3
+    lists = [[], [17], list(range(40)), [-1, 5, 1858, 32767, 9],
+             rng.choice(1858, 300, replace=False).tolist(), rng.choice(1858, 31).tolist()]
+    off = np.concatenate([[0], np.cumsum([len(x) for x in lists])]).astype(np.int32)
+    idx = np.concatenate([np.asarray(x, np.int16) for x in lists]).astype(np.int16)
+    for temp in (1.0, 0.7, 2.3):
+        got = port.priors(pol, off, idx, temp)
+        np.testing.assert_array_equal(got, _priors_py(pol, off, idx, temp))
+        for b in range(B):
+            n = min(off[b + 1] - off[b], 256)
+            if n:
+                assert abs(float(got[off[b]:off[b] + n].sum()) - 1.0) < 1e-5
+        assert (got[off[4] + 256:off[5]] == 0).all()  # past kMaxEdges
+    # an out-of-range index reads logit 0
+    p0 = port.priors(np.zeros((1, 1858), np.float32), np.array([0, 2], np.int32),
+                     np.array([-1, 3], np.int16), 1.0)
+    np.testing.assert_array_equal(p0, np.array([0.5, 0.5], np.float32))
