@@ -20,6 +20,11 @@
  *                          (src/mcts/evaluator.cpp:182-226, NNMCTSEvaluator::Impl::BuildResult)
  *                          and the softmax of ApplyNNPolicyToNode
  *                          (src/mcts/search.cpp:127-197)
+ *   mfb200_encode_history / mfb200_evaluate_history
+ *                       <- NN::EncodePositionForNN (src/nn/encoder.cpp:249-466) on the
+ *                          GPU: position histories in, packed planes (and the forward) out,
+ *                          replacing the host encode of NNMCTSEvaluator
+ *                          (src/mcts/evaluator.cpp:150-158)
  *   mfb200_capabilities <- NN::Network::GetBackendCapabilities / HasWDL / HasMovesLeft /
  *                          GetNetworkInfo (src/nn/network.h:21-51)
  *   mfb200_last_error   <- the std::runtime_error messages the reference throws
@@ -125,6 +130,52 @@ MFB200_API int mfb200_evaluate_priors(mfb200_handle *h, const uint64_t *masks, c
                                       const int16_t *move_index, float softmax_temp,
                                       float *priors, float *wdl, float *moves_left,
                                       mfb200_timing *timing);
+
+/* One position of a game history, as the encoder reads it from a Position
+ * (src/core/position.h): bit i of a bitboard is square i (a1 = 0, h8 = 63). */
+typedef struct mfb200_board {
+  uint64_t pieces[2][6]; /* [white, black][pawn, knight, bishop, rook, queen, king] */
+  int32_t rule50;        /* Position::rule50_count() */
+  int32_t game_ply;      /* Position::game_ply() */
+  int8_t ep_square;      /* Position::ep_square(), -1 for SQ_NONE */
+  uint8_t castling;      /* bit 0 white O-O, 1 white O-O-O, 2 black O-O, 3 black O-O-O */
+  uint8_t black_to_move; /* Position::side_to_move() == BLACK */
+  uint8_t repetition;    /* Position::is_repetition(INT_MAX) */
+  uint32_t reserved;     /* 0 */
+} mfb200_board;
+
+/* Input formats (MetalFishNN::NetworkFormat::InputFormat, src/nn/proto/net.proto:256-263). */
+enum {
+  MFB200_INPUT_CLASSICAL_112 = 1,
+  MFB200_INPUT_112_WITH_CASTLING_PLANE = 2,
+  MFB200_INPUT_112_CANONICAL = 3,
+  MFB200_INPUT_112_CANONICAL_HECTOPLIES = 4,
+  MFB200_INPUT_112_CANONICAL_V2 = 5,
+  MFB200_INPUT_112_CANONICAL_HECTOPLIES_ARMAGEDDON = 132,
+  MFB200_INPUT_112_CANONICAL_V2_ARMAGEDDON = 133
+};
+
+/* Encode `batch` game histories on the GPU as EncodePositionForNN(format,
+ * history, 8 planes, FillEmptyHistory::FEN_ONLY) does, into the packed planes
+ * of PackInputPlanesRaw: boards is a CSR over history_offsets [batch + 1],
+ * each history oldest first and ending with the position to evaluate (pass at
+ * least the plies since the last capture or pawn move; the whole game is
+ * fine). Writes masks / values [batch, 112] and the canonicalisation
+ * transform of each position (transforms [batch], for NN::MoveToNNIndex),
+ * each output optional. Where the reference would extend an empty history
+ * forever (a FEN history of one non-start position with a nonzero rule50 in
+ * the V2 formats) the GPU stops after 8 synthesised entries. */
+MFB200_API int mfb200_encode_history(mfb200_handle *h, const mfb200_board *boards,
+                                     const int32_t *history_offsets, int batch, int input_format,
+                                     uint64_t *masks, float *values, int32_t *transforms);
+
+/* mfb200_evaluate with the encoding on the GPU: histories in (as in
+ * mfb200_encode_history), policy / wdl / moves_left / transforms out. */
+MFB200_API int mfb200_evaluate_history(mfb200_handle *h, const mfb200_board *boards,
+                                       const int32_t *history_offsets, int batch,
+                                       int input_format, float *policy, float *wdl,
+                                       float *moves_left, int32_t *transforms,
+                                       mfb200_timing *timing);
 
 /* Device-buffer evaluation on device `cfg.device`, enqueued on `stream`
  * (a cudaStream_t; NULL = the handle's stream) without synchronising. All

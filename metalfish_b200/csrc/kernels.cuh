@@ -61,6 +61,16 @@ void launch_attention(const __nv_bfloat16 *qkv, long long ldq, const __nv_bfloat
                       int batch, int heads, int d, __nv_bfloat16 *ctx, cudaStream_t s,
                       uint8_t *ctx8 = nullptr, const float *scale8 = nullptr);
 
+}  // namespace mfb200
+extern "C" {
+typedef struct mfb200_board mfb200_board;
+}
+namespace mfb200 {
+// Position histories (CSR over offsets [batch + 1]) -> packed planes
+// masks / values [batch, 112] and transforms [batch] (encoder.cu).
+void launch_encode(const mfb200_board *boards, const int32_t *offsets, int batch, int fmt,
+                   uint64_t *masks, float *values, int32_t *transforms, cudaStream_t s);
+
 // Legal-move priors of `batch` positions from their policy logits
 // [batch, 1858]: offsets [batch + 1] (CSR into index, offsets[0] need not be
 // 0), index = policy index of each legal move; priors has offsets[batch] -

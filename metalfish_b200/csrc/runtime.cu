@@ -229,6 +229,8 @@ class ArenaBuilder {
 // Legal moves per position the priors buffers hold on average (the
 // reference keeps at most 256 edges per node, src/mcts/search.cpp:49).
 constexpr int kMoveCapacity = 256;
+// History records per position the encoder buffers hold on average.
+constexpr int kHistoryCapacity = 128;
 
 struct Shard {  // one GPU
   int device = 0;
@@ -251,6 +253,9 @@ struct Shard {  // one GPU
   int32_t *move_off;      // legal-move priors: CSR offsets [max_batch + 1]
   int16_t *move_idx;      //   policy index per legal move [max_batch * 256]
   float *priors;          //   priors per legal move [max_batch * 256]
+  mfb200_board *boards;   // encoder input: history records [max_batch * 128]
+  int32_t *hist_off;      //   CSR offsets [max_batch + 1]
+  int32_t *transforms;    //   canonicalisation transform per position [max_batch]
   unsigned *status;
   cudaEvent_t ev[4];
   struct Step {
@@ -562,6 +567,9 @@ void alloc_workspace(Shard &S, const mfb200_net_desc &n, int max_batch, bool fp8
       {reinterpret_cast<void **>(&S.move_off), (B + 1) * 4},
       {reinterpret_cast<void **>(&S.move_idx), B * kMoveCapacity * 2},
       {reinterpret_cast<void **>(&S.priors), B * kMoveCapacity * 4},
+      {reinterpret_cast<void **>(&S.boards), B * kHistoryCapacity * sizeof(mfb200_board)},
+      {reinterpret_cast<void **>(&S.hist_off), (B + 1) * 4},
+      {reinterpret_cast<void **>(&S.transforms), B * 4},
       {reinterpret_cast<void **>(&S.status), 256},
       {reinterpret_cast<void **>(&S.scales), size_t(2 + 4 * n.layers) * 4},
       {reinterpret_cast<void **>(&S.absmax), size_t(2 + 4 * n.layers) * 4},
@@ -1074,7 +1082,130 @@ int eval_shard_priors(mfb200_handle *h, Shard &S, const uint64_t *masks, const f
   cudaEventElapsedTime(&ms[3], S.ev[0], S.ev[3]);
   return 0;
 }
+// Upload one shard's histories and encode them into S.masks / S.values.
+void encode_shard(Shard &S, const mfb200_board *boards, const int32_t *offsets, int B, int fmt,
+                  cudaStream_t s) {
+  const int32_t nb = offsets[B] - offsets[0];
+  check(cudaMemcpyAsync(S.hist_off, offsets, size_t(B + 1) * 4, cudaMemcpyHostToDevice, s), "H2D offsets");
+  if (nb > 0)
+    check(cudaMemcpyAsync(S.boards, boards, size_t(nb) * sizeof(mfb200_board), cudaMemcpyHostToDevice, s),
+          "H2D boards");
+  launch_encode(S.boards, S.hist_off, B, fmt, S.masks, S.values, S.transforms, s);
+  check(cudaGetLastError(), "encode launch");
+}
+
+const char *check_histories(const int32_t *offsets, int batch, int fmt, int shards, int per) {
+  if (fmt != 1 && fmt != 2 && fmt != 3 && fmt != 4 && fmt != 5 && fmt != 132 && fmt != 133)
+    return "unknown input format";
+  for (int b = 0; b < batch; ++b)
+    if (offsets[b + 1] < offsets[b]) return "history_offsets must be non-decreasing";
+  for (int i = 0; i < shards; ++i) {
+    const int lo = i * per, hi = std::min(batch, lo + per);
+    if (lo < hi && offsets[hi] - offsets[lo] > int64_t(per) * kHistoryCapacity)
+      return "more than 128 history records per position on average";
+  }
+  return nullptr;
+}
 }  // namespace
+
+extern "C" int mfb200_encode_history(mfb200_handle *h, const mfb200_board *boards,
+                                     const int32_t *history_offsets, int batch, int input_format,
+                                     uint64_t *masks, float *values, int32_t *transforms) {
+  if (!h) return fail(nullptr, "mfb200_encode_history: null handle");
+  std::lock_guard<std::mutex> lock(h->mu);
+  if (batch <= 0) return 0;
+  if (batch > h->cfg.max_batch / static_cast<int>(h->shards.size()))
+    return fail(h, "mfb200_encode_history: batch exceeds one device's share of max_batch");
+  if (!history_offsets || (!boards && history_offsets[batch] != history_offsets[0]))
+    return fail(h, "mfb200_encode_history: null input");
+  if (const char *e = check_histories(history_offsets, batch, input_format, 1, batch))
+    return fail(h, std::string("mfb200_encode_history: ") + e);
+  try {
+    Shard &S = *h->shards[0];
+    check(cudaSetDevice(S.device), "cudaSetDevice");
+    cudaStream_t s = S.stream;
+    encode_shard(S, boards, history_offsets, batch, input_format, s);
+    if (masks) check(cudaMemcpyAsync(masks, S.masks, size_t(batch) * kPlanes * 8, cudaMemcpyDeviceToHost, s), "D2H");
+    if (values) check(cudaMemcpyAsync(values, S.values, size_t(batch) * kPlanes * 4, cudaMemcpyDeviceToHost, s), "D2H");
+    if (transforms) check(cudaMemcpyAsync(transforms, S.transforms, size_t(batch) * 4, cudaMemcpyDeviceToHost, s), "D2H");
+    check(cudaStreamSynchronize(s), "encode");
+  } catch (const std::exception &e) {
+    return fail(h, std::string("mfb200_encode_history: ") + e.what());
+  }
+  return 0;
+}
+
+extern "C" int mfb200_evaluate_history(mfb200_handle *h, const mfb200_board *boards,
+                                       const int32_t *history_offsets, int batch,
+                                       int input_format, float *policy, float *wdl, float *mlh,
+                                       int32_t *transforms, mfb200_timing *timing) {
+  if (!h) return fail(nullptr, "mfb200_evaluate_history: null handle");
+  std::lock_guard<std::mutex> lock(h->mu);
+  if (batch <= 0) return 0;
+  if (batch > h->cfg.max_batch)
+    return fail(h, "mfb200_evaluate_history: batch " + std::to_string(batch) + " exceeds max_batch " +
+                       std::to_string(h->cfg.max_batch));
+  if (!history_offsets || (!boards && history_offsets[batch] != history_offsets[0]))
+    return fail(h, "mfb200_evaluate_history: null input");
+  const int nd = static_cast<int>(h->shards.size());
+  const int per = (batch + nd - 1) / nd;
+  if (const char *e = check_histories(history_offsets, batch, input_format, nd, per))
+    return fail(h, std::string("mfb200_evaluate_history: ") + e);
+  std::vector<std::array<float, 4>> ms(nd, {0, 0, 0, 0});
+  std::vector<std::string> errs(nd);
+  auto work = [&](int i) {
+    const int lo = i * per, hi = std::min(batch, lo + per);
+    if (lo >= hi) return;
+    Shard &S = *h->shards[i];
+    const int B = hi - lo;
+    try {
+      check(cudaSetDevice(S.device), "cudaSetDevice");
+      cudaStream_t s = S.stream;
+      float *m = ms[i].data();
+      check(cudaEventRecord(S.ev[0], s), "event");
+      encode_shard(S, boards + (history_offsets[lo] - history_offsets[0]), history_offsets + lo, B,
+                   input_format, s);
+      check(cudaEventRecord(S.ev[1], s), "event");
+      forward(h, S, B, s);
+      check(cudaEventRecord(S.ev[2], s), "event");
+      if (policy)
+        check(cudaMemcpyAsync(policy + size_t(lo) * kPolicy, S.policy, size_t(B) * kPolicy * 4,
+                              cudaMemcpyDeviceToHost, s), "D2H policy");
+      if (wdl) check(cudaMemcpyAsync(wdl + size_t(lo) * 3, S.wdl, size_t(B) * 12, cudaMemcpyDeviceToHost, s), "D2H wdl");
+      if (mlh) check(cudaMemcpyAsync(mlh + lo, S.mlh, size_t(B) * 4, cudaMemcpyDeviceToHost, s), "D2H mlh");
+      if (transforms)
+        check(cudaMemcpyAsync(transforms + lo, S.transforms, size_t(B) * 4, cudaMemcpyDeviceToHost, s), "D2H");
+      check(cudaEventRecord(S.ev[3], s), "event");
+      check(cudaStreamSynchronize(s), "forward");
+      check_status(S);
+      cudaEventElapsedTime(&m[0], S.ev[0], S.ev[1]);
+      cudaEventElapsedTime(&m[1], S.ev[1], S.ev[2]);
+      cudaEventElapsedTime(&m[2], S.ev[2], S.ev[3]);
+      cudaEventElapsedTime(&m[3], S.ev[0], S.ev[3]);
+    } catch (const std::exception &e) {
+      errs[i] = e.what();
+    }
+  };
+  if (nd == 1) {
+    work(0);
+  } else {
+    std::vector<std::thread> th;
+    for (int i = 0; i < nd; ++i) th.emplace_back(work, i);
+    for (auto &t : th) t.join();
+  }
+  for (auto &e : errs)
+    if (!e.empty()) return fail(h, "mfb200_evaluate_history: " + e);
+  if (timing) {
+    *timing = mfb200_timing{0, 0, 0, 0};
+    for (auto &m : ms) {
+      timing->h2d_ms = std::max(timing->h2d_ms, m[0]);
+      timing->forward_ms = std::max(timing->forward_ms, m[1]);
+      timing->d2h_ms = std::max(timing->d2h_ms, m[2]);
+      timing->total_ms = std::max(timing->total_ms, m[3]);
+    }
+  }
+  return 0;
+}
 
 extern "C" int mfb200_evaluate_priors(mfb200_handle *h, const uint64_t *masks,
                                       const float *values, int batch,

@@ -63,6 +63,11 @@ def _declare(L):
     L.mfb200_evaluate_priors.restype = c_int
     L.mfb200_evaluate_priors.argtypes = [vp, vp, vp, c_int, vp, vp, ctypes.c_float, vp, vp, vp,
                                          ctypes.POINTER(Timing)]
+    L.mfb200_encode_history.restype = c_int
+    L.mfb200_encode_history.argtypes = [vp, vp, vp, c_int, c_int, vp, vp, vp]
+    L.mfb200_evaluate_history.restype = c_int
+    L.mfb200_evaluate_history.argtypes = [vp, vp, vp, c_int, c_int, vp, vp, vp, vp,
+                                          ctypes.POINTER(Timing)]
     L.mfb200_evaluate_device.restype = c_int
     L.mfb200_evaluate_device.argtypes = [vp, vp, vp, c_int, vp, vp, vp, vp]
     L.mfb200_calibrate.restype = c_int
@@ -208,6 +213,43 @@ class B200Network:
         if rc != 0:
             raise self._err()
         return pri, wdl, mlh
+
+    # -- position encoding on the GPU (board records: include/mfb200.h mfb200_board,
+    #    112 bytes each, as uint8 rows or a structured array)
+    def encode_history(self, boards: np.ndarray, history_offsets: np.ndarray,
+                       input_format: int = 5):
+        """EncodePositionForNN on the GPU: packed masks / values [B, 112] and
+        the canonicalisation transforms [B] of B game histories."""
+        boards = np.ascontiguousarray(boards).view(np.uint8)
+        off = np.ascontiguousarray(history_offsets, np.int32)
+        b = len(off) - 1
+        m = np.empty((b, 112), np.uint64)
+        v = np.empty((b, 112), np.float32)
+        t = np.empty(b, np.int32)
+        rc = _lib().mfb200_encode_history(self._h, boards.ctypes.data if boards.size else None,
+                                          off.ctypes.data, b, input_format, m.ctypes.data,
+                                          v.ctypes.data, t.ctypes.data)
+        if rc != 0:
+            raise self._err()
+        return m, v, t
+
+    def evaluate_history(self, boards: np.ndarray, history_offsets: np.ndarray,
+                         input_format: int = 5, timing: Optional[Timing] = None):
+        """Encode on the GPU and evaluate: (Outputs, transforms [B])."""
+        boards = np.ascontiguousarray(boards).view(np.uint8)
+        off = np.ascontiguousarray(history_offsets, np.int32)
+        b = len(off) - 1
+        pol = np.empty((b, POLICY), np.float32)
+        wdl = np.empty((b, 3), np.float32)
+        mlh = np.empty(b, np.float32)
+        t = np.empty(b, np.int32)
+        rc = _lib().mfb200_evaluate_history(self._h, boards.ctypes.data if boards.size else None,
+                                            off.ctypes.data, b, input_format, pol.ctypes.data,
+                                            wdl.ctypes.data, mlh.ctypes.data, t.ctypes.data,
+                                            ctypes.byref(timing) if timing is not None else None)
+        if rc != 0:
+            raise self._err()
+        return Outputs(pol, wdl, wdl[:, 0] - wdl[:, 2], mlh), t
 
     def calibrate(self, inp: PackedInputs) -> None:
         """FP8 only: absmax calibration of the per-tensor activation scales

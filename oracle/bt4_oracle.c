@@ -446,3 +446,257 @@ void bt4o_priors(const float *policy, int batch, const int32_t *offsets, const i
     for (int i = 0; i < n; ++i) priors[lo + i] *= inv_sum;
   }
 }
+
+/* ---------------------------------------------------------------- encoder
+ * NN::EncodePositionForNN (src/nn/encoder.cpp:249-466) for FillEmptyHistory
+ * FEN_ONLY and 8 history planes, followed by PackInputPlaneRaw
+ * (src/nn/input_plane_packing.h:30-61). The history is one record per
+ * position, oldest first; the last record is the position evaluated. This
+ * restatement builds the float planes exactly as the reference does and then
+ * packs them, so it checks the GPU encoder (which works on bitboards) from a
+ * different representation. One deliberate difference: a synthesised
+ * history (before the first record) is cut after 8 entries, where the
+ * reference would loop forever on a V2 format whose oldest record is not
+ * the start position, has a nonzero rule50 and no repetition. */
+typedef struct {
+  uint64_t pieces[2][6]; /* [white, black][pawn, knight, bishop, rook, queen, king] */
+  int32_t rule50, game_ply;
+  int8_t ep_square;      /* -1: none */
+  uint8_t castling;      /* 1 white O-O, 2 white O-O-O, 4 black O-O, 8 black O-O-O */
+  uint8_t black_to_move, repetition;
+  uint32_t reserved;
+} bt4o_board;
+
+int bt4o_board_size(void) { return (int)sizeof(bt4o_board); }
+
+enum { T_FLIP = 1, T_MIRROR = 2, T_TRANSPOSE = 4 };
+enum { C_WOO = 1, C_WOOO = 2, C_BOO = 4, C_BOOO = 8 };
+
+/* encoder.cpp:46-51 */
+static uint64_t rev_bits_in_bytes(uint64_t v) {
+  v = ((v >> 1) & 0x5555555555555555ull) | ((v & 0x5555555555555555ull) << 1);
+  v = ((v >> 2) & 0x3333333333333333ull) | ((v & 0x3333333333333333ull) << 2);
+  v = ((v >> 4) & 0x0F0F0F0F0F0F0F0Full) | ((v & 0x0F0F0F0F0F0F0F0Full) << 4);
+  return v;
+}
+/* encoder.cpp:53-58: byte order reversed (ranks mirrored) */
+static uint64_t rev_bytes(uint64_t v) {
+  v = (v & 0x00000000FFFFFFFFull) << 32 | (v & 0xFFFFFFFF00000000ull) >> 32;
+  v = (v & 0x0000FFFF0000FFFFull) << 16 | (v & 0xFFFF0000FFFF0000ull) >> 16;
+  v = (v & 0x00FF00FF00FF00FFull) << 8 | (v & 0xFF00FF00FF00FF00ull) >> 8;
+  return v;
+}
+/* encoder.cpp:60-68: the 8x8 bit matrix transposed (files <-> ranks) */
+static uint64_t transpose_bits(uint64_t v) {
+  v = (v & 0xAA00AA00AA00AA00ull) >> 9 | (v & 0x0055005500550055ull) << 9 | (v & 0x55AA55AA55AA55AAull);
+  v = (v & 0xCCCC0000CCCC0000ull) >> 18 | (v & 0x0000333300003333ull) << 18 | (v & 0x3333CCCC3333CCCCull);
+  v = (v & 0xF0F0F0F000000000ull) >> 36 | (v & 0x000000000F0F0F0Full) << 36 | (v & 0x0F0F0F0FF0F0F0F0ull);
+  return v;
+}
+/* encoder.cpp:70-86 */
+static uint64_t apply_transform(uint64_t b, int t) {
+  if (b == 0 || b == ~0ull) return b;
+  if (t & T_FLIP) b = rev_bits_in_bytes(b);
+  if (t & T_MIRROR) b = rev_bytes(b);
+  if (t & T_TRANSPOSE) b = transpose_bits(b);
+  return b;
+}
+/* encoder.cpp:88-102 */
+static int compare_transposing(uint64_t board, int t) {
+  uint64_t v = board;
+  if (t & T_FLIP) v = rev_bits_in_bytes(v);
+  if (t & T_MIRROR) v = rev_bytes(v);
+  const uint64_t alt = transpose_bits(v);
+  return v < alt ? -1 : (v > alt ? 1 : 0);
+}
+static uint64_t kind(const bt4o_board *p, int k) { return p->pieces[0][k] | p->pieces[1][k]; }
+static uint64_t side(const bt4o_board *p, int c) {
+  uint64_t b = 0;
+  for (int k = 0; k < 6; ++k) b |= p->pieces[c][k];
+  return b;
+}
+/* encoder.cpp:104-170 */
+static int choose_transform(const bt4o_board *p, int us) {
+  if (p->castling) return 0;
+  uint64_t king = p->pieces[us][5];
+  int t = 0;
+  if (king & 0x0F0F0F0F0F0F0F0Full) {
+    t |= T_FLIP;
+    king = rev_bits_in_bytes(king);
+  }
+  if (kind(p, 0)) return t;
+  if (king & 0xFFFFFFFF00000000ull) {
+    t |= T_MIRROR;
+    king = rev_bytes(king);
+  }
+  if (king & 0xE0C08000ull) return t | T_TRANSPOSE;
+  if (king & 0x10204080ull) {
+    /* tie-breaks in the reference's order: all pieces, ours, kings, queens,
+       rooks, knights, bishops */
+    const uint64_t order[7] = {side(p, 0) | side(p, 1), side(p, us), kind(p, 5), kind(p, 4),
+                               kind(p, 3), kind(p, 1), kind(p, 2)};
+    for (int i = 0; i < 7; ++i) {
+      const int o = compare_transposing(order[i], t);
+      if (o == -1) return t;
+      if (o == 1) return t | T_TRANSPOSE;
+    }
+  }
+  return t;
+}
+/* encoder.cpp:214-238 (IsStartPosition) */
+static int is_start(const bt4o_board *p) {
+  static const uint64_t start[2][6] = {
+      {0x000000000000FF00ull, 0x42ull, 0x24ull, 0x81ull, 0x08ull, 0x10ull},
+      {0x00FF000000000000ull, 0x4200000000000000ull, 0x2400000000000000ull,
+       0x8100000000000000ull, 0x0800000000000000ull, 0x1000000000000000ull}};
+  if (p->black_to_move || p->game_ply != 0 || p->rule50 != 0 || p->ep_square >= 0 ||
+      p->castling != 15)
+    return 0;
+  for (int c = 0; c < 2; ++c)
+    for (int k = 0; k < 6; ++k)
+      if (p->pieces[c][k] != start[c][k]) return 0;
+  return 1;
+}
+/* encoder.cpp:338-360: castling rights, our side first */
+static int castle_mask_for(const bt4o_board *p, int us) {
+  const int c = p->castling;
+  if (!us) return ((c & C_WOO) ? 1 : 0) | ((c & C_WOOO) ? 2 : 0) | ((c & C_BOO) ? 4 : 0) | ((c & C_BOOO) ? 8 : 0);
+  return ((c & C_BOO) ? 1 : 0) | ((c & C_BOOO) ? 2 : 0) | ((c & C_WOO) ? 4 : 0) | ((c & C_WOOO) ? 8 : 0);
+}
+
+static void set_plane(float *pl, float v) {
+  for (int s = 0; s < 64; ++s) pl[s] = v;
+}
+static void set_bits(float *pl, uint64_t b) {
+  for (int s = 0; s < 64; ++s)
+    if ((b >> s) & 1) pl[s] = 1.0f;
+}
+static void fill_from(float *pl, uint64_t b) {
+  set_plane(pl, 0.0f);
+  set_bits(pl, b);
+}
+
+static void encode_one(const bt4o_board *h, int n, int fmt, float (*r)[64], int *transform_out) {
+  memset(r, 0, sizeof(float) * 112 * 64);
+  *transform_out = 0;
+  if (n <= 0) return;
+  const bt4o_board *cur = &h[n - 1];
+  const int us = cur->black_to_move, them = !us;
+  const int canonical = fmt == 3 || fmt == 4 || fmt == 5 || fmt == 132 || fmt == 133;
+  const int v2 = fmt == 5 || fmt == 133;
+  const int hecto = fmt == 4 || fmt == 132 || fmt == 5 || fmt == 133;
+  const int arma = fmt == 132 || fmt == 133;
+  const int transform = canonical ? choose_transform(cur, us) : 0;
+  const int A = 104;
+  /* auxiliary planes, encoder.cpp:279-336 */
+  if (fmt == 1) {
+    const int oq = us ? C_BOOO : C_WOOO, ok = us ? C_BOO : C_WOO;
+    const int tq = us ? C_WOOO : C_BOOO, tk = us ? C_WOO : C_BOO;
+    set_plane(r[A + 0], (cur->castling & oq) ? 1.0f : 0.0f);
+    set_plane(r[A + 1], (cur->castling & ok) ? 1.0f : 0.0f);
+    set_plane(r[A + 2], (cur->castling & tq) ? 1.0f : 0.0f);
+    set_plane(r[A + 3], (cur->castling & tk) ? 1.0f : 0.0f);
+  } else {
+    const int c = cur->castling;
+    if (!us) {
+      if (c & C_WOOO) r[A + 0][0] = 1.0f;
+      if (c & C_WOO) r[A + 1][7] = 1.0f;
+      if (c & C_BOOO) r[A + 0][56] = 1.0f;
+      if (c & C_BOO) r[A + 1][63] = 1.0f;
+    } else {
+      if (c & C_BOOO) r[A + 0][0] = 1.0f;
+      if (c & C_BOO) r[A + 1][7] = 1.0f;
+      if (c & C_WOOO) r[A + 0][56] = 1.0f;
+      if (c & C_WOO) r[A + 1][63] = 1.0f;
+    }
+  }
+  if (canonical) {
+    if (cur->ep_square >= 0) r[A + 4][cur->ep_square] = 1.0f;
+  } else {
+    set_plane(r[A + 4], us ? 1.0f : 0.0f);
+  }
+  set_plane(r[A + 5], hecto ? (float)cur->rule50 / 100.0f : (float)cur->rule50);
+  set_plane(r[A + 6], (arma && us) ? 1.0f : 0.0f);
+  set_plane(r[A + 7], 1.0f);
+  /* history, encoder.cpp:362-437 */
+  const int root_mask = castle_mask_for(cur, us);
+  for (int i = 0, hi = n - 1; i < 8; ++i, --hi) {
+    if (hi < -8) break; /* see the header comment */
+    const bt4o_board *p = &h[hi >= 0 ? hi : 0];
+    if (hi < 0 && is_start(p)) break;
+    if (canonical && hi < n - 1) {
+      if (castle_mask_for(p, us) != root_mask) break;
+      if (p->ep_square >= 0) break;
+    }
+    const int rep = p->repetition != 0;
+    if (v2 && i > 0 && !rep) {
+      if (p->rule50 == 0) break;
+      --i;
+      continue;
+    }
+    const int base = i * 13;
+    uint64_t our[6], their[6];
+    for (int k = 0; k < 6; ++k) {
+      our[k] = p->pieces[us][k];
+      their[k] = p->pieces[them][k];
+      if (us) {
+        our[k] = rev_bytes(our[k]);
+        their[k] = rev_bytes(their[k]);
+      }
+    }
+    for (int k = 0; k < 6; ++k) set_bits(r[base + k], our[k]);
+    for (int k = 0; k < 6; ++k) set_bits(r[base + 6 + k], their[k]);
+    set_plane(r[base + 12], rep ? 1.0f : 0.0f);
+    if (hi < 0 && p->ep_square >= 0) {
+      const int e = p->ep_square;
+      if (e < 8)
+        fill_from(r[base + 0], our[0] + ((0x0000000000000100ull - 0x0000000001000000ull) << e));
+      else if (e >= 56)
+        fill_from(r[base + 6], their[0] + ((0x0001000000000000ull - 0x0000000100000000ull) << (e - 56)));
+    }
+    if (canonical && p->rule50 == 0) break;
+  }
+  /* canonicalisation, encoder.cpp:439-455 */
+  if (transform) {
+    for (int i = 0; i <= A + 4; ++i) {
+      uint64_t b = 0;
+      for (int s = 0; s < 64; ++s)
+        if (r[i][s] > 0.5f) b |= 1ull << s;
+      if (b == 0 || b == ~0ull) continue;
+      fill_from(r[i], apply_transform(b, transform));
+    }
+  }
+  *transform_out = transform;
+}
+
+/* PackInputPlaneRaw (input_plane_packing.h:30-61) */
+static void pack_plane(const float *pl, int p, uint64_t *mask, float *value) {
+  const int uniform = (p < 104 && p % 13 == 12) || p == 106 || p == 107 || p >= 109;
+  if (uniform) {
+    *value = pl[0];
+    *mask = *value != 0.0f ? ~0ull : 0ull;
+    return;
+  }
+  *mask = 0;
+  *value = 0.0f;
+  for (int s = 0; s < 64; ++s)
+    if (pl[s] != 0.0f) {
+      if (*mask == 0) *value = pl[s];
+      *mask |= 1ull << s;
+    }
+}
+
+int bt4o_encode(const bt4o_board *boards, const int32_t *offsets, int batch, int fmt,
+                uint64_t *masks, float *values, int32_t *transforms) {
+  float (*r)[64] = (float (*)[64])malloc(sizeof(float) * 112 * 64);
+  if (!r) return 1;
+  for (int b = 0; b < batch; ++b) {
+    int t = 0;
+    encode_one(boards + (offsets[b] - offsets[0]), offsets[b + 1] - offsets[b], fmt, r, &t);
+    for (int p = 0; p < 112; ++p)
+      pack_plane(r[p], p, &masks[(size_t)b * 112 + p], &values[(size_t)b * 112 + p]);
+    if (transforms) transforms[b] = t;
+  }
+  free(r);
+  return 0;
+}

@@ -122,3 +122,20 @@ def priors(policy: np.ndarray, offsets: np.ndarray, index: np.ndarray, temp: flo
     lib().bt4o_priors(_ptr(policy), ctypes.c_int(policy.shape[0]), _ptr(offsets), _ptr(index),
                       ctypes.c_float(temp), _ptr(out))
     return out
+
+
+def encode(boards: np.ndarray, offsets: np.ndarray, fmt: int):
+    """Reference encoder restatement (bt4o_encode) over board records
+    [n, 112] uint8 with CSR offsets: packed masks, values [B, 112], transforms [B]."""
+    L = lib()
+    assert L.bt4o_board_size() == 112
+    b = len(offsets) - 1
+    boards = np.ascontiguousarray(boards, np.uint8)
+    offsets = np.ascontiguousarray(offsets, np.int32)
+    m = np.zeros((b, 112), np.uint64)
+    v = np.zeros((b, 112), np.float32)
+    t = np.zeros(b, np.int32)
+    if L.bt4o_encode(_ptr(boards), _ptr(offsets), ctypes.c_int(b), ctypes.c_int(fmt), _ptr(m), _ptr(v),
+                     _ptr(t)) != 0:
+        raise RuntimeError("bt4o_encode failed")
+    return m, v, t

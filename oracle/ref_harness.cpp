@@ -47,6 +47,7 @@
 #include <deque>
 #include <fstream>
 #include <iostream>
+#include <limits>
 #include <map>
 #include <random>
 #include <sstream>
@@ -125,7 +126,7 @@ struct Game {
   std::vector<const Position *> ptrs;
 };
 
-void BuildGame(std::uint64_t seed, int i, Game &g) {
+void BuildGame(std::uint64_t seed, int i, Game &g, const char *fen = kStartFen) {
   std::mt19937_64 rng(seed ^ std::uint64_t(i));
   const int target_plies = int(rng() % 81);
   // Play the line once to fix the moves.
@@ -134,7 +135,7 @@ void BuildGame(std::uint64_t seed, int i, Game &g) {
     Position pos;
     StateInfo root;
     std::deque<StateInfo> states;
-    pos.set(kStartFen, false, &root);
+    pos.set(fen, false, &root);
     for (int ply = 0; ply < target_plies; ++ply) {
       MoveList<LEGAL> legal(pos);
       if (legal.size() == 0) break;
@@ -152,7 +153,7 @@ void BuildGame(std::uint64_t seed, int i, Game &g) {
   for (int ply = 0; ply <= total; ++ply) {
     g.positions.push_back(std::make_unique<Position>());
     g.roots.push_back(std::make_unique<StateInfo>());
-    g.positions.back()->set(kStartFen, false, g.roots.back().get());
+    g.positions.back()->set(fen, false, g.roots.back().get());
     auto &stack = g.stacks[ply];
     for (int k = 0; k < ply; ++k) {
       stack.emplace_back();
@@ -232,6 +233,98 @@ int GenMoves(std::uint64_t seed, int count, const std::string &out_path) {
   out.write(reinterpret_cast<const char *>(hdr), sizeof(hdr));
   out.write(reinterpret_cast<const char *>(offsets.data()), offsets.size() * 4);
   out.write(reinterpret_cast<const char *>(index.data()), index.size() * 2);
+  return out.good() ? 0 : 1;
+}
+
+// Every position of each fixture game (oldest first) as the board records
+// the GPU encoder takes (include/mfb200.h, mfb200_board), read through the
+// reference's Position accessors, plus the transform the reference encoder
+// chose for the final position. Output "MFHB", u32 version, u32 count,
+// i32 offsets[count+1], 112-byte records, i32 transforms[count].
+struct BoardRecord {
+  std::uint64_t pieces[2][6];
+  std::int32_t rule50, game_ply;
+  std::int8_t ep_square;
+  std::uint8_t castling, black_to_move, repetition;
+  std::uint32_t reserved;
+};
+static_assert(sizeof(BoardRecord) == 112, "board record layout");
+
+BoardRecord Record(const Position &p) {
+  BoardRecord r{};
+  const PieceType kinds[6] = {PAWN, KNIGHT, BISHOP, ROOK, QUEEN, KING};
+  for (int c = 0; c < 2; ++c)
+    for (int k = 0; k < 6; ++k) r.pieces[c][k] = p.pieces(c ? BLACK : WHITE, kinds[k]);
+  r.rule50 = p.rule50_count();
+  r.game_ply = p.game_ply();
+  r.ep_square = p.ep_square() == SQ_NONE ? std::int8_t(-1) : std::int8_t(p.ep_square());
+  r.castling = std::uint8_t((p.can_castle(WHITE_OO) ? 1 : 0) | (p.can_castle(WHITE_OOO) ? 2 : 0) |
+                            (p.can_castle(BLACK_OO) ? 4 : 0) | (p.can_castle(BLACK_OOO) ? 8 : 0));
+  r.black_to_move = p.side_to_move() == BLACK ? 1 : 0;
+  r.repetition = p.is_repetition(std::numeric_limits<int>::max()) ? 1 : 0;
+  return r;
+}
+
+// After the V2 transforms: u32 n_all, then for each of the seven input
+// formats: i32 format, u64 masks[n_all*112], f32 values[n_all*112],
+// i32 transforms[n_all] -- the reference encoding of the first n_all
+// positions in every format.
+int GenHistory(std::uint64_t seed, int count, int n_all, const std::string &out_path,
+               const char *fen = kStartFen) {
+  using IF = MetalFishNN::NetworkFormat;
+  const IF::InputFormat formats[7] = {
+      IF::INPUT_CLASSICAL_112_PLANE, IF::INPUT_112_WITH_CASTLING_PLANE,
+      IF::INPUT_112_WITH_CANONICALIZATION, IF::INPUT_112_WITH_CANONICALIZATION_HECTOPLIES,
+      IF::INPUT_112_WITH_CANONICALIZATION_V2,
+      IF::INPUT_112_WITH_CANONICALIZATION_HECTOPLIES_ARMAGEDDON,
+      IF::INPUT_112_WITH_CANONICALIZATION_V2_ARMAGEDDON};
+  Bitboards::init();
+  Position::init();
+  n_all = std::min(n_all, count);
+  std::vector<std::int32_t> offsets(1, 0), transforms;
+  std::vector<BoardRecord> boards;
+  std::vector<std::uint64_t> fm[7];
+  std::vector<float> fv[7];
+  std::vector<std::int32_t> ft[7];
+  for (int i = 0; i < count; ++i) {
+    Game g;
+    BuildGame(seed, i, g, fen);
+    for (const Position *p : g.ptrs) boards.push_back(Record(*p));
+    offsets.push_back(std::int32_t(boards.size()));
+    int transform = 0;
+    (void)NN::EncodePositionForNN(IF::INPUT_112_WITH_CANONICALIZATION_V2, g.ptrs,
+                                  NN::kMoveHistory, NN::FillEmptyHistory::FEN_ONLY, &transform);
+    transforms.push_back(transform);
+    if (i < n_all) {
+      for (int f = 0; f < 7; ++f) {
+        int t = 0;
+        const NN::InputPlanes planes = NN::EncodePositionForNN(
+            formats[f], g.ptrs, NN::kMoveHistory, NN::FillEmptyHistory::FEN_ONLY, &t);
+        std::vector<std::uint64_t> m;
+        std::vector<float> v;
+        NN::PackInputPlanesRaw(planes[0].data(), 1, m, v);
+        fm[f].insert(fm[f].end(), m.begin(), m.end());
+        fv[f].insert(fv[f].end(), v.begin(), v.end());
+        ft[f].push_back(t);
+      }
+    }
+  }
+  std::ofstream out(out_path, std::ios::binary);
+  const std::uint32_t hdr[2] = {1, std::uint32_t(count)};
+  out.write("MFHB", 4);
+  out.write(reinterpret_cast<const char *>(hdr), sizeof(hdr));
+  out.write(reinterpret_cast<const char *>(offsets.data()), offsets.size() * 4);
+  out.write(reinterpret_cast<const char *>(boards.data()), boards.size() * sizeof(BoardRecord));
+  out.write(reinterpret_cast<const char *>(transforms.data()), transforms.size() * 4);
+  const std::uint32_t na = std::uint32_t(n_all);
+  out.write(reinterpret_cast<const char *>(&na), 4);
+  for (int f = 0; f < 7; ++f) {
+    const std::int32_t code = formats[f];
+    out.write(reinterpret_cast<const char *>(&code), 4);
+    out.write(reinterpret_cast<const char *>(fm[f].data()), fm[f].size() * 8);
+    out.write(reinterpret_cast<const char *>(fv[f].data()), fv[f].size() * 4);
+    out.write(reinterpret_cast<const char *>(ft[f].data()), ft[f].size() * 4);
+  }
   return out.good() ? 0 : 1;
 }
 
@@ -515,6 +608,9 @@ int main(int argc, char **argv) {
     if (cmd == "gen-moves" && argc == 5)
       return GenMoves(std::stoull(argv[2]), std::stoi(argv[3]), argv[4]);
     if (cmd == "fastexp" && argc == 4) return FastExpFile(argv[2], argv[3]);
+    if (cmd == "gen-history" && (argc == 6 || argc == 7))
+      return GenHistory(std::stoull(argv[2]), std::stoi(argv[3]), std::stoi(argv[4]), argv[5],
+                        argc == 7 ? argv[6] : kStartFen);
 #ifdef MFB_WITH_B200
     if (cmd == "priors-b200" && argc == 7)
       return PriorsB200(argv[2], argv[3], argv[4], std::stof(argv[5]), argv[6]);
@@ -528,6 +624,7 @@ int main(int argc, char **argv) {
                  "       ref_harness to-pb <net.mfnt> <out.pb>\n"
                  "       ref_harness gen-moves <seed> <count> <out.mfmv>\n"
                  "       ref_harness fastexp <in.f32> <out.f32>\n"
+                 "       ref_harness gen-history <seed> <count> <count-all-formats> <out.mfhb> [start-fen]\n"
                  "       ref_harness eval-backend <cpu|b200> <net.mfnt> <in.mfin> <out.mfot> [threads] [first] [count]\n"
                  "       b200_harness priors-b200 <net.mfnt> <in.mfin> <moves.mfmv> <temp> <out.f32>\n");
     return 2;

@@ -16,6 +16,12 @@ by hand in the development container, never by the tests. Outputs:
   transform), CSR ``offsets`` / ``index``.
 * ``fastexp.npz``         -- inputs and outputs of the reference's FastExp
   (src/mcts/core.h:38-44), the exponential of the MCTS policy softmax.
+* ``history.npz``         -- game histories as board records (the GPU
+  encoder's input, include/mfb200.h mfb200_board), read through the
+  reference's Position accessors (oracle/ref_harness gen-history), with the
+  reference encoder's packed planes and transforms for all seven input
+  formats: the first 1024 fixture games (formats on the first 256) and three
+  sets of 64 games from pawnless starts, which reach every canonical transform.
 * ``ref_<config>.npz``     -- outputs of the reference ``Cpu::CpuNetwork`` on the
   first N of those positions, for seeded synthetic weights; plus a SHA-256 of
   the weights so a numpy change that alters the generator is caught.
@@ -65,6 +71,50 @@ def read_moves(path):
     return offsets, index
 
 
+PAWNLESS_FENS = ["8/8/3k4/8/8/4K3/8/R6Q w - - 0 1", "2kr4/8/8/8/8/8/8/4K1NB b - - 0 1",
+                 "8/2q5/8/3k4/8/8/8/B3K1R1 w - - 0 1"]
+
+
+def read_history(path):
+    b = open(path, "rb").read()
+    assert b[:4] == b"MFHB", "bad history file"
+    cnt = int(np.frombuffer(b[8:12], np.uint32)[0])
+    o = 12
+    off = np.frombuffer(b[o:o + 4 * (cnt + 1)], np.int32).copy()
+    o += 4 * (cnt + 1)
+    nb = int(off[-1])
+    boards = np.frombuffer(b[o:o + 112 * nb], np.uint8).reshape(nb, 112).copy()
+    o += 112 * nb
+    tr = np.frombuffer(b[o:o + 4 * cnt], np.int32).copy()
+    o += 4 * cnt
+    na = int(np.frombuffer(b[o:o + 4], np.uint32)[0])
+    o += 4
+    out = {"offsets": off, "boards": boards, "transforms_v2": tr}
+    for _ in range(7):
+        code = int(np.frombuffer(b[o:o + 4], np.int32)[0])
+        o += 4
+        out[f"masks_{code}"] = np.frombuffer(b[o:o + 8 * na * 112], np.uint64).reshape(na, 112).copy()
+        o += 8 * na * 112
+        out[f"values_{code}"] = np.frombuffer(b[o:o + 4 * na * 112], np.float32).reshape(na, 112).copy()
+        o += 4 * na * 112
+        out[f"transforms_{code}"] = np.frombuffer(b[o:o + 4 * na], np.int32).copy()
+        o += 4 * na
+    return out
+
+
+def make_history(tmp) -> None:
+    sets = {}
+    p = os.path.join(tmp, "h0.mfhb")
+    subprocess.run([HARNESS, "gen-history", str(POSITION_SEED), "1024", "256", p], check=True)
+    sets["start"] = read_history(p)
+    for k, fen in enumerate(PAWNLESS_FENS):
+        p = os.path.join(tmp, f"h{k + 1}.mfhb")
+        subprocess.run([HARNESS, "gen-history", str(7 + k), "64", "64", p, fen], check=True)
+        sets[f"pawnless{k}"] = read_history(p)
+    flat = {f"{name}/{key}": val for name, d in sets.items() for key, val in d.items()}
+    np.savez_compressed(os.path.join(HERE, "history.npz"), **flat)
+
+
 def make_moves_and_fastexp(tmp) -> None:
     mv = os.path.join(tmp, "moves.mfmv")
     subprocess.run([HARNESS, "gen-moves", str(POSITION_SEED), str(POSITIONS), mv], check=True)
@@ -84,11 +134,12 @@ def make_moves_and_fastexp(tmp) -> None:
 
 
 def main() -> None:
-    if sys.argv[1:] == ["--moves-only"]:
+    if sys.argv[1:] == ["--moves-only"]:  # legal moves, FastExp and histories only
         subprocess.run(["make", "-s", "-C", os.path.join(ROOT, "oracle"), f"REF={REF}", "ref"],
                        check=True)
         with tempfile.TemporaryDirectory() as tmp:
             make_moves_and_fastexp(tmp)
+            make_history(tmp)
         return
     subprocess.run(["make", "-s", "-C", os.path.join(ROOT, "oracle"), f"REF={REF}", "ref"],
                    check=True)
@@ -103,6 +154,7 @@ def main() -> None:
         np.savez_compressed(os.path.join(HERE, "positions.npz"), masks=inp.masks,
                             values=inp.values, seed=POSITION_SEED)
         make_moves_and_fastexp(tmp)
+        make_history(tmp)
 
         threads = os.cpu_count() or 1
         for name, cfg, seed, perturb, n in CASES:

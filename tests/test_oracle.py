@@ -154,3 +154,41 @@ def test_oracle_priors_semantics():
     p0 = port.priors(np.zeros((1, 1858), np.float32), np.array([0, 2], np.int32),
                      np.array([-1, 3], np.int16), 1.0)
     np.testing.assert_array_equal(p0, np.array([0.5, 0.5], np.float32))
+
+
+# ---------------------------------------------------------------- position encoder
+FORMATS = (1, 2, 3, 4, 5, 132, 133)
+
+
+def _history_sets():
+    z = np.load(os.path.join(GOLDEN, "history.npz"))
+    names = sorted({k.split("/")[0] for k in z.files})
+    return {n: {k.split("/")[1]: z[k] for k in z.files if k.startswith(n + "/")} for n in names}
+
+
+def test_encoder_restatement_matches_reference_all_formats():
+    """bt4o_encode on the reference's own board records reproduces the
+    reference encoder's packed planes and transforms bit for bit, in every
+    input format, including pawnless games that reach every transform."""
+    seen = set()
+    for name, d in _history_sets().items():
+        for fmt in FORMATS:
+            ref_m = d[f"masks_{fmt}"]
+            n = len(ref_m)
+            m, v, t = port.encode(d["boards"], d["offsets"][:n + 1], fmt)
+            np.testing.assert_array_equal(m, ref_m, err_msg=f"{name} format {fmt}")
+            np.testing.assert_array_equal(v, d[f"values_{fmt}"], err_msg=f"{name} format {fmt}")
+            np.testing.assert_array_equal(t, d[f"transforms_{fmt}"], err_msg=f"{name} format {fmt}")
+            seen.update(t.tolist())
+    assert seen == set(range(8))  # flip, mirror, transpose and their combinations
+
+
+def test_encoder_restatement_matches_position_fixture():
+    """The V2 encoding of the 1024 start games equals positions.npz (the
+    reference's encoding the parity fixtures are built on)."""
+    d = _history_sets()["start"]
+    m, v, t = port.encode(d["boards"], d["offsets"], 5)
+    z = np.load(os.path.join(GOLDEN, "positions.npz"))
+    np.testing.assert_array_equal(m, z["masks"][:len(m)])
+    np.testing.assert_array_equal(v, z["values"][:len(v)])
+    np.testing.assert_array_equal(t, d["transforms_v2"])
