@@ -25,6 +25,10 @@
  *                          GPU: position histories in, packed planes (and the forward) out,
  *                          replacing the host encode of NNMCTSEvaluator
  *                          (src/mcts/evaluator.cpp:150-158)
+ *   mfb200_evaluate_leaves <- NNMCTSEvaluator::EvaluateBatchWithHistoryViews
+ *                          (src/mcts/evaluator.cpp:140-170: encode, EvaluateBatch,
+ *                          BuildResult) + ApplyNNPolicyToNode's softmax
+ *                          (src/mcts/search.cpp:127-197), all on the GPU
  *   mfb200_capabilities <- NN::Network::GetBackendCapabilities / HasWDL / HasMovesLeft /
  *                          GetNetworkInfo (src/nn/network.h:21-51)
  *   mfb200_last_error   <- the std::runtime_error messages the reference throws
@@ -176,6 +180,25 @@ MFB200_API int mfb200_evaluate_history(mfb200_handle *h, const mfb200_board *boa
                                        int input_format, float *policy, float *wdl,
                                        float *moves_left, int32_t *transforms,
                                        mfb200_timing *timing);
+
+/* The whole MCTS leaf evaluation on the GPU: game histories in (as in
+ * mfb200_encode_history), the legal moves of each position as
+ * from | to << 6 | promotion << 12 (squares 0..63 a1..h8; promotion 0 none,
+ * 1 queen, 2 rook, 3 bishop, 4 knight; castling as the king's from and the
+ * to square Move::to_sq() gives) in a CSR over move_offsets [batch + 1];
+ * priors / wdl / moves_left out as in mfb200_evaluate_priors. Each move is
+ * mapped to its policy index on the device exactly as the evaluator does
+ * (mirror for black, NN::MoveToNNIndex with the encoder's transform). */
+MFB200_API int mfb200_evaluate_leaves(mfb200_handle *h, const mfb200_board *boards,
+                                      const int32_t *history_offsets, int batch, int input_format,
+                                      const uint16_t *moves, const int32_t *move_offsets,
+                                      float softmax_temp, float *priors, float *wdl,
+                                      float *moves_left, mfb200_timing *timing);
+
+/* NN::MoveToNNIndex (src/nn/policy_map.cpp:316-360) as this library maps
+ * moves: out [8 transforms][5 promotion kinds][64 from][64 to], -1 for no
+ * index. Host only (no GPU needed). Returns 0. */
+MFB200_API int mfb200_policy_index_table(int16_t *out);
 
 /* Device-buffer evaluation on device `cfg.device`, enqueued on `stream`
  * (a cudaStream_t; NULL = the handle's stream) without synchronising. All

@@ -5,6 +5,7 @@
 #include <type_traits>
 
 #include "gemm_sm100.cuh"
+#include "../../include/mfb200.h"
 #include "kernels.cuh"
 #include "pdl.cuh"
 
@@ -628,9 +629,43 @@ __device__ __forceinline__ float fast_exp_mcts(float x) {
 
 constexpr int kMaxEdges = 256;
 
+// Policy index of a move given as from | to << 6 | promotion << 12 for a
+// position with the given side to move and canonicalisation transform, as the
+// evaluator computes it: vertical mirror for black (src/mcts/evaluator.cpp:
+// 24-36, 195-200), then NN::MoveToNNIndex (src/nn/policy_map.cpp:303-360):
+// both squares transformed (rank reversed for mirror / transpose, file for
+// flip / transpose), looked up in table[promotion][from][to].
+__device__ __forceinline__ int move_index(uint32_t raw, bool black, int transform,
+                                          const int16_t *__restrict__ table) {
+  int from = raw & 63, to = (raw >> 6) & 63;
+  const int kind = static_cast<int>(raw >> 12);
+  if (kind > 4) return -1;
+  if (black) {
+    from ^= 56;
+    to ^= 56;
+  }
+  if (transform) {
+    if (transform & 6) {
+      from ^= 56;
+      to ^= 56;
+    }
+    if (transform & 5) {
+      from ^= 7;
+      to ^= 7;
+    }
+  }
+  return table[kind * 4096 + from * 64 + to];
+}
+
+// index: policy index per move, or (raw != nullptr) the moves themselves,
+// mapped through move_index with the side to move of each history's last
+// board and the encoder's transform.
 __global__ void __launch_bounds__(256)
     priors_kernel(const float *__restrict__ policy, int batch, const int32_t *__restrict__ offsets,
-                  const int16_t *__restrict__ index, float inv_temp, float *__restrict__ priors) {
+                  const int16_t *__restrict__ index, float inv_temp, float *__restrict__ priors,
+                  const uint16_t *__restrict__ raw, const int16_t *__restrict__ table,
+                  const mfb200_board *__restrict__ boards, const int32_t *__restrict__ hist_off,
+                  const int32_t *__restrict__ transforms) {
   pdl_wait();
   pdl_launch();
   __shared__ float se[8][kMaxEdges];
@@ -643,8 +678,15 @@ __global__ void __launch_bounds__(256)
   float *e = se[warp];
   const float *pol = policy + static_cast<long long>(b) * kPolicy;
   float mx = -INFINITY;
+  bool black = false;
+  int transform = 0;
+  if (raw) {
+    const int last = hist_off[b + 1] - hist_off[0] - 1;
+    black = hist_off[b + 1] > hist_off[b] && boards[last].black_to_move != 0;
+    transform = transforms[b];
+  }
   for (int i = lane; i < n; i += 32) {
-    const int idx = index[lo + i];
+    const int idx = raw ? move_index(raw[lo + i], black, transform, table) : index[lo + i];
     const float l = (idx >= 0 && idx < kPolicy) ? pol[idx] : 0.0f;
     e[i] = l;
     mx = l > mx ? l : mx;
@@ -676,7 +718,19 @@ void launch_priors(const float *policy, int batch, const int32_t *offsets, const
                    float softmax_temp, float *priors, cudaStream_t s) {
   if (batch <= 0) return;
   launch_k(priors_kernel, dim3((batch + 7) / 8), dim3(256), 0, s, 1, policy, batch, offsets, index,
-           1.0f / softmax_temp, priors);
+           1.0f / softmax_temp, priors, static_cast<const uint16_t *>(nullptr),
+           static_cast<const int16_t *>(nullptr), static_cast<const mfb200_board *>(nullptr),
+           static_cast<const int32_t *>(nullptr), static_cast<const int32_t *>(nullptr));
+}
+
+void launch_leaf_priors(const float *policy, int batch, const int32_t *offsets,
+                        const uint16_t *moves, const int16_t *table, const mfb200_board *boards,
+                        const int32_t *hist_off, const int32_t *transforms, float softmax_temp,
+                        float *priors, cudaStream_t s) {
+  if (batch <= 0) return;
+  launch_k(priors_kernel, dim3((batch + 7) / 8), dim3(256), 0, s, 1, policy, batch, offsets,
+           static_cast<const int16_t *>(nullptr), 1.0f / softmax_temp, priors, moves, table, boards,
+           hist_off, transforms);
 }
 
 // ------------------------------------------------------------------ absmax

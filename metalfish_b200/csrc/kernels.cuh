@@ -77,6 +77,13 @@ void launch_encode(const mfb200_board *boards, const int32_t *offsets, int batch
 // offsets[0] entries (see priors_kernel).
 void launch_priors(const float *policy, int batch, const int32_t *offsets, const int16_t *index,
                    float softmax_temp, float *priors, cudaStream_t s);
+// Same from the moves themselves (from | to << 6 | promotion << 12), mapped to
+// policy indices on the device with `table` [5][64][64], each history's side
+// to move (its last board) and the encoder's transforms.
+void launch_leaf_priors(const float *policy, int batch, const int32_t *offsets,
+                        const uint16_t *moves, const int16_t *table, const mfb200_board *boards,
+                        const int32_t *hist_off, const int32_t *transforms, float softmax_temp,
+                        float *priors, cudaStream_t s);
 
 // FP8 calibration: *slot = max(*slot, max|x|) over n values of format `fmt`;
 // and scales[i] = absmax[i] / 448.

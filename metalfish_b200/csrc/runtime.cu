@@ -190,6 +190,27 @@ std::vector<int16_t> build_gather() {
   return gather;
 }
 
+// Policy index of every move (NN::MoveToNNIndex, src/nn/policy_map.cpp:
+// 316-360) by promotion kind (0 none, 1 queen, 2 rook, 3 bishop, 4 knight),
+// from and to square, derived from the move list of build_gather: plain moves
+// and knight promotions by (from, to) among the 1792 queen-line and knight
+// moves, queen / rook / bishop promotions from the seventh rank by (from
+// file, to file, piece). -1 where the reference has no entry. [5][64][64].
+std::vector<int16_t> build_move_index() {
+  const std::vector<int16_t> g = build_gather();
+  std::vector<int16_t> t(5 * 4096, -1);
+  for (int i = 0; i < kPolicy; ++i) {
+    if (g[i] < 4096) {
+      t[g[i]] = static_cast<int16_t>(i);
+      t[4 * 4096 + g[i]] = static_cast<int16_t>(i);
+    } else {
+      const int r = g[i] - 4096, ff = r / 24, tf = (r % 24) / 3, piece = r % 3;
+      t[(1 + piece) * 4096 + (48 + ff) * 64 + 56 + tf] = static_cast<int16_t>(i);
+    }
+  }
+  return t;
+}
+
 // ------------------------------------------------------------ device state
 struct Mat {  // a weight matrix [rows, ld] on the device (bf16, fp16 or e4m3)
   void *w = nullptr;
@@ -256,6 +277,8 @@ struct Shard {  // one GPU
   mfb200_board *boards;   // encoder input: history records [max_batch * 128]
   int32_t *hist_off;      //   CSR offsets [max_batch + 1]
   int32_t *transforms;    //   canonicalisation transform per position [max_batch]
+  uint16_t *moves;        // legal moves (from | to << 6 | promotion << 12) [max_batch * 256]
+  int16_t *move_table;    // build_move_index() [5 * 4096]
   unsigned *status;
   cudaEvent_t ev[4];
   struct Step {
@@ -570,6 +593,8 @@ void alloc_workspace(Shard &S, const mfb200_net_desc &n, int max_batch, bool fp8
       {reinterpret_cast<void **>(&S.boards), B * kHistoryCapacity * sizeof(mfb200_board)},
       {reinterpret_cast<void **>(&S.hist_off), (B + 1) * 4},
       {reinterpret_cast<void **>(&S.transforms), B * 4},
+      {reinterpret_cast<void **>(&S.moves), B * kMoveCapacity * 2},
+      {reinterpret_cast<void **>(&S.move_table), 5 * 4096 * 2},
       {reinterpret_cast<void **>(&S.status), 256},
       {reinterpret_cast<void **>(&S.scales), size_t(2 + 4 * n.layers) * 4},
       {reinterpret_cast<void **>(&S.absmax), size_t(2 + 4 * n.layers) * 4},
@@ -1009,6 +1034,11 @@ extern "C" int mfb200_create(const mfb200_net_desc *desc, const void *weights, s
       for (auto &f : lay.fix) *f.first = static_cast<uint8_t *>(S->arena) + f.second;
       S->w = proto;
       alloc_workspace(*S, *desc, per, cfg->precision == MFB200_PRECISION_FP8);
+      {
+        const std::vector<int16_t> table = build_move_index();
+        check(cudaMemcpy(S->move_table, table.data(), table.size() * 2, cudaMemcpyHostToDevice),
+              "move table upload");
+      }
       h->weight_bytes = S->arena_bytes;
       h->ws_bytes = S->ws_bytes;
       h->shards.push_back(std::move(S));
@@ -1195,6 +1225,116 @@ extern "C" int mfb200_evaluate_history(mfb200_handle *h, const mfb200_board *boa
   }
   for (auto &e : errs)
     if (!e.empty()) return fail(h, "mfb200_evaluate_history: " + e);
+  if (timing) {
+    *timing = mfb200_timing{0, 0, 0, 0};
+    for (auto &m : ms) {
+      timing->h2d_ms = std::max(timing->h2d_ms, m[0]);
+      timing->forward_ms = std::max(timing->forward_ms, m[1]);
+      timing->d2h_ms = std::max(timing->d2h_ms, m[2]);
+      timing->total_ms = std::max(timing->total_ms, m[3]);
+    }
+  }
+  return 0;
+}
+
+extern "C" int mfb200_policy_index_table(int16_t *out) {
+  if (!out) return 1;
+  const std::vector<int16_t> t = build_move_index();
+  // TransformSquare (src/nn/policy_map.cpp:303-312): rank reversed for
+  // mirror / transpose, file reversed for flip / transpose
+  auto sq = [](int s, int tr) {
+    if (tr & 6) s ^= 56;
+    if (tr & 5) s ^= 7;
+    return s;
+  };
+  for (int tr = 0; tr < 8; ++tr)
+    for (int k = 0; k < 5; ++k)
+      for (int from = 0; from < 64; ++from)
+        for (int to = 0; to < 64; ++to)
+          out[((tr * 5 + k) * 64 + from) * 64 + to] = t[k * 4096 + sq(from, tr) * 64 + sq(to, tr)];
+  return 0;
+}
+
+extern "C" int mfb200_evaluate_leaves(mfb200_handle *h, const mfb200_board *boards,
+                                      const int32_t *history_offsets, int batch, int input_format,
+                                      const uint16_t *moves, const int32_t *move_offsets,
+                                      float softmax_temp, float *priors, float *wdl, float *mlh,
+                                      mfb200_timing *timing) {
+  if (!h) return fail(nullptr, "mfb200_evaluate_leaves: null handle");
+  std::lock_guard<std::mutex> lock(h->mu);
+  if (batch <= 0) return 0;
+  if (batch > h->cfg.max_batch)
+    return fail(h, "mfb200_evaluate_leaves: batch " + std::to_string(batch) + " exceeds max_batch " +
+                       std::to_string(h->cfg.max_batch));
+  if (!history_offsets || !move_offsets ||
+      (!boards && history_offsets[batch] != history_offsets[0]) ||
+      (!moves && move_offsets[batch] != move_offsets[0]))
+    return fail(h, "mfb200_evaluate_leaves: null input");
+  if (!(softmax_temp > 0.0f)) return fail(h, "mfb200_evaluate_leaves: softmax_temp must be positive");
+  const int nd = static_cast<int>(h->shards.size());
+  const int per = (batch + nd - 1) / nd;
+  if (const char *e = check_histories(history_offsets, batch, input_format, nd, per))
+    return fail(h, std::string("mfb200_evaluate_leaves: ") + e);
+  for (int b = 0; b < batch; ++b)
+    if (move_offsets[b + 1] < move_offsets[b])
+      return fail(h, "mfb200_evaluate_leaves: move_offsets must be non-decreasing");
+  for (int i = 0; i < nd; ++i) {
+    const int lo = i * per, hi = std::min(batch, lo + per);
+    if (lo < hi && move_offsets[hi] - move_offsets[lo] > int64_t(per) * kMoveCapacity)
+      return fail(h, "mfb200_evaluate_leaves: more than 256 legal moves per position on average");
+  }
+  std::vector<std::array<float, 4>> ms(nd, {0, 0, 0, 0});
+  std::vector<std::string> errs(nd);
+  auto work = [&](int i) {
+    const int lo = i * per, hi = std::min(batch, lo + per);
+    if (lo >= hi) return;
+    Shard &S = *h->shards[i];
+    const int B = hi - lo;
+    const int32_t mbase = move_offsets[lo] - move_offsets[0];
+    const int32_t nmoves = move_offsets[hi] - move_offsets[lo];
+    try {
+      check(cudaSetDevice(S.device), "cudaSetDevice");
+      cudaStream_t s = S.stream;
+      float *m = ms[i].data();
+      check(cudaEventRecord(S.ev[0], s), "event");
+      encode_shard(S, boards + (history_offsets[lo] - history_offsets[0]), history_offsets + lo, B,
+                   input_format, s);
+      check(cudaMemcpyAsync(S.move_off, move_offsets + lo, size_t(B + 1) * 4, cudaMemcpyHostToDevice, s),
+            "H2D move offsets");
+      if (nmoves > 0)
+        check(cudaMemcpyAsync(S.moves, moves + mbase, size_t(nmoves) * 2, cudaMemcpyHostToDevice, s),
+              "H2D moves");
+      check(cudaEventRecord(S.ev[1], s), "event");
+      forward(h, S, B, s);
+      launch_leaf_priors(S.policy, B, S.move_off, S.moves, S.move_table, S.boards, S.hist_off,
+                         S.transforms, softmax_temp, S.priors, s);
+      check(cudaGetLastError(), "priors launch");
+      check(cudaEventRecord(S.ev[2], s), "event");
+      if (priors && nmoves > 0)
+        check(cudaMemcpyAsync(priors + mbase, S.priors, size_t(nmoves) * 4, cudaMemcpyDeviceToHost, s),
+              "D2H priors");
+      if (wdl) check(cudaMemcpyAsync(wdl + size_t(lo) * 3, S.wdl, size_t(B) * 12, cudaMemcpyDeviceToHost, s), "D2H wdl");
+      if (mlh) check(cudaMemcpyAsync(mlh + lo, S.mlh, size_t(B) * 4, cudaMemcpyDeviceToHost, s), "D2H mlh");
+      check(cudaEventRecord(S.ev[3], s), "event");
+      check(cudaStreamSynchronize(s), "forward");
+      check_status(S);
+      cudaEventElapsedTime(&m[0], S.ev[0], S.ev[1]);
+      cudaEventElapsedTime(&m[1], S.ev[1], S.ev[2]);
+      cudaEventElapsedTime(&m[2], S.ev[2], S.ev[3]);
+      cudaEventElapsedTime(&m[3], S.ev[0], S.ev[3]);
+    } catch (const std::exception &e) {
+      errs[i] = e.what();
+    }
+  };
+  if (nd == 1) {
+    work(0);
+  } else {
+    std::vector<std::thread> th;
+    for (int i = 0; i < nd; ++i) th.emplace_back(work, i);
+    for (auto &t : th) t.join();
+  }
+  for (auto &e : errs)
+    if (!e.empty()) return fail(h, "mfb200_evaluate_leaves: " + e);
   if (timing) {
     *timing = mfb200_timing{0, 0, 0, 0};
     for (auto &m : ms) {

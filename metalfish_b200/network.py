@@ -68,6 +68,11 @@ def _declare(L):
     L.mfb200_evaluate_history.restype = c_int
     L.mfb200_evaluate_history.argtypes = [vp, vp, vp, c_int, c_int, vp, vp, vp, vp,
                                           ctypes.POINTER(Timing)]
+    L.mfb200_evaluate_leaves.restype = c_int
+    L.mfb200_evaluate_leaves.argtypes = [vp, vp, vp, c_int, c_int, vp, vp, ctypes.c_float, vp, vp,
+                                         vp, ctypes.POINTER(Timing)]
+    L.mfb200_policy_index_table.restype = c_int
+    L.mfb200_policy_index_table.argtypes = [vp]
     L.mfb200_evaluate_device.restype = c_int
     L.mfb200_evaluate_device.argtypes = [vp, vp, vp, c_int, vp, vp, vp, vp]
     L.mfb200_calibrate.restype = c_int
@@ -251,6 +256,31 @@ class B200Network:
             raise self._err()
         return Outputs(pol, wdl, wdl[:, 0] - wdl[:, 2], mlh), t
 
+    def evaluate_leaves(self, boards: np.ndarray, history_offsets: np.ndarray, moves: np.ndarray,
+                        move_offsets: np.ndarray, softmax_temp: float = 1.0, input_format: int = 5,
+                        timing: Optional[Timing] = None):
+        """The whole MCTS leaf evaluation on the GPU: histories and legal moves
+        (uint16 from | to << 6 | promotion << 12) in; (priors, wdl, moves_left) out."""
+        boards = np.ascontiguousarray(boards).view(np.uint8)
+        hoff = np.ascontiguousarray(history_offsets, np.int32)
+        mv = np.ascontiguousarray(moves, np.uint16)
+        moff = np.ascontiguousarray(move_offsets, np.int32)
+        b = len(hoff) - 1
+        if moff.shape != (b + 1,):
+            raise ValueError("move_offsets must have batch + 1 entries")
+        pri = np.empty(int(moff[-1] - moff[0]), np.float32)
+        wdl = np.empty((b, 3), np.float32)
+        mlh = np.empty(b, np.float32)
+        rc = _lib().mfb200_evaluate_leaves(self._h, boards.ctypes.data if boards.size else None,
+                                           hoff.ctypes.data, b, input_format,
+                                           mv.ctypes.data if mv.size else None, moff.ctypes.data,
+                                           ctypes.c_float(softmax_temp), pri.ctypes.data,
+                                           wdl.ctypes.data, mlh.ctypes.data,
+                                           ctypes.byref(timing) if timing is not None else None)
+        if rc != 0:
+            raise self._err()
+        return pri, wdl, mlh
+
     def calibrate(self, inp: PackedInputs) -> None:
         """FP8 only: absmax calibration of the per-tensor activation scales
         over the given positions (a bf16 forward with probes)."""
@@ -308,6 +338,13 @@ class B200Network:
             raise self._err()
         nm = names.value.decode().split("\n")
         return [(nm[i], ms[i], fl[i]) for i in range(k)]
+
+
+def policy_index_table() -> np.ndarray:
+    """The library's NN::MoveToNNIndex table [8 transforms][5 promotions][64][64]."""
+    t = np.empty((8, 5, 64, 64), np.int16)
+    _lib().mfb200_policy_index_table(t.ctypes.data)
+    return t
 
 
 def create_network(cfg: NetConfig, tensors: Dict[str, np.ndarray], backend: str = "b200",

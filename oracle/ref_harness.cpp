@@ -206,13 +206,16 @@ Move MirrorVertical(Move m) {
 // move, in MoveList<LEGAL> order, as the evaluator maps it
 // (src/mcts/evaluator.cpp:195-206: mirror for black, then
 // NN::MoveToNNIndex(move, transform) with the encoder's transform).
-// Output "MFMV", u32 version, u32 count, i32 offsets[count+1], i16 index[total].
+// Output "MFMV", u32 version, u32 count, i32 offsets[count+1], i16 index[total],
+// u16 raw[total] (the move itself: from | to << 6 | promotion << 12 with
+// 0 none, 1 queen, 2 rook, 3 bishop, 4 knight).
 int GenMoves(std::uint64_t seed, int count, const std::string &out_path) {
   Bitboards::init();
   Position::init();
   NN::InitPolicyTables();
   std::vector<std::int32_t> offsets(1, 0);
   std::vector<std::int16_t> index;
+  std::vector<std::uint16_t> raw;  // from | to << 6 | promotion << 12 (1 Q, 2 R, 3 B, 4 N)
   for (int i = 0; i < count; ++i) {
     Game g;
     BuildGame(seed, i, g);
@@ -224,6 +227,12 @@ int GenMoves(std::uint64_t seed, int count, const std::string &out_path) {
     for (Move m : MoveList<LEGAL>(pos)) {
       const Move pm = pos.side_to_move() == BLACK ? MirrorVertical(m) : m;
       index.push_back(std::int16_t(NN::MoveToNNIndex(pm, transform)));
+      int kind = 0;
+      if (m.type_of() == PROMOTION) {
+        const PieceType pt = m.promotion_type();
+        kind = pt == QUEEN ? 1 : pt == ROOK ? 2 : pt == BISHOP ? 3 : 4;
+      }
+      raw.push_back(std::uint16_t(int(m.from_sq()) | (int(m.to_sq()) << 6) | (kind << 12)));
     }
     offsets.push_back(std::int32_t(index.size()));
   }
@@ -233,6 +242,7 @@ int GenMoves(std::uint64_t seed, int count, const std::string &out_path) {
   out.write(reinterpret_cast<const char *>(hdr), sizeof(hdr));
   out.write(reinterpret_cast<const char *>(offsets.data()), offsets.size() * 4);
   out.write(reinterpret_cast<const char *>(index.data()), index.size() * 2);
+  out.write(reinterpret_cast<const char *>(raw.data()), raw.size() * 2);
   return out.good() ? 0 : 1;
 }
 
@@ -325,6 +335,27 @@ int GenHistory(std::uint64_t seed, int count, int n_all, const std::string &out_
     out.write(reinterpret_cast<const char *>(fv[f].data()), fv[f].size() * 4);
     out.write(reinterpret_cast<const char *>(ft[f].data()), ft[f].size() * 4);
   }
+  return out.good() ? 0 : 1;
+}
+
+// NN::MoveToNNIndex (src/nn/policy_map.cpp:316-360) for every transform
+// (0..7), promotion kind (none, queen, rook, bishop, knight) and (from, to)
+// pair: int16 [8][5][64][64], -1 where the reference returns -1.
+int DumpMoveIndex(const std::string &out_path) {
+  NN::InitPolicyTables();
+  const PieceType promo[5] = {NO_PIECE_TYPE, QUEEN, ROOK, BISHOP, KNIGHT};
+  std::vector<std::int16_t> table;
+  table.reserve(8 * 5 * 4096);
+  for (int t = 0; t < 8; ++t)
+    for (int k = 0; k < 5; ++k)
+      for (int from = 0; from < 64; ++from)
+        for (int to = 0; to < 64; ++to) {
+          const Move m = k == 0 ? Move(Square(from), Square(to))
+                                : Move::make<PROMOTION>(Square(from), Square(to), promo[k]);
+          table.push_back(std::int16_t(NN::MoveToNNIndex(m, t)));
+        }
+  std::ofstream out(out_path, std::ios::binary);
+  out.write(reinterpret_cast<const char *>(table.data()), table.size() * 2);
   return out.good() ? 0 : 1;
 }
 
@@ -608,6 +639,7 @@ int main(int argc, char **argv) {
     if (cmd == "gen-moves" && argc == 5)
       return GenMoves(std::stoull(argv[2]), std::stoi(argv[3]), argv[4]);
     if (cmd == "fastexp" && argc == 4) return FastExpFile(argv[2], argv[3]);
+    if (cmd == "dump-move-index" && argc == 3) return DumpMoveIndex(argv[2]);
     if (cmd == "gen-history" && (argc == 6 || argc == 7))
       return GenHistory(std::stoull(argv[2]), std::stoi(argv[3]), std::stoi(argv[4]), argv[5],
                         argc == 7 ? argv[6] : kStartFen);
@@ -624,6 +656,7 @@ int main(int argc, char **argv) {
                  "       ref_harness to-pb <net.mfnt> <out.pb>\n"
                  "       ref_harness gen-moves <seed> <count> <out.mfmv>\n"
                  "       ref_harness fastexp <in.f32> <out.f32>\n"
+                 "       ref_harness dump-move-index <out.i16>\n"
                  "       ref_harness gen-history <seed> <count> <count-all-formats> <out.mfhb> [start-fen]\n"
                  "       ref_harness eval-backend <cpu|b200> <net.mfnt> <in.mfin> <out.mfot> [threads] [first] [count]\n"
                  "       b200_harness priors-b200 <net.mfnt> <in.mfin> <moves.mfmv> <temp> <out.f32>\n");

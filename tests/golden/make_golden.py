@@ -14,6 +14,9 @@ by hand in the development container, never by the tests. Outputs:
   legal move as the reference evaluator maps it (oracle/ref_harness gen-moves:
   MoveList<LEGAL>, the black-side mirror, NN::MoveToNNIndex with the encoder's
   transform), CSR ``offsets`` / ``index``.
+  ``raw`` holds each move itself (from | to << 6 | promotion << 12).
+* ``move_index.npz``      -- NN::MoveToNNIndex (src/nn/policy_map.cpp:316-360)
+  for every transform, promotion kind and (from, to) pair.
 * ``fastexp.npz``         -- inputs and outputs of the reference's FastExp
   (src/mcts/core.h:38-44), the exponential of the MCTS policy softmax.
 * ``history.npz``         -- game histories as board records (the GPU
@@ -66,9 +69,11 @@ def read_moves(path):
     assert b[:4] == b"MFMV", "bad legal-move file"
     count = int(np.frombuffer(b[8:12], np.uint32)[0])
     offsets = np.frombuffer(b[12:12 + 4 * (count + 1)], np.int32).copy()
-    index = np.frombuffer(b[12 + 4 * (count + 1):], np.int16).copy()
-    assert len(index) == offsets[-1]
-    return offsets, index
+    o = 12 + 4 * (count + 1)
+    n = int(offsets[-1])
+    index = np.frombuffer(b[o:o + 2 * n], np.int16).copy()
+    raw = np.frombuffer(b[o + 2 * n:o + 4 * n], np.uint16).copy()
+    return offsets, index, raw
 
 
 PAWNLESS_FENS = ["8/8/3k4/8/8/4K3/8/R6Q w - - 0 1", "2kr4/8/8/8/8/8/8/4K1NB b - - 0 1",
@@ -118,9 +123,13 @@ def make_history(tmp) -> None:
 def make_moves_and_fastexp(tmp) -> None:
     mv = os.path.join(tmp, "moves.mfmv")
     subprocess.run([HARNESS, "gen-moves", str(POSITION_SEED), str(POSITIONS), mv], check=True)
-    offsets, index = read_moves(mv)
+    offsets, index, raw = read_moves(mv)
     np.savez_compressed(os.path.join(HERE, "legal_moves.npz"), offsets=offsets, index=index,
-                        seed=POSITION_SEED)
+                        raw=raw, seed=POSITION_SEED)
+    mi = os.path.join(tmp, "move_index.i16")
+    subprocess.run([HARNESS, "dump-move-index", mi], check=True)
+    np.savez_compressed(os.path.join(HERE, "move_index.npz"),
+                        table=np.fromfile(mi, np.int16).reshape(8, 5, 64, 64))
     rng = np.random.default_rng(5)
     x = np.concatenate([
         np.linspace(-100.0, 100.0, 20001, dtype=np.float32),

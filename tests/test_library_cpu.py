@@ -76,3 +76,13 @@ def test_noalloc_rejects_oversize_without_touching_gpu():
     rc = L.mfb200_splitk_gemm_noalloc(ctypes.c_void_p(16), ctypes.c_void_p(16), 4096, 1024, 1024, 4,
                                       None, ctypes.c_void_p(16), None)
     assert rc != 0 and b"exceeds" in L.mfb200_noalloc_last_error()
+
+
+def test_policy_index_table_matches_reference():
+    """The move -> policy index mapping the GPU uses (derived from the
+    library's own 1858-move list) equals the reference's NN::MoveToNNIndex
+    for every transform, promotion kind and square pair (host only)."""
+    import os
+    from metalfish_b200.network import policy_index_table
+    ref = np.load(os.path.join(os.path.dirname(__file__), "golden", "move_index.npz"))["table"]
+    np.testing.assert_array_equal(policy_index_table(), ref)
