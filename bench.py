@@ -22,6 +22,11 @@ batch is sharded, weights replicated, no collective in the forward
                 host round trip, returning the softmax priors of each
                 position's legal moves (computed on the GPU) instead of the
                 1858 logits.
+* e2e_leaves -- the whole MCTS leaf evaluation through mfb200_evaluate_leaves:
+                game histories (board records) and legal moves in, priors
+                out; position encoding, forward, move mapping and softmax on
+                the GPU (the host-side encode of the reference evaluator is
+                gone).
 * cpu_baseline -- the reference CPU backend (oracle/_ref, built from the
                 reference sources) or, if that binary is absent, the C
                 restatement, on a bounded sample on the host cores.
@@ -353,6 +358,44 @@ def main():
                   "d2h_bytes_per_step": int(len(m_idx) * 4 + B * 16),
                   "legal_moves_per_step": int(len(m_idx))}
 
+    # ---- the whole MCTS leaf path through mfb200_evaluate_leaves: game
+    # histories (board records of the fixture games) and their legal moves
+    # in, priors out -- encoding, forward, move mapping and softmax on the GPU
+    hz = np.load(os.path.join(ROOT, "tests", "golden", "history.npz"))
+    h_off_all, h_boards_all = hz["start/offsets"], hz["start/boards"]
+    gid = np.arange(rank * B, (rank + 1) * B) % (len(h_off_all) - 1)
+    h_counts = h_off_all[gid + 1] - h_off_all[gid]
+    h_off = np.concatenate([[0], np.cumsum(h_counts)]).astype(np.int32)
+    h_boards = np.concatenate([h_boards_all[h_off_all[i]:h_off_all[i + 1]] for i in gid])
+    l_counts = mv["offsets"][gid + 1] - mv["offsets"][gid]
+    l_off = np.concatenate([[0], np.cumsum(l_counts)]).astype(np.int32)
+    l_raw = np.concatenate([mv["raw"][mv["offsets"][i]:mv["offsets"][i + 1]] for i in gid]).astype(np.uint16)
+    pin_hb = torch.from_numpy(h_boards).pin_memory()
+    pin_ho = torch.from_numpy(h_off).pin_memory()
+    pin_lr = torch.from_numpy(l_raw.view(np.int16)).pin_memory()
+    pin_lo = torch.from_numpy(l_off).pin_memory()
+    h_lpri = torch.empty(int(l_off[-1]), dtype=torch.float32).pin_memory()
+
+    def leaves_step():
+        rc = L.mfb200_evaluate_leaves(net._h, pin_hb.data_ptr(), pin_ho.data_ptr(), B, 5,
+                                      pin_lr.data_ptr(), pin_lo.data_ptr(), ctypes.c_float(1.0),
+                                      h_lpri.data_ptr(), h_wdl.data_ptr(), h_mlh.data_ptr(), None)
+        if rc:
+            raise RuntimeError(L.mfb200_last_error(net._h).decode())
+
+    for _ in range(args.warmup):
+        leaves_step()
+    barrier(world)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        leaves_step()
+    lv_s = all_max(time.perf_counter() - t0, world)
+    barrier(world)
+    e2e_leaves = {"value": B * world * args.steps / lv_s, "unit": "positions/s",
+                  "h2d_bytes_per_step": int(h_boards.nbytes + h_off.nbytes + l_raw.nbytes + l_off.nbytes),
+                  "d2h_bytes_per_step": int(len(l_raw) * 4 + B * 16),
+                  "history_boards_per_step": int(len(h_boards))}
+
     # ---- batch-1 latency (the per-leaf MCTS case): device time of one
     # graph-launched forward, and the host round trip through mfb200_evaluate
     lat = batch1_latency(net, dev, stream, shard, L) if rank == 0 else None
@@ -419,6 +462,7 @@ def main():
                         "measured cuBLAS bf16 burst peak (x2 for e4m3) and the nominal dense peak"},
             "latency_batch1_ms": lat,
             "e2e_priors": e2e_priors,
+            "e2e_leaves": e2e_leaves,
             "stage_ms": stage_summary(stages),
             "stage_ms_total": total_stage_ms,
             "clocks": clocks,

@@ -3,6 +3,7 @@
 
 #include <algorithm>
 #include <cstring>
+#include <limits>
 #include <sstream>
 #include <stdexcept>
 
@@ -97,6 +98,32 @@ std::vector<float> WeightBlob(const MultiHeadWeights &w, const MultiHeadWeights:
       put(*v);
   }
   return blob;
+}
+
+// One history entry as the GPU encoder reads it (include/mfb200.h).
+mfb200_board ToBoard(const Position &p) {
+  mfb200_board r{};
+  const PieceType kinds[6] = {PAWN, KNIGHT, BISHOP, ROOK, QUEEN, KING};
+  for (int c = 0; c < 2; ++c)
+    for (int k = 0; k < 6; ++k) r.pieces[c][k] = p.pieces(c ? BLACK : WHITE, kinds[k]);
+  r.rule50 = p.rule50_count();
+  r.game_ply = p.game_ply();
+  r.ep_square = p.ep_square() == SQ_NONE ? std::int8_t(-1) : std::int8_t(p.ep_square());
+  r.castling = std::uint8_t((p.can_castle(WHITE_OO) ? 1 : 0) | (p.can_castle(WHITE_OOO) ? 2 : 0) |
+                            (p.can_castle(BLACK_OO) ? 4 : 0) | (p.can_castle(BLACK_OOO) ? 8 : 0));
+  r.black_to_move = p.side_to_move() == BLACK ? 1 : 0;
+  r.repetition = p.is_repetition(std::numeric_limits<int>::max()) ? 1 : 0;
+  return r;
+}
+
+// from | to << 6 | promotion << 12 (1 queen, 2 rook, 3 bishop, 4 knight).
+std::uint16_t ToRawMove(Move m) {
+  int kind = 0;
+  if (m.type_of() == PROMOTION) {
+    const PieceType pt = m.promotion_type();
+    kind = pt == QUEEN ? 1 : pt == ROOK ? 2 : pt == BISHOP ? 3 : 4;
+  }
+  return std::uint16_t(int(m.from_sq()) | (int(m.to_sq()) << 6) | (kind << 12));
 }
 
 B200Options FromConfig(const BackendConfig &config) {
@@ -214,6 +241,50 @@ B200Network::EvaluatePriors(const std::vector<InputPlanes> &inputs,
                                move_offsets_.data() + lo, move_index_.data() + base, softmax_temp,
                                priors_.data() + base, wdl_.data() + size_t(lo) * 3,
                                mlh_.data() + lo, nullptr) != 0)
+      throw std::runtime_error(std::string("B200 backend: ") + mfb200_last_error(handle_));
+  }
+  for (int b = 0; b < n; ++b) {
+    LeafResult &r = out[b];
+    r.priors.assign(priors_.begin() + move_offsets_[b], priors_.begin() + move_offsets_[b + 1]);
+    r.wdl[0] = wdl_[3 * b];
+    r.wdl[1] = wdl_[3 * b + 1];
+    r.wdl[2] = wdl_[3 * b + 2];
+    r.value = r.wdl[0] - r.wdl[2];
+    r.moves_left = mlh_[b];
+  }
+  return out;
+}
+
+std::vector<B200Network::LeafResult>
+B200Network::EvaluateLeaves(const std::vector<std::vector<const Position *>> &histories,
+                            const std::vector<std::vector<Move>> &legal_moves, float softmax_temp,
+                            int input_format) {
+  if (legal_moves.size() != histories.size())
+    throw std::invalid_argument("legal move list count must match history count");
+  std::vector<LeafResult> out(histories.size());
+  if (histories.empty()) return out;
+  std::lock_guard<std::mutex> lock(mutex_);
+  const int n = static_cast<int>(histories.size());
+  boards_.clear();
+  history_offsets_.assign(1, 0);
+  moves_.clear();
+  move_offsets_.assign(1, 0);
+  for (int b = 0; b < n; ++b) {
+    for (const Position *p : histories[b]) boards_.push_back(ToBoard(*p));
+    history_offsets_.push_back(static_cast<std::int32_t>(boards_.size()));
+    for (Move m : legal_moves[b]) moves_.push_back(ToRawMove(m));
+    move_offsets_.push_back(static_cast<std::int32_t>(moves_.size()));
+  }
+  priors_.resize(moves_.size());
+  wdl_.resize(size_t(n) * 3);
+  mlh_.resize(n);
+  for (int lo = 0; lo < n; lo += options_.max_batch) {
+    const int cnt = std::min(options_.max_batch, n - lo);
+    if (mfb200_evaluate_leaves(handle_, boards_.data() + history_offsets_[lo],
+                               history_offsets_.data() + lo, cnt, input_format,
+                               moves_.data() + move_offsets_[lo], move_offsets_.data() + lo,
+                               softmax_temp, priors_.data() + move_offsets_[lo],
+                               wdl_.data() + size_t(lo) * 3, mlh_.data() + lo, nullptr) != 0)
       throw std::runtime_error(std::string("B200 backend: ") + mfb200_last_error(handle_));
   }
   for (int b = 0; b < n; ++b) {

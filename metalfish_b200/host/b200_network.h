@@ -14,9 +14,11 @@
 #include <string>
 #include <vector>
 
+#include "core/position.h"
 #include "nn/network.h"
 
 struct mfb200_handle;
+struct mfb200_board;
 
 namespace MetalFish {
 namespace NN {
@@ -59,6 +61,16 @@ public:
                                          const std::vector<std::vector<std::int16_t>> &move_indices,
                                          float softmax_temp);
 
+  // The whole leaf evaluation on the GPU (mfb200_evaluate_leaves): what
+  // NNMCTSEvaluator::EvaluateBatchWithHistoryViews does (encode each history,
+  // evaluate, gather the legal moves' logits: src/mcts/evaluator.cpp:140-226)
+  // plus ApplyNNPolicyToNode's softmax. histories[i] is the game so far,
+  // oldest first, ending with the leaf; legal_moves[i] its moves in edge
+  // order; input_format the network's (NetworkFormat::InputFormat).
+  std::vector<LeafResult> EvaluateLeaves(const std::vector<std::vector<const Position *>> &histories,
+                                         const std::vector<std::vector<Move>> &legal_moves,
+                                         float softmax_temp, int input_format);
+
 private:
   mfb200_handle *handle_ = nullptr;
   B200Options options_;
@@ -69,6 +81,9 @@ private:
   std::vector<std::int32_t> move_offsets_;  // EvaluatePriors scratch
   std::vector<std::int16_t> move_index_;
   std::vector<float> priors_;
+  std::vector<mfb200_board> boards_;        // EvaluateLeaves scratch
+  std::vector<std::int32_t> history_offsets_;
+  std::vector<std::uint16_t> moves_;
   std::mutex mutex_;
 };
 

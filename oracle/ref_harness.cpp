@@ -623,6 +623,32 @@ int PriorsB200(const std::string &net_path, const std::string &in_path,
     out.write(reinterpret_cast<const char *>(x.priors.data()), x.priors.size() * 4);
   return out.good() ? 0 : 1;
 }
+
+// The C++ backend's whole leaf evaluation: B200Network::EvaluateLeaves on
+// the fixture games' real Positions and MoveList<LEGAL> moves.
+int LeavesB200(const std::string &net_path, std::uint64_t seed, int count, float temp,
+               const std::string &out_path) {
+  Bitboards::init();
+  Position::init();
+  const NN::WeightsFile file = ReadNet(net_path);
+  std::vector<Game> games(count);
+  std::vector<std::vector<const Position *>> hist(count);
+  std::vector<std::vector<Move>> moves(count);
+  for (int i = 0; i < count; ++i) {
+    BuildGame(seed, i, games[i]);
+    hist[i] = games[i].ptrs;
+    for (Move m : MoveList<LEGAL>(*games[i].ptrs.back())) moves[i].push_back(m);
+  }
+  NN::B200::B200Options opt;
+  opt.max_batch = std::max(1, count);
+  NN::B200::B200Network net(file, opt);
+  const auto res = net.EvaluateLeaves(
+      hist, moves, temp, MetalFishNN::NetworkFormat::INPUT_112_WITH_CANONICALIZATION_V2);
+  std::ofstream out(out_path, std::ios::binary);
+  for (const auto &x : res)
+    out.write(reinterpret_cast<const char *>(x.priors.data()), x.priors.size() * 4);
+  return out.good() ? 0 : 1;
+}
 #endif
 
 } // namespace
@@ -646,6 +672,8 @@ int main(int argc, char **argv) {
 #ifdef MFB_WITH_B200
     if (cmd == "priors-b200" && argc == 7)
       return PriorsB200(argv[2], argv[3], argv[4], std::stof(argv[5]), argv[6]);
+    if (cmd == "leaves-b200" && argc == 7)
+      return LeavesB200(argv[2], std::stoull(argv[3]), std::stoi(argv[4]), std::stof(argv[5]), argv[6]);
 #endif
     if (cmd == "eval-backend" && argc >= 6)
       return Eval(argv[3], argv[4], argv[5], argc > 6 ? std::stoi(argv[6]) : 1,
@@ -659,7 +687,8 @@ int main(int argc, char **argv) {
                  "       ref_harness dump-move-index <out.i16>\n"
                  "       ref_harness gen-history <seed> <count> <count-all-formats> <out.mfhb> [start-fen]\n"
                  "       ref_harness eval-backend <cpu|b200> <net.mfnt> <in.mfin> <out.mfot> [threads] [first] [count]\n"
-                 "       b200_harness priors-b200 <net.mfnt> <in.mfin> <moves.mfmv> <temp> <out.f32>\n");
+                 "       b200_harness priors-b200 <net.mfnt> <in.mfin> <moves.mfmv> <temp> <out.f32>\n"
+                 "       b200_harness leaves-b200 <net.mfnt> <seed> <count> <temp> <out.f32>\n");
     return 2;
   } catch (const std::exception &e) {
     std::fprintf(stderr, "ref_harness error: %s\n", e.what());

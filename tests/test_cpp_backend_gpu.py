@@ -68,3 +68,33 @@ def test_cpp_evaluate_priors_matches_python_api(positions, tmp_path):
     finally:
         py_net.close()
     np.testing.assert_array_equal(cpp, py)
+
+
+@pytest.mark.skipif(not os.path.exists(HARNESS), reason="b200_harness not built (needs the reference tree)")
+def test_cpp_evaluate_leaves_from_engine_positions(tmp_path):
+    """B200Network::EvaluateLeaves on the engine's own Position objects and
+    MoveList<LEGAL> moves (the reference's game replay in the harness) gives
+    the priors the Python mirror computes from the committed board records
+    and raw moves of the same games, bit for bit."""
+    from metalfish_b200.network import create_network
+    g = load_golden("small")
+    cfg = synthetic.CONFIGS[str(g["config"])]
+    t = synthetic.generate(cfg, int(g["weight_seed"]), bool(g["perturb_norms"]))
+    n = 64
+    net, out = tmp_path / "n.mfnt", tmp_path / "o.f32"
+    netfile.write_net(str(net), cfg.header(), t)
+    r = subprocess.run([HARNESS, "leaves-b200", str(net), "20251201", str(n), "0.9", str(out)],
+                       capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stderr
+    cpp = np.fromfile(str(out), np.float32)
+    h = np.load(os.path.join(ROOT, "tests", "golden", "history.npz"))
+    lm = np.load(os.path.join(ROOT, "tests", "golden", "legal_moves.npz"))
+    hoff = h["start/offsets"][:n + 1]
+    moff = lm["offsets"][:n + 1].astype(np.int32)
+    py_net = create_network(cfg, t, max_batch=n)
+    try:
+        py, _, _ = py_net.evaluate_leaves(h["start/boards"][:hoff[-1]], hoff, lm["raw"][:moff[-1]],
+                                          moff, 0.9)
+    finally:
+        py_net.close()
+    np.testing.assert_array_equal(cpp, py)
