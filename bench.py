@@ -391,7 +391,34 @@ def main():
         leaves_step()
     lv_s = all_max(time.perf_counter() - t0, world)
     barrier(world)
+    # the same, double-buffered: batch i+1 is submitted before batch i is
+    # waited for (mfb200_submit_leaves / mfb200_wait), so the host's
+    # submission work overlaps the GPU's
+    tickets = [ctypes.c_uint64(0), ctypes.c_uint64(0)]
+
+    def submit(k):
+        rc = L.mfb200_submit_leaves(net._h, pin_hb.data_ptr(), pin_ho.data_ptr(), B, 5,
+                                    pin_lr.data_ptr(), pin_lo.data_ptr(), ctypes.c_float(1.0),
+                                    h_lpri.data_ptr(), h_wdl.data_ptr(), h_mlh.data_ptr(),
+                                    ctypes.byref(tickets[k & 1]))
+        if rc:
+            raise RuntimeError(L.mfb200_last_error(net._h).decode())
+
+    def wait(k):
+        if L.mfb200_wait(net._h, tickets[k & 1].value):
+            raise RuntimeError(L.mfb200_last_error(net._h).decode())
+
+    barrier(world)
+    t0 = time.perf_counter()
+    submit(0)
+    for k in range(1, args.steps):
+        submit(k)
+        wait(k - 1)
+    wait(args.steps - 1)
+    la_s = all_max(time.perf_counter() - t0, world)
+    barrier(world)
     e2e_leaves = {"value": B * world * args.steps / lv_s, "unit": "positions/s",
+                  "pipelined_value": B * world * args.steps / la_s,
                   "h2d_bytes_per_step": int(h_boards.nbytes + h_off.nbytes + l_raw.nbytes + l_off.nbytes),
                   "d2h_bytes_per_step": int(len(l_raw) * 4 + B * 16),
                   "history_boards_per_step": int(len(h_boards))}

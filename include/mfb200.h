@@ -29,6 +29,10 @@
  *                          (src/mcts/evaluator.cpp:140-170: encode, EvaluateBatch,
  *                          BuildResult) + ApplyNNPolicyToNode's softmax
  *                          (src/mcts/search.cpp:127-197), all on the GPU
+ *   mfb200_submit_leaves / mfb200_wait
+ *                       <- the same, asynchronous, for the double-buffered batch
+ *                          assembly of src/mcts/search.cpp:1955-2232 (no counterpart API
+ *                          in the reference, whose backends evaluate synchronously)
  *   mfb200_capabilities <- NN::Network::GetBackendCapabilities / HasWDL / HasMovesLeft /
  *                          GetNetworkInfo (src/nn/network.h:21-51)
  *   mfb200_last_error   <- the std::runtime_error messages the reference throws
@@ -194,6 +198,24 @@ MFB200_API int mfb200_evaluate_leaves(mfb200_handle *h, const mfb200_board *boar
                                       const uint16_t *moves, const int32_t *move_offsets,
                                       float softmax_temp, float *priors, float *wdl,
                                       float *moves_left, mfb200_timing *timing);
+
+/* Asynchronous mfb200_evaluate_leaves, for MCTS batch assembly that keeps
+ * building the next batch while the GPU works: enqueues the whole leaf
+ * evaluation and returns at once with a ticket. The caller's input and
+ * output buffers must stay valid (and unchanged) until mfb200_wait(ticket)
+ * returns; page-locked buffers make the copies asynchronous. At most 4
+ * submissions are in flight per handle (a fifth waits for the oldest).
+ * Submissions on one handle run in order. */
+MFB200_API int mfb200_submit_leaves(mfb200_handle *h, const mfb200_board *boards,
+                                    const int32_t *history_offsets, int batch, int input_format,
+                                    const uint16_t *moves, const int32_t *move_offsets,
+                                    float softmax_temp, float *priors, float *wdl,
+                                    float *moves_left, uint64_t *ticket);
+
+/* Blocks until submission `ticket` has completed (its outputs are in the
+ * caller's buffers) and reports a device error it met. Returns 0 for a
+ * ticket already waited for. */
+MFB200_API int mfb200_wait(mfb200_handle *h, uint64_t ticket);
 
 /* NN::MoveToNNIndex (src/nn/policy_map.cpp:316-360) as this library maps
  * moves: out [8 transforms][5 promotion kinds][64 from][64 to], -1 for no

@@ -281,6 +281,7 @@ struct Shard {  // one GPU
   int16_t *move_table;    // build_move_index() [5 * 4096]
   unsigned *status;
   cudaEvent_t ev[4];
+  cudaEvent_t done[4];  // completion of the asynchronous submission in each ticket slot
   struct Step {
     std::string name;
     double flops = 0;
@@ -306,6 +307,11 @@ struct mfb200_handle {
   size_t weight_bytes = 0, ws_bytes = 0;
   std::string device_name;
   bool calibrated = false;  // FP8 activation scales set
+  // asynchronous submissions (mfb200_submit_leaves): ticket t uses slot
+  // t % kTickets; pending[slot] is the ticket not yet waited for, 0 if none
+  static constexpr int kTickets = 4;
+  uint64_t next_ticket = 1;
+  uint64_t pending[kTickets] = {};
 };
 
 namespace {
@@ -1026,6 +1032,7 @@ extern "C" int mfb200_create(const mfb200_net_desc *desc, const void *weights, s
       h->device_name = prop.name;
       check(cudaStreamCreateWithFlags(&S->stream, cudaStreamNonBlocking), "stream");
       for (auto &e : S->ev) check(cudaEventCreate(&e), "event");
+      for (auto &e : S->done) check(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "event");
       check(cudaMalloc(&S->arena, ab.host.size()), "weight allocation");
       S->arena_bytes = ab.host.size();
       check(cudaMemcpy(S->arena, ab.host.data(), ab.host.size(), cudaMemcpyHostToDevice),
@@ -1255,69 +1262,100 @@ extern "C" int mfb200_policy_index_table(int16_t *out) {
   return 0;
 }
 
-extern "C" int mfb200_evaluate_leaves(mfb200_handle *h, const mfb200_board *boards,
-                                      const int32_t *history_offsets, int batch, int input_format,
-                                      const uint16_t *moves, const int32_t *move_offsets,
-                                      float softmax_temp, float *priors, float *wdl, float *mlh,
-                                      mfb200_timing *timing) {
-  if (!h) return fail(nullptr, "mfb200_evaluate_leaves: null handle");
-  std::lock_guard<std::mutex> lock(h->mu);
+namespace {
+// Blocks until the submission in `slot` has completed on every device and
+// checks the devices' status words; the slot is free afterwards.
+void finish_ticket(mfb200_handle *h, int slot) {
+  if (!h->pending[slot]) return;
+  h->pending[slot] = 0;
+  for (auto &S : h->shards) {
+    check(cudaSetDevice(S->device), "cudaSetDevice");
+    check(cudaEventSynchronize(S->done[slot]), "submission");
+    check_status(*S);
+  }
+}
+
+// mfb200_evaluate_leaves, synchronous (ticket == nullptr) or enqueued into
+// ticket slot `slot` (returns at once; the caller's buffers must stay valid
+// until the ticket is waited for).
+int leaves_impl(mfb200_handle *h, const mfb200_board *boards, const int32_t *history_offsets,
+                int batch, int input_format, const uint16_t *moves, const int32_t *move_offsets,
+                float softmax_temp, float *priors, float *wdl, float *mlh, mfb200_timing *timing,
+                uint64_t *ticket, const char *fn) {
   if (batch <= 0) return 0;
   if (batch > h->cfg.max_batch)
-    return fail(h, "mfb200_evaluate_leaves: batch " + std::to_string(batch) + " exceeds max_batch " +
+    return fail(h, std::string(fn) + ": batch " + std::to_string(batch) + " exceeds max_batch " +
                        std::to_string(h->cfg.max_batch));
   if (!history_offsets || !move_offsets ||
       (!boards && history_offsets[batch] != history_offsets[0]) ||
       (!moves && move_offsets[batch] != move_offsets[0]))
-    return fail(h, "mfb200_evaluate_leaves: null input");
-  if (!(softmax_temp > 0.0f)) return fail(h, "mfb200_evaluate_leaves: softmax_temp must be positive");
+    return fail(h, std::string(fn) + ": null input");
+  if (!(softmax_temp > 0.0f)) return fail(h, std::string(fn) + ": softmax_temp must be positive");
   const int nd = static_cast<int>(h->shards.size());
   const int per = (batch + nd - 1) / nd;
   if (const char *e = check_histories(history_offsets, batch, input_format, nd, per))
-    return fail(h, std::string("mfb200_evaluate_leaves: ") + e);
+    return fail(h, std::string(fn) + ": " + e);
   for (int b = 0; b < batch; ++b)
     if (move_offsets[b + 1] < move_offsets[b])
-      return fail(h, "mfb200_evaluate_leaves: move_offsets must be non-decreasing");
+      return fail(h, std::string(fn) + ": move_offsets must be non-decreasing");
   for (int i = 0; i < nd; ++i) {
     const int lo = i * per, hi = std::min(batch, lo + per);
     if (lo < hi && move_offsets[hi] - move_offsets[lo] > int64_t(per) * kMoveCapacity)
-      return fail(h, "mfb200_evaluate_leaves: more than 256 legal moves per position on average");
+      return fail(h, std::string(fn) + ": more than 256 legal moves per position on average");
+  }
+  int slot = -1;
+  if (ticket) {
+    const uint64_t t = h->next_ticket++;
+    slot = static_cast<int>(t % mfb200_handle::kTickets);
+    try {
+      finish_ticket(h, slot);  // at most kTickets submissions in flight
+    } catch (const std::exception &e) {
+      return fail(h, std::string(fn) + ": " + e.what());
+    }
+    h->pending[slot] = t;
+    *ticket = t;
   }
   std::vector<std::array<float, 4>> ms(nd, {0, 0, 0, 0});
   std::vector<std::string> errs(nd);
   auto work = [&](int i) {
     const int lo = i * per, hi = std::min(batch, lo + per);
-    if (lo >= hi) return;
     Shard &S = *h->shards[i];
     const int B = hi - lo;
-    const int32_t mbase = move_offsets[lo] - move_offsets[0];
-    const int32_t nmoves = move_offsets[hi] - move_offsets[lo];
     try {
       check(cudaSetDevice(S.device), "cudaSetDevice");
       cudaStream_t s = S.stream;
-      float *m = ms[i].data();
-      check(cudaEventRecord(S.ev[0], s), "event");
-      encode_shard(S, boards + (history_offsets[lo] - history_offsets[0]), history_offsets + lo, B,
-                   input_format, s);
-      check(cudaMemcpyAsync(S.move_off, move_offsets + lo, size_t(B + 1) * 4, cudaMemcpyHostToDevice, s),
-            "H2D move offsets");
-      if (nmoves > 0)
-        check(cudaMemcpyAsync(S.moves, moves + mbase, size_t(nmoves) * 2, cudaMemcpyHostToDevice, s),
-              "H2D moves");
-      check(cudaEventRecord(S.ev[1], s), "event");
-      forward(h, S, B, s);
-      launch_leaf_priors(S.policy, B, S.move_off, S.moves, S.move_table, S.boards, S.hist_off,
-                         S.transforms, softmax_temp, S.priors, s);
-      check(cudaGetLastError(), "priors launch");
-      check(cudaEventRecord(S.ev[2], s), "event");
-      if (priors && nmoves > 0)
-        check(cudaMemcpyAsync(priors + mbase, S.priors, size_t(nmoves) * 4, cudaMemcpyDeviceToHost, s),
-              "D2H priors");
-      if (wdl) check(cudaMemcpyAsync(wdl + size_t(lo) * 3, S.wdl, size_t(B) * 12, cudaMemcpyDeviceToHost, s), "D2H wdl");
-      if (mlh) check(cudaMemcpyAsync(mlh + lo, S.mlh, size_t(B) * 4, cudaMemcpyDeviceToHost, s), "D2H mlh");
-      check(cudaEventRecord(S.ev[3], s), "event");
+      if (B > 0) {
+        const int32_t mbase = move_offsets[lo] - move_offsets[0];
+        const int32_t nmoves = move_offsets[hi] - move_offsets[lo];
+        check(cudaEventRecord(S.ev[0], s), "event");
+        encode_shard(S, boards + (history_offsets[lo] - history_offsets[0]), history_offsets + lo, B,
+                     input_format, s);
+        check(cudaMemcpyAsync(S.move_off, move_offsets + lo, size_t(B + 1) * 4, cudaMemcpyHostToDevice, s),
+              "H2D move offsets");
+        if (nmoves > 0)
+          check(cudaMemcpyAsync(S.moves, moves + mbase, size_t(nmoves) * 2, cudaMemcpyHostToDevice, s),
+                "H2D moves");
+        check(cudaEventRecord(S.ev[1], s), "event");
+        forward(h, S, B, s);
+        launch_leaf_priors(S.policy, B, S.move_off, S.moves, S.move_table, S.boards, S.hist_off,
+                           S.transforms, softmax_temp, S.priors, s);
+        check(cudaGetLastError(), "priors launch");
+        check(cudaEventRecord(S.ev[2], s), "event");
+        if (priors && nmoves > 0)
+          check(cudaMemcpyAsync(priors + mbase, S.priors, size_t(nmoves) * 4, cudaMemcpyDeviceToHost, s),
+                "D2H priors");
+        if (wdl) check(cudaMemcpyAsync(wdl + size_t(lo) * 3, S.wdl, size_t(B) * 12, cudaMemcpyDeviceToHost, s), "D2H wdl");
+        if (mlh) check(cudaMemcpyAsync(mlh + lo, S.mlh, size_t(B) * 4, cudaMemcpyDeviceToHost, s), "D2H mlh");
+        check(cudaEventRecord(S.ev[3], s), "event");
+      }
+      if (slot >= 0) {
+        check(cudaEventRecord(S.done[slot], s), "event");
+        return;
+      }
+      if (B <= 0) return;
       check(cudaStreamSynchronize(s), "forward");
       check_status(S);
+      float *m = ms[i].data();
       cudaEventElapsedTime(&m[0], S.ev[0], S.ev[1]);
       cudaEventElapsedTime(&m[1], S.ev[1], S.ev[2]);
       cudaEventElapsedTime(&m[2], S.ev[2], S.ev[3]);
@@ -1334,7 +1372,7 @@ extern "C" int mfb200_evaluate_leaves(mfb200_handle *h, const mfb200_board *boar
     for (auto &t : th) t.join();
   }
   for (auto &e : errs)
-    if (!e.empty()) return fail(h, "mfb200_evaluate_leaves: " + e);
+    if (!e.empty()) return fail(h, std::string(fn) + ": " + e);
   if (timing) {
     *timing = mfb200_timing{0, 0, 0, 0};
     for (auto &m : ms) {
@@ -1343,6 +1381,45 @@ extern "C" int mfb200_evaluate_leaves(mfb200_handle *h, const mfb200_board *boar
       timing->d2h_ms = std::max(timing->d2h_ms, m[2]);
       timing->total_ms = std::max(timing->total_ms, m[3]);
     }
+  }
+  return 0;
+}
+}  // namespace
+
+extern "C" int mfb200_evaluate_leaves(mfb200_handle *h, const mfb200_board *boards,
+                                      const int32_t *history_offsets, int batch, int input_format,
+                                      const uint16_t *moves, const int32_t *move_offsets,
+                                      float softmax_temp, float *priors, float *wdl, float *mlh,
+                                      mfb200_timing *timing) {
+  if (!h) return fail(nullptr, "mfb200_evaluate_leaves: null handle");
+  std::lock_guard<std::mutex> lock(h->mu);
+  return leaves_impl(h, boards, history_offsets, batch, input_format, moves, move_offsets,
+                     softmax_temp, priors, wdl, mlh, timing, nullptr, "mfb200_evaluate_leaves");
+}
+
+extern "C" int mfb200_submit_leaves(mfb200_handle *h, const mfb200_board *boards,
+                                    const int32_t *history_offsets, int batch, int input_format,
+                                    const uint16_t *moves, const int32_t *move_offsets,
+                                    float softmax_temp, float *priors, float *wdl, float *mlh,
+                                    uint64_t *ticket) {
+  if (!h) return fail(nullptr, "mfb200_submit_leaves: null handle");
+  if (!ticket) return fail(h, "mfb200_submit_leaves: null ticket");
+  std::lock_guard<std::mutex> lock(h->mu);
+  *ticket = 0;
+  return leaves_impl(h, boards, history_offsets, batch, input_format, moves, move_offsets,
+                     softmax_temp, priors, wdl, mlh, nullptr, ticket, "mfb200_submit_leaves");
+}
+
+extern "C" int mfb200_wait(mfb200_handle *h, uint64_t ticket) {
+  if (!h) return fail(nullptr, "mfb200_wait: null handle");
+  std::lock_guard<std::mutex> lock(h->mu);
+  if (ticket == 0 || ticket >= h->next_ticket) return fail(h, "mfb200_wait: unknown ticket");
+  const int slot = static_cast<int>(ticket % mfb200_handle::kTickets);
+  if (h->pending[slot] != ticket) return 0;  // already waited for (or its slot was reused)
+  try {
+    finish_ticket(h, slot);
+  } catch (const std::exception &e) {
+    return fail(h, std::string("mfb200_wait: ") + e.what());
   }
   return 0;
 }
@@ -1601,6 +1678,7 @@ extern "C" void mfb200_destroy(mfb200_handle *h) {
     for (auto &kv : S->plans)
       if (kv.second->graph) cudaGraphExecDestroy(kv.second->graph);
     for (auto &e : S->ev) cudaEventDestroy(e);
+    for (auto &e : S->done) cudaEventDestroy(e);
     if (S->arena) cudaFree(S->arena);
     if (S->ws) cudaFree(S->ws);
     cudaStreamDestroy(S->stream);

@@ -71,6 +71,11 @@ def _declare(L):
     L.mfb200_evaluate_leaves.restype = c_int
     L.mfb200_evaluate_leaves.argtypes = [vp, vp, vp, c_int, c_int, vp, vp, ctypes.c_float, vp, vp,
                                          vp, ctypes.POINTER(Timing)]
+    L.mfb200_submit_leaves.restype = c_int
+    L.mfb200_submit_leaves.argtypes = [vp, vp, vp, c_int, c_int, vp, vp, ctypes.c_float, vp, vp,
+                                       vp, ctypes.POINTER(ctypes.c_uint64)]
+    L.mfb200_wait.restype = c_int
+    L.mfb200_wait.argtypes = [vp, ctypes.c_uint64]
     L.mfb200_policy_index_table.restype = c_int
     L.mfb200_policy_index_table.argtypes = [vp]
     L.mfb200_evaluate_device.restype = c_int
@@ -281,6 +286,31 @@ class B200Network:
             raise self._err()
         return pri, wdl, mlh
 
+    def submit_leaves(self, boards: np.ndarray, history_offsets: np.ndarray, moves: np.ndarray,
+                      move_offsets: np.ndarray, softmax_temp: float = 1.0, input_format: int = 5):
+        """Asynchronous evaluate_leaves: returns a LeafTicket whose wait()
+        gives (priors, wdl, moves_left). The arrays are kept alive by the
+        ticket until it is waited for."""
+        boards = np.ascontiguousarray(boards).view(np.uint8)
+        hoff = np.ascontiguousarray(history_offsets, np.int32)
+        mv = np.ascontiguousarray(moves, np.uint16)
+        moff = np.ascontiguousarray(move_offsets, np.int32)
+        b = len(hoff) - 1
+        if moff.shape != (b + 1,):
+            raise ValueError("move_offsets must have batch + 1 entries")
+        pri = np.empty(int(moff[-1] - moff[0]), np.float32)
+        wdl = np.empty((b, 3), np.float32)
+        mlh = np.empty(b, np.float32)
+        t = ctypes.c_uint64(0)
+        rc = _lib().mfb200_submit_leaves(self._h, boards.ctypes.data if boards.size else None,
+                                         hoff.ctypes.data, b, input_format,
+                                         mv.ctypes.data if mv.size else None, moff.ctypes.data,
+                                         ctypes.c_float(softmax_temp), pri.ctypes.data,
+                                         wdl.ctypes.data, mlh.ctypes.data, ctypes.byref(t))
+        if rc != 0:
+            raise self._err()
+        return LeafTicket(self, t.value, (boards, hoff, mv, moff), (pri, wdl, mlh))
+
     def calibrate(self, inp: PackedInputs) -> None:
         """FP8 only: absmax calibration of the per-tensor activation scales
         over the given positions (a bf16 forward with probes)."""
@@ -338,6 +368,20 @@ class B200Network:
             raise self._err()
         nm = names.value.decode().split("\n")
         return [(nm[i], ms[i], fl[i]) for i in range(k)]
+
+
+class LeafTicket:
+    """An in-flight mfb200_submit_leaves; wait() returns its outputs."""
+
+    def __init__(self, net, ticket: int, inputs, outputs):
+        self.net, self.ticket, self._inputs, self._outputs = net, ticket, inputs, outputs
+
+    def wait(self):
+        if self._inputs is not None:
+            if _lib().mfb200_wait(self.net._h, self.ticket) != 0:
+                raise self.net._err()
+            self._inputs = None
+        return self._outputs
 
 
 def policy_index_table() -> np.ndarray:
