@@ -7,6 +7,9 @@
   python -m metalfish_b200.profiling forward [BATCH] [bf16|fp8]
       runs two eager forwards (no CUDA graph, so every kernel is a separate
       launch) of the seeded BT4-shaped network on fixture positions.
+  python -m metalfish_b200.profiling leaves [BATCH]
+      runs two eager leaf evaluations (mfb200_evaluate_leaves: encoder,
+      forward, move mapping + priors) on the fixture game histories.
 """
 from __future__ import annotations
 
@@ -51,6 +54,21 @@ def forward(argv) -> None:
     print(f"forward ok: BT4 batch {batch} {precision}")
 
 
+def leaves(argv) -> None:
+    from .network import create_network
+    from .synthetic import BT4, generate
+    batch = min(int(argv[0]) if argv else 1024, 1024)
+    h = np.load(os.path.join(ROOT, "tests", "golden", "history.npz"))
+    lm = np.load(os.path.join(ROOT, "tests", "golden", "legal_moves.npz"))
+    hoff = h["start/offsets"][:batch + 1]
+    moff = lm["offsets"][:batch + 1].astype(np.int32)
+    net = create_network(BT4, generate(BT4, 3), max_batch=batch, use_graphs=False)
+    for _ in range(2):
+        net.evaluate_leaves(h["start/boards"][:hoff[-1]], hoff, lm["raw"][:moff[-1]], moff, 1.0)
+    net.close()
+    print(f"leaves ok: BT4 batch {batch}")
+
+
 if __name__ == "__main__":
     cmd, rest = sys.argv[1], sys.argv[2:]
-    {"gemm": gemm, "forward": forward}[cmd](rest)
+    {"gemm": gemm, "forward": forward, "leaves": leaves}[cmd](rest)
