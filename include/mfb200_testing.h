@@ -17,6 +17,12 @@ extern "C" {
  * planned afterwards (tests run both kernels). */
 MFB200_API void mfb200_debug_set_gemm_pairs(int enable);
 
+/* Run the bf16 encoder of forwards planned afterwards with (1, the default)
+ * or without (0) the deferred LayerNorm: residual GEMMs that store the
+ * un-normalised stream with row statistics and consumer GEMMs that fold the
+ * normalisation into their epilogue, instead of separate ln1 / ln2 passes. */
+MFB200_API void mfb200_debug_set_fold_ln(int enable);
+
 /* Launch the kernels of forwards planned afterwards with (1, the default) or
  * without (0) programmatic dependent launch. */
 MFB200_API void mfb200_debug_set_pdl(int enable);

@@ -233,6 +233,17 @@ const char *plan_gemm(GemmLaunch &g, const void *A, long long lda_elems, const v
   if (args.mode == kEpiAccum && ((!args.out_f32 && !args.out_f16) || args.out2 || args.out_fp8))
     return "gemm: the accumulate epilogue adds into one fp32 or fp16 output";
   if (args.out_f16 && (args.out_f32 || args.out_fp8)) return "gemm: one output format";
+  if (args.mode == kEpiResidNorm) {
+    if (!args.out_f16 || args.out2 || args.k_splits > 1 || !args.resid16 || !args.stats_out)
+      return "gemm: the residual-norm epilogue writes one fp16 output and its row statistics "
+             "from an fp16 residual (no K split)";
+    if (args.rn_stats && (!args.rn_gamma || !args.rn_beta))
+      return "gemm: normalising the residual needs its LayerNorm gamma and beta";
+  }
+  if (args.fold_stats && (args.mode != kEpiStore || args.k_splits > 1 || args.K % 32 ||
+                          !args.fold_colsum || fp8))
+    return "gemm: a folded LayerNorm input needs the store epilogue, K a multiple of 32, "
+           "column sums and 16-bit operands (no K split)";
   if (args.k_splits > 1 && (args.bias || args.mode != kEpiStore || args.out2))
     return "gemm: split-K writes raw fp32 partials (no bias, residual or column split)";
   const uint32_t elem = fp8 ? 1 : 2;
@@ -310,6 +321,13 @@ const char *plan_gemm(GemmLaunch &g, const void *A, long long lda_elems, const v
         if (!make_tmap(&g.tmOut2, args.out2, odt, 2, d2, s2, box3, oswz))
           return "gemm: cannot build the second output tensor map";
       }
+    }
+    if (args.mode == kEpiResidNorm) {
+      const uint64_t dims[2] = {uint64_t(args.N), uint64_t(args.M)};
+      const uint64_t st[1] = {uint64_t(args.ldr16) * 2};
+      if (!make_tmap(&g.tmRes, args.resid16, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, dims, st, box3,
+                     CU_TENSOR_MAP_SWIZZLE_64B))
+        return "gemm: cannot build the fp16 residual tensor map";
     }
     if (args.mode == kEpiResid || args.mode == kEpiResidLN) {
       const uint64_t dims[2] = {uint64_t(args.N), uint64_t(args.M)};

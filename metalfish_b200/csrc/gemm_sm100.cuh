@@ -35,6 +35,10 @@ enum EpiMode : int {
                     // (the row spans the cluster_n CTAs of a thread-block cluster)
   kEpiAccum = 3,    // out (fp32 or fp16, holding the residual) += alpha * (scale*acc + bias),
                     // added in place by TMA reduce stores: no residual reads
+  kEpiResidNorm = 4,  // y = LN_prev(resid16) + alpha * (scale*acc + bias), stored fp16 (in place
+                      // over resid16 allowed), with per-32-column row statistics of y written
+                      // to stats_out; LN_prev applies the row statistics rn_stats of the
+                      // residual with rn_gamma / rn_beta (rn_stats == nullptr: residual as is)
 };
 
 enum Act : int {
@@ -69,6 +73,20 @@ struct GemmArgs {
   int k_splits;               // >1: split-K; K slice s writes fp32 partials at
   long long split_stride;     //     out + s * split_stride (raw accumulator)
   unsigned *status;           // device status word
+  // Deferred LayerNorm (the residual stream is kept un-normalised). The
+  // residual GEMM writes per-row partials: float2 (chunk sum, chunk sum of
+  // squared deviations from the chunk mean) per 32-column chunk, chunk-major
+  // [N / 32, M] so that a warp's 32 rows store 256 contiguous bytes;
+  // launch_row_stats turns them into per-row float2 (mean, 1/sqrt(var + eps)).
+  const __half *resid16;      // kEpiResidNorm: fp16 residual [M, ldr16]
+  long long ldr16;
+  const float2 *rn_stats;     // kEpiResidNorm: (mean, rstd) [M] of the residual rows, or nullptr
+  const float *rn_gamma, *rn_beta;  // kEpiResidNorm: affine parameters of that LayerNorm [N]
+  float2 *stats_out;          // kEpiResidNorm: partials of the stored rows [N / 32, M]
+  const float2 *fold_stats;   // kEpiStore: A holds un-normalised rows with (mean, rstd) [M];
+                              // W holds gamma-scaled rows and the epilogue computes
+                              // rstd * (acc - mean * fold_colsum) before the bias
+  const float *fold_colsum;   // [N] column sums of the gamma-scaled W
 };
 
 // mish(x) = x * tanh(softplus(x)). With e = exp(x), tanh(log(1 + e)) =
@@ -134,7 +152,61 @@ struct EpiCtx {
   uint32_t rank;       // CTA rank in the cluster
   uint8_t *stage2;     // second staging tile (kEpiResidLN kernels)
   uint32_t chunks;     // chunks staged so far (selects the half of a 2-byte-output tile)
+  uint32_t res_issued; // residual loads issued (kEpiResidNorm prefetch)
+  float2 rowst;        // deferred LayerNorm: this lane's row (mean, rstd), loaded by epi_pre
 };
+
+// Deferred LayerNorm, issued before the accumulator wait so that the latency
+// overlaps the mainloop: this lane's row (mean, rstd) and, into L1, the
+// tile's gamma / beta / column-sum lines.
+__device__ __forceinline__ void epi_pre(const GemmArgs &args, EpiCtx &e, int row0, int n0, int bn) {
+  const float2 *st = args.mode == kEpiResidNorm ? args.rn_stats : args.fold_stats;
+  if (!st) return;
+  const int row = row0 + e.lane < args.M ? row0 + e.lane : args.M - 1;
+  e.rowst = __ldcg(st + row);
+  if (e.lane < bn / 32 && n0 + 32 * e.lane < args.N) {
+    if (args.mode == kEpiResidNorm) {
+      prefetch_l1(args.rn_gamma + n0 + 32 * e.lane);
+      prefetch_l1(args.rn_beta + n0 + 32 * e.lane);
+    } else {
+      prefetch_l1(args.fold_colsum + n0 + 32 * e.lane);
+    }
+  }
+}
+
+// kEpiResidNorm: before the accumulator is ready, lane 0 of each epilogue
+// warp pulls the fp16 residual chunks of its rows (at most two 32 x 32
+// chunks per tile: one per staging half) into its staging tile by TMA.
+template <int BN, int EW>
+__device__ __forceinline__ void resid_issue(const GemmArgs &args, EpiCtx &e, int row0, int n0,
+                                            int group) {
+  constexpr int STEP = 32 * (EW / 4);
+  static_assert(BN / STEP <= 2, "at most two residual chunks per warp and tile");
+  int nch = 0;
+  for (int c = group * 32; c < BN && n0 + c < args.N; c += STEP) ++nch;
+  if (nch == 0) return;
+  if (e.lane == 0) {
+    bulk_wait_read0();  // earlier stores have finished reading the staging tile
+    mbar_arrive_expect_tx(e.res_bar, static_cast<uint32_t>(nch) * (kStageBytes / 2));
+    int i = 0;
+    for (int c = group * 32; c < BN && n0 + c < args.N; c += STEP, ++i)
+      tma_load_2d(e.stage + i * (kStageBytes / 2), e.res, e.res_bar, n0 + c, row0);
+  }
+  ++e.res_issued;
+}
+
+// An epilogue warp that stopped early waits (bounded) for a residual load it
+// issued and never consumed before the CTA releases its shared memory.
+__device__ __forceinline__ void resid_drain(const GemmArgs &args, EpiCtx &e) {
+  if (args.mode != kEpiResidNorm || e.res_issued == e.res_loads) return;
+  const unsigned long long t0 = global_ns();
+  while (!mbar_try_wait(e.res_bar, e.res_loads & 1)) {
+    if (global_ns() - t0 > kWaitLimitNs) {
+      atomicCAS(args.status, 0u, static_cast<unsigned>(kErrTimeoutDrain));
+      break;
+    }
+  }
+}
 
 __device__ __forceinline__ uint32_t pack_bf16x2_f(float a, float b) {
   const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
@@ -204,8 +276,28 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs &args, EpiCtx &e, u
   uint32_t raw[32];
   int c = group * 32;
   if (c >= BN) return true;
+  // consumer side of the deferred LayerNorm: this row's statistics
+  const bool fold = MODE == kEpiStore && ks < 0 && args.fold_stats != nullptr;
+  const float f_mean = fold ? e.rowst.x : 0.0f, f_rstd = fold ? e.rowst.y : 1.0f;
+  // kEpiResidNorm: the residual chunks (prefetched by resid_issue into staging
+  // halves 0 and 1) have landed; each lane later reads its own row of a chunk
+  // and overwrites the same bytes with its output row, so the chunk is staged
+  // for its store in place
+  float r_mean = 0.0f, r_rstd = 1.0f;
+  if constexpr (MODE == kEpiResidNorm) {
+    if (e.res_issued != e.res_loads) {
+      if (!mbar_wait(e.res_bar, e.res_loads & 1, args.status, kErrTimeoutEpilogue, e.abort_flag))
+        return false;
+      ++e.res_loads;
+    }
+    if (args.rn_stats) {
+      r_mean = e.rowst.x;
+      r_rstd = e.rowst.y;
+    }
+  }
+  int ci = 0;  // this warp's chunk index within the tile
   if (PREFETCH) tmem_ld32(taddr + c, raw);
-  for (; c < BN; c += STEP) {
+  for (; c < BN; c += STEP, ++ci) {
     if (!PREFETCH) tmem_ld32(taddr + c, raw);
     tmem_wait_ld();
     float v[32];
@@ -218,16 +310,30 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs &args, EpiCtx &e, u
     // the two halves alternate and only the store before last must have
     // finished reading; fp32 chunks (and residual tiles) use the whole tile.
     const bool halves = !f32 && MODE != kEpiResid;
-    uint8_t *st = halves ? e.stage + (e.chunks & 1u) * (kStageBytes / 2) : e.stage;
+    uint8_t *st = MODE == kEpiResidNorm ? e.stage + ci * (kStageBytes / 2)
+                                        : (halves ? e.stage + (e.chunks & 1u) * (kStageBytes / 2) : e.stage);
     ++e.chunks;
-    if (lane == 0) {
-      if (halves) bulk_wait_read1(); else bulk_wait_read0();
+    if (MODE != kEpiResidNorm) {  // (residual-norm: resid_issue waited for all earlier stores)
+      if (lane == 0) {
+        if (halves) bulk_wait_read1(); else bulk_wait_read0();
+      }
+      __syncwarp();
     }
-    __syncwarp();
     if (ks < 0) {
       if (a_scale != 1.0f) {
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] *= a_scale;
+      }
+      if (fold) {
+        const float4 *cs = reinterpret_cast<const float4 *>(args.fold_colsum + nb);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const float4 f = __ldg(cs + q);
+          v[4 * q] = f_rstd * (v[4 * q] - f_mean * f.x);
+          v[4 * q + 1] = f_rstd * (v[4 * q + 1] - f_mean * f.y);
+          v[4 * q + 2] = f_rstd * (v[4 * q + 2] - f_mean * f.z);
+          v[4 * q + 3] = f_rstd * (v[4 * q + 3] - f_mean * f.w);
+        }
       }
       if (args.col_scale) {
         const float4 *cs = reinterpret_cast<const float4 *>(args.col_scale + nb);
@@ -249,6 +355,42 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs &args, EpiCtx &e, u
     if constexpr (MODE == kEpiAccum) {
 #pragma unroll
       for (int j = 0; j < 32; ++j) v[j] *= args.alpha;
+    } else if constexpr (MODE == kEpiResidNorm) {
+      // y = LN_prev(r) + alpha * v (stored as fp16 by stage_row) and this
+      // chunk's statistics of y (fp32, before the rounding to fp16)
+      float s = 0.0f, sq = 0.0f;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const uint4 w = *reinterpret_cast<const uint4 *>(st + lane * 64 + ((q ^ ((lane >> 1) & 3)) << 4));
+        const uint32_t w4[4] = {w.x, w.y, w.z, w.w};
+        float r[8];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&w4[k]));
+          r[2 * k] = f.x;
+          r[2 * k + 1] = f.y;
+        }
+        if (args.rn_stats) {
+          const float4 *gp = reinterpret_cast<const float4 *>(args.rn_gamma + nb + 8 * q);
+          const float4 *bp = reinterpret_cast<const float4 *>(args.rn_beta + nb + 8 * q);
+          const float4 g0 = __ldg(gp), g1 = __ldg(gp + 1), b0 = __ldg(bp), b1 = __ldg(bp + 1);
+          const float g[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+          const float b[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+          for (int k = 0; k < 8; ++k) r[k] = (r[k] - r_mean) * r_rstd * g[k] + b[k];
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const int j = 8 * q + k;
+          v[j] = r[k] + args.alpha * v[j];
+          s += v[j];
+          sq += v[j] * v[j];
+        }
+      }
+      // chunk sum of squared deviations from the chunk mean
+      const float m2 = fmaxf(sq - s * s * (1.0f / 32.0f), 0.0f);
+      if (row0 + lane < args.M)
+        args.stats_out[static_cast<long long>(nb / 32) * args.M + row0 + lane] = make_float2(s, m2);
     } else if constexpr (MODE == kEpiResid) {
       if (lane == 0) {
         mbar_arrive_expect_tx(e.res_bar, kStageBytes);
@@ -443,6 +585,8 @@ __device__ __forceinline__ bool epilogue_dispatch(const GemmArgs &args, EpiCtx &
 #define MFB_EPI(MODE, ACT) return epilogue_tile<BN, MODE, ACT, EW>(args, e, taddr, row0, n0, group, ks)
   if (ks < 0 && args.mode == kEpiResid) MFB_EPI(kEpiResid, kActNone);
   if (ks < 0 && args.mode == kEpiAccum) MFB_EPI(kEpiAccum, kActNone);
+  if constexpr (EW == kEpiWarpsMax)
+    if (ks < 0 && args.mode == kEpiResidNorm) MFB_EPI(kEpiResidNorm, kActNone);
   switch (ks >= 0 ? kActNone : args.act) {
   case kActRelu: MFB_EPI(kEpiStore, kActRelu);
   case kActRelu2: MFB_EPI(kEpiStore, kActRelu2);
@@ -563,10 +707,10 @@ __global__ void __launch_bounds__(64 + 32 * (LN ? kEpiWarpsLN : kEpiWarpsMax), 1
         const int m0 = (t / tiles_n) * S::BM;
         const int n0 = (t % tiles_n) * BN;
         const int kb1 = min(kblocks, (ks + 1) * kb_per);
-        if (ln) {
+        if (ln || (ks == 0 && args.mode == kEpiResidNorm)) {
           // pull this tile's residual into L2 while its mainloop runs
           for (int y = m0; y < min(m0 + S::BM, args.M); y += 32)
-            for (int x = n0; x < n0 + BN; x += 32) tma_prefetch_l2_2d(&tmRes, x, y);
+            for (int x = n0; x < min(n0 + BN, args.N); x += 32) tma_prefetch_l2_2d(&tmRes, x, y);
         }
         for (int kb = ks * kb_per; kb < kb1; ++kb) {
           if (!mbar_wait(&empty[stage], (round & 1) ^ 1, args.status, kErrTimeoutProducer,
@@ -661,7 +805,7 @@ __global__ void __launch_bounds__(64 + 32 * (LN ? kEpiWarpsLN : kEpiWarpsMax), 1
     if (lane == 0) {
       tma_prefetch_desc(&tmOut);
       if (args.out2) tma_prefetch_desc(&tmOut2);
-      if (args.mode == kEpiResid) tma_prefetch_desc(&tmRes);
+      if (args.mode == kEpiResid || args.mode == kEpiResidNorm) tma_prefetch_desc(&tmRes);
     }
     int local = 0;
     for (int u = u_begin; u < u_end; u += u_step, ++local) {
@@ -678,6 +822,11 @@ __global__ void __launch_bounds__(64 + 32 * (LN ? kEpiWarpsLN : kEpiWarpsMax), 1
         if (args.bias) prefetch_l1(args.bias + n0 + 32 * lane);
         if (args.col_scale) prefetch_l1(args.col_scale + n0 + 32 * lane);
       }
+      if constexpr (!LN) {
+        if (ks < 0 && args.mode == kEpiResidNorm)
+          resid_issue<BN, S::EW>(args, e, m0 + quarter * 32, n0, group);
+        if (ks < 0) epi_pre(args, e, m0 + quarter * 32, n0, BN);
+      }
       if (!mbar_wait(&tfull[acc], aphase, args.status, kErrTimeoutEpilogue, abort_flag)) break;
       tc_fence_after();
       const uint32_t taddr =
@@ -687,6 +836,7 @@ __global__ void __launch_bounds__(64 + 32 * (LN ? kEpiWarpsLN : kEpiWarpsMax), 1
       mbar_arrive(&tempty[acc]);
       if (!ok) break;
     }
+    resid_drain(args, e);
     if (lane == 0) bulk_wait0();  // all TMA stores of this warp have landed
   }
 
@@ -801,6 +951,13 @@ __global__ void __launch_bounds__(64 + 32 * kEpiWarpsMax, 1)
       for (int u = u_begin; u < units && ok; u += u_step) {
         const int m0 = (u / tiles_n) * 2 * S::BM + static_cast<int>(rank) * S::BM;
         const int nb0 = (u % tiles_n) * BN + static_cast<int>(rank) * (BN / 2);
+        if (args.mode == kEpiResidNorm) {
+          // pull this CTA's residual rows of the tile into L2 while its
+          // mainloop runs; the epilogue's TMA loads then hit L2
+          const int n0 = (u % tiles_n) * BN;
+          for (int y = m0; y < min(m0 + S::BM, args.M); y += 32)
+            for (int x = n0; x < min(n0 + BN, args.N); x += 32) tma_prefetch_l2_2d(&tmRes, x, y);
+        }
         for (int kb = 0; kb < kblocks; ++kb) {
           if (!mbar_wait(&empty[stage], (round & 1) ^ 1, args.status, kErrTimeoutProducer,
                          abort_flag)) {
@@ -892,7 +1049,7 @@ __global__ void __launch_bounds__(64 + 32 * kEpiWarpsMax, 1)
     if (lane == 0) {
       tma_prefetch_desc(&tmOut);
       if (args.out2) tma_prefetch_desc(&tmOut2);
-      if (args.mode == kEpiResid) tma_prefetch_desc(&tmRes);
+      if (args.mode == kEpiResid || args.mode == kEpiResidNorm) tma_prefetch_desc(&tmRes);
     }
     const uint32_t tempty0 = mapa_shared(smem_u32(&tempty[0]), 0);
     const uint32_t tempty1 = mapa_shared(smem_u32(&tempty[1]), 0);
@@ -906,6 +1063,8 @@ __global__ void __launch_bounds__(64 + 32 * kEpiWarpsMax, 1)
         if (args.bias) prefetch_l1(args.bias + n0 + 32 * lane);
         if (args.col_scale) prefetch_l1(args.col_scale + n0 + 32 * lane);
       }
+      if (args.mode == kEpiResidNorm) resid_issue<BN, S::EW>(args, e, m0 + quarter * 32, n0, group);
+      epi_pre(args, e, m0 + quarter * 32, n0, BN);
       if (!mbar_wait(&tfull[acc], aphase, args.status, kErrTimeoutEpilogue, abort_flag)) break;
       tc_fence_after();
       const uint32_t taddr =
@@ -916,6 +1075,7 @@ __global__ void __launch_bounds__(64 + 32 * kEpiWarpsMax, 1)
       if (lane == 0) mbar_arrive_remote(acc ? tempty1 : tempty0);
       if (!ok) break;
     }
+    resid_drain(args, e);
     if (lane == 0) bulk_wait0();
   }
 

@@ -346,6 +346,51 @@ static void ln_warp(const void *in, Fmt in_fmt, int rows, const float *gamma, co
   }
 }
 
+// Deferred LayerNorm: (mean, 1/sqrt(var + eps)) of each row from its CH
+// per-32-column partials (chunk sum, chunk sum of squared deviations from the
+// chunk mean; written chunk-major [CH, rows] by the residual GEMM epilogue):
+// var = (sum_i M2_i + sum_i (s_i - 32 mean)^2 / 32) / width, the
+// decomposition of the two-pass variance the LayerNorm kernel computes
+// (src/nn/cpu/cpu_network.cpp:424-460 normalises with the row's mean and
+// variance). One thread per row, all CH loads in flight at once, each
+// warp-wide load 256 contiguous bytes.
+template <int CH>
+__global__ void __launch_bounds__(256)
+    row_stats_kernel(const float2 *__restrict__ part, int rows, float eps,
+                     float2 *__restrict__ out) {
+  pdl_wait();
+  pdl_launch();
+  const long long row = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (row >= rows) return;
+  float2 v[CH];
+#pragma unroll
+  for (int i = 0; i < CH; ++i) v[i] = __ldcg(part + static_cast<long long>(i) * rows + row);
+  float s = 0.0f;
+#pragma unroll
+  for (int i = 0; i < CH; ++i) s += v[i].x;
+  constexpr float width = 32.0f * CH;
+  const float mean = s / width;
+  float m2 = 0.0f;
+#pragma unroll
+  for (int i = 0; i < CH; ++i) {
+    const float dv = v[i].x - 32.0f * mean;
+    m2 += v[i].y + dv * dv * (1.0f / 32.0f);
+  }
+  out[row] = make_float2(mean, 1.0f / sqrtf(m2 / width + eps));
+}
+
+void launch_row_stats(const float2 *part, int rows, int width, float eps, float2 *out,
+                      cudaStream_t s) {
+  const dim3 grid(static_cast<unsigned>((rows + 255) / 256)), block(256);
+  switch (width) {
+  case 128: launch_k(row_stats_kernel<4>, grid, block, 0, s, 1, part, rows, eps, out); return;
+  case 256: launch_k(row_stats_kernel<8>, grid, block, 0, s, 1, part, rows, eps, out); return;
+  case 512: launch_k(row_stats_kernel<16>, grid, block, 0, s, 1, part, rows, eps, out); return;
+  case 1024: launch_k(row_stats_kernel<32>, grid, block, 0, s, 1, part, rows, eps, out); return;
+  default: return;
+  }
+}
+
 void launch_layernorm_q(const void *in, Fmt in_fmt, int rows, int width, const float *gamma,
                         const float *beta, float eps, const float *multT, const float *addT,
                         __nv_bfloat16 *out, void *out_res, Fmt res_fmt, uint8_t *out8,

@@ -48,6 +48,11 @@ bool launch_splitk_act_ln(const float *part, int splits, long long stride, int r
 // `res_fmt` (F32 or F16: the residual stream) and an optional e4m3 copy
 // out8 = value / *scale8 (FP8 GEMM input); `out` may be null when only the
 // other copies are needed. Widths 128/256/512/1024 only.
+// Deferred LayerNorm: per-row (mean, 1/sqrt(var + eps)) [rows] from the
+// per-32-column partials [width / 32, rows] of a residual GEMM (width <= 1024).
+void launch_row_stats(const float2 *part, int rows, int width, float eps, float2 *out,
+                      cudaStream_t s);
+
 void launch_layernorm_q(const void *in, Fmt in_fmt, int rows, int width, const float *gamma,
                         const float *beta, float eps, const float *multT, const float *addT,
                         __nv_bfloat16 *out, void *out_res, Fmt res_fmt, uint8_t *out8,

@@ -36,6 +36,7 @@
 #include <vector>
 
 #include "../../include/mfb200.h"
+#include "../../include/mfb200_testing.h"
 #include "gemm_host.h"
 #include "kernels.cuh"
 
@@ -223,6 +224,11 @@ struct Mat {  // a weight matrix [rows, ld] on the device (bf16, fp16 or e4m3)
 struct LayerW {
   Mat qkvc, o, f1, f2, sg1, sg2;
   Mat qkvc8, o8, f1_8, f2_8;  // e4m3 copies (FP8 handles only)
+  // Deferred-LayerNorm copies (bf16 handles): QKV+compress scaled by the
+  // preceding LayerNorm's gamma along K, FFN1 by ln1's gamma; with their
+  // column sums and biases b + W.beta
+  Mat qkvc_f, f1_f;
+  float *cs_qkvc = nullptr, *bb_qkvc = nullptr, *cs_f1 = nullptr, *bb_f1 = nullptr;
   float *b_qkvc, *b_o, *ln1_g, *ln1_b, *b_f1, *b_f2, *ln2_g, *ln2_b;
   float *b_sg1, *sg_ln1_g, *sg_ln1_b, *b_sg2, *sg_ln2_g, *sg_ln2_b;
 };
@@ -268,6 +274,8 @@ struct Shard {  // one GPU
       *VM, *VH;
   __half *Xh, *X1h;  // fp16 residual stream (LN outputs; the residual GEMMs add into it in place)
   float *T, *SK;     // fp32 embedding sum, split-K partials
+  float2 *STA, *STB;  // deferred LayerNorm: per-chunk row partials [d / 32, M] of the fp16 stream
+  float2 *SA, *SB;    //   and the rows' (mean, rstd) [M]
   uint8_t *X8, *X1_8, *CTX8, *H8;  // e4m3 GEMM inputs (FP8 handles)
   float *scales, *absmax;    // per-tensor activation scales / calibration maxima
   float *policy, *wdl, *mlh;
@@ -420,6 +428,31 @@ void put_mat_fp8(ArenaBuilder &ab, Layout &lay, Mat &m, int rows, int cols, int 
   put_f32(ab, lay, const_cast<float **>(&m.scale), sc.data(), sc.size());
 }
 
+// A matrix that multiplies the output of a LayerNorm z = (y - mean) * rstd *
+// gamma + beta, prepared for un-normalised input rows y: stored (fp16) as
+// W[r][c] * gamma[c], with colsum[r] = sum_c of those stored values and
+// bias[r] = b[r] + sum_c W[r][c] * beta[c], so that
+// z . W^T + b = rstd * (y . Wg^T - mean * colsum) + bias.
+template <class F>
+void put_folded(ArenaBuilder &ab, Layout &lay, Mat &m, float **colsum, float **bias, int rows,
+                int K, F at, const float *gamma, const float *beta, const float *b) {
+  put_mat(ab, lay, m, rows, K, K, [&](int r, int c) { return at(r, c) * gamma[c]; }, true);
+  const size_t off = lay.fix.back().second;
+  std::vector<float> cs(rows), bb(rows);
+  for (int r = 0; r < rows; ++r) {
+    const uint16_t *row = reinterpret_cast<const uint16_t *>(ab.host.data() + off) + size_t(r) * K;
+    double sc = 0.0, sb = b ? b[r] : 0.0;
+    for (int c = 0; c < K; ++c) {
+      sc += __half2float(__ushort_as_half(row[c]));
+      sb += double(at(r, c)) * beta[c];
+    }
+    cs[r] = static_cast<float>(sc);
+    bb[r] = static_cast<float>(sb);
+  }
+  put_f32(ab, lay, colsum, cs.data(), cs.size());
+  put_f32(ab, lay, bias, bb.data(), bb.size());
+}
+
 void pack_weights(const mfb200_net_desc &n, const float *blob, ArenaBuilder &ab, Layout &lay,
                   Weights &W, bool fp8) {
   Packer P(n, blob);
@@ -547,6 +580,20 @@ void pack_weights(const mfb200_net_desc &n, const float *blob, ArenaBuilder &ab,
     put_f32(ab, lay, &Lw.ln1_g, l[L_LN1_G], d);
     put_f32(ab, lay, &Lw.ln1_b, l[L_LN1_B], d);
     dense(Lw.f1, l[L_FFN_W1], n.dff, d, true);
+    if (!fp8) {
+      // deferred LayerNorm: QKV reads the stream before the preceding LN
+      // (the embedding FFN's for layer 0, else the previous layer's ln2)
+      const float *pg = k == 0 ? g[G_EFFN_LN_G] : P.lp[k - 1][L_LN2_G];
+      const float *pb = k == 0 ? g[G_EFFN_LN_B] : P.lp[k - 1][L_LN2_B];
+      std::vector<float> bq(3 * size_t(d) + c, 0.0f);
+      std::memcpy(bq.data(), l[L_Q_B], d * 4);
+      std::memcpy(bq.data() + d, l[L_K_B], d * 4);
+      std::memcpy(bq.data() + 2 * d, l[L_V_B], d * 4);
+      put_folded(ab, lay, Lw.qkvc_f, &Lw.cs_qkvc, &Lw.bb_qkvc, 3 * d + c, d, qkvc_at, pg, pb, bq.data());
+      put_folded(ab, lay, Lw.f1_f, &Lw.cs_f1, &Lw.bb_f1, n.dff, d,
+                 [&](int r, int col) { return l[L_FFN_W1][size_t(r) * d + col]; }, l[L_LN1_G],
+                 l[L_LN1_B], l[L_FFN_B1]);
+    }
     put_f32(ab, lay, &Lw.b_f1, l[L_FFN_B1], n.dff);
     dense(Lw.f2, l[L_FFN_W2], d, n.dff);
     put_f32(ab, lay, &Lw.b_f2, l[L_FFN_B2], d);
@@ -578,6 +625,10 @@ void alloc_workspace(Shard &S, const mfb200_net_desc &n, int max_batch, bool fp8
       {reinterpret_cast<void **>(&S.Xh), M * d * 2},
       {reinterpret_cast<void **>(&S.SK), size_t(kMaxSplits) * B * n.smolgen_hidden * 4},
       {reinterpret_cast<void **>(&S.X1h), M * d * 2},
+      {reinterpret_cast<void **>(&S.STA), M * (d / 32) * 8},
+      {reinterpret_cast<void **>(&S.STB), M * (d / 32) * 8},
+      {reinterpret_cast<void **>(&S.SA), M * 8},
+      {reinterpret_cast<void **>(&S.SB), M * 8},
       {reinterpret_cast<void **>(&S.QKV), M * 3 * d * 2},
       {reinterpret_cast<void **>(&S.C), M * n.smolgen_compress * 2},
       {reinterpret_cast<void **>(&S.S1), B * n.smolgen_hidden * 2},
@@ -670,6 +721,16 @@ void add_fn(Shard::Plan &P, const char *name, double flops, std::function<void(c
 // with absmax probes that calibrates those scales.
 enum PlanMode { kPlanBF16 = 0, kPlanFP8 = 1, kPlanCalibrate = 2 };
 
+// Deferred LayerNorm in the bf16 forward (default on; the unit tests also run
+// it off). The encoder's ln1 / ln2 are not separate passes: the residual GEMMs
+// (output projection, FFN2, embedding FFN2) store the un-normalised sum
+// y = LN_prev(stream) + alpha * (x W^T + b) in fp16 with per-32-column row
+// statistics, and the GEMMs that read the stream (QKV, FFN1) fold the
+// normalisation into their epilogue (rstd * (acc - mean * colsum) + bias, with
+// gamma folded into W and beta into the bias). Only the last layer's ln2 runs
+// as a kernel, for the heads.
+bool g_fold_ln = true;
+
 // activation-scale slots: embedding LN output, embedding FFN hidden, then per
 // layer l: layer input, attention context, ln1 output, FFN hidden
 inline int slot_x(int l) { return 2 + 4 * l; }
@@ -681,6 +742,10 @@ std::unique_ptr<Shard::Plan> build_plan(Shard &S, const mfb200_net_desc &n, int 
                                         int fp8_gemms) {
   auto P = std::make_unique<Shard::Plan>();
   const bool fp8_plan = mode == kPlanFP8, cal = mode == kPlanCalibrate;
+  const bool fold = mode == kPlanBF16 && g_fold_ln && !S.w.layers.empty() &&
+                    S.w.layers[0].qkvc_f.w != nullptr &&
+                    (n.embedding == 128 || n.embedding == 256 || n.embedding == 512 ||
+                     n.embedding == 1024);
   // Which GEMM groups run in e4m3 under FP8 (mfb200_config.fp8_gemms bit
   // mask: 1 embedding FFN, 2 QKV, 4 output projection, 8 FFN1, 16 FFN2).
   const int fp8_mask = fp8_gemms ? fp8_gemms : 31;
@@ -699,6 +764,11 @@ std::unique_ptr<Shard::Plan> build_plan(Shard &S, const mfb200_net_desc &n, int 
   const float alpha = std::pow(2.0f * static_cast<float>(n.layers), -0.25f);  // plan :1152-1162
   const float eps = 1e-3f;  // PE_DENSE epsilons (plan :1164-1193)
   Weights &W = S.w;
+  auto row_stats = [&](float2 *part, float2 *out) {
+    add_fn(*P, "row_stats", 0, [part, out, M, d, eps](cudaStream_t s) {
+      launch_row_stats(part, M, d, eps, out, s);
+    });
+  };
 
   add_fn(*P, "unpack", 0, [&S, B](cudaStream_t s) { launch_unpack(S.masks, S.values, B, S.x0, S.p, s); });
   {
@@ -743,6 +813,13 @@ std::unique_ptr<Shard::Plan> build_plan(Shard &S, const mfb200_net_desc &n, int 
     GemmArgs b = base_args(S, M, d, n.emb_dff);
     // x1 (fp16 stream) += alpha * ffn (in place; the LN below reads the sum)
     b.mode = kEpiAccum;
+    if (fold) {  // same sum, plus its row statistics for layer 0's folded QKV
+      b.mode = kEpiResidNorm;
+      b.resid16 = S.X1h;
+      b.ldr16 = d;
+      b.stats_out = S.STA;
+      b.ln_eps = eps;
+    }
     b.bias = W.b_effn2;
     b.alpha = alpha;
     b.out = S.X1h;
@@ -755,11 +832,13 @@ std::unique_ptr<Shard::Plan> build_plan(Shard &S, const mfb200_net_desc &n, int 
     } else {
       add_gemm(*P, S, "emb_ffn2", S.H, n.emb_dff, W.effn2, b);
     }
+    if (fold) row_stats(S.STA, S.SA);
   }
-  add_fn(*P, "emb_ffn_ln", 0, [&S, &W, M, d, eps, f8q](cudaStream_t s) {
-    launch_layernorm_q(S.X1h, Fmt::F16, M, d, W.ln_effn_g, W.ln_effn_b, eps, nullptr, nullptr,
-                       nullptr, S.Xh, Fmt::F16, f8q ? S.X8 : nullptr, S.scales + slot_x(0), s);
-  });
+  if (!fold)
+    add_fn(*P, "emb_ffn_ln", 0, [&S, &W, M, d, eps, f8q](cudaStream_t s) {
+      launch_layernorm_q(S.X1h, Fmt::F16, M, d, W.ln_effn_g, W.ln_effn_b, eps, nullptr, nullptr,
+                         nullptr, S.Xh, Fmt::F16, f8q ? S.X8 : nullptr, S.scales + slot_x(0), s);
+    });
   probe("absmax_x", S.Xh, Fmt::F16, Md, slot_x(0));
   for (int k = 0; k < n.layers; ++k) {
     LayerW &Lw = W.layers[k];
@@ -775,6 +854,12 @@ std::unique_ptr<Shard::Plan> build_plan(Shard &S, const mfb200_net_desc &n, int 
         a.a_scale_ptr = S.scales + slot_x(k);
         a.col_scale = Lw.qkvc8.scale;
         add_gemm(*P, S, "qkv", S.X8, d, Lw.qkvc8, a);
+      } else if (fold) {
+        a.bias = Lw.bb_qkvc;
+        a.fold_stats = S.SA;
+        a.fold_colsum = Lw.cs_qkvc;
+        a.ln_eps = eps;
+        add_gemm(*P, S, "qkv", S.X1h, d, Lw.qkvc_f, a);
       } else {
         add_gemm(*P, S, "qkv", S.Xh, d, Lw.qkvc, a);
       }
@@ -829,6 +914,18 @@ std::unique_ptr<Shard::Plan> build_plan(Shard &S, const mfb200_net_desc &n, int 
       a.out = S.Xh;
       a.out_f16 = 1;
       a.ldo = d;
+      if (fold) {
+        // stream y (X1h) -> LN_prev(y) + alpha * attention output, in place
+        a.mode = kEpiResidNorm;
+        a.out = S.X1h;
+        a.resid16 = S.X1h;
+        a.ldr16 = d;
+        a.rn_stats = S.SA;
+        a.rn_gamma = k == 0 ? W.ln_effn_g : W.layers[k - 1].ln2_g;
+        a.rn_beta = k == 0 ? W.ln_effn_b : W.layers[k - 1].ln2_b;
+        a.stats_out = S.STB;
+        a.ln_eps = eps;
+      }
       if (f8o) {
         a.a_scale_ptr = S.scales + slot_ctx(k);
         a.col_scale = Lw.o8.scale;
@@ -836,11 +933,13 @@ std::unique_ptr<Shard::Plan> build_plan(Shard &S, const mfb200_net_desc &n, int 
       } else {
         add_gemm(*P, S, "out_proj", S.CTX, d, Lw.o, a);
       }
+      if (fold) row_stats(S.STB, S.SB);
     }
-    add_fn(*P, "ln1", 0, [&S, &Lw, M, d, eps, f8f1, k](cudaStream_t s) {
-      launch_layernorm_q(S.Xh, Fmt::F16, M, d, Lw.ln1_g, Lw.ln1_b, eps, nullptr, nullptr,
-                         nullptr, S.X1h, Fmt::F16, f8f1 ? S.X1_8 : nullptr, S.scales + slot_x1(k), s);
-    });
+    if (!fold)
+      add_fn(*P, "ln1", 0, [&S, &Lw, M, d, eps, f8f1, k](cudaStream_t s) {
+        launch_layernorm_q(S.Xh, Fmt::F16, M, d, Lw.ln1_g, Lw.ln1_b, eps, nullptr, nullptr,
+                           nullptr, S.X1h, Fmt::F16, f8f1 ? S.X1_8 : nullptr, S.scales + slot_x1(k), s);
+      });
     probe("absmax_x1", S.X1h, Fmt::F16, Md, slot_x1(k));
     {
       GemmArgs a = base_args(S, M, n.dff, d);
@@ -857,6 +956,12 @@ std::unique_ptr<Shard::Plan> build_plan(Shard &S, const mfb200_net_desc &n, int 
         a.a_scale_ptr = S.scales + slot_x1(k);
         a.col_scale = Lw.f1_8.scale;
         add_gemm(*P, S, "ffn1", S.X1_8, d, Lw.f1_8, a);
+      } else if (fold) {
+        a.bias = Lw.bb_f1;
+        a.fold_stats = S.SB;
+        a.fold_colsum = Lw.cs_f1;
+        a.ln_eps = eps;
+        add_gemm(*P, S, "ffn1", S.X1h, d, Lw.f1_f, a);
       } else {
         add_gemm(*P, S, "ffn1", S.X1h, d, Lw.f1, a);
       }
@@ -869,6 +974,16 @@ std::unique_ptr<Shard::Plan> build_plan(Shard &S, const mfb200_net_desc &n, int 
       b.out = S.X1h;
       b.out_f16 = 1;
       b.ldo = d;
+      if (fold) {
+        b.mode = kEpiResidNorm;
+        b.resid16 = S.X1h;
+        b.ldr16 = d;
+        b.rn_stats = S.SB;
+        b.rn_gamma = Lw.ln1_g;
+        b.rn_beta = Lw.ln1_b;
+        b.stats_out = S.STA;
+        b.ln_eps = eps;
+      }
       if (f8f2) {
         b.a_scale_ptr = S.scales + slot_h(k);
         b.col_scale = Lw.f2_8.scale;
@@ -876,16 +991,18 @@ std::unique_ptr<Shard::Plan> build_plan(Shard &S, const mfb200_net_desc &n, int 
       } else {
         add_gemm(*P, S, "ffn2", S.H, n.dff, Lw.f2, b);
       }
+      if (fold) row_stats(S.STA, S.SA);
     }
     {
       // the last layer's output feeds the bf16 heads; earlier ones feed the
       // next layer's (e4m3, under FP8) QKV projection
       const bool last = k + 1 == n.layers;
       const bool q8 = f8q && !last;
-      add_fn(*P, "ln2", 0, [&S, &Lw, M, d, eps, q8, k](cudaStream_t s) {
-        launch_layernorm_q(S.X1h, Fmt::F16, M, d, Lw.ln2_g, Lw.ln2_b, eps, nullptr, nullptr,
-                           nullptr, S.Xh, Fmt::F16, q8 ? S.X8 : nullptr, S.scales + slot_x(k + 1), s);
-      });
+      if (!fold || last)  // deferred LayerNorm: only the heads' input is normalised here
+        add_fn(*P, "ln2", 0, [&S, &Lw, M, d, eps, q8, k](cudaStream_t s) {
+          launch_layernorm_q(S.X1h, Fmt::F16, M, d, Lw.ln2_g, Lw.ln2_b, eps, nullptr, nullptr,
+                             nullptr, S.Xh, Fmt::F16, q8 ? S.X8 : nullptr, S.scales + slot_x(k + 1), s);
+        });
       if (!last) probe("absmax_x", S.Xh, Fmt::F16, Md, slot_x(k + 1));
     }
   }
@@ -990,6 +1107,8 @@ int fail(mfb200_handle *h, const std::string &msg) {
 }  // namespace
 
 // ============================================================ C ABI
+extern "C" void mfb200_debug_set_fold_ln(int enable) { g_fold_ln = enable != 0; }
+
 extern "C" size_t mfb200_weight_bytes(const mfb200_net_desc *desc) {
   return desc ? blob_floats(*desc) * sizeof(float) : 0;
 }

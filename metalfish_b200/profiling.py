@@ -4,9 +4,11 @@
       times ITERS back-to-back launches of one tcgen05 GEMM on synthetic
       device data (mfb200_debug_gemm_bench) and prints TFLOP/s. DTYPE: 0
       bf16, 1 e4m3, 2 fp16 operands; PAIRS 0 forbids the CTA-pair kernel.
-  python -m metalfish_b200.profiling forward [BATCH] [bf16|fp8]
+  python -m metalfish_b200.profiling forward [BATCH] [bf16|fp8|bf16-nofold]
       runs two eager forwards (no CUDA graph, so every kernel is a separate
-      launch) of the seeded BT4-shaped network on fixture positions.
+      launch) of the seeded BT4-shaped network on fixture positions;
+      bf16-nofold runs the encoder with separate ln1 / ln2 passes instead of
+      the deferred LayerNorm.
   python -m metalfish_b200.profiling leaves [BATCH]
       runs two eager leaf evaluations (mfb200_evaluate_leaves: encoder,
       forward, move mapping + priors) on the fixture game histories.
@@ -41,6 +43,10 @@ def forward(argv) -> None:
     from .synthetic import BT4, generate
     batch = int(argv[0]) if argv else 512
     precision = argv[1] if len(argv) > 1 else "bf16"
+    if precision == "bf16-nofold":
+        from ._lib import lib
+        lib().mfb200_debug_set_fold_ln(0)
+        precision = "bf16"
     z = np.load(os.path.join(ROOT, "tests", "golden", "positions.npz"))
     m, v = z["masks"], z["values"]
     reps = (batch + 2048 + len(m) - 1) // len(m)

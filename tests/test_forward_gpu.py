@@ -49,6 +49,36 @@ def test_forward_matches_reference(name, positions):
     check(out, g, n)
 
 
+@pytest.mark.parametrize("name", ["tiny", "small_perturbed", "bt4"])
+def test_deferred_layernorm_on_and_off(name, positions):
+    """The bf16 encoder with the deferred LayerNorm (the default: residual
+    GEMMs store the un-normalised stream plus row statistics, QKV / FFN1 fold
+    the normalisation into their epilogue) and with separate ln1 / ln2 passes
+    both meet the tolerance, at a batch that fills whole tiles and a ragged one."""
+    from metalfish_b200._lib import lib
+    g = load_golden(name)
+    cfg = synthetic.CONFIGS[str(g["config"])]
+    t = synthetic.generate(cfg, int(g["weight_seed"]), bool(g["perturb_norms"]))
+    n = int(g["positions"])
+    outs = {}
+    try:
+        for fold in (0, 1):
+            lib().mfb200_debug_set_fold_ln(fold)
+            net = create_network(cfg, t, max_batch=n, use_graphs=False)
+            try:
+                for b in (n, max(1, n - 5)):
+                    out = net.evaluate_packed(positions.slice(0, b))
+                    check(out, g, b)
+                    outs[(fold, b)] = out
+            finally:
+                net.close()
+    finally:
+        lib().mfb200_debug_set_fold_ln(1)
+    d = np.abs(outs[(0, n)].policy - outs[(1, n)].policy).max()
+    print(f"{name}: fold on/off policy max diff {d:.4g}")
+    assert d <= POLICY_TOL
+
+
 @pytest.mark.parametrize("batch", [1, 3, 17])
 def test_ragged_batches(batch, positions):
     g = load_golden("small")
