@@ -23,6 +23,11 @@ MFB200_API void mfb200_debug_set_gemm_pairs(int enable);
  * normalisation into their epilogue, instead of separate ln1 / ln2 passes. */
 MFB200_API void mfb200_debug_set_fold_ln(int enable);
 
+/* Split K (1, the default) or not (0) in the GEMMs of forwards planned
+ * afterwards whose output tiles would occupy at most half of the SMs (small
+ * batches): fp32 partial products, then one reduction + epilogue kernel. */
+MFB200_API void mfb200_debug_set_auto_split(int enable);
+
 /* Launch the kernels of forwards planned afterwards with (1, the default) or
  * without (0) programmatic dependent launch. */
 MFB200_API void mfb200_debug_set_pdl(int enable);

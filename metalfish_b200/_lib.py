@@ -36,6 +36,8 @@ def _declare(L: ctypes.CDLL) -> None:
     L.mfb200_debug_set_gemm_pairs.argtypes = [c_int]
     L.mfb200_debug_set_fold_ln.restype = None
     L.mfb200_debug_set_fold_ln.argtypes = [c_int]
+    L.mfb200_debug_set_auto_split.restype = None
+    L.mfb200_debug_set_auto_split.argtypes = [c_int]
     L.mfb200_debug_gemm_bench.restype = c_int
     L.mfb200_debug_gemm_bench.argtypes = [c_int] * 9 + [ctypes.POINTER(c_float)]
     L.mfb200_debug_gemm_ln.restype = c_int

@@ -216,6 +216,96 @@ cudaError_t launch_gemm(const GemmLaunch &g, cudaStream_t stream) {
   return cudaErrorInvalidValue;
 }
 
+// Second half of a split-K GEMM: one warp per (row, 32-column chunk), lane =
+// column. Sums the K slices' fp32 partial products [splits, M, N] in slice
+// order and applies the epilogue the single-pass kernel would have applied
+// (activation scale, deferred-LayerNorm fold, column scale, bias, then the
+// store / accumulate / residual / residual-norm mode and the output format).
+__global__ void __launch_bounds__(256)
+    splitk_epilogue_kernel(const float *__restrict__ part, int splits, long long stride,
+                           const GemmArgs a) {
+  pdl_wait();
+  pdl_launch();
+  const int chunks = a.N / 32;
+  const long long w = static_cast<long long>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (w >= static_cast<long long>(a.M) * chunks) return;
+  const int row = static_cast<int>(w / chunks), ch = static_cast<int>(w % chunks);
+  const int c = ch * 32 + lane;
+  const float *p = part + static_cast<long long>(row) * a.N + c;
+  float v = 0.0f;
+  int s = 0;
+  for (; s + 4 <= splits; s += 4) {
+    const float x0 = __ldcg(p + s * stride), x1 = __ldcg(p + (s + 1) * stride);
+    const float x2 = __ldcg(p + (s + 2) * stride), x3 = __ldcg(p + (s + 3) * stride);
+    v += x0;
+    v += x1;
+    v += x2;
+    v += x3;
+  }
+  for (; s < splits; ++s) v += __ldcg(p + s * stride);
+  const float as = a.a_scale_ptr ? a.a_scale * __ldg(a.a_scale_ptr) : a.a_scale;
+  if (as != 1.0f) v *= as;
+  if (a.fold_stats) {
+    const float2 st = __ldcg(a.fold_stats + row);
+    v = st.y * (v - st.x * __ldg(a.fold_colsum + c));
+  }
+  if (a.col_scale) v *= __ldg(a.col_scale + c);
+  if (a.bias) v += __ldg(a.bias + c);
+  if (a.mode == kEpiAccum) {
+    v *= a.alpha;
+    if (a.out_f32) {
+      float *o = static_cast<float *>(a.out) + static_cast<long long>(row) * a.ldo + c;
+      *o += v;
+    } else {
+      __half *o = static_cast<__half *>(a.out) + static_cast<long long>(row) * a.ldo + c;
+      *o = __float2half_rn(__half2float(*o) + v);
+    }
+    return;
+  }
+  if (a.mode == kEpiResidNorm) {
+    float r = __half2float(a.resid16[static_cast<long long>(row) * a.ldr16 + c]);
+    if (a.rn_stats) {
+      const float2 st = __ldcg(a.rn_stats + row);
+      r = (r - st.x) * st.y * __ldg(a.rn_gamma + c) + __ldg(a.rn_beta + c);
+    }
+    const float y = r + a.alpha * v;
+    static_cast<__half *>(a.out)[static_cast<long long>(row) * a.ldo + c] = __float2half_rn(y);
+    float sum = y, sq = y * y;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      sum += __shfl_xor_sync(0xffffffffu, sum, o);
+      sq += __shfl_xor_sync(0xffffffffu, sq, o);
+    }
+    if (lane == 0)
+      a.stats_out[static_cast<long long>(ch) * a.M + row] =
+          make_float2(sum, fmaxf(sq - sum * sum * (1.0f / 32.0f), 0.0f));
+    return;
+  }
+  if (a.mode == kEpiResid) v = a.resid[static_cast<long long>(row) * a.ldr + c] + a.alpha * v;
+  else v = apply_act(v, a.act);
+  const bool second = a.out2 && c >= a.split;
+  void *base = second ? a.out2 : a.out;
+  const long long idx = static_cast<long long>(row) * (second ? a.ldo2 : a.ldo) + (second ? c - a.split : c);
+  if (a.out_f32) {
+    static_cast<float *>(base)[idx] = v;
+  } else if (a.out_fp8) {
+    const float is = a.out_scale_ptr ? 1.0f / __ldg(a.out_scale_ptr) : a.out_inv_scale;
+    static_cast<__nv_fp8_e4m3 *>(base)[idx] = __nv_fp8_e4m3(v * is);
+  } else if (a.out_f16) {
+    static_cast<__half *>(base)[idx] = __float2half_rn(v);
+  } else {
+    static_cast<__nv_bfloat16 *>(base)[idx] = __float2bfloat16_rn(v);
+  }
+}
+
+cudaError_t launch_splitk_epilogue(const float *part, int splits, const GemmArgs &a,
+                                   cudaStream_t stream) {
+  const long long warps = static_cast<long long>(a.M) * (a.N / 32);
+  return launch_k(splitk_epilogue_kernel, dim3(static_cast<unsigned>((warps + 7) / 8)), dim3(256),
+                  0, stream, 1, part, splits, static_cast<long long>(a.M) * a.N, a);
+}
+
 const char *plan_gemm(GemmLaunch &g, const void *A, long long lda_elems, const void *W,
                       long long ldw_elems, int bn, bool fp8, const GemmArgs &args) {
   if (bn != 64 && bn != 128 && bn != 256) return "gemm: BN must be 64, 128 or 256";

@@ -32,4 +32,10 @@ const char *plan_gemm(GemmLaunch &g, const void *A, long long lda_elems, const v
 
 cudaError_t launch_gemm(const GemmLaunch &g, cudaStream_t stream);
 
+// The reduction and epilogue of a GEMM whose K slices were computed by a
+// split-K launch into `part` ([splits, a.M, a.N] fp32): applies `a`'s
+// epilogue (any mode but the LayerNorm cluster one) to the sums.
+cudaError_t launch_splitk_epilogue(const float *part, int splits, const GemmArgs &a,
+                                   cudaStream_t stream);
+
 }  // namespace mfb200

@@ -447,8 +447,18 @@ __global__ void splitk_act_ln_kernel(const float *__restrict__ part, int splits,
   for (int q = 0; q < VPL / 4; ++q) {
     const int c = q * 128 + lane * 4;
     float4 a = *reinterpret_cast<const float4 *>(bias + c);
-    for (int sidx = 0; sidx < splits; ++sidx) {
-      const float4 f = *reinterpret_cast<const float4 *>(part + sidx * stride + row * W + c);
+    // slices in order; four loads in flight at a time
+    int sidx = 0;
+    for (; sidx + 4 <= splits; sidx += 4) {
+      float4 f[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        f[k] = __ldcg(reinterpret_cast<const float4 *>(part + (sidx + k) * stride + row * W + c));
+#pragma unroll
+      for (int k = 0; k < 4; ++k) { a.x += f[k].x; a.y += f[k].y; a.z += f[k].z; a.w += f[k].w; }
+    }
+    for (; sidx < splits; ++sidx) {
+      const float4 f = __ldcg(reinterpret_cast<const float4 *>(part + sidx * stride + row * W + c));
       a.x += f.x; a.y += f.y; a.z += f.z; a.w += f.w;
     }
     v[4 * q] = apply_act(a.x, act);

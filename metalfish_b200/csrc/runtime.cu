@@ -276,6 +276,8 @@ struct Shard {  // one GPU
   float *T, *SK;     // fp32 embedding sum, split-K partials
   float2 *STA, *STB;  // deferred LayerNorm: per-chunk row partials [d / 32, M] of the fp16 stream
   float2 *SA, *SB;    //   and the rows' (mean, rstd) [M]
+  float *SPK = nullptr;      // split-K partial products of small-batch GEMMs
+  long long spk_floats = 0;
   uint8_t *X8, *X1_8, *CTX8, *H8;  // e4m3 GEMM inputs (FP8 handles)
   float *scales, *absmax;    // per-tensor activation scales / calibration maxima
   float *policy, *wdl, *mlh;
@@ -628,6 +630,7 @@ void alloc_workspace(Shard &S, const mfb200_net_desc &n, int max_batch, bool fp8
       {reinterpret_cast<void **>(&S.STA), M * (d / 32) * 8},
       {reinterpret_cast<void **>(&S.STB), M * (d / 32) * 8},
       {reinterpret_cast<void **>(&S.SA), M * 8},
+      {reinterpret_cast<void **>(&S.SPK), size_t(num_sms()) * 128 * 256 * 4},
       {reinterpret_cast<void **>(&S.SB), M * 8},
       {reinterpret_cast<void **>(&S.QKV), M * 3 * d * 2},
       {reinterpret_cast<void **>(&S.C), M * n.smolgen_compress * 2},
@@ -666,6 +669,7 @@ void alloc_workspace(Shard &S, const mfb200_net_desc &n, int max_batch, bool fp8
     offs.push_back(total);
     total += (p.second + 1023) & ~size_t(1023);
   }
+  S.spk_floats = static_cast<long long>(num_sms()) * 128 * 256;
   check(cudaMalloc(&S.ws, total), "workspace allocation");
   S.ws_bytes = total;
   check(cudaMemset(S.ws, 0, total), "workspace clear");
@@ -674,6 +678,10 @@ void alloc_workspace(Shard &S, const mfb200_net_desc &n, int max_batch, bool fp8
 }
 
 // ------------------------------------------------------------ plan
+// Split K for GEMMs whose output tiles fill at most half the SMs (small
+// batches); the unit tests also run it off.
+bool g_auto_split = true;
+
 int pick_bn(int M, int N) {
   if (N < 128) return 64;
   if (N < 256) return 128;
@@ -695,6 +703,8 @@ GemmArgs base_args(Shard &S, int M, int N, int K) {
   return a;
 }
 
+void add_fn(Shard::Plan &P, const char *name, double flops, std::function<void(cudaStream_t)> fn);
+
 void add_gemm(Shard::Plan &P, Shard &S, const char *name, const void *A, long long lda,
               const Mat &W, GemmArgs a) {
   Shard::Step st;
@@ -703,6 +713,35 @@ void add_gemm(Shard::Plan &P, Shard &S, const char *name, const void *A, long lo
   st.flops = 2.0 * a.M * double(a.N) * a.K;
   const int bn = pick_bn(a.M, a.N);
   a.ab_f16 = W.f16 ? 1 : 0;
+  // Small M (few positions): the output tiles would occupy only a fraction of
+  // the SMs, each streaming its weight rows through the whole K loop. Split K
+  // instead so that about one CTA per SM streams a slice of the weights
+  // (fp32 partials in S.SPK), and apply the epilogue in a second kernel.
+  const long long tiles = static_cast<long long>((a.M + 127) / 128) * ((a.N + bn - 1) / bn);
+  const int kblocks = (a.K + (W.fp8 ? 127 : 63)) / (W.fp8 ? 128 : 64);
+  if (g_auto_split && a.k_splits <= 1 && a.mode != kEpiResidLN && tiles * 2 <= num_sms() &&
+      kblocks >= 2) {
+    const int splits = static_cast<int>(std::min<long long>({kblocks, num_sms() / tiles, 16}));
+    // (at least 3 slices: below that the extra kernel costs more than it saves)
+    if (splits >= 3 && static_cast<long long>(splits) * a.M * a.N <= S.spk_floats) {
+      GemmArgs p = base_args(S, a.M, a.N, a.K);
+      p.ab_f16 = a.ab_f16;
+      p.out = S.SPK;
+      p.out_f32 = 1;
+      p.ldo = a.N;
+      p.k_splits = splits;
+      p.split_stride = static_cast<long long>(a.M) * a.N;
+      if (const char *err = plan_gemm(st.g, A, lda, W.w, W.ld, bn, W.fp8, p))
+        throw Fail(std::string(name) + " (split-K): " + err);
+      const int used = st.g.args.k_splits;
+      P.steps.push_back(std::move(st));
+      float *part = S.SPK;
+      add_fn(P, (std::string(name) + "_splitk").c_str(), 0, [part, used, a](cudaStream_t s) {
+        check(launch_splitk_epilogue(part, used, a, s), "split-K epilogue");
+      });
+      return;
+    }
+  }
   if (const char *err = plan_gemm(st.g, A, lda, W.w, W.ld, bn, W.fp8, a))
     throw Fail(std::string(name) + ": " + err);
   P.steps.push_back(std::move(st));
@@ -1108,6 +1147,8 @@ int fail(mfb200_handle *h, const std::string &msg) {
 
 // ============================================================ C ABI
 extern "C" void mfb200_debug_set_fold_ln(int enable) { g_fold_ln = enable != 0; }
+
+extern "C" void mfb200_debug_set_auto_split(int enable) { g_auto_split = enable != 0; }
 
 extern "C" size_t mfb200_weight_bytes(const mfb200_net_desc *desc) {
   return desc ? blob_floats(*desc) * sizeof(float) : 0;

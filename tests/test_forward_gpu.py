@@ -79,6 +79,35 @@ def test_deferred_layernorm_on_and_off(name, positions):
     assert d <= POLICY_TOL
 
 
+@pytest.mark.parametrize("name", ["small_perturbed", "bt4"])
+def test_small_batch_split_k_on_and_off(name, positions):
+    """Small batches split K across the SMs (fp32 partials + a reduction /
+    epilogue kernel) by default; with and without it the forward meets the
+    tolerance, at batch 1 and a ragged batch."""
+    from metalfish_b200._lib import lib
+    g = load_golden(name)
+    cfg = synthetic.CONFIGS[str(g["config"])]
+    t = synthetic.generate(cfg, int(g["weight_seed"]), bool(g["perturb_norms"]))
+    n = min(int(g["positions"]), 17)
+    outs = {}
+    try:
+        for split in (0, 1):
+            lib().mfb200_debug_set_auto_split(split)
+            net = create_network(cfg, t, max_batch=n)
+            try:
+                for b in (1, n):
+                    out = net.evaluate_packed(positions.slice(0, b))
+                    check(out, g, b)
+                    outs[(split, b)] = out
+            finally:
+                net.close()
+    finally:
+        lib().mfb200_debug_set_auto_split(1)
+    d = np.abs(outs[(0, n)].policy - outs[(1, n)].policy).max()
+    print(f"{name}: split on/off policy max diff {d:.4g}")
+    assert d <= POLICY_TOL
+
+
 @pytest.mark.parametrize("batch", [1, 3, 17])
 def test_ragged_batches(batch, positions):
     g = load_golden("small")
@@ -92,8 +121,14 @@ def test_batch_vs_single_and_graph_vs_eager(positions):
     net = net_for("small")
     many = net.evaluate_packed(positions.slice(0, 8))
     for i in (0, 5):
+        # a single position takes the split-K GEMMs, the batch does not, so
+        # the fp32 sums run in another order: the tolerances are the ones the
+        # reference applies to its CUDA transformer backend (policy 7.5e-2,
+        # tests/test_nn_comparison.cpp:825-832) and its default value
+        # tolerance (1e-2, :609-613)
         one = net.evaluate_packed(positions.slice(i, i + 1))
-        np.testing.assert_allclose(one.policy[0], many.policy[i], atol=1e-2)
+        np.testing.assert_allclose(one.policy[0], many.policy[i], atol=7.5e-2)
+        np.testing.assert_allclose(one.value[0], many.value[i], atol=1e-2)
     eager = net_for("small", use_graphs=False).evaluate_packed(positions.slice(0, 8))
     np.testing.assert_array_equal(eager.policy, many.policy)
     np.testing.assert_array_equal(eager.wdl, many.wdl)
