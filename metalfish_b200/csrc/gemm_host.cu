@@ -299,8 +299,67 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// kEpiResidNorm of a split-K GEMM with the row statistics finalised in the
+// same pass: one CTA (N threads, one column each) per row, so the mean and
+// variance come from the whole row (two-pass, as the LayerNorm kernel).
+__global__ void __launch_bounds__(1024)
+    splitk_residnorm_row_kernel(const float *__restrict__ part, int splits, long long stride,
+                                const GemmArgs a) {
+  pdl_wait();
+  pdl_launch();
+  __shared__ float red[32];
+  const int row = blockIdx.x, c = threadIdx.x, lane = c & 31, warp = c >> 5;
+  const int warps = blockDim.x >> 5;
+  const float *p = part + static_cast<long long>(row) * a.N + c;
+  float v = 0.0f;
+  int s = 0;
+  for (; s + 4 <= splits; s += 4) {
+    const float x0 = __ldcg(p + s * stride), x1 = __ldcg(p + (s + 1) * stride);
+    const float x2 = __ldcg(p + (s + 2) * stride), x3 = __ldcg(p + (s + 3) * stride);
+    v += x0;
+    v += x1;
+    v += x2;
+    v += x3;
+  }
+  for (; s < splits; ++s) v += __ldcg(p + s * stride);
+  if (a.bias) v += __ldg(a.bias + c);
+  float r = __half2float(a.resid16[static_cast<long long>(row) * a.ldr16 + c]);
+  if (a.rn_stats) {
+    const float2 st = __ldcg(a.rn_stats + row);
+    r = (r - st.x) * st.y * __ldg(a.rn_gamma + c) + __ldg(a.rn_beta + c);
+  }
+  const float y = r + a.alpha * v;
+  static_cast<__half *>(a.out)[static_cast<long long>(row) * a.ldo + c] = __float2half_rn(y);
+  // block sums: mean, then the squared deviations from it
+  float t = y;
+#pragma unroll
+  for (int o = 16; o; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+  if (lane == 0) red[warp] = t;
+  __syncthreads();
+  float sum = 0.0f;
+  for (int w = 0; w < warps; ++w) sum += red[w];
+  const float mean = sum / static_cast<float>(a.N);
+  __syncthreads();
+  t = (y - mean) * (y - mean);
+#pragma unroll
+  for (int o = 16; o; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+  if (lane == 0) red[warp] = t;
+  __syncthreads();
+  if (c == 0) {
+    float sq = 0.0f;
+    for (int w = 0; w < warps; ++w) sq += red[w];
+    a.stats_final[row] = make_float2(mean, 1.0f / sqrtf(sq / static_cast<float>(a.N) + a.ln_eps));
+  }
+}
+
 cudaError_t launch_splitk_epilogue(const float *part, int splits, const GemmArgs &a,
                                    cudaStream_t stream) {
+  if (a.mode == kEpiResidNorm && a.stats_final && a.N <= 1024 && a.N % 32 == 0 &&
+      a.a_scale == 1.0f && !a.a_scale_ptr && !a.col_scale && !a.fold_stats)
+    return launch_k(splitk_residnorm_row_kernel, dim3(static_cast<unsigned>(a.M)),
+                    dim3(static_cast<unsigned>(a.N)), 0, stream, 1, part, splits,
+                    static_cast<long long>(a.M) * a.N, a);
+  if (a.stats_final) return cudaErrorInvalidValue;  // finalised statistics need the row kernel
   const long long warps = static_cast<long long>(a.M) * (a.N / 32);
   return launch_k(splitk_epilogue_kernel, dim3(static_cast<unsigned>((warps + 7) / 8)), dim3(256),
                   0, stream, 1, part, splits, static_cast<long long>(a.M) * a.N, a);

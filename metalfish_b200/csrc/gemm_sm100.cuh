@@ -87,6 +87,8 @@ struct GemmArgs {
                               // W holds gamma-scaled rows and the epilogue computes
                               // rstd * (acc - mean * fold_colsum) before the bias
   const float *fold_colsum;   // [N] column sums of the gamma-scaled W
+  float2 *stats_final;        // kEpiResidNorm through the split-K epilogue kernel (N <= 1024):
+                              // the rows' (mean, rstd) [M] written directly (stats_out unused)
 };
 
 // mish(x) = x * tanh(softplus(x)). With e = exp(x), tanh(log(1 + e)) =

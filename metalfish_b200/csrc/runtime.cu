@@ -705,7 +705,10 @@ GemmArgs base_args(Shard &S, int M, int N, int K) {
 
 void add_fn(Shard::Plan &P, const char *name, double flops, std::function<void(cudaStream_t)> fn);
 
-void add_gemm(Shard::Plan &P, Shard &S, const char *name, const void *A, long long lda,
+// Returns true when the GEMM was split along K (its epilogue then runs in the
+// split-K epilogue kernel, which also finalises residual-norm row statistics
+// into a.stats_final when that is set).
+bool add_gemm(Shard::Plan &P, Shard &S, const char *name, const void *A, long long lda,
               const Mat &W, GemmArgs a) {
   Shard::Step st;
   st.name = name;
@@ -739,12 +742,13 @@ void add_gemm(Shard::Plan &P, Shard &S, const char *name, const void *A, long lo
       add_fn(P, (std::string(name) + "_splitk").c_str(), 0, [part, used, a](cudaStream_t s) {
         check(launch_splitk_epilogue(part, used, a, s), "split-K epilogue");
       });
-      return;
+      return true;
     }
   }
   if (const char *err = plan_gemm(st.g, A, lda, W.w, W.ld, bn, W.fp8, a))
     throw Fail(std::string(name) + ": " + err);
   P.steps.push_back(std::move(st));
+  return false;
 }
 
 void add_fn(Shard::Plan &P, const char *name, double flops, std::function<void(cudaStream_t)> fn) {
@@ -857,6 +861,7 @@ std::unique_ptr<Shard::Plan> build_plan(Shard &S, const mfb200_net_desc &n, int 
       b.resid16 = S.X1h;
       b.ldr16 = d;
       b.stats_out = S.STA;
+      b.stats_final = S.SA;
       b.ln_eps = eps;
     }
     b.bias = W.b_effn2;
@@ -869,9 +874,8 @@ std::unique_ptr<Shard::Plan> build_plan(Shard &S, const mfb200_net_desc &n, int 
       b.col_scale = W.effn2_8.scale;
       add_gemm(*P, S, "emb_ffn2", S.H8, n.emb_dff, W.effn2_8, b);
     } else {
-      add_gemm(*P, S, "emb_ffn2", S.H, n.emb_dff, W.effn2, b);
+      if (!add_gemm(*P, S, "emb_ffn2", S.H, n.emb_dff, W.effn2, b) && fold) row_stats(S.STA, S.SA);
     }
-    if (fold) row_stats(S.STA, S.SA);
   }
   if (!fold)
     add_fn(*P, "emb_ffn_ln", 0, [&S, &W, M, d, eps, f8q](cudaStream_t s) {
@@ -963,6 +967,7 @@ std::unique_ptr<Shard::Plan> build_plan(Shard &S, const mfb200_net_desc &n, int 
         a.rn_gamma = k == 0 ? W.ln_effn_g : W.layers[k - 1].ln2_g;
         a.rn_beta = k == 0 ? W.ln_effn_b : W.layers[k - 1].ln2_b;
         a.stats_out = S.STB;
+        a.stats_final = S.SB;
         a.ln_eps = eps;
       }
       if (f8o) {
@@ -970,9 +975,8 @@ std::unique_ptr<Shard::Plan> build_plan(Shard &S, const mfb200_net_desc &n, int 
         a.col_scale = Lw.o8.scale;
         add_gemm(*P, S, "out_proj", S.CTX8, d, Lw.o8, a);
       } else {
-        add_gemm(*P, S, "out_proj", S.CTX, d, Lw.o, a);
+        if (!add_gemm(*P, S, "out_proj", S.CTX, d, Lw.o, a) && fold) row_stats(S.STB, S.SB);
       }
-      if (fold) row_stats(S.STB, S.SB);
     }
     if (!fold)
       add_fn(*P, "ln1", 0, [&S, &Lw, M, d, eps, f8f1, k](cudaStream_t s) {
@@ -1021,6 +1025,7 @@ std::unique_ptr<Shard::Plan> build_plan(Shard &S, const mfb200_net_desc &n, int 
         b.rn_gamma = Lw.ln1_g;
         b.rn_beta = Lw.ln1_b;
         b.stats_out = S.STA;
+        b.stats_final = S.SA;
         b.ln_eps = eps;
       }
       if (f8f2) {
@@ -1028,9 +1033,8 @@ std::unique_ptr<Shard::Plan> build_plan(Shard &S, const mfb200_net_desc &n, int 
         b.col_scale = Lw.f2_8.scale;
         add_gemm(*P, S, "ffn2", S.H8, n.dff, Lw.f2_8, b);
       } else {
-        add_gemm(*P, S, "ffn2", S.H, n.dff, Lw.f2, b);
+        if (!add_gemm(*P, S, "ffn2", S.H, n.dff, Lw.f2, b) && fold) row_stats(S.STA, S.SA);
       }
-      if (fold) row_stats(S.STA, S.SA);
     }
     {
       // the last layer's output feeds the bf16 heads; earlier ones feed the
