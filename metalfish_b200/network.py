@@ -403,3 +403,13 @@ def create_network(cfg: NetConfig, tensors: Dict[str, np.ndarray], backend: str 
             raise RuntimeError("an FP8 network needs calibration positions")
         net.calibrate(calibration)
     return net
+
+
+def create_network_from_file(path: str, backend: str = "b200",
+                             calibration: Optional[PackedInputs] = None, **kwargs) -> B200Network:
+    """``CreateNetwork(LoadWeightsFromFile(path), BackendConfig)``
+    (``src/nn/network.cpp:137-208``, ``src/nn/loader.cpp:156-175``) for the
+    B200 backend: a ``.pb`` / ``.pb.gz`` weight file, shape inferred from it."""
+    from .weightsfile import load_weights
+    cfg, tensors = load_weights(path)
+    return create_network(cfg, tensors, backend=backend, calibration=calibration, **kwargs)
