@@ -1,6 +1,10 @@
 """One handle over two GPUs: the batch is sharded contiguously (one host
-thread per GPU), weights replicated, no collective. Results must equal a
-single-GPU handle's (same kernels, same per-position arithmetic)."""
+thread per GPU), weights replicated, no collective. Results match a
+single-GPU handle's within the tolerances the reference applies between
+batch sizes on its CUDA transformer backend (policy 7.5e-2, value 2e-3,
+moves-left 1.25e-1; tests/test_nn_comparison.cpp:825-832): a shard's smaller
+batch can split a GEMM's K differently (small-batch split-K), which changes
+the fp32 summation order."""
 import numpy as np
 import pytest
 
@@ -21,6 +25,7 @@ def test_two_gpu_handle_matches_one_gpu(positions):
     two_net = create_network(cfg, t, max_batch=128, num_devices=2)
     assert two_net.get_backend_capabilities().num_devices == 2
     two = two_net.evaluate_packed(inp)
-    np.testing.assert_array_equal(two.policy, one.policy)
-    np.testing.assert_array_equal(two.wdl, one.wdl)
-    np.testing.assert_array_equal(two.moves_left, one.moves_left)
+    np.testing.assert_allclose(two.policy, one.policy, rtol=0, atol=7.5e-2)
+    np.testing.assert_allclose(two.wdl, one.wdl, rtol=0, atol=2e-3)
+    np.testing.assert_allclose(two.value, one.value, rtol=0, atol=2e-3)
+    np.testing.assert_allclose(two.moves_left, one.moves_left, rtol=0, atol=1.25e-1)
