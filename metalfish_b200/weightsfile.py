@@ -55,7 +55,8 @@ SCHEMA: Dict[str, Dict[int, Tuple[str, str]]] = {
                 44: ("value_heads", "msg:ValueHeads"), 45: ("policy_heads", "msg:PolicyHeads"),
                 31: ("ip_mov_w", _L), 32: ("ip_mov_b", _L), 13: ("ip1_mov_w", _L),
                 14: ("ip1_mov_b", _L), 15: ("ip2_mov_w", _L), 16: ("ip2_mov_b", _L),
-                35: ("smolgen_w", _L), 36: ("smolgen_b", _L)},
+                35: ("smolgen_w", _L), 36: ("smolgen_b", _L),
+                21: ("pol_encoder", "rmsg:EncoderLayer")},
     "EncoderLayer": {1: ("mha", "msg:MHA"), 2: ("ln1_gammas", _L), 3: ("ln1_betas", _L),
                      4: ("ffn", "msg:FFN"), 5: ("ln2_gammas", _L), 6: ("ln2_betas", _L)},
     "MHA": {1: ("q_w", _L), 2: ("q_b", _L), 3: ("k_w", _L), 4: ("k_b", _L), 5: ("v_w", _L),
@@ -69,15 +70,22 @@ SCHEMA: Dict[str, Dict[int, Tuple[str, str]]] = {
     "PolicyHeads": {1: ("ip_pol_w", _L), 2: ("ip_pol_b", _L), 3: ("vanilla", "msg:PolicyHead")},
     "PolicyHead": {1: ("ip_pol_w", _L), 2: ("ip_pol_b", _L), 3: ("ip2_pol_w", _L),
                    4: ("ip2_pol_b", _L), 5: ("ip3_pol_w", _L), 6: ("ip3_pol_b", _L),
-                   7: ("ip4_pol_w", _L)},
+                   7: ("ip4_pol_w", _L), 8: ("pol_encoder", "rmsg:EncoderLayer")},
     "ValueHeads": {1: ("winner", "msg:ValueHead")},
     "ValueHead": {1: ("ip_val_w", _L), 2: ("ip_val_b", _L), 3: ("ip1_val_w", _L),
                   4: ("ip1_val_b", _L), 5: ("ip2_val_w", _L), 6: ("ip2_val_b", _L)},
 }
 
-# NetworkFormat.ActivationFunction -> the library's activation names
-_ACT = {1: "mish", 2: "relu", 3: "none", 4: "tanh", 5: "sigmoid", 6: "selu", 7: "swish",
-        8: "relu_2"}
+# NetworkFormat.ActivationFunction -> name, as ActivationToString
+# (src/nn/network_format.cpp:50-70): every other value (NONE, SOFTMAX,
+# DEFAULT) reads "relu"
+_ACT = {1: "mish", 2: "relu", 4: "tanh", 5: "sigmoid", 6: "selu", 7: "swish", 8: "relu_2"}
+
+# NetworkFormat enum values used below
+_NET_CLASSICAL, _NET_SE, _NET_CLASSICAL_HF, _NET_SE_HF = 1, 2, 3, 4
+_NET_AB_HF, _NET_AB_MHF, _NET_AB_LEGACY_MHF = 6, 7, 134
+_POLICY_ATTENTION, _VALUE_WDL, _MOVES_LEFT_V1 = 3, 2, 1
+_EMB_PE_MAP, _EMB_PE_DENSE = 1, 2
 
 
 def _varint(buf: bytes, pos: int) -> Tuple[int, int]:
@@ -235,19 +243,55 @@ def _heads(t: Dict[str, np.ndarray]) -> Dict[str, np.ndarray]:
 
 
 def _activation(code: int, default: str) -> str:
-    # src/nn/network_format.cpp:101-123: ACTIVATION_DEFAULT takes the default
+    # src/nn/network_format.cpp:108-123: ACTIVATION_DEFAULT takes the default
     if code == 0:
         return default
-    if code not in _ACT:
-        raise RuntimeError(f"B200 backend: unsupported activation function {code}")
-    return _ACT[code]
+    return _ACT.get(code, "relu")
+
+
+def fix_older_format(scalars: Dict[str, int], t: Dict[str, np.ndarray]) -> Dict[str, int]:
+    """``FixOlderWeightsFile`` (``src/nn/loader.cpp:87-133``) on the
+    NetworkFormat fields (``format.network_format.*``; a missing field is
+    absent from `scalars`). Returns the fixed fields by bare name."""
+    nfp = "format.network_format."
+    has_nf = any(k.startswith(nfp) for k in scalars)
+    f = {k[len(nfp):]: v for k, v in scalars.items() if k.startswith(nfp)}
+    if not has_nf:
+        f.update(input=1, output=1, network=_NET_CLASSICAL_HF, value=1, policy=1)
+    net = f.get("network", 0)
+    has_encoder = any(k.startswith("encoder.") for k in t)
+    if net == _NET_CLASSICAL:
+        f.update(network=_NET_CLASSICAL_HF, value=1, policy=1)
+    elif net == _NET_SE:
+        f.update(network=_NET_SE_HF, value=1, policy=1)
+    elif net == _NET_SE_HF and has_encoder:
+        f["network"] = _NET_AB_HF
+        if "smolgen_w" in t:
+            f.update(ffn_activation=8, smolgen_activation=7)  # RELU_2, SWISH
+    elif net == _NET_AB_LEGACY_MHF:
+        f["network"] = _NET_AB_MHF
+    if f.get("network") == _NET_AB_HF:
+        if (any(k.startswith("policy_heads.") for k in t)
+                and any(k.startswith("value_heads.") for k in t)):
+            f.update(network=_NET_AB_MHF, input_embedding=_EMB_PE_DENSE)
+        if "input_embedding" not in f:
+            f["input_embedding"] = _EMB_PE_MAP
+    return f
+
+
+def _require(ok: bool, what: str) -> None:
+    if not ok:
+        raise RuntimeError("B200 backend does not support this network: " + what)
 
 
 def config_from_weights(t: Dict[str, np.ndarray], scalars: Dict[str, int],
+                        fmt: Dict[str, int], has_policy_heads: bool,
                         name: str = "pb") -> NetConfig:
     """The network shape from the tensor sizes (the C++ backend infers it the
     same way); raises RuntimeError for anything but the attention body with
-    PE_DENSE embedding, smolgen, attention policy, WDL and moves-left heads."""
+    PE_DENSE embedding, smolgen, attention policy, WDL and moves-left heads.
+    `t` holds the resolved head tensors (``_heads``), `fmt` the fixed-up
+    NetworkFormat (``fix_older_format`` of the file as read)."""
     def need(key: str) -> np.ndarray:
         if key not in t:
             raise RuntimeError(f"B200 backend: weight file lacks {key} (attention body with "
@@ -255,11 +299,24 @@ def config_from_weights(t: Dict[str, np.ndarray], scalars: Dict[str, int],
                                "moves-left heads required)")
         return t[key]
 
+    # the checks of the C++ backend (host/b200_network.cpp DescribeNet) on
+    # DescribeNetworkFormat (src/nn/network_format.cpp:73-125)
+    f = fmt
+    _require(f.get("network") in (_NET_AB_HF, _NET_AB_MHF), "not an attention-body network")
+    _require(f.get("policy") == _POLICY_ATTENTION, "policy head is not attention policy")
+    _require(f.get("value") == _VALUE_WDL and f.get("moves_left") == _MOVES_LEFT_V1,
+             "needs WDL value and moves-left heads")
+    _require(f.get("input_embedding", _EMB_PE_MAP) == _EMB_PE_DENSE,
+             "input embedding is not PE_DENSE")
+    _require(not any(k.startswith("policy_heads.vanilla.pol_encoder.") for k in t)
+             and (has_policy_heads or not any(k.startswith("pol_encoder.") for k in t)),
+             "policy-head encoder layers")
     layers = 0
     while f"encoder.{layers}.mha.q_w" in t:
         layers += 1
-    if layers == 0:
-        raise RuntimeError("B200 backend: not an attention-body network (no encoder layers)")
+    _require(layers > 0, "no encoder layers")
+    _require("encoder.0.mha.smolgen.compress" in t and t.get("smolgen_w", np.zeros(0)).size > 0,
+             "encoder without smolgen")
     heads = int(scalars.get("weights.headcount", 0))
     if heads <= 0:
         raise RuntimeError("B200 backend: weight file has no encoder head count")
@@ -267,8 +324,7 @@ def config_from_weights(t: Dict[str, np.ndarray], scalars: Dict[str, int],
     pe = need("ip_emb_preproc_b").size // 64
     sg = "encoder.0.mha.smolgen."
     hidden_x_heads = need(sg + "dense2_b").size
-    nf = "format.network_format."
-    default = "mish" if scalars.get(nf + "default_activation", 0) == 1 else "relu"
+    default = "mish" if f.get("default_activation", 0) == 1 else "relu"
     cfg = NetConfig(
         name=name, embedding=d, layers=layers, heads=heads,
         dff=need("encoder.0.ffn.dense1_b").size, emb_dff=need("ip_emb_ffn.dense1_b").size,
@@ -279,8 +335,8 @@ def config_from_weights(t: Dict[str, np.ndarray], scalars: Dict[str, int],
         value_hidden=need("value_heads.winner.ip1_val_b").size,
         mlh_emb=need("ip_mov_b").size, mlh_hidden=need("ip1_mov_b").size,
         default_activation=default,
-        smolgen_activation=_activation(scalars.get(nf + "smolgen_activation", 0), default),
-        ffn_activation=_activation(scalars.get(nf + "ffn_activation", 0), default))
+        smolgen_activation=_activation(f.get("smolgen_activation", 0), default),
+        ffn_activation=_activation(f.get("ffn_activation", 0), default))
     need("smolgen_w")
     need("policy_heads.vanilla.ip4_pol_w")
     need("value_heads.winner.ip2_val_w")
@@ -337,8 +393,10 @@ def load_weights(path: str, name: Optional[str] = None) -> Tuple[NetConfig, Dict
     ``.pb`` / ``.pb.gz`` file: returns the inferred ``NetConfig`` and the fp32
     tensors keyed by schema path, validated against the packed sizes."""
     tensors, scalars = parse_weights(_read_bytes(path))
+    fmt = fix_older_format(scalars, tensors)
+    has_policy_heads = any(k.startswith("policy_heads.") for k in tensors)
     t = _heads(tensors)
-    cfg = config_from_weights(t, scalars, name or path)
+    cfg = config_from_weights(t, scalars, fmt, has_policy_heads, name or path)
     out: Dict[str, np.ndarray] = {}
     missing: List[str] = []
     for key, n in expected_sizes(cfg).items():

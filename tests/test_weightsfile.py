@@ -134,9 +134,11 @@ SG = {"compress": 1, "dense1_w": 2, "dense1_b": 3, "ln1_gammas": 4, "ln1_betas":
 ENC = {"ln1_gammas": 2, "ln1_betas": 3, "ln2_gammas": 5, "ln2_betas": 6}
 
 
-def _legacy_file(cfg, t, magic=0x1C0):
+def _legacy_file(cfg, t, magic=0x1C0, network=4, input_embedding=2):
     """Single-head legacy layout: policy and value head layers at the top
-    level of Weights (no policy_heads / value_heads messages)."""
+    level of Weights (no policy_heads / value_heads messages), network
+    NETWORK_SE_WITH_HEADFORMAT (FixOlderWeightsFile turns it into an attention
+    body and forces RELU_2 / SWISH because smolgen_w is present)."""
     w = b""
     pv, vw = "policy_heads.vanilla.", "value_heads.winner."
     for k, num in W.items():
@@ -151,8 +153,11 @@ def _legacy_file(cfg, t, magic=0x1C0):
         enc = _ld(1, mha) + _ld(4, ffn) + b"".join(_ld(n, _layer_f16(t[p + k])) for k, n in ENC.items())
         w += _ld(27, enc)
     w += _vi(28, cfg.heads)
-    # default activation MISH, smolgen SWISH, ffn RELU_2
-    nf = _vi(7, 1) + _vi(8, 7) + _vi(9, 8)
+    # network, policy ATTENTION, value WDL, moves-left V1, default activation
+    # MISH, smolgen / ffn ACTIVATION_DEFAULT (fixed up), input embedding
+    nf = _vi(3, network) + _vi(4, 3) + _vi(5, 2) + _vi(6, 1) + _vi(7, 1)
+    if input_embedding is not None:
+        nf += _vi(10, input_embedding)
     return _varint(1 << 3 | 5) + struct.pack("<I", magic) + _ld(4, _ld(2, nf)) + _ld(10, w)
 
 
@@ -192,7 +197,7 @@ def test_missing_smolgen_is_rejected(tmp_path):
     t["smolgen_w"] = np.zeros(0, np.float32)  # an empty layer
     f = tmp_path / "nosg.pb"
     f.write_bytes(_legacy_file(cfg, t))
-    with pytest.raises(RuntimeError, match="smolgen_w"):
+    with pytest.raises(RuntimeError, match="smolgen"):
         load_weights(str(f))
 
 
@@ -215,3 +220,19 @@ def test_network_from_weight_file_matches_tensors(tmp_path, positions):
     np.testing.assert_array_equal(oa.policy, ob.policy)
     np.testing.assert_array_equal(oa.wdl, ob.wdl)
     np.testing.assert_array_equal(oa.moves_left, ob.moves_left)
+
+
+def test_format_checks_of_the_backend(tmp_path):
+    """The C++ backend's format requirements, after the reference's
+    FixOlderWeightsFile: a classical network and a file without the PE_DENSE
+    input embedding are refused."""
+    cfg = synthetic.TINY
+    t = synthetic.generate(cfg, 9)
+    f = tmp_path / "fmt.pb"
+    f.write_bytes(_legacy_file(cfg, t, network=1))
+    with pytest.raises(RuntimeError, match="not an attention-body network"):
+        load_weights(str(f))
+    f.write_bytes(_legacy_file(cfg, t, input_embedding=None))
+    with pytest.raises(RuntimeError, match="PE_DENSE"):
+        load_weights(str(f))
+
