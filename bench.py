@@ -27,6 +27,19 @@ batch is sharded, weights replicated, no collective in the forward
                 out; position encoding, forward, move mapping and softmax on
                 the GPU (the host-side encode of the reference evaluator is
                 gone).
+* int8 / fp8  -- the 8-bit configurations of the same forward at the same
+                batch (config 2): device-timed and end-to-end positions/s, and
+                the QKV GEMM's roofline against twice the bf16 tensor peak.
+                INT8 (signed 8-bit operands, per-row / per-channel scales)
+                meets the 8-bit parity bound; FP8-e4m3 in every encoder GEMM
+                does not (tests/test_bt4_bench_parity_gpu.py).
+* sweep        -- (1 GPU) config 3: ms per batch and positions/s of the bf16
+                forward at batch 1, 8, 32, 128, 512, 1024 and 4096.
+* config4      -- config 4: a global batch of 8192 split evenly over the N
+                GPUs (8192 / N per GPU), inputs from pinned host memory and
+                policy / WDL / moves-left gathered back to host memory every
+                step through mfb200_evaluate; whole-job positions/s from the
+                slowest rank's wall time.
 * cpu_baseline -- the reference CPU backend (oracle/_ref, built from the
                 reference sources) or, if that binary is absent, the C
                 restatement, on a bounded sample on the host cores.
@@ -144,11 +157,13 @@ def cpu_baseline(cfg, tensors, sample_positions: int | None = None):
             "sample": f"{n} positions, C restatement oracle (fp32), {threads} threads, {dt:.1f} s"}
 
 
-# DRAM bytes (read + write) of one QKV GEMM launch at batch 1024, from the
-# ncu capture named beside it (a M=16384 capture scaled by 4: traffic grows
-# with M). Part of the output is still in L2 when a launch ends.
+# DRAM bytes (read + write) of one QKV GEMM launch at batch 1024: an ncu
+# capture of the same kernel at M=16384 (batch 256; dram__bytes_read.sum +
+# dram__bytes_write.sum = 40.2 + 54.0 MB) scaled by 4 to M=65536, since the
+# operand and output bytes grow with M. Part of the output is still in L2
+# when a launch ends, so the write half is an upper estimate.
 QKV_TRAFFIC = {
-    "bf16": (4 * (40.235e6 + 53.987e6), "profiles/gemm_pair_qkv_m16384.md (x4 to M=65536)"),
+    "bf16": (4 * (40.235e6 + 53.987e6), "ncu capture at M=16384, scaled x4 to M=65536"),
 }
 
 
@@ -238,6 +253,8 @@ def main():
     ap.add_argument("--precision", default="bf16", choices=["bf16", "fp8"])
     ap.add_argument("--fp8-gemms", type=int, default=0, help="FP8 GEMM-group mask (0 = all)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--headline-only", action="store_true",
+                    help="skip the 8-bit, sweep and config-4 measurements")
     ap.add_argument("--sweep", default="",
                     help="comma-separated batch sizes: print one latency/throughput JSON line per "
                          "batch on 1 GPU instead of the contract line")
@@ -429,6 +446,14 @@ def main():
     # ---- batch-1 latency (the per-leaf MCTS case): device time of one
     # graph-launched forward, and the host round trip through mfb200_evaluate
     lat = batch1_latency(net, dev, stream, shard, L) if rank == 0 else None
+    net.close()
+    extra = {}
+    if args.precision == "bf16" and not args.headline_only:
+        for prec in ("int8", "fp8"):
+            extra[prec] = eight_bit_line(cfg, tensors, prec, B, local, dev, stream, shard, L, args, world)
+        if world == 1:
+            extra["sweep"] = run_sweep_rows(cfg, tensors, local, dev, stream, args)
+        extra["config4"] = run_config4(cfg, tensors, rank, local, world, args, L)
 
     # ---- roofline. Dominant kernel: the QKV(+smolgen compress) projection
     # GEMM, the largest single stage (15 launches per forward; the CTA-pair
@@ -497,10 +522,124 @@ def main():
             "stage_ms_total": total_stage_ms,
             "clocks": clocks,
         }
+        line.update(extra)
         if not args.no_cpu_baseline and world == 1:
             line["cpu_baseline"] = cpu_baseline(cfg, tensors)
         print(json.dumps(line), flush=True)
+
+
+def device_ms(net, dev, stream, shard, B, steps, warmup, world):
+    """Device time (CUDA events on the launching stream, max over ranks) of
+    `steps` forwards at batch B with the inputs resident in HBM."""
+    import torch
+    d_m = torch.from_numpy(shard.masks[:B].view(np.int64)).to(dev)
+    d_v = torch.from_numpy(shard.values[:B]).to(dev)
+    d_p = torch.empty((B, 1858), dtype=torch.float32, device=dev)
+    d_w = torch.empty((B, 3), dtype=torch.float32, device=dev)
+    d_l = torch.empty((B,), dtype=torch.float32, device=dev)
+
+    def step():
+        net.evaluate_device(d_m.data_ptr(), d_v.data_ptr(), B, d_p.data_ptr(), d_w.data_ptr(),
+                            d_l.data_ptr(), stream.cuda_stream)
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    return all_max(e0.elapsed_time(e1), world)
+
+
+def host_s(net, L, shard, B, steps, warmup, world):
+    """Wall time (max over ranks) of `steps` host round trips through
+    mfb200_evaluate: pinned inputs copied in, all outputs copied back."""
+    import torch
+    pin_m = torch.from_numpy(shard.masks[:B].view(np.int64)).pin_memory()
+    pin_v = torch.from_numpy(shard.values[:B]).pin_memory()
+    h_pol = torch.empty((B, 1858), dtype=torch.float32).pin_memory()
+    h_wdl = torch.empty((B, 3), dtype=torch.float32).pin_memory()
+    h_mlh = torch.empty((B,), dtype=torch.float32).pin_memory()
+
+    def step():
+        rc = L.mfb200_evaluate(net._h, pin_m.data_ptr(), pin_v.data_ptr(), B, h_pol.data_ptr(),
+                               h_wdl.data_ptr(), h_mlh.data_ptr(), None)
+        if rc:
+            raise RuntimeError(L.mfb200_last_error(net._h).decode())
+
+    for _ in range(warmup):
+        step()
+    barrier(world)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        step()
+    dt = all_max(time.perf_counter() - t0, world)
+    barrier(world)
+    return dt
+
+
+def eight_bit_line(cfg, tensors, precision, B, local, dev, stream, shard, L, args, world):
+    """Config 2: the 8-bit forward at the headline batch."""
+    from metalfish_b200.network import create_network
+    net = create_network(cfg, tensors, device=local, max_batch=B, precision=precision,
+                         calibration=load_positions(2048).slice(1024, 2048))
+    ms = device_ms(net, dev, stream, shard, B, args.steps, args.warmup, world)
+    e2e = host_s(net, L, shard, B, args.steps, args.warmup, world)
+    stages = net.profile(B, iters=3)
     net.close()
+    burst, sustained, src = measured_peaks()
+    qkv = [(m, f) for (n, m, f) in stages if n == "qkv"]
+    q_ms, q_fl = sum(m for m, _ in qkv), sum(f for _, f in qkv)
+    achieved = q_fl / (q_ms / 1e3) / 1e12 if q_ms > 0 else 0.0
+    enc = cfg.flops_per_position()["encoder_gemm_flops"]
+    value = B * world * args.steps / (ms / 1e3)
+    return {"value": value, "unit": "positions/s", "ms_per_step": ms / args.steps,
+            "dtype": "s8 operands, s32 accumulate" if precision == "int8" else "e4m3 operands, f32 accumulate",
+            "e2e": {"value": B * world * args.steps / e2e, "unit": "positions/s"},
+            "parity": ("meets the 8-bit bound (top-1 >= 99%, |dWDL| <= 2e-2)" if precision == "int8"
+                       else "misses the 8-bit |dWDL| bound (e4m3 mantissa noise, ~0.05)"),
+            "roofline": {"bound": "tensor", "kernel": "QKV+compress GEMM", "achieved": achieved,
+                         "peak": 2.0 * sustained, "unit": "TFLOP/s",
+                         "frac": achieved / (2.0 * sustained),
+                         "peak_source": f"2 x {src} bf16_tflops_sustained (8-bit dense = 2x bf16)"},
+            "encoder_tflops_per_gpu": value * enc / 1e12 / world,
+            "frac_of_bf16_burst": value * enc / 1e12 / world / burst,
+            "stage_ms": stage_summary(stages)}
+
+
+def run_sweep_rows(cfg, tensors, local, dev, stream, args, batches=(1, 8, 32, 128, 512, 1024, 4096)):
+    """Config 3 on one GPU: device ms per batch and positions/s (bf16)."""
+    from metalfish_b200.network import create_network
+    net = create_network(cfg, tensors, device=local, max_batch=max(batches))
+    inp = load_positions(max(batches))
+    rows = {}
+    for B in batches:
+        steps = max(5, min(args.steps, 20))
+        ms = device_ms(net, dev, stream, inp, B, steps, args.warmup, 1) / steps
+        rows[str(B)] = {"ms": ms, "positions_per_s": B / (ms / 1e3)}
+    net.close()
+    return rows
+
+
+def run_config4(cfg, tensors, rank, local, world, args, L, global_batch=8192):
+    """Config 4: global batch split evenly over the ranks, host round trips."""
+    from metalfish_b200.network import create_network
+    per = global_batch // world
+    net = create_network(cfg, tensors, device=local, max_batch=per)
+    inp = load_positions(global_batch).slice(rank * per, (rank + 1) * per)
+    steps = max(3, min(args.steps, 10))
+    dt = host_s(net, L, inp, per, steps, args.warmup, world)
+    net.close()
+    return {"global_batch": global_batch, "per_gpu": per, "n_gpus": world, "steps": steps,
+            "value": global_batch * steps / dt, "unit": "positions/s",
+            "ms_per_step": dt / steps * 1e3,
+            "timing": "wall time of mfb200_evaluate round trips (pinned H2D of the packed planes, "
+                      "forward, D2H of policy / WDL / moves-left), max over ranks"}
 
 
 def batch1_latency(net, dev, stream, shard, L, iters: int = 200):

@@ -62,7 +62,14 @@ enum {
   MFB200_ACT_NONE = 0, MFB200_ACT_RELU = 1, MFB200_ACT_RELU2 = 2, MFB200_ACT_TANH = 3,
   MFB200_ACT_SIGMOID = 4, MFB200_ACT_SWISH = 5, MFB200_ACT_MISH = 6, MFB200_ACT_SELU = 7
 };
-enum { MFB200_PRECISION_BF16 = 0, MFB200_PRECISION_FP8 = 1 };
+/* BF16: bf16/fp16 tensor-core GEMMs throughout. FP8: the encoder and
+ * embedding-FFN GEMMs in e4m3 with per-output-channel weight scales and
+ * calibrated per-tensor activation scales. INT8: the same GEMMs at the same
+ * 8-bit tensor-core rate with signed 8-bit integer operands: per-output-channel
+ * weight scales, per-row (per-square) activation scales computed when the
+ * LayerNorm writes the input, calibrated per-tensor scales for the attention
+ * context; int32 accumulation. */
+enum { MFB200_PRECISION_BF16 = 0, MFB200_PRECISION_FP8 = 1, MFB200_PRECISION_INT8 = 2 };
 
 /* Shape of an attention-body network with PE_DENSE input embedding, smolgen,
  * attention policy, WDL value and moves-left heads (the BT4 family). */
@@ -88,8 +95,12 @@ typedef struct {
   int32_t precision;  /* MFB200_PRECISION_* */
   int32_t max_batch;  /* largest batch one evaluate call accepts */
   int32_t use_graphs; /* capture one CUDA graph per batch size (1) or launch eagerly (0) */
-  int32_t fp8_gemms;  /* FP8 handles: GEMM groups run in e4m3 (bit mask: 1 embedding FFN,
-                         2 QKV, 4 attention output, 8 FFN1, 16 FFN2; 0 = all) */
+  int32_t fp8_gemms;  /* FP8 / INT8 handles: GEMM groups run with 8-bit operands (bit mask:
+                         2 QKV, 4 attention output, 8 FFN1, 16 FFN2; 1 the embedding FFN --
+                         both of its GEMMs in FP8 handles, its first in INT8 handles, whose
+                         bit 16 also covers the embedding FFN2). 0 = the default: every group
+                         in FP8 handles; 1|2|4|8 in INT8 handles (the two GEMMs that read the
+                         FFN hidden stay bf16) */
 } mfb200_config;
 
 typedef struct {
@@ -229,7 +240,7 @@ MFB200_API int mfb200_evaluate_device(mfb200_handle *h, const uint64_t *d_masks,
                            int batch, float *d_policy, float *d_wdl, float *d_moves_left,
                            void *stream);
 
-/* FP8 handles only: set the per-tensor activation scales from the absmax of
+/* FP8 / INT8 handles only: set the per-tensor activation scales from the absmax of
  * a bf16 forward over `count` calibration positions (host buffers). Must be
  * called before the first FP8 evaluation. */
 MFB200_API int mfb200_calibrate(mfb200_handle *h, const uint64_t *masks, const float *values, int count);

@@ -165,6 +165,18 @@ extern "C" int mfb200_debug_gemm_bench(int M, int N, int K, int bn, int mode, in
     a.cluster_n = N / bn;
     a.row_stats = static_cast<float2 *>(dRS.p);
   }
+  if (mode == kEpiResidNorm) {  // deferred-LayerNorm residual GEMM: fp16 stream in place
+    a.out_f32 = 0;
+    a.out_f16 = 1;
+    a.resid16 = static_cast<const __half *>(dO.p);
+    a.ldr16 = N;
+    a.rn_stats = reinterpret_cast<const float2 *>(dRS.p);  // (0, 0): normalised residual = beta
+    a.rn_gamma = static_cast<float *>(dG.p);
+    a.rn_beta = static_cast<float *>(dG.p);
+    a.stats_out = reinterpret_cast<float2 *>(dR.p);
+    a.ln_eps = 1e-3f;
+    cudaMemset(dRS.p, 0, size_t(M) * 8);
+  }
   GemmLaunch g;
   if (plan_gemm(g, dA.p, K, dW.p, K, bn, dtype == 1, a)) return 2;
   for (int i = 0; i < 2; ++i)

@@ -244,7 +244,8 @@ __global__ void __launch_bounds__(256)
     v += x3;
   }
   for (; s < splits; ++s) v += __ldcg(p + s * stride);
-  const float as = a.a_scale_ptr ? a.a_scale * __ldg(a.a_scale_ptr) : a.a_scale;
+  float as = a.a_scale_ptr ? a.a_scale * __ldg(a.a_scale_ptr) : a.a_scale;
+  if (a.a_row_scale) as *= __ldcg(a.a_row_scale + row);
   if (as != 1.0f) v *= as;
   if (a.fold_stats) {
     const float2 st = __ldcg(a.fold_stats + row);
@@ -291,7 +292,10 @@ __global__ void __launch_bounds__(256)
     static_cast<float *>(base)[idx] = v;
   } else if (a.out_fp8) {
     const float is = a.out_scale_ptr ? 1.0f / __ldg(a.out_scale_ptr) : a.out_inv_scale;
-    static_cast<__nv_fp8_e4m3 *>(base)[idx] = __nv_fp8_e4m3(v * is);
+    if (a.out_i8)
+      static_cast<int8_t *>(base)[idx] = static_cast<int8_t>(quant_s8(v * is));
+    else
+      static_cast<__nv_fp8_e4m3 *>(base)[idx] = __nv_fp8_e4m3(v * is);
   } else if (a.out_f16) {
     static_cast<__half *>(base)[idx] = __float2half_rn(v);
   } else {
@@ -355,7 +359,7 @@ __global__ void __launch_bounds__(1024)
 cudaError_t launch_splitk_epilogue(const float *part, int splits, const GemmArgs &a,
                                    cudaStream_t stream) {
   if (a.mode == kEpiResidNorm && a.stats_final && a.N <= 1024 && a.N % 32 == 0 &&
-      a.a_scale == 1.0f && !a.a_scale_ptr && !a.col_scale && !a.fold_stats)
+      a.a_scale == 1.0f && !a.a_scale_ptr && !a.a_row_scale && !a.col_scale && !a.fold_stats)
     return launch_k(splitk_residnorm_row_kernel, dim3(static_cast<unsigned>(a.M)),
                     dim3(static_cast<unsigned>(a.N)), 0, stream, 1, part, splits,
                     static_cast<long long>(a.M) * a.N, a);
@@ -382,6 +386,9 @@ const char *plan_gemm(GemmLaunch &g, const void *A, long long lda_elems, const v
   if (args.mode == kEpiAccum && ((!args.out_f32 && !args.out_f16) || args.out2 || args.out_fp8))
     return "gemm: the accumulate epilogue adds into one fp32 or fp16 output";
   if (args.out_f16 && (args.out_f32 || args.out_fp8)) return "gemm: one output format";
+  if (args.ab_i8 && (!fp8 || args.mode == kEpiResidLN))
+    return "gemm: 8-bit integer operands need the 8-bit kernels (no LN epilogue)";
+  if (args.out_i8 && !args.out_fp8) return "gemm: integer 8-bit output is an 8-bit output (out_fp8)";
   if (args.mode == kEpiResidNorm) {
     if (!args.out_f16 || args.out2 || args.k_splits > 1 || !args.resid16 || !args.stats_out)
       return "gemm: the residual-norm epilogue writes one fp16 output and its row statistics "

@@ -48,6 +48,11 @@ enum Act : int {
 struct GemmArgs {
   int M, N, K;
   int ab_f16;                 // 16-bit operands are fp16 (else bf16); both A and W
+  int ab_i8;                  // 8-bit operands are signed integers (kind::i8, int32
+                              // accumulator converted to float) instead of e4m3
+  const float *a_row_scale;   // if set: the accumulator of row m is multiplied by a_row_scale[m]
+                              // (per-row dequantisation scale of 8-bit integer activations)
+  int out_i8;                 // store signed 8-bit integers round(v / *out_scale_ptr), saturated
   int mode, act;
   const float *bias;          // [N] or nullptr
   void *out;                  // [M, ldo] bf16 (or e4m3 / fp32)
@@ -156,12 +161,15 @@ struct EpiCtx {
   uint32_t chunks;     // chunks staged so far (selects the half of a 2-byte-output tile)
   uint32_t res_issued; // residual loads issued (kEpiResidNorm prefetch)
   float2 rowst;        // deferred LayerNorm: this lane's row (mean, rstd), loaded by epi_pre
+  float arow;          // this lane's row scale (args.a_row_scale), loaded by epi_pre
 };
 
 // Deferred LayerNorm, issued before the accumulator wait so that the latency
 // overlaps the mainloop: this lane's row (mean, rstd) and, into L1, the
 // tile's gamma / beta / column-sum lines.
 __device__ __forceinline__ void epi_pre(const GemmArgs &args, EpiCtx &e, int row0, int n0, int bn) {
+  if (args.a_row_scale)
+    e.arow = __ldcg(args.a_row_scale + (row0 + e.lane < args.M ? row0 + e.lane : args.M - 1));
   const float2 *st = args.mode == kEpiResidNorm ? args.rn_stats : args.fold_stats;
   if (!st) return;
   const int row = row0 + e.lane < args.M ? row0 + e.lane : args.M - 1;
@@ -220,6 +228,12 @@ __device__ __forceinline__ uint32_t pack_f16x2_f(float a, float b) {
   return *reinterpret_cast<const uint32_t *>(&h);
 }
 
+// Round to the nearest integer (ties to even) and saturate to [-127, 127].
+__device__ __forceinline__ int quant_s8(float x) {
+  const int r = __float2int_rn(x);
+  return r > 127 ? 127 : (r < -127 ? -127 : r);
+}
+
 __device__ __forceinline__ void stage_row(const GemmArgs &args, uint8_t *st, int r,
                                           const float (&v)[32], bool f32, float out_is) {
   if (f32) {
@@ -237,8 +251,14 @@ __device__ __forceinline__ void stage_row(const GemmArgs &args, uint8_t *st, int
         uint32_t x = 0;
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const __nv_fp8_e4m3 f(v[16 * q + 4 * k + e] * is);
-          x |= static_cast<uint32_t>(f.__x) << (8 * e);
+          uint32_t byte;
+          if (args.out_i8) {
+            byte = static_cast<uint32_t>(quant_s8(v[16 * q + 4 * k + e] * is)) & 0xFFu;
+          } else {
+            const __nv_fp8_e4m3 f(v[16 * q + 4 * k + e] * is);
+            byte = f.__x;
+          }
+          x |= byte << (8 * e);
         }
         w[k] = x;
       }
@@ -303,8 +323,13 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs &args, EpiCtx &e, u
     if (!PREFETCH) tmem_ld32(taddr + c, raw);
     tmem_wait_ld();
     float v[32];
+    if (args.ab_i8) {
 #pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(raw[j]);
+      for (int j = 0; j < 32; ++j) v[j] = static_cast<float>(static_cast<int>(raw[j]));
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(raw[j]);
+    }
     if (PREFETCH && c + STEP < BN) tmem_ld32(taddr + c + STEP, raw);  // warp-collective prefetch
     const int nb = n0 + c;
     if (nb >= args.N) continue;
@@ -322,9 +347,10 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs &args, EpiCtx &e, u
       __syncwarp();
     }
     if (ks < 0) {
-      if (a_scale != 1.0f) {
+      const float as = args.a_row_scale ? a_scale * e.arow : a_scale;
+      if (as != 1.0f) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] *= a_scale;
+        for (int j = 0; j < 32; ++j) v[j] *= as;
       }
       if (fold) {
         const float4 *cs = reinterpret_cast<const float4 *>(args.fold_colsum + nb);
@@ -744,7 +770,8 @@ __global__ void __launch_bounds__(64 + 32 * (LN ? kEpiWarpsLN : kEpiWarpsMax), 1
   } else if (warp == 1) {
     if (lane == 0) {
       // ---------------------------------------------------------- MMA issuer
-      const uint32_t idesc = FP8 ? umma_idesc(128, BN, kFmtE4M3, kFmtE4M3)
+      const bool i8 = FP8 && args.ab_i8;
+      const uint32_t idesc = FP8 ? (i8 ? umma_idesc_s8(128, BN) : umma_idesc(128, BN, kFmtE4M3, kFmtE4M3))
                                  : (args.ab_f16 ? umma_idesc(128, BN, kFmtF16, kFmtF16)
                                                 : umma_idesc(128, BN, kFmtBF16, kFmtBF16));
       int stage = 0;
@@ -774,7 +801,9 @@ __global__ void __launch_bounds__(64 + 32 * (LN ? kEpiWarpsLN : kEpiWarpsMax), 1
           for (int kk = 0; kk < 4; ++kk) {
             // advance 32 bytes along K inside the 128-byte swizzled row
             const uint32_t accumulate = (kb > kb0 || kk > 0) ? 1u : 0u;
-            if (FP8)
+            if (FP8 && i8)
+              umma_i8(d, ad + 2 * kk, bd + 2 * kk, idesc, accumulate);
+            else if (FP8)
               umma_f8(d, ad + 2 * kk, bd + 2 * kk, idesc, accumulate);
             else
               umma_f16(d, ad + 2 * kk, bd + 2 * kk, idesc, accumulate);
@@ -991,7 +1020,8 @@ __global__ void __launch_bounds__(64 + 32 * kEpiWarpsMax, 1)
   } else if (warp == 1) {
     if (lane == 0 && rank == 0) {
       // ---------------------------------------------------------- MMA issuer
-      const uint32_t idesc = FP8 ? umma_idesc(256, BN, kFmtE4M3, kFmtE4M3)
+      const bool i8 = FP8 && args.ab_i8;
+      const uint32_t idesc = FP8 ? (i8 ? umma_idesc_s8(256, BN) : umma_idesc(256, BN, kFmtE4M3, kFmtE4M3))
                                  : (args.ab_f16 ? umma_idesc(256, BN, kFmtF16, kFmtF16)
                                                 : umma_idesc(256, BN, kFmtBF16, kFmtBF16));
       int stage = 0;
@@ -1019,7 +1049,9 @@ __global__ void __launch_bounds__(64 + 32 * kEpiWarpsMax, 1)
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {
             const uint32_t accumulate = (kb > 0 || kk > 0) ? 1u : 0u;
-            if (FP8)
+            if (FP8 && i8)
+              umma_i8_pair(d, ad + 2 * kk, bd + 2 * kk, idesc, accumulate);
+            else if (FP8)
               umma_f8_pair(d, ad + 2 * kk, bd + 2 * kk, idesc, accumulate);
             else
               umma_f16_pair(d, ad + 2 * kk, bd + 2 * kk, idesc, accumulate);

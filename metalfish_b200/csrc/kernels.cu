@@ -19,6 +19,15 @@ void set_pdl(bool enable) { g_pdl = enable; }
 
 
 // ------------------------------------------------------------------ helpers
+// Two values rounded to the nearest integer and saturated to [-127, 127],
+// as the low and high byte of a 16-bit word.
+__device__ __forceinline__ uint16_t pack_s8x2(float a, float b) {
+  int x = __float2int_rn(a), y = __float2int_rn(b);
+  x = x > 127 ? 127 : (x < -127 ? -127 : x);
+  y = y > 127 ? 127 : (y < -127 ? -127 : y);
+  return static_cast<uint16_t>((static_cast<uint32_t>(x) & 0xFFu) | ((static_cast<uint32_t>(y) & 0xFFu) << 8));
+}
+
 __device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
   const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
   return *reinterpret_cast<const uint32_t *>(&h);
@@ -167,7 +176,7 @@ __global__ void __launch_bounds__(256)
                           float eps, const float *__restrict__ multT,
                           const float *__restrict__ addT, __nv_bfloat16 *__restrict__ out,
                           void *__restrict__ out_res, uint8_t *__restrict__ out8,
-                          const float *__restrict__ scale8) {
+                          const float *__restrict__ scale8, float *__restrict__ row_scale8) {
   pdl_wait();
   pdl_launch();
   constexpr int W = 32 * VPL;
@@ -196,7 +205,8 @@ __global__ void __launch_bounds__(256)
   for (int o = 16; o; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
   const float inv = 1.0f / sqrtf(sq / static_cast<float>(W) + eps);
   const int sqr = static_cast<int>(row % kSquares);
-  const float inv8 = out8 ? 1.0f / __ldg(scale8) : 0.0f;
+  const bool e4m3 = out8 && !row_scale8;
+  const float inv8 = e4m3 ? 1.0f / __ldg(scale8) : 0.0f;
 #pragma unroll
   for (int q = 0; q < NG; ++q) {
     const int c = q * 32 * G + lane * G;
@@ -212,6 +222,8 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
       for (int e = 0; e < G; ++e) r[e] = r[e] * mt[e] + at[e];
     }
+#pragma unroll
+    for (int e = 0; e < G; ++e) v[q * G + e] = r[e];  // kept for the 8-bit integer copy
     const long long o = row * W + c;
     if (out) {
       uint32_t w[G / 2];
@@ -220,7 +232,7 @@ __global__ void __launch_bounds__(256)
       if constexpr (G == 8) *reinterpret_cast<uint4 *>(out + o) = make_uint4(w[0], w[1], w[2], w[3]);
       else *reinterpret_cast<uint2 *>(out + o) = make_uint2(w[0], w[1]);
     }
-    if (out8) {
+    if (e4m3) {
       uint32_t w[G / 4];
 #pragma unroll
       for (int k = 0; k < G / 4; ++k) {
@@ -249,6 +261,37 @@ __global__ void __launch_bounds__(256)
         for (int k = 0; k < G / 4; ++k)
           dst[k] = make_float4(r[4 * k], r[4 * k + 1], r[4 * k + 2], r[4 * k + 3]);
       }
+    }
+  }
+  if (out8 && row_scale8) {
+    // 8-bit integer copy with a per-row scale: absmax / 127, values rounded
+    // to the nearest integer (the GEMM multiplies its int32 accumulator of
+    // the row by this scale)
+    float amax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) amax = fmaxf(amax, fabsf(v[i]));
+#pragma unroll
+    for (int o = 16; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float scale = fmaxf(amax, 1e-20f) * (1.0f / 127.0f);
+    const float is = 1.0f / scale;
+    if (lane == 0) row_scale8[row] = scale;
+#pragma unroll
+    for (int q = 0; q < NG; ++q) {
+      const long long o = row * W + q * 32 * G + lane * G;
+      uint32_t w[G / 4];
+#pragma unroll
+      for (int k = 0; k < G / 4; ++k) {
+        uint32_t x = 0;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          int t = __float2int_rn(v[q * G + 4 * k + e] * is);
+          t = t > 127 ? 127 : (t < -127 ? -127 : t);
+          x |= (static_cast<uint32_t>(t) & 0xFFu) << (8 * e);
+        }
+        w[k] = x;
+      }
+      if constexpr (G == 8) *reinterpret_cast<uint2 *>(out8 + o) = make_uint2(w[0], w[1]);
+      else *reinterpret_cast<uint32_t *>(out8 + o) = w[0];
     }
   }
 }
@@ -320,28 +363,30 @@ __global__ void __launch_bounds__(256)
 template <int VPL, Fmt IN>
 static void ln_warp_in(const void *in, int rows, const float *gamma, const float *beta, float eps,
                        const float *multT, const float *addT, __nv_bfloat16 *out, void *out_res,
-                       Fmt res_fmt, uint8_t *out8, const float *scale8, cudaStream_t s) {
+                       Fmt res_fmt, uint8_t *out8, const float *scale8, float *row_scale8,
+                       cudaStream_t s) {
   const int wpb = 8;
   const unsigned grid = static_cast<unsigned>((rows + wpb - 1) / wpb);
   if (res_fmt == Fmt::F16)
-    launch_k(layernorm_warp_kernel<VPL, IN, Fmt::F16>, dim3(grid), dim3(32 * wpb), 0, s, 1, in, rows, gamma, beta, eps, multT, addT, out, out_res, out8, scale8);
+    launch_k(layernorm_warp_kernel<VPL, IN, Fmt::F16>, dim3(grid), dim3(32 * wpb), 0, s, 1, in, rows, gamma, beta, eps, multT, addT, out, out_res, out8, scale8, row_scale8);
   else
-    launch_k(layernorm_warp_kernel<VPL, IN, Fmt::F32>, dim3(grid), dim3(32 * wpb), 0, s, 1, in, rows, gamma, beta, eps, multT, addT, out, out_res, out8, scale8);
+    launch_k(layernorm_warp_kernel<VPL, IN, Fmt::F32>, dim3(grid), dim3(32 * wpb), 0, s, 1, in, rows, gamma, beta, eps, multT, addT, out, out_res, out8, scale8, row_scale8);
 }
 
 template <int VPL>
 static void ln_warp(const void *in, Fmt in_fmt, int rows, const float *gamma, const float *beta,
                     float eps, const float *multT, const float *addT, __nv_bfloat16 *out,
-                    void *out_res, Fmt res_fmt, uint8_t *out8, const float *scale8, cudaStream_t s) {
+                    void *out_res, Fmt res_fmt, uint8_t *out8, const float *scale8,
+                    float *row_scale8, cudaStream_t s) {
   switch (in_fmt) {
   case Fmt::F32:
-    ln_warp_in<VPL, Fmt::F32>(in, rows, gamma, beta, eps, multT, addT, out, out_res, res_fmt, out8, scale8, s);
+    ln_warp_in<VPL, Fmt::F32>(in, rows, gamma, beta, eps, multT, addT, out, out_res, res_fmt, out8, scale8, row_scale8, s);
     return;
   case Fmt::F16:
-    ln_warp_in<VPL, Fmt::F16>(in, rows, gamma, beta, eps, multT, addT, out, out_res, res_fmt, out8, scale8, s);
+    ln_warp_in<VPL, Fmt::F16>(in, rows, gamma, beta, eps, multT, addT, out, out_res, res_fmt, out8, scale8, row_scale8, s);
     return;
   default:
-    ln_warp_in<VPL, Fmt::BF16>(in, rows, gamma, beta, eps, multT, addT, out, out_res, res_fmt, out8, scale8, s);
+    ln_warp_in<VPL, Fmt::BF16>(in, rows, gamma, beta, eps, multT, addT, out, out_res, res_fmt, out8, scale8, row_scale8, s);
     return;
   }
 }
@@ -394,8 +439,8 @@ void launch_row_stats(const float2 *part, int rows, int width, float eps, float2
 void launch_layernorm_q(const void *in, Fmt in_fmt, int rows, int width, const float *gamma,
                         const float *beta, float eps, const float *multT, const float *addT,
                         __nv_bfloat16 *out, void *out_res, Fmt res_fmt, uint8_t *out8,
-                        const float *scale8, cudaStream_t s) {
-#define MFB_LN(V) ln_warp<V>(in, in_fmt, rows, gamma, beta, eps, multT, addT, out, out_res, res_fmt, out8, scale8, s)
+                        const float *scale8, cudaStream_t s, float *row_scale8) {
+#define MFB_LN(V) ln_warp<V>(in, in_fmt, rows, gamma, beta, eps, multT, addT, out, out_res, res_fmt, out8, scale8, row_scale8, s)
   switch (width) {
   case 128: MFB_LN(4); return;
   case 256: MFB_LN(8); return;
@@ -515,7 +560,7 @@ __global__ void __launch_bounds__(128)
     attention_kernel(const __nv_bfloat16 *__restrict__ qkv, long long ldq,
                      const __nv_bfloat16 *__restrict__ bias, int heads, int d,
                      __nv_bfloat16 *__restrict__ ctx, uint8_t *__restrict__ ctx8,
-                     const float *__restrict__ scale8) {
+                     const float *__restrict__ scale8, int ctx_i8) {
   pdl_wait();
   pdl_launch();
   __shared__ __align__(16) __nv_bfloat16 sQ[kSquares * kQkvStride];
@@ -636,8 +681,20 @@ __global__ void __launch_bounds__(128)
   }
   const long long base_off = (static_cast<long long>(b) * kSquares + q0) * d + h * kDh;
   if (ctx8) {
-    // e4m3 context for an FP8 output projection: value / *scale8
+    // 8-bit context for an 8-bit output projection: value / *scale8 as e4m3
+    // or (ctx_i8) as a saturated signed integer
     const float inv = 1.0f / __ldg(scale8);
+    if (ctx_i8) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int col = 8 * j + 2 * t;
+        const uint16_t lo = pack_s8x2(O[j][0] * inv, O[j][1] * inv);
+        const uint16_t hi = pack_s8x2(O[j][2] * inv, O[j][3] * inv);
+        *reinterpret_cast<uint16_t *>(ctx8 + base_off + static_cast<long long>(g) * d + col) = lo;
+        *reinterpret_cast<uint16_t *>(ctx8 + base_off + static_cast<long long>(g + 8) * d + col) = hi;
+      }
+      return;
+    }
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const int col = 8 * j + 2 * t;
@@ -661,8 +718,8 @@ __global__ void __launch_bounds__(128)
 
 void launch_attention(const __nv_bfloat16 *qkv, long long ldq, const __nv_bfloat16 *bias,
                       int batch, int heads, int d, __nv_bfloat16 *ctx, cudaStream_t s,
-                      uint8_t *ctx8, const float *scale8) {
-  launch_k(attention_kernel, dim3(batch * heads), dim3(128), 0, s, 1, qkv, ldq, bias, heads, d, ctx, ctx8, scale8);
+                      uint8_t *ctx8, const float *scale8, int ctx_i8) {
+  launch_k(attention_kernel, dim3(batch * heads), dim3(128), 0, s, 1, qkv, ldq, bias, heads, d, ctx, ctx8, scale8, ctx_i8);
 }
 
 // ------------------------------------------------------------------ legal-move priors
@@ -818,16 +875,17 @@ void launch_absmax(const void *x, Fmt fmt, long long n, float *slot, cudaStream_
     launch_k(absmax_kernel<__nv_bfloat16>, dim3(296), dim3(256), 0, s, 1, static_cast<const __nv_bfloat16 *>(x), n, slot);
 }
 
-// scales[i] = max(absmax[i], tiny) / 448 (e4m3's largest finite value)
-__global__ void absmax_to_scale_kernel(const float *absmax, int n, float *scales) {
+// scales[i] = max(absmax[i], tiny) / qmax (448, e4m3's largest finite value,
+// or 127 for signed 8-bit integers)
+__global__ void absmax_to_scale_kernel(const float *absmax, int n, float *scales, float qmax) {
   pdl_wait();
   pdl_launch();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i < n) scales[i] = fmaxf(absmax[i], 1e-6f) / 448.0f;
+  if (i < n) scales[i] = fmaxf(absmax[i], 1e-6f) / qmax;
 }
 
-void launch_absmax_to_scale(const float *absmax, int n, float *scales, cudaStream_t s) {
-  launch_k(absmax_to_scale_kernel, dim3((n + 127) / 128), dim3(128), 0, s, 1, absmax, n, scales);
+void launch_absmax_to_scale(const float *absmax, int n, float *scales, cudaStream_t s, float qmax) {
+  launch_k(absmax_to_scale_kernel, dim3((n + 127) / 128), dim3(128), 0, s, 1, absmax, n, scales, qmax);
 }
 
 // ------------------------------------------------------------------ policy

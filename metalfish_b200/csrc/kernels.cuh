@@ -56,15 +56,16 @@ void launch_row_stats(const float2 *part, int rows, int width, float eps, float2
 void launch_layernorm_q(const void *in, Fmt in_fmt, int rows, int width, const float *gamma,
                         const float *beta, float eps, const float *multT, const float *addT,
                         __nv_bfloat16 *out, void *out_res, Fmt res_fmt, uint8_t *out8,
-                        const float *scale8, cudaStream_t s);
+                        const float *scale8, cudaStream_t s, float *row_scale8 = nullptr);
 
 // 64-token attention per (position, head) with the smolgen bias added before
 // the softmax: ctx[b*64+q, h*dh:..] = softmax(Q K^T / sqrt(dh) + bias) V.
 // qkv: [B*64, ldq] with Q at column 0, K at d, V at 2d. bias: [B*H, 4096].
-// With ctx8 set, the context is written as e4m3 (value / *scale8) instead.
+// With ctx8 set, the context is written as e4m3 (value / *scale8) instead,
+// or with ctx_i8 as signed 8-bit integers round(value / *scale8), saturated.
 void launch_attention(const __nv_bfloat16 *qkv, long long ldq, const __nv_bfloat16 *bias,
                       int batch, int heads, int d, __nv_bfloat16 *ctx, cudaStream_t s,
-                      uint8_t *ctx8 = nullptr, const float *scale8 = nullptr);
+                      uint8_t *ctx8 = nullptr, const float *scale8 = nullptr, int ctx_i8 = 0);
 
 }  // namespace mfb200
 extern "C" {
@@ -93,7 +94,8 @@ void launch_leaf_priors(const float *policy, int batch, const int32_t *offsets,
 // FP8 calibration: *slot = max(*slot, max|x|) over n values of format `fmt`;
 // and scales[i] = absmax[i] / 448.
 void launch_absmax(const void *x, Fmt fmt, long long n, float *slot, cudaStream_t s);
-void launch_absmax_to_scale(const float *absmax, int n, float *scales, cudaStream_t s);
+void launch_absmax_to_scale(const float *absmax, int n, float *scales, cudaStream_t s,
+                            float qmax = 448.0f);
 
 // Attention-policy logits: raw = q k^T / sqrt(dp) (64x64), the 8x24 promotion
 // logits, gathered onto the 1858 moves. qk: [B*64, 2*dp] (q | k);

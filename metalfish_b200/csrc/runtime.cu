@@ -213,17 +213,18 @@ std::vector<int16_t> build_move_index() {
 }
 
 // ------------------------------------------------------------ device state
-struct Mat {  // a weight matrix [rows, ld] on the device (bf16, fp16 or e4m3)
+struct Mat {  // a weight matrix [rows, ld] on the device (bf16, fp16, e4m3 or int8)
   void *w = nullptr;
-  const float *scale = nullptr;  // per-row (output channel) scale for e4m3
+  const float *scale = nullptr;  // per-row (output channel) scale for e4m3 / int8
   int rows = 0, ld = 0;
-  bool fp8 = false;
+  bool fp8 = false;  // 8-bit (e4m3, or signed integers when i8)
+  bool i8 = false;
   bool f16 = false;  // fp16: multiplies the fp16 residual stream directly
 };
 
 struct LayerW {
   Mat qkvc, o, f1, f2, sg1, sg2;
-  Mat qkvc8, o8, f1_8, f2_8;  // e4m3 copies (FP8 handles only)
+  Mat qkvc8, o8, f1_8, f2_8;  // 8-bit copies (e4m3 in FP8 handles, int8 in INT8 handles)
   // Deferred-LayerNorm copies (bf16 handles): QKV+compress scaled by the
   // preceding LayerNorm's gamma along K, FFN1 by ln1's gamma; with their
   // column sums and biases b + W.beta
@@ -235,7 +236,7 @@ struct LayerW {
 
 struct Weights {
   Mat pe, emb, effn1, effn2, sg_global, pol, qk, vm, vm1;
-  Mat effn1_8, effn2_8;  // e4m3 copies (FP8 handles only)
+  Mat effn1_8, effn2_8;  // 8-bit copies (FP8 / INT8 handles)
   float *b_pe, *b_emb, *ln_emb_g, *ln_emb_b, *multT, *addT, *b_effn1, *b_effn2, *ln_effn_g,
       *ln_effn_b, *b_pol, *b_qk, *ppo3, *b_vm, *b_vm1, *w2v, *b2v, *w2m, *b2m;
   int16_t *gather;
@@ -278,7 +279,9 @@ struct Shard {  // one GPU
   float2 *SA, *SB;    //   and the rows' (mean, rstd) [M]
   float *SPK = nullptr;      // split-K partial products of small-batch GEMMs
   long long spk_floats = 0;
-  uint8_t *X8, *X1_8, *CTX8, *H8;  // e4m3 GEMM inputs (FP8 handles)
+  uint8_t *X8, *X1_8, *CTX8, *H8;  // 8-bit GEMM inputs (FP8 / INT8 handles)
+  float *RSX, *RSX1;  // INT8 handles: per-row scales of X8 / X1_8 [M]
+  bool int8 = false;  // INT8 handle: the 8-bit GEMMs use signed integer operands
   float *scales, *absmax;    // per-tensor activation scales / calibration maxima
   float *policy, *wdl, *mlh;
   int32_t *move_off;      // legal-move priors: CSR offsets [max_batch + 1]
@@ -325,6 +328,11 @@ struct mfb200_handle {
 };
 
 namespace {
+
+// FP8 and INT8 handles run the 8-bit plan (e4m3 or signed-integer operands).
+bool eight_bit(const mfb200_config &c) {
+  return c.precision == MFB200_PRECISION_FP8 || c.precision == MFB200_PRECISION_INT8;
+}
 
 // ------------------------------------------------------------ packing
 struct Packer {
@@ -430,6 +438,32 @@ void put_mat_fp8(ArenaBuilder &ab, Layout &lay, Mat &m, int rows, int cols, int 
   put_f32(ab, lay, const_cast<float **>(&m.scale), sc.data(), sc.size());
 }
 
+// Signed 8-bit integer matrix with a per-row (output channel) scale: row r is
+// stored as round(W[r] / scale[r]) (nearest, ties away from zero) where
+// scale[r] = max|W[r]| / 127.
+template <class F>
+void put_mat_i8(ArenaBuilder &ab, Layout &lay, Mat &m, int rows, int cols, int ld, F at) {
+  const size_t off = ab.add(size_t(rows) * ld);
+  std::vector<float> sc(rows);
+  for (int r = 0; r < rows; ++r) {
+    float mx = 0.0f;
+    for (int c = 0; c < cols; ++c) mx = std::max(mx, std::fabs(at(r, c)));
+    sc[r] = mx > 0.0f ? mx / 127.0f : 1.0f;
+  }
+  int8_t *dst = reinterpret_cast<int8_t *>(ab.host.data() + off);
+  for (int r = 0; r < rows; ++r)
+    for (int c = 0; c < ld; ++c) {
+      const float q = c < cols ? std::round(at(r, c) / sc[r]) : 0.0f;
+      dst[size_t(r) * ld + c] = static_cast<int8_t>(std::max(-127.0f, std::min(127.0f, q)));
+    }
+  m.rows = rows;
+  m.ld = ld;
+  m.fp8 = true;
+  m.i8 = true;
+  lay.fix.push_back({&m.w, off});
+  put_f32(ab, lay, const_cast<float **>(&m.scale), sc.data(), sc.size());
+}
+
 // A matrix that multiplies the output of a LayerNorm z = (y - mean) * rstd *
 // gamma + beta, prepared for un-normalised input rows y: stored (fp16) as
 // W[r][c] * gamma[c], with colsum[r] = sum_c of those stored values and
@@ -456,7 +490,7 @@ void put_folded(ArenaBuilder &ab, Layout &lay, Mat &m, float **colsum, float **b
 }
 
 void pack_weights(const mfb200_net_desc &n, const float *blob, ArenaBuilder &ab, Layout &lay,
-                  Weights &W, bool fp8) {
+                  Weights &W, bool fp8, bool i8) {
   Packer P(n, blob);
   const int d = n.embedding, T = 64, dp = n.policy_d, pe = n.pe;
   const auto &g = P.gp;
@@ -484,7 +518,10 @@ void pack_weights(const mfb200_net_desc &n, const float *blob, ArenaBuilder &ab,
     put_f32(ab, lay, &W.addT, at.data(), at.size());
   }
   auto dense8 = [&](Mat &m, const float *src, int rows, int cols) {
-    put_mat_fp8(ab, lay, m, rows, cols, cols, [&](int r, int c) { return src[size_t(r) * cols + c]; });
+    if (i8)
+      put_mat_i8(ab, lay, m, rows, cols, cols, [&](int r, int c) { return src[size_t(r) * cols + c]; });
+    else
+      put_mat_fp8(ab, lay, m, rows, cols, cols, [&](int r, int c) { return src[size_t(r) * cols + c]; });
   };
   // matrices applied to the fp16 residual stream are stored in fp16
   dense(W.effn1, g[G_EFFN_W1], n.emb_dff, d, true);
@@ -565,7 +602,10 @@ void pack_weights(const mfb200_net_desc &n, const float *blob, ArenaBuilder &ab,
     };
     put_mat(ab, lay, Lw.qkvc, 3 * d + c, d, d, qkvc_at, true);
     if (fp8) {
-      put_mat_fp8(ab, lay, Lw.qkvc8, 3 * d + c, d, d, qkvc_at);
+      if (i8)
+        put_mat_i8(ab, lay, Lw.qkvc8, 3 * d + c, d, d, qkvc_at);
+      else
+        put_mat_fp8(ab, lay, Lw.qkvc8, 3 * d + c, d, d, qkvc_at);
       dense8(Lw.o8, l[L_O_W], d, d);
       dense8(Lw.f1_8, l[L_FFN_W1], n.dff, d);
       dense8(Lw.f2_8, l[L_FFN_W2], d, n.dff);
@@ -662,6 +702,8 @@ void alloc_workspace(Shard &S, const mfb200_net_desc &n, int max_batch, bool fp8
       {reinterpret_cast<void **>(&S.X1_8), fp8 ? M * d : 16},
       {reinterpret_cast<void **>(&S.CTX8), fp8 ? M * d : 16},
       {reinterpret_cast<void **>(&S.H8), fp8 ? M * hid : 16},
+      {reinterpret_cast<void **>(&S.RSX), fp8 ? M * 4 : 16},
+      {reinterpret_cast<void **>(&S.RSX1), fp8 ? M * 4 : 16},
   };
   size_t total = 0;
   std::vector<size_t> offs;
@@ -791,10 +833,26 @@ std::unique_ptr<Shard::Plan> build_plan(Shard &S, const mfb200_net_desc &n, int 
                      n.embedding == 1024);
   // Which GEMM groups run in e4m3 under FP8 (mfb200_config.fp8_gemms bit
   // mask: 1 embedding FFN, 2 QKV, 4 output projection, 8 FFN1, 16 FFN2).
-  const int fp8_mask = fp8_gemms ? fp8_gemms : 31;
+  // INT8 handles: signed 8-bit operands; the LayerNorm outputs (inputs of
+  // the embedding FFN1, QKV, FFN1) carry per-row scales, the attention
+  // context and the FFN hidden calibrated per-tensor scales.
+  const bool i8 = fp8_plan && S.int8;
+  const int fp8_mask = fp8_gemms ? fp8_gemms : (S.int8 ? 15 : 31);
   const bool f8e = fp8_plan && (fp8_mask & 1), f8q = fp8_plan && (fp8_mask & 2),
              f8o = fp8_plan && (fp8_mask & 4), f8f1 = fp8_plan && (fp8_mask & 8),
              f8f2 = fp8_plan && (fp8_mask & 16);
+  const bool f8e2 = i8 ? f8f2 : f8e;  // the embedding FFN2 (reads the FFN hidden)
+  float *rs_x = i8 ? S.RSX : nullptr, *rs_x1 = i8 ? S.RSX1 : nullptr;
+  // A operand of an 8-bit GEMM: per-row scales (INT8, LayerNorm outputs) or
+  // the per-tensor scale of calibration slot `slot`
+  auto set_a8 = [&](GemmArgs &a, const Mat &Wm, const float *row_scale, int slot) {
+    a.col_scale = Wm.scale;
+    a.ab_i8 = Wm.i8 ? 1 : 0;
+    if (Wm.i8 && row_scale)
+      a.a_row_scale = row_scale;
+    else
+      a.a_scale_ptr = S.scales + slot;
+  };
   const long long Md = static_cast<long long>(B) * 64 * n.embedding;
   auto probe = [&](const char *name, const void *x, Fmt fmt, long long cnt, int slot) {
     if (cal)
@@ -831,9 +889,9 @@ std::unique_ptr<Shard::Plan> build_plan(Shard &S, const mfb200_net_desc &n, int 
     a.ldo = d;
     add_gemm(*P, S, "emb_dense", S.x0, kEmbIn, W.emb, a);
   }
-  add_fn(*P, "emb_ln_gates", 0, [&S, &W, M, d, eps, f8e](cudaStream_t s) {
+  add_fn(*P, "emb_ln_gates", 0, [&S, &W, M, d, eps, f8e, rs_x1](cudaStream_t s) {
     launch_layernorm_q(S.T, Fmt::F32, M, d, W.ln_emb_g, W.ln_emb_b, eps, W.multT, W.addT,
-                       nullptr, S.X1h, Fmt::F16, f8e ? S.X1_8 : nullptr, S.scales + 0, s);
+                       nullptr, S.X1h, Fmt::F16, f8e ? S.X1_8 : nullptr, S.scales + 0, s, f8e ? rs_x1 : nullptr);
   });
   probe("absmax_emb_x", S.X1h, Fmt::F16, Md, 0);
   {
@@ -842,12 +900,14 @@ std::unique_ptr<Shard::Plan> build_plan(Shard &S, const mfb200_net_desc &n, int 
     a.act = n.act_ffn;
     a.out = S.H;
     a.ldo = n.emb_dff;
-    if (f8e) {
-      a.a_scale_ptr = S.scales + 0;
-      a.col_scale = W.effn1_8.scale;
+    if (f8e2) {  // 8-bit hidden for an 8-bit embedding FFN2
       a.out = S.H8;
       a.out_fp8 = 1;
+      a.out_i8 = i8 ? 1 : 0;
       a.out_scale_ptr = S.scales + 1;
+    }
+    if (f8e) {
+      set_a8(a, W.effn1_8, rs_x1, 0);
       add_gemm(*P, S, "emb_ffn1", S.X1_8, d, W.effn1_8, a);
     } else {
       add_gemm(*P, S, "emb_ffn1", S.X1h, d, W.effn1, a);
@@ -869,18 +929,17 @@ std::unique_ptr<Shard::Plan> build_plan(Shard &S, const mfb200_net_desc &n, int 
     b.out = S.X1h;
     b.out_f16 = 1;
     b.ldo = d;
-    if (f8e) {
-      b.a_scale_ptr = S.scales + 1;
-      b.col_scale = W.effn2_8.scale;
+    if (f8e2) {
+      set_a8(b, W.effn2_8, nullptr, 1);
       add_gemm(*P, S, "emb_ffn2", S.H8, n.emb_dff, W.effn2_8, b);
     } else {
       if (!add_gemm(*P, S, "emb_ffn2", S.H, n.emb_dff, W.effn2, b) && fold) row_stats(S.STA, S.SA);
     }
   }
   if (!fold)
-    add_fn(*P, "emb_ffn_ln", 0, [&S, &W, M, d, eps, f8q](cudaStream_t s) {
+    add_fn(*P, "emb_ffn_ln", 0, [&S, &W, M, d, eps, f8q, rs_x](cudaStream_t s) {
       launch_layernorm_q(S.X1h, Fmt::F16, M, d, W.ln_effn_g, W.ln_effn_b, eps, nullptr, nullptr,
-                         nullptr, S.Xh, Fmt::F16, f8q ? S.X8 : nullptr, S.scales + slot_x(0), s);
+                         nullptr, S.Xh, Fmt::F16, f8q ? S.X8 : nullptr, S.scales + slot_x(0), s, f8q ? rs_x : nullptr);
     });
   probe("absmax_x", S.Xh, Fmt::F16, Md, slot_x(0));
   for (int k = 0; k < n.layers; ++k) {
@@ -894,8 +953,7 @@ std::unique_ptr<Shard::Plan> build_plan(Shard &S, const mfb200_net_desc &n, int 
       a.ldo2 = n.smolgen_compress;
       a.split = 3 * d;
       if (f8q) {
-        a.a_scale_ptr = S.scales + slot_x(k);
-        a.col_scale = Lw.qkvc8.scale;
+        set_a8(a, Lw.qkvc8, rs_x, slot_x(k));
         add_gemm(*P, S, "qkv", S.X8, d, Lw.qkvc8, a);
       } else if (fold) {
         a.bias = Lw.bb_qkvc;
@@ -943,9 +1001,9 @@ std::unique_ptr<Shard::Plan> build_plan(Shard &S, const mfb200_net_desc &n, int 
       a.ldo = 4096;
       add_gemm(*P, S, "smolgen_global", S.S2, n.smolgen_gen, W.sg_global, a);
     }
-    add_fn(*P, "attention", 4.0 * B * H * 64.0 * 64.0 * 32.0, [&S, B, H, d, f8o, k](cudaStream_t s) {
+    add_fn(*P, "attention", 4.0 * B * H * 64.0 * 64.0 * 32.0, [&S, B, H, d, f8o, i8, k](cudaStream_t s) {
       launch_attention(S.QKV, 3LL * d, S.BIAS, B, H, d, S.CTX, s, f8o ? S.CTX8 : nullptr,
-                       S.scales + slot_ctx(k));
+                       S.scales + slot_ctx(k), i8 ? 1 : 0);
     });
     probe("absmax_ctx", S.CTX, Fmt::BF16, Md, slot_ctx(k));
     {
@@ -971,17 +1029,17 @@ std::unique_ptr<Shard::Plan> build_plan(Shard &S, const mfb200_net_desc &n, int 
         a.ln_eps = eps;
       }
       if (f8o) {
-        a.a_scale_ptr = S.scales + slot_ctx(k);
-        a.col_scale = Lw.o8.scale;
+        set_a8(a, Lw.o8, nullptr, slot_ctx(k));
         add_gemm(*P, S, "out_proj", S.CTX8, d, Lw.o8, a);
       } else {
         if (!add_gemm(*P, S, "out_proj", S.CTX, d, Lw.o, a) && fold) row_stats(S.STB, S.SB);
       }
     }
     if (!fold)
-      add_fn(*P, "ln1", 0, [&S, &Lw, M, d, eps, f8f1, k](cudaStream_t s) {
+      add_fn(*P, "ln1", 0, [&S, &Lw, M, d, eps, f8f1, k, rs_x1](cudaStream_t s) {
         launch_layernorm_q(S.Xh, Fmt::F16, M, d, Lw.ln1_g, Lw.ln1_b, eps, nullptr, nullptr,
-                           nullptr, S.X1h, Fmt::F16, f8f1 ? S.X1_8 : nullptr, S.scales + slot_x1(k), s);
+                           nullptr, S.X1h, Fmt::F16, f8f1 ? S.X1_8 : nullptr, S.scales + slot_x1(k), s,
+                           f8f1 ? rs_x1 : nullptr);
       });
     probe("absmax_x1", S.X1h, Fmt::F16, Md, slot_x1(k));
     {
@@ -990,14 +1048,14 @@ std::unique_ptr<Shard::Plan> build_plan(Shard &S, const mfb200_net_desc &n, int 
       a.act = n.act_ffn;
       a.out = S.H;
       a.ldo = n.dff;
-      if (f8f2) {  // e4m3 hidden for an FP8 FFN2
+      if (f8f2) {  // 8-bit hidden for an 8-bit FFN2
         a.out = S.H8;
         a.out_fp8 = 1;
+        a.out_i8 = i8 ? 1 : 0;
         a.out_scale_ptr = S.scales + slot_h(k);
       }
       if (f8f1) {
-        a.a_scale_ptr = S.scales + slot_x1(k);
-        a.col_scale = Lw.f1_8.scale;
+        set_a8(a, Lw.f1_8, rs_x1, slot_x1(k));
         add_gemm(*P, S, "ffn1", S.X1_8, d, Lw.f1_8, a);
       } else if (fold) {
         a.bias = Lw.bb_f1;
@@ -1029,8 +1087,7 @@ std::unique_ptr<Shard::Plan> build_plan(Shard &S, const mfb200_net_desc &n, int 
         b.ln_eps = eps;
       }
       if (f8f2) {
-        b.a_scale_ptr = S.scales + slot_h(k);
-        b.col_scale = Lw.f2_8.scale;
+        set_a8(b, Lw.f2_8, nullptr, slot_h(k));
         add_gemm(*P, S, "ffn2", S.H8, n.dff, Lw.f2_8, b);
       } else {
         if (!add_gemm(*P, S, "ffn2", S.H, n.dff, Lw.f2, b) && fold) row_stats(S.STA, S.SA);
@@ -1042,9 +1099,10 @@ std::unique_ptr<Shard::Plan> build_plan(Shard &S, const mfb200_net_desc &n, int 
       const bool last = k + 1 == n.layers;
       const bool q8 = f8q && !last;
       if (!fold || last)  // deferred LayerNorm: only the heads' input is normalised here
-        add_fn(*P, "ln2", 0, [&S, &Lw, M, d, eps, q8, k](cudaStream_t s) {
+        add_fn(*P, "ln2", 0, [&S, &Lw, M, d, eps, q8, k, rs_x](cudaStream_t s) {
           launch_layernorm_q(S.X1h, Fmt::F16, M, d, Lw.ln2_g, Lw.ln2_b, eps, nullptr, nullptr,
-                             nullptr, S.Xh, Fmt::F16, q8 ? S.X8 : nullptr, S.scales + slot_x(k + 1), s);
+                             nullptr, S.Xh, Fmt::F16, q8 ? S.X8 : nullptr, S.scales + slot_x(k + 1), s,
+                             q8 ? rs_x : nullptr);
         });
       if (!last) probe("absmax_x", S.Xh, Fmt::F16, Md, slot_x(k + 1));
     }
@@ -1096,7 +1154,7 @@ void run_steps(Shard::Plan &P, cudaStream_t s) {
 }
 
 Shard::Plan &get_plan(mfb200_handle *h, Shard &S, int B, int mode = -1) {
-  if (mode < 0) mode = h->cfg.precision == MFB200_PRECISION_FP8 ? kPlanFP8 : kPlanBF16;
+  if (mode < 0) mode = eight_bit(h->cfg) ? kPlanFP8 : kPlanBF16;
   if (mode == kPlanFP8 && !h->calibrated)
     throw Fail("FP8 handle used before mfb200_calibrate set its activation scales");
   const int key = B * 4 + mode;
@@ -1166,7 +1224,8 @@ extern "C" int mfb200_create(const mfb200_net_desc *desc, const void *weights, s
   if (bytes != blob_floats(*desc) * sizeof(float))
     return fail(nullptr, "mfb200_create: weight blob has " + std::to_string(bytes) +
                              " bytes, expected " + std::to_string(blob_floats(*desc) * 4));
-  if (cfg->precision != MFB200_PRECISION_BF16 && cfg->precision != MFB200_PRECISION_FP8)
+  if (cfg->precision != MFB200_PRECISION_BF16 && cfg->precision != MFB200_PRECISION_FP8 &&
+      cfg->precision != MFB200_PRECISION_INT8)
     return fail(nullptr, "mfb200_create: unknown precision");
   if (cfg->max_batch <= 0) return fail(nullptr, "mfb200_create: max_batch must be positive");
   auto h = std::make_unique<mfb200_handle>();
@@ -1183,8 +1242,8 @@ extern "C" int mfb200_create(const mfb200_net_desc *desc, const void *weights, s
     ArenaBuilder ab;
     Layout lay;
     Weights proto;
-    pack_weights(*desc, static_cast<const float *>(weights), ab, lay, proto,
-                 cfg->precision == MFB200_PRECISION_FP8);
+    pack_weights(*desc, static_cast<const float *>(weights), ab, lay, proto, eight_bit(*cfg),
+                 cfg->precision == MFB200_PRECISION_INT8);
     const int per = (cfg->max_batch + h->cfg.num_devices - 1) / h->cfg.num_devices;
     for (int i = 0; i < h->cfg.num_devices; ++i) {
       auto S = std::make_unique<Shard>();
@@ -1204,7 +1263,8 @@ extern "C" int mfb200_create(const mfb200_net_desc *desc, const void *weights, s
       // point the weight directory at this device's arena, then copy it
       for (auto &f : lay.fix) *f.first = static_cast<uint8_t *>(S->arena) + f.second;
       S->w = proto;
-      alloc_workspace(*S, *desc, per, cfg->precision == MFB200_PRECISION_FP8);
+      alloc_workspace(*S, *desc, per, eight_bit(*cfg));
+      S->int8 = cfg->precision == MFB200_PRECISION_INT8;
       {
         const std::vector<int16_t> table = build_move_index();
         check(cudaMemcpy(S->move_table, table.data(), table.size() * 2, cudaMemcpyHostToDevice),
@@ -1712,7 +1772,7 @@ extern "C" int mfb200_evaluate_device(mfb200_handle *h, const uint64_t *d_masks,
       check(cudaMemcpyAsync(S.masks, d_masks, size_t(batch) * kPlanes * 8, cudaMemcpyDeviceToDevice, s), "masks");
     if (d_values != S.values)
       check(cudaMemcpyAsync(S.values, d_values, size_t(batch) * kPlanes * 4, cudaMemcpyDeviceToDevice, s), "values");
-    if (stream && !S.plans.count(batch * 4 + (h->cfg.precision == MFB200_PRECISION_FP8 ? 1 : 0))) {
+    if (stream && !S.plans.count(batch * 4 + (eight_bit(h->cfg) ? 1 : 0))) {
       // build (and capture) on the handle's own stream first
       check(cudaStreamSynchronize(s), "sync");
       get_plan(h, S, batch);
@@ -1732,8 +1792,8 @@ extern "C" int mfb200_calibrate(mfb200_handle *h, const uint64_t *masks, const f
                                 int count) {
   if (!h) return fail(nullptr, "mfb200_calibrate: null handle");
   std::lock_guard<std::mutex> lock(h->mu);
-  if (h->cfg.precision != MFB200_PRECISION_FP8)
-    return fail(h, "mfb200_calibrate: only FP8 handles have activation scales");
+  if (!eight_bit(h->cfg))
+    return fail(h, "mfb200_calibrate: only FP8 / INT8 handles have activation scales");
   if (!masks || !values || count <= 0) return fail(h, "mfb200_calibrate: no calibration positions");
   try {
     Shard &S0 = *h->shards[0];
@@ -1749,7 +1809,8 @@ extern "C" int mfb200_calibrate(mfb200_handle *h, const uint64_t *masks, const f
                             cudaMemcpyHostToDevice, S0.stream), "H2D values");
       run_steps(get_plan(h, S0, b, kPlanCalibrate), S0.stream);
     }
-    launch_absmax_to_scale(S0.absmax, nscale, S0.scales, S0.stream);
+    launch_absmax_to_scale(S0.absmax, nscale, S0.scales, S0.stream,
+                           h->cfg.precision == MFB200_PRECISION_INT8 ? 127.0f : 448.0f);
     check(cudaStreamSynchronize(S0.stream), "calibration");
     check_status(S0);
     std::vector<float> sc(nscale);

@@ -289,6 +289,17 @@ __device__ __forceinline__ void umma_f8(uint32_t tmem_d, uint64_t adesc, uint64_
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+// Signed 8-bit integer operands, 32-bit integer accumulator (kind::i8; the
+// instruction descriptor must carry kFmtS8 operands and the S32 accumulator).
+__device__ __forceinline__ void umma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                        uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
 
 // Arrive on `bar` once every previously issued tcgen05.mma of this thread completes.
 __device__ __forceinline__ void umma_commit(uint64_t *bar) {
@@ -380,6 +391,15 @@ __device__ __forceinline__ void umma_f8_pair(uint32_t tmem_d, uint64_t adesc, ui
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+__device__ __forceinline__ void umma_i8_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc,
+                                             uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
 // Arrive on the mbarrier at this shared-memory offset in every CTA of
 // `cta_mask` once the pair's previously issued MMAs have completed.
 __device__ __forceinline__ void umma_commit_pair_mc(uint64_t *bar, uint16_t cta_mask) {
@@ -433,5 +453,11 @@ __host__ __device__ constexpr uint32_t umma_idesc(int m, int n, uint32_t a_fmt, 
 constexpr uint32_t kFmtF16 = 0;   // kind::f16 operand format code for fp16
 constexpr uint32_t kFmtBF16 = 1;  // kind::f16 operand format code for bf16
 constexpr uint32_t kFmtE4M3 = 0;  // kind::f8f6f4 operand format code for e4m3
+constexpr uint32_t kFmtS8 = 1;    // kind::i8 operand format code for signed 8-bit integers
+// kind::i8: signed 8-bit A and B, signed 32-bit accumulator (bits [4,6) = 2).
+__host__ __device__ constexpr uint32_t umma_idesc_s8(int m, int n) {
+  return (2u << 4) | (kFmtS8 << 7) | (kFmtS8 << 10) | (static_cast<uint32_t>(n >> 3) << 17) |
+         (static_cast<uint32_t>(m >> 4) << 24);
+}
 
 }  // namespace mfb200

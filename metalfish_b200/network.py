@@ -48,7 +48,7 @@ class Caps(ctypes.Structure):
                 ("device_name", ctypes.c_char * 96)]
 
 
-PRECISIONS = {"bf16": 0, "fp8": 1}
+PRECISIONS = {"bf16": 0, "fp8": 1, "int8": 2}
 
 
 def _declare(L):
@@ -312,7 +312,7 @@ class B200Network:
         return LeafTicket(self, t.value, (boards, hoff, mv, moff), (pri, wdl, mlh))
 
     def calibrate(self, inp: PackedInputs) -> None:
-        """FP8 only: absmax calibration of the per-tensor activation scales
+        """FP8 / INT8 only: absmax calibration of the per-tensor activation scales
         over the given positions (a bf16 forward with probes)."""
         masks = np.ascontiguousarray(inp.masks, np.uint64)
         values = np.ascontiguousarray(inp.values, np.float32)
@@ -393,14 +393,14 @@ def policy_index_table() -> np.ndarray:
 
 def create_network(cfg: NetConfig, tensors: Dict[str, np.ndarray], backend: str = "b200",
                    calibration: Optional[PackedInputs] = None, **kwargs) -> B200Network:
-    """``CreateNetwork(weights, BackendConfig)`` for the B200 backend. FP8
-    networks (precision="fp8") are calibrated on `calibration` positions."""
+    """``CreateNetwork(weights, BackendConfig)`` for the B200 backend. 8-bit
+    networks (precision="fp8" or "int8") are calibrated on `calibration` positions."""
     if backend not in ("b200", "auto"):
         raise RuntimeError(f"Unknown NN backend: {backend}")
     net = B200Network(cfg, tensors, **kwargs)
-    if net.precision == "fp8":
+    if net.precision in ("fp8", "int8"):
         if calibration is None:
-            raise RuntimeError("an FP8 network needs calibration positions")
+            raise RuntimeError("an 8-bit (FP8 / INT8) network needs calibration positions")
         net.calibrate(calibration)
     return net
 

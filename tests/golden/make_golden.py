@@ -1,8 +1,8 @@
 #!/usr/bin/env python3
 """Regenerate the golden fixtures in tests/golden/ from the REFERENCE itself.
 
-Needs the reference source tree (default /root/reference, override with
-MF_REFERENCE) and builds oracle/_ref/ with ``make -C oracle ref``; it is run
+Needs the reference source tree, named by the MF_REFERENCE environment
+variable (the script stops when it is unset), and builds oracle/_ref/ with ``make -C oracle ref``; it is run
 by hand in the development container, never by the tests. Outputs:
 
 * ``attn_policy_map.npy``  -- the reference's 4288-entry gather table
@@ -25,6 +25,11 @@ by hand in the development container, never by the tests. Outputs:
   reference encoder's packed planes and transforms for all seven input
   formats: the first 1024 fixture games (formats on the first 256) and three
   sets of 64 games from pawnless starts, which reach every canonical transform.
+* ``ref_bt4_1024.npz``    -- the BT4 net of ``ref_bt4`` (weight seed 3, the
+  weights bench.py measures) on the first 1024 positions: full policy logits
+  for the first 256 (``policy``), and for all 1024 the WDL, value, moves-left,
+  the reference's top-1 policy index and its top-1/top-2 logit gap
+  (``top1`` / ``gap``). ``--bt4-large`` regenerates only this file.
 * ``ref_<config>.npz``     -- outputs of the reference ``Cpu::CpuNetwork`` on the
   first N of those positions, for seeded synthetic weights; plus a SHA-256 of
   the weights so a numpy change that alters the generator is caught.
@@ -42,7 +47,7 @@ sys.path.insert(0, ROOT)
 from metalfish_b200 import netfile, synthetic  # noqa: E402
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF = os.environ.get("MF_REFERENCE", "/root/reference")
+REF = os.environ.get("MF_REFERENCE", "")
 HARNESS = os.path.join(ROOT, "oracle", "_ref", "ref_harness")
 POSITION_SEED = 20251201
 POSITIONS = 4096
@@ -142,7 +147,43 @@ def make_moves_and_fastexp(tmp) -> None:
     np.savez_compressed(os.path.join(HERE, "fastexp.npz"), x=x, y=np.fromfile(yout, np.float32))
 
 
+def make_bt4_large(tmp, pos) -> None:
+    """BT4 reference outputs at the bench's batch (1024 positions)."""
+    n, full = 1024, 256
+    tensors = synthetic.generate(synthetic.BT4, 3, perturb_norms=False)
+    net = os.path.join(tmp, "bt4.mfnt")
+    netfile.write_net(net, synthetic.BT4.header(), tensors)
+    out = os.path.join(tmp, "bt4_1024.mfot")
+    threads = os.cpu_count() or 1
+    r = subprocess.run([HARNESS, "eval", net, pos, out, str(threads), "0", str(n)],
+                       check=True, capture_output=True, text=True)
+    print("bt4_1024", r.stdout.strip())
+    o = netfile.read_outputs(out)
+    srt = np.sort(o.policy, axis=1)
+    np.savez_compressed(os.path.join(HERE, "ref_bt4_1024.npz"), policy=o.policy[:full],
+                        wdl=o.wdl, value=o.value, moves_left=o.moves_left,
+                        top1=np.argmax(o.policy, axis=1).astype(np.int16),
+                        gap=(srt[:, -1] - srt[:, -2]).astype(np.float32),
+                        config=synthetic.BT4.name, weight_seed=3, perturb_norms=False,
+                        positions=n, full_policy_positions=full,
+                        weights_sha256=weights_digest(tensors))
+
+
 def main() -> None:
+    if not REF or not os.path.isdir(os.path.join(REF, "src", "nn")):
+        sys.exit("set MF_REFERENCE to the reference source tree")
+    if sys.argv[1:] == ["--bt4-large"]:
+        subprocess.run(["make", "-s", "-C", os.path.join(ROOT, "oracle"), f"REF={REF}", "ref"],
+                       check=True)
+        with tempfile.TemporaryDirectory() as tmp:
+            pos = os.path.join(tmp, "pos.mfin")
+            subprocess.run([HARNESS, "gen-inputs", str(POSITION_SEED), str(POSITIONS), pos],
+                           check=True)
+            inp = netfile.read_inputs(pos)
+            z = np.load(os.path.join(HERE, "positions.npz"))
+            assert np.array_equal(inp.masks, z["masks"]) and np.array_equal(inp.values, z["values"])
+            make_bt4_large(tmp, pos)
+        return
     if sys.argv[1:] == ["--moves-only"]:  # legal moves, FastExp and histories only
         subprocess.run(["make", "-s", "-C", os.path.join(ROOT, "oracle"), f"REF={REF}", "ref"],
                        check=True)
@@ -179,6 +220,7 @@ def main() -> None:
                                 value=o.value, moves_left=o.moves_left, config=cfg.name,
                                 weight_seed=seed, perturb_norms=perturb, positions=n,
                                 weights_sha256=weights_digest(tensors))
+        make_bt4_large(tmp, pos)
 
 
 if __name__ == "__main__":
