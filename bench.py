@@ -446,6 +446,7 @@ def main():
     # ---- batch-1 latency (the per-leaf MCTS case): device time of one
     # graph-launched forward, and the host round trip through mfb200_evaluate
     lat = batch1_latency(net, dev, stream, shard, L) if rank == 0 else None
+    e2e_leaves["small_batches"] = leaves_small_batches(net, L) if rank == 0 else None
     net.close()
     extra = {}
     if args.precision == "bf16" and not args.headline_only:
@@ -526,6 +527,72 @@ def main():
         if not args.no_cpu_baseline and world == 1:
             line["cpu_baseline"] = cpu_baseline(cfg, tensors)
         print(json.dumps(line), flush=True)
+
+
+def leaves_small_batches(net, L, batches=(16, 32), steps=200):
+    """The MCTS leaf path at the batch sizes the reference search uses
+    (minibatch 32, 16 on CUDA): synchronous mfb200_evaluate_leaves round trips
+    against double-buffered mfb200_submit_leaves / mfb200_wait, positions/s
+    from wall time."""
+    import ctypes
+    import torch
+    mv = np.load(os.path.join(ROOT, "tests", "golden", "legal_moves.npz"))
+    hz = np.load(os.path.join(ROOT, "tests", "golden", "history.npz"))
+    h_off_all, h_boards_all = hz["start/offsets"], hz["start/boards"]
+    out = {}
+    for B in batches:
+        bufs = []
+        for k in range(2):  # two input / output sets, alternated by the pipelined loop
+            gid = (np.arange(B) + k * B) % (len(h_off_all) - 1)
+            hc = h_off_all[gid + 1] - h_off_all[gid]
+            h_off = np.concatenate([[0], np.cumsum(hc)]).astype(np.int32)
+            hb = np.concatenate([h_boards_all[h_off_all[i]:h_off_all[i + 1]] for i in gid])
+            lc = mv["offsets"][gid + 1] - mv["offsets"][gid]
+            l_off = np.concatenate([[0], np.cumsum(lc)]).astype(np.int32)
+            lr = np.concatenate([mv["raw"][mv["offsets"][i]:mv["offsets"][i + 1]] for i in gid]).astype(np.uint16)
+            bufs.append([torch.from_numpy(hb).pin_memory(), torch.from_numpy(h_off).pin_memory(),
+                         torch.from_numpy(lr.view(np.int16)).pin_memory(),
+                         torch.from_numpy(l_off).pin_memory(),
+                         torch.empty(int(l_off[-1]), dtype=torch.float32).pin_memory(),
+                         torch.empty((B, 3), dtype=torch.float32).pin_memory(),
+                         torch.empty((B,), dtype=torch.float32).pin_memory()])
+
+        def args(k):
+            b = bufs[k & 1]
+            return (net._h, b[0].data_ptr(), b[1].data_ptr(), B, 5, b[2].data_ptr(), b[3].data_ptr(),
+                    ctypes.c_float(1.0), b[4].data_ptr(), b[5].data_ptr(), b[6].data_ptr())
+
+        def sync_step(k):
+            if L.mfb200_evaluate_leaves(*args(k), None):
+                raise RuntimeError(L.mfb200_last_error(net._h).decode())
+
+        for k in range(10):
+            sync_step(k)
+        t0 = time.perf_counter()
+        for k in range(steps):
+            sync_step(k)
+        sync_s = time.perf_counter() - t0
+        tickets = [ctypes.c_uint64(0), ctypes.c_uint64(0)]
+
+        def submit(k):
+            if L.mfb200_submit_leaves(*args(k), ctypes.byref(tickets[k & 1])):
+                raise RuntimeError(L.mfb200_last_error(net._h).decode())
+
+        def wait(k):
+            if L.mfb200_wait(net._h, tickets[k & 1].value):
+                raise RuntimeError(L.mfb200_last_error(net._h).decode())
+
+        t0 = time.perf_counter()
+        submit(0)
+        for k in range(1, steps):
+            submit(k)
+            wait(k - 1)
+        wait(steps - 1)
+        pipe_s = time.perf_counter() - t0
+        out[str(B)] = {"sync_value": B * steps / sync_s, "pipelined_value": B * steps / pipe_s,
+                       "sync_ms_per_batch": sync_s / steps * 1e3,
+                       "pipelined_ms_per_batch": pipe_s / steps * 1e3, "unit": "positions/s"}
+    return out
 
 
 def device_ms(net, dev, stream, shard, B, steps, warmup, world):

@@ -216,7 +216,9 @@ MFB200_API int mfb200_evaluate_leaves(mfb200_handle *h, const mfb200_board *boar
  * output buffers must stay valid (and unchanged) until mfb200_wait(ticket)
  * returns; page-locked buffers make the copies asynchronous. At most 4
  * submissions are in flight per handle (a fifth waits for the oldest).
- * Submissions on one handle run in order. */
+ * Submissions on one handle run in order, pipelined on three streams per GPU:
+ * the input copies of submission i+1 and the output copies of submission i-1
+ * overlap the GPU work of submission i. */
 MFB200_API int mfb200_submit_leaves(mfb200_handle *h, const mfb200_board *boards,
                                     const int32_t *history_offsets, int batch, int input_format,
                                     const uint16_t *moves, const int32_t *move_offsets,
@@ -224,8 +226,9 @@ MFB200_API int mfb200_submit_leaves(mfb200_handle *h, const mfb200_board *boards
                                     float *moves_left, uint64_t *ticket);
 
 /* Blocks until submission `ticket` has completed (its outputs are in the
- * caller's buffers) and reports a device error it met. Returns 0 for a
- * ticket already waited for. */
+ * caller's buffers) and reports a device error that submission met (the
+ * error stays with its ticket, also when a later submission had to wait for
+ * it to free its slot). Returns 0 for a ticket that completed without error. */
 MFB200_API int mfb200_wait(mfb200_handle *h, uint64_t ticket);
 
 /* NN::MoveToNNIndex (src/nn/policy_map.cpp:316-360) as this library maps
@@ -270,8 +273,12 @@ MFB200_API const char *mfb200_last_error(mfb200_handle *h);
  * All calls on a device share the array: calls that overlap on the GPU (other
  * streams, other threads) race and must be serialised by the caller. Every
  * partial the reduction reads is written by the same call; the one word that
- * must start at zero (a timeout status flag) is cleared by each call. Requires N % 32 == 0 and K % 8 == 0. Returns 0 on success;
- * mfb200_noalloc_last_error() gives the calling thread's last message. */
+ * must start at zero (a timeout status flag) is cleared by each call. If a
+ * barrier wait inside the GEMM timed out (the kernel gives up after 2 s
+ * instead of hanging), every element of d_out is set to NaN, so an
+ * incomplete result is never mistaken for a valid one. Requires N % 32 == 0
+ * and K % 8 == 0. Returns 0 on success; mfb200_noalloc_last_error() gives the
+ * calling thread's last message. */
 MFB200_API int mfb200_splitk_gemm_noalloc(const void *d_A, const void *d_W, int M, int N, int K,
                                           int k_splits, const float *d_bias, float *d_out,
                                           void *stream);

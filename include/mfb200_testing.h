@@ -61,6 +61,34 @@ MFB200_API int mfb200_debug_gemm_ln(int M, int N, int K, int bn, const void *A, 
 MFB200_API int mfb200_debug_gemm_bench(int M, int N, int K, int bn, int mode, int act, int out_f32,
                                        int iters, int dtype, float *ms_out);
 
+/* As mfb200_debug_gemm_bench, also returning the kernel's per-role clock-cycle
+ * counters summed over the timed launches and all CTAs: [0] epilogue waiting
+ * for an accumulator, [1] epilogue processing, [2] MMA issuer waiting for a
+ * free accumulator, [3] MMA issuer waiting for operands, [4] producer waiting
+ * for a free stage, [5] CTA lifetime, [6] epilogue tiles (per warp), [7] unused. */
+MFB200_API int mfb200_debug_gemm_trace(int M, int N, int K, int bn, int mode, int act, int out_f32,
+                                       int iters, int dtype, float *ms_out,
+                                       unsigned long long *trace_out);
+
+/* Bounded-wait error path of the GEMM kernels: an M x N x K bf16 GEMM
+ * (random operands, BN 256; the CTA-pair kernel when pair = 1, which needs
+ * K >= 768 and M > 128) in which CTA 0 (pair 0) announces the bytes of its
+ * first pipeline stage but never loads them, with every barrier wait limited
+ * to wait_ns nanoseconds. The waits on that stage run out; the kernel records
+ * a timeout code in the status word, drains its loads and MMAs, frees its
+ * TMEM and returns. Returns 0 when the kernel returned (the code is in
+ * *status_out), nonzero if it could not be launched. */
+MFB200_API int mfb200_debug_gemm_withheld(int M, int N, int K, int pair,
+                                          unsigned long long wait_ns, unsigned *status_out);
+
+/* One eager forward on the handle in which layer 0's QKV GEMM withholds its
+ * first stage as above (waits limited to wait_ns). Returns the error the
+ * forward reports (nonzero; mfb200_last_error names the timeout); later calls
+ * on the handle are unaffected. */
+struct mfb200_handle;
+MFB200_API int mfb200_debug_forward_withheld(struct mfb200_handle *h, int batch,
+                                             unsigned long long wait_ns);
+
 #ifdef __cplusplus
 }
 #endif

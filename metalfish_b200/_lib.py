@@ -43,3 +43,11 @@ def _declare(L: ctypes.CDLL) -> None:
     L.mfb200_debug_gemm_ln.restype = c_int
     L.mfb200_debug_gemm_ln.argtypes = [c_int, c_int, c_int, c_int, vp, vp, vp, vp, c_float, vp, vp,
                                        c_float, vp, vp, vp]
+    L.mfb200_debug_gemm_withheld.restype = c_int
+    L.mfb200_debug_gemm_withheld.argtypes = [c_int, c_int, c_int, c_int, ctypes.c_ulonglong,
+                                             ctypes.POINTER(ctypes.c_uint)]
+    L.mfb200_debug_forward_withheld.restype = c_int
+    L.mfb200_debug_forward_withheld.argtypes = [vp, c_int, ctypes.c_ulonglong]
+    L.mfb200_debug_gemm_trace.restype = c_int
+    L.mfb200_debug_gemm_trace.argtypes = [c_int] * 9 + [ctypes.POINTER(c_float),
+                                                        ctypes.POINTER(ctypes.c_ulonglong)]

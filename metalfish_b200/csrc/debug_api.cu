@@ -81,6 +81,7 @@ extern "C" int mfb200_debug_gemm(int M, int N, int K, int bn, int fp8, const voi
   a.out_f16 = out_f32 == 2;  // 2: fp16 output
   GemmLaunch g;
   a.ab_f16 = fp8 == 2;
+  a.no_pair = gemm_pairs_enabled() ? 0 : 1;
   if (plan_gemm(g, dA.p, K, dW.p, K, bn, fp8 == 1, a)) return 2;
   if (launch_gemm(g, 0) != cudaSuccess) return 3;
   if (cudaDeviceSynchronize() != cudaSuccess) return 4;
@@ -118,8 +119,24 @@ __global__ void fill_random_kernel(uint16_t *p, long long n, int dtype, uint32_t
   }
 }
 
+static int gemm_bench_impl(int M, int N, int K, int bn, int mode, int act, int out_f32, int iters,
+                           int dtype, float *ms_out, unsigned long long *trace_out);
+
 extern "C" int mfb200_debug_gemm_bench(int M, int N, int K, int bn, int mode, int act,
                                        int out_f32, int iters, int dtype, float *ms_out) {
+  return gemm_bench_impl(M, N, K, bn, mode, act, out_f32, iters, dtype, ms_out, nullptr);
+}
+
+// As mfb200_debug_gemm_bench, and the kernel's per-role cycle counters
+// (GemmArgs::trace, 8 values summed over the `iters` timed launches).
+extern "C" int mfb200_debug_gemm_trace(int M, int N, int K, int bn, int mode, int act,
+                                       int out_f32, int iters, int dtype, float *ms_out,
+                                       unsigned long long *trace_out) {
+  return gemm_bench_impl(M, N, K, bn, mode, act, out_f32, iters, dtype, ms_out, trace_out);
+}
+
+static int gemm_bench_impl(int M, int N, int K, int bn, int mode, int act, int out_f32, int iters,
+                           int dtype, float *ms_out, unsigned long long *trace_out) {
   DevBuf dA, dW, dB, dR, dO, dS, dO2, dG, dRS;
   if (!dA.alloc(size_t(M) * K * 2) || !dW.alloc(size_t(N) * K * 2) || !dB.alloc(N * 4) ||
       !dR.alloc(size_t(M) * N * 4) || !dO.alloc(size_t(M) * N * 4) || !dS.alloc(4) ||
@@ -178,9 +195,16 @@ extern "C" int mfb200_debug_gemm_bench(int M, int N, int K, int bn, int mode, in
     cudaMemset(dRS.p, 0, size_t(M) * 8);
   }
   GemmLaunch g;
+  a.no_pair = gemm_pairs_enabled() ? 0 : 1;
   if (plan_gemm(g, dA.p, K, dW.p, K, bn, dtype == 1, a)) return 2;
   for (int i = 0; i < 2; ++i)
     if (launch_gemm(g, 0) != cudaSuccess) return 3;
+  DevBuf dT;
+  if (trace_out) {
+    if (!dT.alloc(8 * 8)) return 1;
+    cudaMemset(dT.p, 0, 64);
+    g.args.trace = static_cast<unsigned long long *>(dT.p);
+  }
   cudaEvent_t e0, e1;
   cudaEventCreate(&e0);
   cudaEventCreate(&e1);
@@ -193,9 +217,48 @@ extern "C" int mfb200_debug_gemm_bench(int M, int N, int K, int bn, int mode, in
   cudaEventDestroy(e0);
   cudaEventDestroy(e1);
   *ms_out = ms / iters;
+  if (trace_out) cudaMemcpy(trace_out, dT.p, 64, cudaMemcpyDeviceToHost);
   unsigned st = 0;
   cudaMemcpy(&st, dS.p, 4, cudaMemcpyDeviceToHost);
   return st ? 5 : 0;
+}
+
+// A GEMM on random operands whose first pipeline stage in CTA 0 (or CTA
+// pair 0) is announced on its barrier but never loaded, with every barrier
+// wait limited to wait_ns: the waits on that stage run out, the kernel
+// records a timeout code in the status word, drains and returns.
+extern "C" int mfb200_debug_gemm_withheld(int M, int N, int K, int pair,
+                                          unsigned long long wait_ns, unsigned *status_out) {
+  DevBuf dA, dW, dO, dS;
+  if (!dA.alloc(size_t(M) * K * 2) || !dW.alloc(size_t(N) * K * 2) ||
+      !dO.alloc(size_t(M) * N * 2) || !dS.alloc(4))
+    return 1;
+  fill_random_kernel<<<static_cast<unsigned>((size_t(M) * K + 255) / 256), 256>>>(
+      static_cast<uint16_t *>(dA.p), static_cast<long long>(M) * K, 0, 1u);
+  fill_random_kernel<<<static_cast<unsigned>((size_t(N) * K + 255) / 256), 256>>>(
+      static_cast<uint16_t *>(dW.p), static_cast<long long>(N) * K, 0, 2u);
+  cudaMemset(dS.p, 0, 4);
+  GemmArgs a{};
+  a.M = M;
+  a.N = N;
+  a.K = K;
+  a.out = dO.p;
+  a.ldo = N;
+  a.alpha = 1.0f;
+  a.a_scale = 1.0f;
+  a.status = static_cast<unsigned *>(dS.p);
+  a.wait_ns = wait_ns;
+  a.debug_withhold = 1;
+  a.no_pair = pair ? 0 : 1;
+  GemmLaunch g;
+  if (plan_gemm(g, dA.p, K, dW.p, K, 256, false, a)) return 2;
+  if (pair && !g.pair) return 6;
+  if (launch_gemm(g, 0) != cudaSuccess) return 3;
+  if (cudaDeviceSynchronize() != cudaSuccess) return 4;
+  unsigned st = 0;
+  cudaMemcpy(&st, dS.p, 4, cudaMemcpyDeviceToHost);
+  if (status_out) *status_out = st;
+  return 0;
 }
 
 // Residual + LayerNorm GEMM (kEpiResidLN): y = resid + alpha*(A.W^T + bias),
@@ -240,6 +303,7 @@ extern "C" int mfb200_debug_gemm_ln(int M, int N, int K, int bn, const void *A, 
   a.row_stats = static_cast<float2 *>(dRS.p);
   a.status = static_cast<unsigned *>(dS.p);
   GemmLaunch g;
+  a.no_pair = gemm_pairs_enabled() ? 0 : 1;
   if (const char *e = plan_gemm(g, dA.p, K, dW.p, K, bn, false, a)) {
     std::fprintf(stderr, "%s\n", e);
     return 2;

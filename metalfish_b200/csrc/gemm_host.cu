@@ -2,6 +2,7 @@
 // launch configuration and the template instantiations.
 #include <cstdio>
 #include <algorithm>
+#include <atomic>
 #include <mutex>
 
 #include "gemm_host.h"
@@ -29,10 +30,11 @@ EncodeTiledFn encode_fn() {
 }
 
 int g_num_sms = 0;
-bool g_pairs = true;
+std::atomic<bool> g_pairs{true};
 }  // namespace
 
 void set_gemm_pairs(bool enable) { g_pairs = enable; }
+bool gemm_pairs_enabled() { return g_pairs; }
 
 int num_sms() {
   if (g_num_sms == 0) {
@@ -414,7 +416,7 @@ const char *plan_gemm(GemmLaunch &g, const void *A, long long lda_elems, const v
   // measured on B200 at M=65536, bf16 K=1024 (16 steps) gains 8%, e4m3
   // K=1024 (8 steps) loses 15%, e4m3 K=1536 (12 steps) gains 9%.
   const int ksteps = (args.K + (fp8 ? 127 : 63)) / (fp8 ? 128 : 64);
-  g.pair = g_pairs && bn == 256 && args.k_splits <= 1 && args.mode != kEpiResidLN &&
+  g.pair = !args.no_pair && bn == 256 && args.k_splits <= 1 && args.mode != kEpiResidLN &&
            args.M > 128 && ksteps >= 12;
   {
     // every K slice must be non-empty

@@ -20,6 +20,8 @@ struct GemmLaunch {
 
 // Whether plan_gemm may choose the CTA-pair kernel (default on).
 void set_gemm_pairs(bool enable);
+// Whether GEMMs planned from now on may use the CTA-pair kernel (tests can forbid it).
+bool gemm_pairs_enabled();
 
 int num_sms();
 

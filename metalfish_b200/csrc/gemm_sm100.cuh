@@ -78,6 +78,12 @@ struct GemmArgs {
   int k_splits;               // >1: split-K; K slice s writes fp32 partials at
   long long split_stride;     //     out + s * split_stride (raw accumulator)
   unsigned *status;           // device status word
+  unsigned long long wait_ns; // limit of every barrier wait (0: kWaitLimitNs)
+  int debug_withhold;         // tests only: CTA 0 (pair 0) announces its first stage's bytes
+                              // but never loads them, so the waits on it run out
+  int no_pair;                // never use the CTA-pair kernel for this GEMM
+  unsigned long long *trace;  // profiling only (null in the product): per-role clock-cycle sums,
+                              // see gemm_trace_add
   // Deferred LayerNorm (the residual stream is kept un-normalised). The
   // residual GEMM writes per-row partials: float2 (chunk sum, chunk sum of
   // squared deviations from the chunk mean) per 32-column chunk, chunk-major
@@ -205,13 +211,30 @@ __device__ __forceinline__ void resid_issue(const GemmArgs &args, EpiCtx &e, int
   ++e.res_issued;
 }
 
+// Profiling counters (args.trace, 8 values, summed over all CTAs with
+// atomics): 0 epilogue cycles waiting for an accumulator, 1 epilogue cycles
+// processing tiles, 2 MMA-issuer cycles waiting for a free accumulator,
+// 3 MMA-issuer cycles waiting for operands, 4 producer cycles waiting for a
+// free stage, 5 CTA cycles from start to end, 6 epilogue tiles (per warp),
+// 7 producer cycles issuing loads.
+__device__ __forceinline__ long long trace_clock(const GemmArgs &a) {
+  return a.trace ? clock64() : 0;
+}
+__device__ __forceinline__ void gemm_trace_add(const GemmArgs &a, int i, long long v) {
+  if (a.trace && v) atomicAdd(a.trace + i, static_cast<unsigned long long>(v));
+}
+
+__device__ __forceinline__ unsigned long long wait_limit(const GemmArgs &a) {
+  return a.wait_ns ? a.wait_ns : kWaitLimitNs;
+}
+
 // An epilogue warp that stopped early waits (bounded) for a residual load it
 // issued and never consumed before the CTA releases its shared memory.
 __device__ __forceinline__ void resid_drain(const GemmArgs &args, EpiCtx &e) {
   if (args.mode != kEpiResidNorm || e.res_issued == e.res_loads) return;
   const unsigned long long t0 = global_ns();
   while (!mbar_try_wait(e.res_bar, e.res_loads & 1)) {
-    if (global_ns() - t0 > kWaitLimitNs) {
+    if (global_ns() - t0 > wait_limit(args)) {
       atomicCAS(args.status, 0u, static_cast<unsigned>(kErrTimeoutDrain));
       break;
     }
@@ -308,7 +331,7 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs &args, EpiCtx &e, u
   float r_mean = 0.0f, r_rstd = 1.0f;
   if constexpr (MODE == kEpiResidNorm) {
     if (e.res_issued != e.res_loads) {
-      if (!mbar_wait(e.res_bar, e.res_loads & 1, args.status, kErrTimeoutEpilogue, e.abort_flag))
+      if (!mbar_wait(e.res_bar, e.res_loads & 1, args.status, kErrTimeoutEpilogue, e.abort_flag, wait_limit(args)))
         return false;
       ++e.res_loads;
     }
@@ -424,7 +447,7 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs &args, EpiCtx &e, u
         mbar_arrive_expect_tx(e.res_bar, kStageBytes);
         tma_load_2d(e.stage, e.res, e.res_bar, nb, row0);
       }
-      if (!mbar_wait(e.res_bar, e.res_loads & 1, args.status, kErrTimeoutEpilogue, e.abort_flag))
+      if (!mbar_wait(e.res_bar, e.res_loads & 1, args.status, kErrTimeoutEpilogue, e.abort_flag, wait_limit(args)))
         return false;
       ++e.res_loads;
 #pragma unroll
@@ -542,7 +565,7 @@ __device__ __forceinline__ bool epilogue_tile_ln(const GemmArgs &args, EpiCtx &e
   __syncwarp();
   if (lane == 0)
     for (int p = 0; p < C; ++p) mbar_arrive_remote(mapa_shared(bar, static_cast<uint32_t>(p)));
-  if (!mbar_wait_cluster(e.xbar, e.xtiles & 1, args.status, kErrTimeoutRowStats, e.abort_flag))
+  if (!mbar_wait_cluster(e.xbar, e.xtiles & 1, args.status, kErrTimeoutRowStats, e.abort_flag, wait_limit(args)))
     return false;
   ++e.xtiles;
   float ts = 0.0f, tq = 0.0f;
@@ -721,6 +744,8 @@ __global__ void __launch_bounds__(64 + 32 * (LN ? kEpiWarpsLN : kEpiWarpsMax), 1
   // are touched only after it has completed
   pdl_wait();
   pdl_launch();
+  const long long t_start = trace_clock(args);
+  long long tr_a = 0, tr_b = 0, tr_c = 0;  // per-role trace sums
 
   if (warp == 0) {
     if (lane == 0) {
@@ -741,14 +766,20 @@ __global__ void __launch_bounds__(64 + 32 * (LN ? kEpiWarpsLN : kEpiWarpsMax), 1
             for (int x = n0; x < min(n0 + BN, args.N); x += 32) tma_prefetch_l2_2d(&tmRes, x, y);
         }
         for (int kb = ks * kb_per; kb < kb1; ++kb) {
-          if (!mbar_wait(&empty[stage], (round & 1) ^ 1, args.status, kErrTimeoutProducer,
-                         abort_flag)) {
+          const long long tw = trace_clock(args);
+          const bool got = mbar_wait(&empty[stage], (round & 1) ^ 1, args.status, kErrTimeoutProducer,
+                         abort_flag, wait_limit(args));
+          tr_a += trace_clock(args) - tw;
+          if (!got) {
             ok = false;
             break;
           }
           mbar_arrive_expect_tx(&full[stage], S::A_BYTES + S::B_BYTES);
-          tma_load_2d(smA + stage * S::A_BYTES, &tmA, &full[stage], kb * S::BK, m0);
-          tma_load_2d(smB + stage * S::B_BYTES, &tmB, &full[stage], kb * S::BK, n0);
+          // (tests: the first stage of CTA 0 is announced but never loaded)
+          if (!(args.debug_withhold && blockIdx.x == 0 && issued == 0)) {
+            tma_load_2d(smA + stage * S::A_BYTES, &tmA, &full[stage], kb * S::BK, m0);
+            tma_load_2d(smB + stage * S::B_BYTES, &tmB, &full[stage], kb * S::BK, n0);
+          }
           ++issued;
           if (++stage == STAGES) { stage = 0; ++round; }
         }
@@ -759,7 +790,7 @@ __global__ void __launch_bounds__(64 + 32 * (LN ? kEpiWarpsLN : kEpiWarpsMax), 1
         for (long long i = first; i < issued; ++i) {
           const unsigned long long t0 = global_ns();
           while (!mbar_try_wait(&full[i % STAGES], static_cast<uint32_t>((i / STAGES) & 1))) {
-            if (global_ns() - t0 > kWaitLimitNs) {
+            if (global_ns() - t0 > wait_limit(args)) {
               atomicCAS(args.status, 0u, static_cast<unsigned>(kErrTimeoutDrain));
               break;
             }
@@ -782,7 +813,10 @@ __global__ void __launch_bounds__(64 + 32 * (LN ? kEpiWarpsLN : kEpiWarpsMax), 1
         const int ks = ln ? 0 : u % splits;
         const int acc = local & 1;
         const uint32_t aphase = (local >> 1) & 1;
-        if (!mbar_wait(&tempty[acc], aphase ^ 1, args.status, kErrTimeoutMma, abort_flag)) {
+        const long long tw = trace_clock(args);
+        const bool got = mbar_wait(&tempty[acc], aphase ^ 1, args.status, kErrTimeoutMma, abort_flag, wait_limit(args));
+        tr_a += trace_clock(args) - tw;
+        if (!got) {
           ok = false;
           break;
         }
@@ -790,7 +824,10 @@ __global__ void __launch_bounds__(64 + 32 * (LN ? kEpiWarpsLN : kEpiWarpsMax), 1
         const uint32_t d = tmem_base + static_cast<uint32_t>(acc * BN);
         const int kb0 = ks * kb_per, kb1 = min(kblocks, kb0 + kb_per);
         for (int kb = kb0; kb < kb1; ++kb) {
-          if (!mbar_wait(&full[stage], round & 1, args.status, kErrTimeoutMma, abort_flag)) {
+          const long long tw = trace_clock(args);
+          const bool got = mbar_wait(&full[stage], round & 1, args.status, kErrTimeoutMma, abort_flag, wait_limit(args));
+          tr_b += trace_clock(args) - tw;
+          if (!got) {
             ok = false;
             break;
           }
@@ -819,7 +856,7 @@ __global__ void __launch_bounds__(64 + 32 * (LN ? kEpiWarpsLN : kEpiWarpsMax), 1
         umma_commit(drain);
         const unsigned long long t0 = global_ns();
         while (!mbar_try_wait(drain, 0)) {
-          if (global_ns() - t0 > kWaitLimitNs) {
+          if (global_ns() - t0 > wait_limit(args)) {
             atomicCAS(args.status, 0u, static_cast<unsigned>(kErrTimeoutDrain));
             break;
           }
@@ -858,11 +895,17 @@ __global__ void __launch_bounds__(64 + 32 * (LN ? kEpiWarpsLN : kEpiWarpsMax), 1
           resid_issue<BN, S::EW>(args, e, m0 + quarter * 32, n0, group);
         if (ks < 0) epi_pre(args, e, m0 + quarter * 32, n0, BN);
       }
-      if (!mbar_wait(&tfull[acc], aphase, args.status, kErrTimeoutEpilogue, abort_flag)) break;
+      const long long tw = trace_clock(args);
+      const bool got = mbar_wait(&tfull[acc], aphase, args.status, kErrTimeoutEpilogue, abort_flag, wait_limit(args));
+      tr_a += trace_clock(args) - tw;
+      if (!got) break;
       tc_fence_after();
       const uint32_t taddr =
           tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
+      const long long te = trace_clock(args);
       const bool ok = epilogue_dispatch<BN, LN, S::EW>(args, e, taddr, m0 + quarter * 32, n0, group, ks);
+      tr_b += trace_clock(args) - te;
+      tr_c += 1;
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
       if (!ok) break;
@@ -871,6 +914,19 @@ __global__ void __launch_bounds__(64 + 32 * (LN ? kEpiWarpsLN : kEpiWarpsMax), 1
     if (lane == 0) bulk_wait0();  // all TMA stores of this warp have landed
   }
 
+  if (args.trace && lane == 0) {
+    if (warp == 0) {
+      gemm_trace_add(args, 4, tr_a);
+    } else if (warp == 1) {
+      gemm_trace_add(args, 2, tr_a);
+      gemm_trace_add(args, 3, tr_b);
+    } else {
+      gemm_trace_add(args, 0, tr_a);
+      gemm_trace_add(args, 1, tr_b);
+      gemm_trace_add(args, 6, tr_c);
+    }
+    if (threadIdx.x == 0) gemm_trace_add(args, 5, trace_clock(args) - t_start);
+  }
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -971,6 +1027,8 @@ __global__ void __launch_bounds__(64 + 32 * kEpiWarpsMax, 1)
   const uint32_t tmem_base = *tmem_slot;
   pdl_wait();
   pdl_launch();
+  const long long t_start = trace_clock(args);
+  long long tr_a = 0, tr_b = 0, tr_c = 0;  // per-role trace sums
 
   if (warp == 0) {
     if (lane == 0) {
@@ -990,15 +1048,21 @@ __global__ void __launch_bounds__(64 + 32 * kEpiWarpsMax, 1)
             for (int x = n0; x < min(n0 + BN, args.N); x += 32) tma_prefetch_l2_2d(&tmRes, x, y);
         }
         for (int kb = 0; kb < kblocks; ++kb) {
-          if (!mbar_wait(&empty[stage], (round & 1) ^ 1, args.status, kErrTimeoutProducer,
-                         abort_flag)) {
+          const long long tw = trace_clock(args);
+          const bool got = mbar_wait(&empty[stage], (round & 1) ^ 1, args.status, kErrTimeoutProducer,
+                         abort_flag, wait_limit(args));
+          tr_a += trace_clock(args) - tw;
+          if (!got) {
             ok = false;
             break;
           }
           const uint32_t fb = mapa_shared(smem_u32(&full[stage]), 0);
           if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * (S::A_BYTES + S::B_BYTES));
-          tma_load_2d_pair(smA + stage * S::A_BYTES, &tmA, fb, kb * S::BK, m0);
-          tma_load_2d_pair(smB + stage * S::B_BYTES, &tmB, fb, kb * S::BK, nb0);
+          // (tests: the first stage of pair 0 is announced but never loaded)
+          if (!(args.debug_withhold && (blockIdx.x >> 1) == 0 && issued == 0)) {
+            tma_load_2d_pair(smA + stage * S::A_BYTES, &tmA, fb, kb * S::BK, m0);
+            tma_load_2d_pair(smB + stage * S::B_BYTES, &tmB, fb, kb * S::BK, nb0);
+          }
           ++issued;
           if (++stage == STAGES) { stage = 0; ++round; }
         }
@@ -1009,7 +1073,7 @@ __global__ void __launch_bounds__(64 + 32 * kEpiWarpsMax, 1)
         for (long long i = first; i < issued; ++i) {
           const unsigned long long t0 = global_ns();
           while (!mbar_try_wait(&full[i % STAGES], static_cast<uint32_t>((i / STAGES) & 1))) {
-            if (global_ns() - t0 > kWaitLimitNs) {
+            if (global_ns() - t0 > wait_limit(args)) {
               atomicCAS(args.status, 0u, static_cast<unsigned>(kErrTimeoutDrain));
               break;
             }
@@ -1032,14 +1096,20 @@ __global__ void __launch_bounds__(64 + 32 * kEpiWarpsMax, 1)
       for (int u = u_begin; u < units && ok; u += u_step, ++local) {
         const int acc = local & 1;
         const uint32_t aphase = (local >> 1) & 1;
-        if (!mbar_wait_cluster(&tempty[acc], aphase ^ 1, args.status, kErrTimeoutMma, abort_flag)) {
+        const long long tw = trace_clock(args);
+        const bool got = mbar_wait_cluster(&tempty[acc], aphase ^ 1, args.status, kErrTimeoutMma, abort_flag, wait_limit(args));
+        tr_a += trace_clock(args) - tw;
+        if (!got) {
           ok = false;
           break;
         }
         tc_fence_after();
         const uint32_t d = tmem_base + static_cast<uint32_t>(acc * BN);
         for (int kb = 0; kb < kblocks; ++kb) {
-          if (!mbar_wait(&full[stage], round & 1, args.status, kErrTimeoutMma, abort_flag)) {
+          const long long tw = trace_clock(args);
+          const bool got = mbar_wait(&full[stage], round & 1, args.status, kErrTimeoutMma, abort_flag, wait_limit(args));
+          tr_b += trace_clock(args) - tw;
+          if (!got) {
             ok = false;
             break;
           }
@@ -1067,7 +1137,7 @@ __global__ void __launch_bounds__(64 + 32 * kEpiWarpsMax, 1)
         umma_commit_pair(drain);
         const unsigned long long t0 = global_ns();
         while (!mbar_try_wait(drain, 0)) {
-          if (global_ns() - t0 > kWaitLimitNs) {
+          if (global_ns() - t0 > wait_limit(args)) {
             atomicCAS(args.status, 0u, static_cast<unsigned>(kErrTimeoutDrain));
             break;
           }
@@ -1099,11 +1169,17 @@ __global__ void __launch_bounds__(64 + 32 * kEpiWarpsMax, 1)
       }
       if (args.mode == kEpiResidNorm) resid_issue<BN, S::EW>(args, e, m0 + quarter * 32, n0, group);
       epi_pre(args, e, m0 + quarter * 32, n0, BN);
-      if (!mbar_wait(&tfull[acc], aphase, args.status, kErrTimeoutEpilogue, abort_flag)) break;
+      const long long tw = trace_clock(args);
+      const bool got = mbar_wait(&tfull[acc], aphase, args.status, kErrTimeoutEpilogue, abort_flag, wait_limit(args));
+      tr_a += trace_clock(args) - tw;
+      if (!got) break;
       tc_fence_after();
       const uint32_t taddr =
           tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
+      const long long te = trace_clock(args);
       const bool ok = epilogue_dispatch<BN, false, S::EW>(args, e, taddr, m0 + quarter * 32, n0, group, -1);
+      tr_b += trace_clock(args) - te;
+      tr_c += 1;
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_remote(acc ? tempty1 : tempty0);
@@ -1113,6 +1189,19 @@ __global__ void __launch_bounds__(64 + 32 * kEpiWarpsMax, 1)
     if (lane == 0) bulk_wait0();
   }
 
+  if (args.trace && lane == 0) {
+    if (warp == 0) {
+      gemm_trace_add(args, 4, tr_a);
+    } else if (warp == 1) {
+      gemm_trace_add(args, 2, tr_a);
+      gemm_trace_add(args, 3, tr_b);
+    } else {
+      gemm_trace_add(args, 0, tr_a);
+      gemm_trace_add(args, 1, tr_b);
+      gemm_trace_add(args, 6, tr_c);
+    }
+    if (threadIdx.x == 0) gemm_trace_add(args, 5, trace_clock(args) - t_start);
+  }
   tc_fence_before();
   __syncthreads();
   cluster_sync();  // rank 0's MMAs and both CTAs' loads are finished before release

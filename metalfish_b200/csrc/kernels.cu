@@ -2,6 +2,7 @@
 #include <cuda_bf16.h>
 #include <cuda_fp8.h>
 
+#include <atomic>
 #include <type_traits>
 
 #include "gemm_sm100.cuh"
@@ -12,7 +13,7 @@
 namespace mfb200 {
 
 namespace {
-bool g_pdl = true;
+std::atomic<bool> g_pdl{true};
 }
 bool pdl_enabled() { return g_pdl; }
 void set_pdl(bool enable) { g_pdl = enable; }
@@ -550,11 +551,27 @@ bool launch_splitk_act_ln(const float *part, int splits, long long stride, int r
 // ------------------------------------------------------------------ attention
 // One CTA (4 warps) per (position, head); head depth 32. Warp w owns query
 // rows 16w..16w+15. S = Q K^T via mma.sync (2 k-steps x 8 key tiles), plus
-// scale and the smolgen bias, row softmax in registers (exp(x - max) / sum
-// as src/nn/cpu/cpu_network.cpp:405-422), then O = P V (4 k-steps x 4 tiles).
+// the smolgen bias, row softmax in registers, then O = P V (4 k-steps x 4
+// tiles) and O / rowsum (src/nn/cpu/cpu_network.cpp:1175-1254 and the
+// softmax of :405-422: exp(x - max) / sum).
+//
+// The softmax runs in base 2: the smolgen generator GEMM writes the bias
+// already multiplied by log2(e), the scores are scaled by log2(e)/sqrt(dh),
+// and exp(x - max) = 2^(x' - max') with one ex2.approx per element. The bias
+// arrives in "fragment order" (the generator's output columns are permuted
+// when the weights are packed, attention_bias_column()): thread (warp w,
+// lane l) finds the 32 values its score fragments need as 64 contiguous
+// bytes at w*1024 + l*32, loaded with four 16-byte global loads while Q, K
+// and V are still in flight. P stays unnormalised through P V; the 16
+// outputs of each thread are divided by the row sum at the end.
 constexpr int kDh = 32;
 constexpr int kQkvStride = 40;   // padded smem row (80 bytes): conflict-free ldmatrix
-constexpr int kBiasStride = 72;  // padded smem row (144 bytes)
+
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 
 __global__ void __launch_bounds__(128)
     attention_kernel(const __nv_bfloat16 *__restrict__ qkv, long long ldq,
@@ -566,7 +583,6 @@ __global__ void __launch_bounds__(128)
   __shared__ __align__(16) __nv_bfloat16 sQ[kSquares * kQkvStride];
   __shared__ __align__(16) __nv_bfloat16 sK[kSquares * kQkvStride];
   __shared__ __align__(16) __nv_bfloat16 sV[kSquares * kQkvStride];
-  __shared__ __align__(16) __nv_bfloat16 sB[kSquares * kBiasStride];
   const int bh = blockIdx.x;
   const int b = bh / heads, h = bh % heads;
   const int tid = threadIdx.x;
@@ -579,18 +595,28 @@ __global__ void __launch_bounds__(128)
     cp_async16(&sK[r * kQkvStride + c], g + d);
     cp_async16(&sV[r * kQkvStride + c], g + 2 * d);
   }
-  const __nv_bfloat16 *gb = bias + static_cast<long long>(bh) * kSquares * kSquares;
-  for (int i = tid; i < kSquares * 8; i += 128) {
-    const int r = i >> 3, c = (i & 7) * 8;
-    cp_async16(&sB[r * kBiasStride + c], gb + r * kSquares + c);
-  }
   cp_async_commit();
-  cp_async_wait<0>();
-  __syncthreads();
-
   const int warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, t = lane & 3;
   const int q0 = warp * 16;
+  // this thread's 32 bias values (fragment order), word 2j: row g, keys
+  // 8j+2t and 8j+2t+1; word 2j+1: row g+8, the same keys
+  uint32_t bw[16];
+  {
+    const uint4 *bp = reinterpret_cast<const uint4 *>(
+        bias + static_cast<long long>(bh) * kSquares * kSquares + warp * 1024 + lane * 32);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint4 v = __ldg(bp + i);
+      bw[4 * i] = v.x;
+      bw[4 * i + 1] = v.y;
+      bw[4 * i + 2] = v.z;
+      bw[4 * i + 3] = v.w;
+    }
+  }
+  cp_async_wait<0>();
+  __syncthreads();
+
   // ---- S = Q K^T
   float S[8][4];
 #pragma unroll
@@ -617,20 +643,17 @@ __global__ void __launch_bounds__(128)
       mma_bf16_16816(S[j + 1], a, bf[2], bf[3]);
     }
   }
-  // ---- scale + bias, softmax over 64 keys (row g and row g+8 of this warp)
-  const float scale = 1.0f / sqrtf(static_cast<float>(kDh));
+  // ---- x = S log2(e) / sqrt(dh) + bias log2(e); rows g and g+8 of this warp
+  const float c2 = 1.4426950408889634f / sqrtf(static_cast<float>(kDh));
   float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
-    const int col = 8 * j + 2 * t;
-    const float2 b0 = unpack_bf16x2(
-        *reinterpret_cast<const uint32_t *>(&sB[(q0 + g) * kBiasStride + col]));
-    const float2 b1 = unpack_bf16x2(
-        *reinterpret_cast<const uint32_t *>(&sB[(q0 + g + 8) * kBiasStride + col]));
-    S[j][0] = S[j][0] * scale + b0.x;
-    S[j][1] = S[j][1] * scale + b0.y;
-    S[j][2] = S[j][2] * scale + b1.x;
-    S[j][3] = S[j][3] * scale + b1.y;
+    const float2 b0 = unpack_bf16x2(bw[2 * j]);
+    const float2 b1 = unpack_bf16x2(bw[2 * j + 1]);
+    S[j][0] = fmaf(S[j][0], c2, b0.x);
+    S[j][1] = fmaf(S[j][1], c2, b0.y);
+    S[j][2] = fmaf(S[j][2], c2, b1.x);
+    S[j][3] = fmaf(S[j][3], c2, b1.y);
     mx0 = fmaxf(mx0, fmaxf(S[j][0], S[j][1]));
     mx1 = fmaxf(mx1, fmaxf(S[j][2], S[j][3]));
   }
@@ -642,10 +665,10 @@ __global__ void __launch_bounds__(128)
   float sum0 = 0.0f, sum1 = 0.0f;
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
-    S[j][0] = expf(S[j][0] - mx0);
-    S[j][1] = expf(S[j][1] - mx0);
-    S[j][2] = expf(S[j][2] - mx1);
-    S[j][3] = expf(S[j][3] - mx1);
+    S[j][0] = ex2_approx(S[j][0] - mx0);
+    S[j][1] = ex2_approx(S[j][1] - mx0);
+    S[j][2] = ex2_approx(S[j][2] - mx1);
+    S[j][3] = ex2_approx(S[j][3] - mx1);
     sum0 += S[j][0] + S[j][1];
     sum1 += S[j][2] + S[j][3];
   }
@@ -655,7 +678,7 @@ __global__ void __launch_bounds__(128)
     sum1 += __shfl_xor_sync(0xffffffffu, sum1, o);
   }
   const float inv0 = 1.0f / sum0, inv1 = 1.0f / sum1;
-  // ---- O = P V
+  // ---- O = P V (P unnormalised, each entry in (0, 1])
   float O[4][4];
 #pragma unroll
   for (int j = 0; j < 4; ++j)
@@ -664,10 +687,10 @@ __global__ void __launch_bounds__(128)
 #pragma unroll
   for (int ks = 0; ks < 4; ++ks) {
     uint32_t a[4];
-    a[0] = pack_bf16x2(S[2 * ks][0] * inv0, S[2 * ks][1] * inv0);
-    a[1] = pack_bf16x2(S[2 * ks][2] * inv1, S[2 * ks][3] * inv1);
-    a[2] = pack_bf16x2(S[2 * ks + 1][0] * inv0, S[2 * ks + 1][1] * inv0);
-    a[3] = pack_bf16x2(S[2 * ks + 1][2] * inv1, S[2 * ks + 1][3] * inv1);
+    a[0] = pack_bf16x2(S[2 * ks][0], S[2 * ks][1]);
+    a[1] = pack_bf16x2(S[2 * ks][2], S[2 * ks][3]);
+    a[2] = pack_bf16x2(S[2 * ks + 1][0], S[2 * ks + 1][1]);
+    a[3] = pack_bf16x2(S[2 * ks + 1][2], S[2 * ks + 1][3]);
 #pragma unroll
     for (int j = 0; j < 4; j += 2) {
       uint32_t bf[4];
@@ -678,6 +701,13 @@ __global__ void __launch_bounds__(128)
       mma_bf16_16816(O[j], a, bf[0], bf[1]);
       mma_bf16_16816(O[j + 1], a, bf[2], bf[3]);
     }
+  }
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    O[j][0] *= inv0;
+    O[j][1] *= inv0;
+    O[j][2] *= inv1;
+    O[j][3] *= inv1;
   }
   const long long base_off = (static_cast<long long>(b) * kSquares + q0) * d + h * kDh;
   if (ctx8) {

@@ -58,9 +58,23 @@ void launch_layernorm_q(const void *in, Fmt in_fmt, int rows, int width, const f
                         __nv_bfloat16 *out, void *out_res, Fmt res_fmt, uint8_t *out8,
                         const float *scale8, cudaStream_t s, float *row_scale8 = nullptr);
 
+// Fragment order of the smolgen attention bias: the generator GEMM's output
+// column c (its weight row) holds the reference's bias entry q * 64 + k
+// returned here (query q, key k), so that each attention thread finds its 32
+// values contiguous: c = w * 1024 + lane * 32 + j * 4 + e, with query
+// 16w + lane/4 + 8*(e/2) and key 8j + 2*(lane%4) + e%2 (the accumulator
+// fragment layout of mma.m16n8k16).
+inline int attention_bias_column(int c) {
+  const int w = c >> 10, lane = (c >> 5) & 31, j = (c >> 2) & 7, e = c & 3;
+  const int q = 16 * w + (lane >> 2) + 8 * (e >> 1);
+  const int k = 8 * j + 2 * (lane & 3) + (e & 1);
+  return q * 64 + k;
+}
+
 // 64-token attention per (position, head) with the smolgen bias added before
 // the softmax: ctx[b*64+q, h*dh:..] = softmax(Q K^T / sqrt(dh) + bias) V.
-// qkv: [B*64, ldq] with Q at column 0, K at d, V at 2d. bias: [B*H, 4096].
+// qkv: [B*64, ldq] with Q at column 0, K at d, V at 2d. bias: [B*H, 4096],
+// each row in fragment order (attention_bias_column) and multiplied by log2(e).
 // With ctx8 set, the context is written as e4m3 (value / *scale8) instead,
 // or with ctx_i8 as signed 8-bit integers round(value / *scale8), saturated.
 void launch_attention(const __nv_bfloat16 *qkv, long long ldq, const __nv_bfloat16 *bias,

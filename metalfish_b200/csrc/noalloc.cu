@@ -34,12 +34,17 @@ int fail(const char *msg) {
   return 1;
 }
 
-// out[r, c] = bias[c] + sum_s part[s, r, c]
+// out[r, c] = bias[c] + sum_s part[s, r, c]; NaN everywhere if a barrier
+// wait of the GEMM timed out (*status != 0), whose partials are incomplete.
 __global__ void splitk_sum_kernel(const float *__restrict__ part, int splits, long long stride,
                                   long long total, int n, const float *__restrict__ bias,
-                                  float *__restrict__ out) {
+                                  const unsigned *__restrict__ status, float *__restrict__ out) {
   const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= total) return;
+  if (*status != 0u) {
+    out[i] = __int_as_float(0x7FC00000);
+    return;
+  }
   float acc = bias ? bias[i % n] : 0.0f;
   for (int s = 0; s < splits; ++s) acc += part[s * stride + i];
   out[i] = acc;
@@ -105,7 +110,7 @@ extern "C" MFB200_API int mfb200_splitk_gemm_noalloc(const void *d_A, const void
   if (launch_gemm(g, s) != cudaSuccess) return fail("mfb200_splitk_gemm_noalloc: GEMM launch failed");
   const long long total = static_cast<long long>(M) * N;
   splitk_sum_kernel<<<static_cast<unsigned>((total + 255) / 256), 256, 0, s>>>(
-      scratch, splits, total, total, N, d_bias, d_out);
+      scratch, splits, total, total, N, d_bias, a.status, d_out);
   if (cudaGetLastError() != cudaSuccess) return fail("mfb200_splitk_gemm_noalloc: reduce launch failed");
   return 0;
 }

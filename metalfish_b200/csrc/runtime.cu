@@ -20,6 +20,7 @@
 #include <cuda_fp8.h>
 
 #include <algorithm>
+#include <atomic>
 #include <array>
 #include <chrono>
 #include <cmath>
@@ -295,6 +296,22 @@ struct Shard {  // one GPU
   unsigned *status;
   cudaEvent_t ev[4];
   cudaEvent_t done[4];  // completion of the asynchronous submission in each ticket slot
+  // Asynchronous submissions (mfb200_submit_leaves) run in three stages on
+  // three streams so that consecutive submissions overlap: the inputs of
+  // slot k are copied in on copy_in (in_done[k]), the encode + forward +
+  // priors run on `stream` (comp_done[k]) and the outputs go back on
+  // copy_out (done[k]). Each slot has its own device inputs and outputs; the
+  // forward's workspace is shared (its users are serialised on `stream`).
+  cudaStream_t copy_in = nullptr, copy_out = nullptr;
+  cudaEvent_t in_done[4], comp_done[4];
+  struct SlotBufs {
+    mfb200_board *boards;
+    int32_t *hist_off, *move_off, *transforms;
+    uint16_t *moves;
+    float *priors, *wdl, *mlh;
+    unsigned *status;  // the status word as it was after this slot's forward
+  } slots[4] = {};
+  void *slot_mem = nullptr;
   struct Step {
     std::string name;
     double flops = 0;
@@ -305,6 +322,8 @@ struct Shard {  // one GPU
   struct Plan {
     std::vector<Step> steps;
     cudaGraphExec_t graph = nullptr;
+    // test switches (mfb200_testing.h), read once when the plan is built
+    bool auto_split = true, pairs = true;
   };
   std::map<int, std::unique_ptr<Plan>> plans;
 };
@@ -325,6 +344,8 @@ struct mfb200_handle {
   static constexpr int kTickets = 4;
   uint64_t next_ticket = 1;
   uint64_t pending[kTickets] = {};
+  // errors of finished submissions, kept for mfb200_wait (oldest dropped first)
+  std::map<uint64_t, std::string> ticket_errors;
 };
 
 namespace {
@@ -534,7 +555,11 @@ void pack_weights(const mfb200_net_desc &n, const float *blob, ArenaBuilder &ab,
   put_f32(ab, lay, &W.b_effn2, g[G_EFFN_B2], d);
   put_f32(ab, lay, &W.ln_effn_g, g[G_EFFN_LN_G], d);
   put_f32(ab, lay, &W.ln_effn_b, g[G_EFFN_LN_B], d);
-  dense(W.sg_global, g[G_SMOLGEN_W], T * T, n.smolgen_gen);
+  // shared smolgen generator [4096, gen], its output columns (rows here) in
+  // the attention kernel's fragment order
+  put_mat(ab, lay, W.sg_global, T * T, n.smolgen_gen, n.smolgen_gen, [&](int r, int c) {
+    return g[G_SMOLGEN_W][size_t(attention_bias_column(r)) * n.smolgen_gen + c];
+  });
   dense(W.pol, g[G_POL_W], dp, d, true);
   put_f32(ab, lay, &W.b_pol, g[G_POL_B], dp);
   // wq and wk as one [2*dp, dp] matrix (q rows first)
@@ -719,10 +744,44 @@ void alloc_workspace(Shard &S, const mfb200_net_desc &n, int max_batch, bool fp8
     *parts[i].first = static_cast<uint8_t *>(S.ws) + offs[i];
 }
 
+// Device inputs / outputs of the asynchronous submission slots, their copy
+// streams and events.
+void alloc_slots(Shard &S, int max_batch) {
+  const size_t B = max_batch;
+  const size_t sizes[] = {B * kHistoryCapacity * sizeof(mfb200_board), (B + 1) * 4, (B + 1) * 4,
+                          B * 4, B * kMoveCapacity * 2, B * kMoveCapacity * 4, B * 12, B * 4, 256};
+  size_t per = 0;
+  for (size_t x : sizes) per += (x + 255) & ~size_t(255);
+  check(cudaMalloc(&S.slot_mem, per * 4), "submission buffers");
+  check(cudaMemset(S.slot_mem, 0, per * 4), "submission buffers clear");
+  for (int k = 0; k < 4; ++k) {
+    uint8_t *p = static_cast<uint8_t *>(S.slot_mem) + per * k;
+    void *ptrs[9];
+    for (int i = 0; i < 9; ++i) {
+      ptrs[i] = p;
+      p += (sizes[i] + 255) & ~size_t(255);
+    }
+    Shard::SlotBufs &b = S.slots[k];
+    b.boards = static_cast<mfb200_board *>(ptrs[0]);
+    b.hist_off = static_cast<int32_t *>(ptrs[1]);
+    b.move_off = static_cast<int32_t *>(ptrs[2]);
+    b.transforms = static_cast<int32_t *>(ptrs[3]);
+    b.moves = static_cast<uint16_t *>(ptrs[4]);
+    b.priors = static_cast<float *>(ptrs[5]);
+    b.wdl = static_cast<float *>(ptrs[6]);
+    b.mlh = static_cast<float *>(ptrs[7]);
+    b.status = static_cast<unsigned *>(ptrs[8]);
+    check(cudaEventCreateWithFlags(&S.in_done[k], cudaEventDisableTiming), "event");
+    check(cudaEventCreateWithFlags(&S.comp_done[k], cudaEventDisableTiming), "event");
+  }
+  check(cudaStreamCreateWithFlags(&S.copy_in, cudaStreamNonBlocking), "stream");
+  check(cudaStreamCreateWithFlags(&S.copy_out, cudaStreamNonBlocking), "stream");
+}
+
 // ------------------------------------------------------------ plan
 // Split K for GEMMs whose output tiles fill at most half the SMs (small
 // batches); the unit tests also run it off.
-bool g_auto_split = true;
+std::atomic<bool> g_auto_split{true};
 
 int pick_bn(int M, int N) {
   if (N < 128) return 64;
@@ -764,13 +823,16 @@ bool add_gemm(Shard::Plan &P, Shard &S, const char *name, const void *A, long lo
   // (fp32 partials in S.SPK), and apply the epilogue in a second kernel.
   const long long tiles = static_cast<long long>((a.M + 127) / 128) * ((a.N + bn - 1) / bn);
   const int kblocks = (a.K + (W.fp8 ? 127 : 63)) / (W.fp8 ? 128 : 64);
-  if (g_auto_split && a.k_splits <= 1 && a.mode != kEpiResidLN && tiles * 2 <= num_sms() &&
+  a.no_pair = P.pairs ? 0 : 1;
+  if (P.auto_split && a.k_splits <= 1 && a.mode != kEpiResidLN && tiles * 2 <= num_sms() &&
       kblocks >= 2) {
     const int splits = static_cast<int>(std::min<long long>({kblocks, num_sms() / tiles, 16}));
     // (at least 3 slices: below that the extra kernel costs more than it saves)
     if (splits >= 3 && static_cast<long long>(splits) * a.M * a.N <= S.spk_floats) {
       GemmArgs p = base_args(S, a.M, a.N, a.K);
       p.ab_f16 = a.ab_f16;
+      p.ab_i8 = a.ab_i8;
+      p.no_pair = a.no_pair;
       p.out = S.SPK;
       p.out_f32 = 1;
       p.ldo = a.N;
@@ -814,7 +876,7 @@ enum PlanMode { kPlanBF16 = 0, kPlanFP8 = 1, kPlanCalibrate = 2 };
 // normalisation into their epilogue (rstd * (acc - mean * colsum) + bias, with
 // gamma folded into W and beta into the bias). Only the last layer's ln2 runs
 // as a kernel, for the heads.
-bool g_fold_ln = true;
+std::atomic<bool> g_fold_ln{true};
 
 // activation-scale slots: embedding LN output, embedding FFN hidden, then per
 // layer l: layer input, attention context, ln1 output, FFN hidden
@@ -826,8 +888,10 @@ inline int slot_h(int l) { return 5 + 4 * l; }
 std::unique_ptr<Shard::Plan> build_plan(Shard &S, const mfb200_net_desc &n, int B, int mode,
                                         int fp8_gemms) {
   auto P = std::make_unique<Shard::Plan>();
+  P->auto_split = g_auto_split;
+  P->pairs = gemm_pairs_enabled();
   const bool fp8_plan = mode == kPlanFP8, cal = mode == kPlanCalibrate;
-  const bool fold = mode == kPlanBF16 && g_fold_ln && !S.w.layers.empty() &&
+  const bool fold = mode == kPlanBF16 && g_fold_ln.load() && !S.w.layers.empty() &&
                     S.w.layers[0].qkvc_f.w != nullptr &&
                     (n.embedding == 128 || n.embedding == 256 || n.embedding == 512 ||
                      n.embedding == 1024);
@@ -999,6 +1063,7 @@ std::unique_ptr<Shard::Plan> build_plan(Shard &S, const mfb200_net_desc &n, int 
       GemmArgs a = base_args(S, B * H, 4096, n.smolgen_gen);
       a.out = S.BIAS;
       a.ldo = 4096;
+      a.a_scale = 1.4426950408889634f;  // log2(e): the attention's softmax runs in base 2
       add_gemm(*P, S, "smolgen_global", S.S2, n.smolgen_gen, W.sg_global, a);
     }
     add_fn(*P, "attention", 4.0 * B * H * 64.0 * 64.0 * 32.0, [&S, B, H, d, f8o, i8, k](cudaStream_t s) {
@@ -1210,6 +1275,43 @@ int fail(mfb200_handle *h, const std::string &msg) {
 // ============================================================ C ABI
 extern "C" void mfb200_debug_set_fold_ln(int enable) { g_fold_ln = enable != 0; }
 
+// One eager forward of `batch` positions on the handle's first GPU in which
+// layer 0's QKV GEMM announces its first pipeline stage but never loads it,
+// with that GEMM's barrier waits limited to wait_ns. Returns the error the
+// forward reports (nonzero, "device wait timed out ..."); the handle stays
+// usable.
+extern "C" int mfb200_debug_forward_withheld(mfb200_handle *h, int batch,
+                                             unsigned long long wait_ns) {
+  if (!h) return fail(nullptr, "mfb200_debug_forward_withheld: null handle");
+  std::lock_guard<std::mutex> lock(h->mu);
+  try {
+    Shard &S = *h->shards[0];
+    check(cudaSetDevice(S.device), "cudaSetDevice");
+    if (batch <= 0 || batch > h->cfg.max_batch / static_cast<int>(h->shards.size()))
+      throw Fail("batch out of range");
+    Shard::Plan &P = get_plan(h, S, batch);
+    bool injected = false;
+    for (auto &st : P.steps) {
+      if (st.is_gemm && !injected && st.name == "qkv") {
+        GemmLaunch g = st.g;
+        g.args.debug_withhold = 1;
+        g.args.wait_ns = wait_ns;
+        check(launch_gemm(g, S.stream), "withheld qkv");
+        injected = true;
+      } else if (st.is_gemm) {
+        check(launch_gemm(st.g, S.stream), st.name.c_str());
+      } else {
+        st.fn(S.stream);
+      }
+    }
+    check(cudaStreamSynchronize(S.stream), "forward");
+    check_status(S);
+  } catch (const std::exception &e) {
+    return fail(h, std::string("mfb200_debug_forward_withheld: ") + e.what());
+  }
+  return 0;
+}
+
 extern "C" void mfb200_debug_set_auto_split(int enable) { g_auto_split = enable != 0; }
 
 extern "C" size_t mfb200_weight_bytes(const mfb200_net_desc *desc) {
@@ -1265,6 +1367,7 @@ extern "C" int mfb200_create(const mfb200_net_desc *desc, const void *weights, s
       S->w = proto;
       alloc_workspace(*S, *desc, per, eight_bit(*cfg));
       S->int8 = cfg->precision == MFB200_PRECISION_INT8;
+      alloc_slots(*S, per);
       {
         const std::vector<int16_t> table = build_move_index();
         check(cudaMemcpy(S->move_table, table.data(), table.size() * 2, cudaMemcpyHostToDevice),
@@ -1489,14 +1592,29 @@ extern "C" int mfb200_policy_index_table(int16_t *out) {
 namespace {
 // Blocks until the submission in `slot` has completed on every device and
 // checks the devices' status words; the slot is free afterwards.
-void finish_ticket(mfb200_handle *h, int slot) {
-  if (!h->pending[slot]) return;
+// Any error is recorded for the ticket (mfb200_wait returns it, also after
+// the slot has been reused) and returned as a message, empty if none.
+std::string finish_ticket(mfb200_handle *h, int slot) {
+  const uint64_t t = h->pending[slot];
+  if (!t) return {};
   h->pending[slot] = 0;
+  std::string err;
   for (auto &S : h->shards) {
-    check(cudaSetDevice(S->device), "cudaSetDevice");
-    check(cudaEventSynchronize(S->done[slot]), "submission");
-    check_status(*S);
+    try {
+      check(cudaSetDevice(S->device), "cudaSetDevice");
+      check(cudaEventSynchronize(S->done[slot]), "submission");
+      unsigned st = 0;
+      check(cudaMemcpy(&st, S->slots[slot].status, 4, cudaMemcpyDeviceToHost), "status read");
+      if (st) throw Fail("device wait timed out in a GEMM (code " + std::to_string(st) + ")");
+    } catch (const std::exception &e) {
+      if (err.empty()) err = e.what();
+    }
   }
+  if (!err.empty()) {
+    h->ticket_errors[t] = err;
+    while (h->ticket_errors.size() > 64) h->ticket_errors.erase(h->ticket_errors.begin());
+  }
+  return err;
 }
 
 // mfb200_evaluate_leaves, synchronous (ticket == nullptr) or enqueued into
@@ -1531,11 +1649,7 @@ int leaves_impl(mfb200_handle *h, const mfb200_board *boards, const int32_t *his
   if (ticket) {
     const uint64_t t = h->next_ticket++;
     slot = static_cast<int>(t % mfb200_handle::kTickets);
-    try {
-      finish_ticket(h, slot);  // at most kTickets submissions in flight
-    } catch (const std::exception &e) {
-      return fail(h, std::string(fn) + ": " + e.what());
-    }
+    finish_ticket(h, slot);  // at most kTickets in flight (an error stays with its ticket)
     h->pending[slot] = t;
     *ticket = t;
   }
@@ -1548,6 +1662,54 @@ int leaves_impl(mfb200_handle *h, const mfb200_board *boards, const int32_t *his
     try {
       check(cudaSetDevice(S.device), "cudaSetDevice");
       cudaStream_t s = S.stream;
+      if (slot >= 0) {
+        // asynchronous: copy in / compute / copy out on three streams
+        Shard::SlotBufs &sb = S.slots[slot];
+        if (B > 0) {
+          const int32_t mbase = move_offsets[lo] - move_offsets[0];
+          const int32_t nmoves = move_offsets[hi] - move_offsets[lo];
+          const int32_t hbase = history_offsets[lo] - history_offsets[0];
+          const int32_t nb = history_offsets[hi] - history_offsets[lo];
+          check(cudaMemcpyAsync(sb.hist_off, history_offsets + lo, size_t(B + 1) * 4,
+                                cudaMemcpyHostToDevice, S.copy_in), "H2D offsets");
+          if (nb > 0)
+            check(cudaMemcpyAsync(sb.boards, boards + hbase, size_t(nb) * sizeof(mfb200_board),
+                                  cudaMemcpyHostToDevice, S.copy_in), "H2D boards");
+          check(cudaMemcpyAsync(sb.move_off, move_offsets + lo, size_t(B + 1) * 4,
+                                cudaMemcpyHostToDevice, S.copy_in), "H2D move offsets");
+          if (nmoves > 0)
+            check(cudaMemcpyAsync(sb.moves, moves + mbase, size_t(nmoves) * 2,
+                                  cudaMemcpyHostToDevice, S.copy_in), "H2D moves");
+          check(cudaEventRecord(S.in_done[slot], S.copy_in), "event");
+          check(cudaStreamWaitEvent(s, S.in_done[slot], 0), "wait inputs");
+          launch_encode(sb.boards, sb.hist_off, B, input_format, S.masks, S.values, sb.transforms, s);
+          check(cudaGetLastError(), "encode launch");
+          forward(h, S, B, s);
+          launch_leaf_priors(S.policy, B, sb.move_off, sb.moves, S.move_table, sb.boards, sb.hist_off,
+                             sb.transforms, softmax_temp, sb.priors, s);
+          check(cudaGetLastError(), "priors launch");
+          check(cudaMemcpyAsync(sb.wdl, S.wdl, size_t(B) * 12, cudaMemcpyDeviceToDevice, s), "wdl");
+          check(cudaMemcpyAsync(sb.mlh, S.mlh, size_t(B) * 4, cudaMemcpyDeviceToDevice, s), "mlh");
+          // the status word now holds this submission's errors only
+          check(cudaMemcpyAsync(sb.status, S.status, 4, cudaMemcpyDeviceToDevice, s), "status");
+          check(cudaMemsetAsync(S.status, 0, 4, s), "status clear");
+          check(cudaEventRecord(S.comp_done[slot], s), "event");
+          check(cudaStreamWaitEvent(S.copy_out, S.comp_done[slot], 0), "wait forward");
+          if (priors && nmoves > 0)
+            check(cudaMemcpyAsync(priors + mbase, sb.priors, size_t(nmoves) * 4,
+                                  cudaMemcpyDeviceToHost, S.copy_out), "D2H priors");
+          if (wdl)
+            check(cudaMemcpyAsync(wdl + size_t(lo) * 3, sb.wdl, size_t(B) * 12,
+                                  cudaMemcpyDeviceToHost, S.copy_out), "D2H wdl");
+          if (mlh)
+            check(cudaMemcpyAsync(mlh + lo, sb.mlh, size_t(B) * 4, cudaMemcpyDeviceToHost,
+                                  S.copy_out), "D2H mlh");
+        } else {
+          check(cudaMemsetAsync(sb.status, 0, 4, S.copy_out), "status clear");
+        }
+        check(cudaEventRecord(S.done[slot], S.copy_out), "event");
+        return;
+      }
       if (B > 0) {
         const int32_t mbase = move_offsets[lo] - move_offsets[0];
         const int32_t nmoves = move_offsets[hi] - move_offsets[lo];
@@ -1571,10 +1733,6 @@ int leaves_impl(mfb200_handle *h, const mfb200_board *boards, const int32_t *his
         if (wdl) check(cudaMemcpyAsync(wdl + size_t(lo) * 3, S.wdl, size_t(B) * 12, cudaMemcpyDeviceToHost, s), "D2H wdl");
         if (mlh) check(cudaMemcpyAsync(mlh + lo, S.mlh, size_t(B) * 4, cudaMemcpyDeviceToHost, s), "D2H mlh");
         check(cudaEventRecord(S.ev[3], s), "event");
-      }
-      if (slot >= 0) {
-        check(cudaEventRecord(S.done[slot], s), "event");
-        return;
       }
       if (B <= 0) return;
       check(cudaStreamSynchronize(s), "forward");
@@ -1639,12 +1797,10 @@ extern "C" int mfb200_wait(mfb200_handle *h, uint64_t ticket) {
   std::lock_guard<std::mutex> lock(h->mu);
   if (ticket == 0 || ticket >= h->next_ticket) return fail(h, "mfb200_wait: unknown ticket");
   const int slot = static_cast<int>(ticket % mfb200_handle::kTickets);
-  if (h->pending[slot] != ticket) return 0;  // already waited for (or its slot was reused)
-  try {
-    finish_ticket(h, slot);
-  } catch (const std::exception &e) {
-    return fail(h, std::string("mfb200_wait: ") + e.what());
-  }
+  if (h->pending[slot] == ticket) finish_ticket(h, slot);
+  // (a ticket whose slot was reused was finished then; its error, if any, is kept)
+  auto it = h->ticket_errors.find(ticket);
+  if (it != h->ticket_errors.end()) return fail(h, "mfb200_wait: " + it->second);
   return 0;
 }
 
@@ -1904,6 +2060,15 @@ extern "C" void mfb200_destroy(mfb200_handle *h) {
       if (kv.second->graph) cudaGraphExecDestroy(kv.second->graph);
     for (auto &e : S->ev) cudaEventDestroy(e);
     for (auto &e : S->done) cudaEventDestroy(e);
+    if (S->copy_in) {
+      cudaStreamSynchronize(S->copy_in);
+      cudaStreamSynchronize(S->copy_out);
+      for (auto &e : S->in_done) cudaEventDestroy(e);
+      for (auto &e : S->comp_done) cudaEventDestroy(e);
+      cudaStreamDestroy(S->copy_in);
+      cudaStreamDestroy(S->copy_out);
+    }
+    if (S->slot_mem) cudaFree(S->slot_mem);
     if (S->arena) cudaFree(S->arena);
     if (S->ws) cudaFree(S->ws);
     cudaStreamDestroy(S->stream);

@@ -3,9 +3,10 @@
 // tcgen05 MMA / commit / TMEM alloc+load, and the shared-memory matrix and
 // instruction descriptors of tcgen05.mma.
 //
-// Every wait is bounded: after kWaitLimitNs of global-timer time the wait
-// gives up, records an error code in the library's device status word and
-// returns false, so a kernel never spins forever on a barrier.
+// Every wait is bounded: after a limit of global-timer time (kWaitLimitNs
+// unless the launch passes a shorter one) the wait gives up, records an
+// error code in the library's device status word and returns false, so a
+// kernel never spins forever on a barrier.
 #pragma once
 #include <cstdint>
 #include <cuda.h>
@@ -86,14 +87,15 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t *bar, uint32_t pari
 // *status and raises *abort_flag) on timeout or when another role already
 // aborted.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, unsigned *status,
-                                          unsigned code, volatile int *abort_flag) {
+                                          unsigned code, volatile int *abort_flag,
+                                          unsigned long long limit = kWaitLimitNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = global_ns();
   for (uint32_t it = 1;; ++it) {
     if (mbar_try_wait_sleep(bar, parity)) return true;
     if ((it & 7u) == 0) {
       if (*abort_flag) return false;
-      if (global_ns() - t0 > kWaitLimitNs) {
+      if (global_ns() - t0 > limit) {
         atomicCAS(status, 0u, code);
         *abort_flag = 1;
         return false;
@@ -150,14 +152,15 @@ __device__ __forceinline__ bool mbar_try_wait_cluster_sleep(uint64_t *bar, uint3
   return ok != 0;
 }
 __device__ __forceinline__ bool mbar_wait_cluster(uint64_t *bar, uint32_t parity, unsigned *status,
-                                                  unsigned code, volatile int *abort_flag) {
+                                                  unsigned code, volatile int *abort_flag,
+                                                  unsigned long long limit = kWaitLimitNs) {
   if (mbar_try_wait_cluster(bar, parity)) return true;
   const unsigned long long t0 = global_ns();
   for (uint32_t it = 1;; ++it) {
     if (mbar_try_wait_cluster_sleep(bar, parity)) return true;
     if ((it & 7u) == 0) {
       if (*abort_flag) return false;
-      if (global_ns() - t0 > kWaitLimitNs) {
+      if (global_ns() - t0 > limit) {
         atomicCAS(status, 0u, code);
         *abort_flag = 1;
         return false;

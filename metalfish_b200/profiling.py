@@ -4,6 +4,10 @@
       times ITERS back-to-back launches of one tcgen05 GEMM on synthetic
       device data (mfb200_debug_gemm_bench) and prints TFLOP/s. DTYPE: 0
       bf16, 1 e4m3, 2 fp16 operands; PAIRS 0 forbids the CTA-pair kernel.
+  python -m metalfish_b200.profiling trace M N K [BN MODE ACT OUT_F32 ITERS DTYPE PAIRS]
+      the same, with the kernel's per-role clock-cycle counters
+      (mfb200_debug_gemm_trace): how long the epilogue, MMA and producer
+      roles spend waiting and working, per CTA and launch.
   python -m metalfish_b200.profiling forward [BATCH] [bf16|fp8|bf16-nofold]
       runs two eager forwards (no CUDA graph, so every kernel is a separate
       launch) of the seeded BT4-shaped network on fixture positions;
@@ -35,6 +39,30 @@ def gemm(argv) -> None:
     if rc:
         raise SystemExit(f"gemm bench failed: rc={rc}")
     print(f"M={M} N={N} K={K} bn={bn} dtype={dtype} pairs={pairs}: {ms.value:.4f} ms  {2.0 * M * N * K / ms.value / 1e9:.1f} TFLOP/s")
+
+
+def trace(argv) -> None:
+    from ._lib import lib
+    M, N, K = (int(x) for x in argv[:3])
+    bn, mode, act, out_f32, iters, dtype, pairs = (
+        int(x) for x in (argv[3:10] + ["256", "0", "0", "0", "10", "0", "1"][len(argv) - 3:]))
+    ms = ctypes.c_float()
+    tr = (ctypes.c_ulonglong * 8)()
+    lib().mfb200_debug_set_gemm_pairs(pairs)
+    rc = lib().mfb200_debug_gemm_trace(M, N, K, bn, mode, act, out_f32, iters, dtype,
+                                       ctypes.byref(ms), tr)
+    if rc:
+        raise SystemExit(f"gemm trace failed: rc={rc}")
+    ctas = tr[5]
+    names = ["epi_wait_acc", "epi_busy", "mma_wait_acc", "mma_wait_operands", "prod_wait_stage",
+             "cta_cycles", "epi_tiles", "-"]
+    print(f"M={M} N={N} K={K} bn={bn} mode={mode} dtype={dtype} pairs={pairs}: {ms.value:.4f} ms "
+          f"{2.0 * M * N * K / ms.value / 1e9:.1f} TFLOP/s; cycles summed over CTAs and launches:")
+    print("  " + "  ".join(f"{n}={tr[i]:,}" for i, n in enumerate(names[:7])))
+    if ctas:
+        print("  fractions of CTA lifetime (epilogue per warp: / epilogue warps): "
+              f"mma_wait_acc {tr[2] / ctas:.3f} mma_wait_operands {tr[3] / ctas:.3f} "
+              f"prod_wait_stage {tr[4] / ctas:.3f}")
 
 
 def forward(argv) -> None:
@@ -77,4 +105,4 @@ def leaves(argv) -> None:
 
 if __name__ == "__main__":
     cmd, rest = sys.argv[1], sys.argv[2:]
-    {"gemm": gemm, "forward": forward, "leaves": leaves}[cmd](rest)
+    {"gemm": gemm, "trace": trace, "forward": forward, "leaves": leaves}[cmd](rest)

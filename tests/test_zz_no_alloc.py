@@ -3,12 +3,14 @@
 It exists for callers that cannot allocate GPU memory (code living inside
 another framework's memory pool, or a search thread that must not take the
 driver's allocation locks mid-game): its scratch is a fixed device array inside
-the library. This test calls it through the C ABI twice in a row, with
-different shapes, and compares each result with the existing GEMM entry point
-(mfb200_debug_gemm, unsplit, fp32 output) within the split-K tolerance of
-tests/test_gemm_gpu.py. The test allocates its own input/output buffers (with
-torch); the entry point itself allocates nothing. It sits in its own file,
-collected last.
+the library. This test calls it through the C ABI several times in a row, with
+different shapes (a ragged M, more slices than K blocks), and compares each
+result with an fp64 host product of the same bf16 operands plus the bias,
+within the split-K tolerance of tests/test_gemm_gpu.py; the first shape is
+also checked against the library's existing GEMM entry point
+(mfb200_debug_gemm, unsplit, fp32 output). The test allocates its own
+input/output buffers (with torch); the entry point itself allocates nothing.
+It sits in its own file, collected last.
 """
 import ctypes
 
@@ -16,7 +18,7 @@ import numpy as np
 import pytest
 
 from metalfish_b200._lib import lib
-from metalfish_b200.bf16 import to_bf16_bits
+from metalfish_b200.bf16 import from_bf16_bits, to_bf16_bits
 
 pytestmark = pytest.mark.gpu
 
@@ -35,7 +37,8 @@ def _reference(Ab, Wb, b, M, N, K):
     return out
 
 
-@pytest.mark.parametrize("shapes", [[(1024, 256, 2048, 7), (64, 128, 1024, 16)]])
+@pytest.mark.parametrize("shapes", [[(1024, 256, 2048, 7), (64, 128, 1024, 16),
+                                     (300, 96, 256, 8), (130, 512, 1024, 3)]])
 def test_noalloc_splitk_matches_existing_gemm(shapes):
     import torch
     L = lib()
@@ -47,7 +50,7 @@ def test_noalloc_splitk_matches_existing_gemm(shapes):
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     rng = np.random.default_rng(7)
-    for M, N, K, splits in shapes:   # two calls in a row; the second must not see stale scratch
+    for i, (M, N, K, splits) in enumerate(shapes):  # calls in a row: none may see stale scratch
         A = rng.standard_normal((M, K), dtype=np.float32)
         W = rng.standard_normal((N, K), dtype=np.float32) / np.float32(np.sqrt(K))
         b = (0.1 * rng.standard_normal(N)).astype(np.float32)
@@ -62,8 +65,11 @@ def test_noalloc_splitk_matches_existing_gemm(shapes):
         assert rc == 0, L.mfb200_noalloc_last_error().decode()
         torch.cuda.synchronize(dev)
         got = dout.cpu().numpy()
-        ref = _reference(Ab, Wb, b, M, N, K)
-        np.testing.assert_allclose(got, ref, rtol=1e-4, atol=1e-3)
+        exact = (from_bf16_bits(Ab).astype(np.float64) @ from_bf16_bits(Wb).astype(np.float64).T
+                 + b.astype(np.float64))
+        np.testing.assert_allclose(got, exact, rtol=1e-4, atol=1e-3)
+        if i == 0:
+            np.testing.assert_allclose(got, _reference(Ab, Wb, b, M, N, K), rtol=1e-4, atol=1e-3)
 
 
 def test_noalloc_rejects_oversize():
