@@ -410,14 +410,16 @@ const char *plan_gemm(GemmLaunch &g, const void *A, long long lda_elems, const v
   g.fp8 = fp8;
   g.args = args;
   // CTA pairs for the large store / accumulate / residual GEMMs with at
-  // least 12 K steps. With fewer, a tile is bound by its epilogue, and the
-  // pair's shared accumulator hand-off (both CTAs must drain an accumulator
-  // before it is reused) costs more than the halved W traffic saves:
-  // measured on B200 at M=65536, bf16 K=1024 (16 steps) gains 8%, e4m3
-  // K=1024 (8 steps) loses 15%, e4m3 K=1536 (12 steps) gains 9%.
+  // least 8 K steps (K >= 512 in 16-bit, K >= 1024 in 8-bit). With fewer, a
+  // tile is bound by its epilogue, and the pair's shared accumulator
+  // hand-off (both CTAs must drain an accumulator before it is reused) costs
+  // more than the halved W traffic saves. Measured on B200 (M=65536, one
+  // process, back-to-back launches): bf16 K=1024 N=1024 gains 14%; 8-bit
+  // K=1024 gains 7% (N=3104) and 15% (N=1024, accumulate epilogue); bf16
+  // K=256 (4 steps) loses 20%.
   const int ksteps = (args.K + (fp8 ? 127 : 63)) / (fp8 ? 128 : 64);
   g.pair = !args.no_pair && bn == 256 && args.k_splits <= 1 && args.mode != kEpiResidLN &&
-           args.M > 128 && ksteps >= 12;
+           args.M > 128 && ksteps >= 8;
   {
     // every K slice must be non-empty
     const int kblocks = (args.K + (fp8 ? 128 : 64) - 1) / (fp8 ? 128 : 64);

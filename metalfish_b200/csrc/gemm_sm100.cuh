@@ -760,7 +760,7 @@ __global__ void __launch_bounds__(64 + 32 * (LN ? kEpiWarpsLN : kEpiWarpsMax), 1
         const int m0 = (t / tiles_n) * S::BM;
         const int n0 = (t % tiles_n) * BN;
         const int kb1 = min(kblocks, (ks + 1) * kb_per);
-        if (ln || (ks == 0 && args.mode == kEpiResidNorm)) {
+        if (ln) {
           // pull this tile's residual into L2 while its mainloop runs
           for (int y = m0; y < min(m0 + S::BM, args.M); y += 32)
             for (int x = n0; x < min(n0 + BN, args.N); x += 32) tma_prefetch_l2_2d(&tmRes, x, y);
@@ -1040,13 +1040,8 @@ __global__ void __launch_bounds__(64 + 32 * kEpiWarpsMax, 1)
       for (int u = u_begin; u < units && ok; u += u_step) {
         const int m0 = (u / tiles_n) * 2 * S::BM + static_cast<int>(rank) * S::BM;
         const int nb0 = (u % tiles_n) * BN + static_cast<int>(rank) * (BN / 2);
-        if (args.mode == kEpiResidNorm) {
-          // pull this CTA's residual rows of the tile into L2 while its
-          // mainloop runs; the epilogue's TMA loads then hit L2
-          const int n0 = (u % tiles_n) * BN;
-          for (int y = m0; y < min(m0 + S::BM, args.M); y += 32)
-            for (int x = n0; x < min(n0 + BN, args.N); x += 32) tma_prefetch_l2_2d(&tmRes, x, y);
-        }
+        // (no L2 prefetch of the residual tile: the producer's prefetches
+        // delayed its operand loads; measured 5% slower with them)
         for (int kb = 0; kb < kblocks; ++kb) {
           const long long tw = trace_clock(args);
           const bool got = mbar_wait(&empty[stage], (round & 1) ^ 1, args.status, kErrTimeoutProducer,
