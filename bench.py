@@ -183,6 +183,8 @@ def dist_setup(n_gpus):
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if world > 1:
+        # keep stdout to the one JSON line (NCCL otherwise announces its version there)
+        os.environ.setdefault("NCCL_DEBUG", "WARN")
         import torch.distributed as dist
         import torch
         backend = "nccl" if torch.cuda.is_available() else "gloo"
@@ -197,6 +199,8 @@ def dist_setup(n_gpus):
 
 def barrier(world):
     if world > 1:
+        # keep stdout to the one JSON line (NCCL otherwise announces its version there)
+        os.environ.setdefault("NCCL_DEBUG", "WARN")
         import torch.distributed as dist
         dist.barrier()
 
