@@ -254,7 +254,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--batch", type=int, default=1024, help="positions per GPU per step")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--precision", default="bf16", choices=["bf16", "fp8"])
+    ap.add_argument("--precision", default="bf16", choices=["bf16", "fp8", "int8"])
     ap.add_argument("--fp8-gemms", type=int, default=0, help="FP8 GEMM-group mask (0 = all)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--headline-only", action="store_true",
@@ -283,7 +283,7 @@ def main():
     # (positions 1024..2047 of the fixture, disjoint from the first shard)
     net = create_network(cfg, tensors, device=local, max_batch=B, precision=args.precision,
                          fp8_gemms=args.fp8_gemms,
-                         calibration=load_positions(2048).slice(1024, 2048) if args.precision == "fp8" else None)
+                         calibration=load_positions(2048).slice(1024, 2048) if args.precision in ("fp8", "int8") else None)
     inp = load_positions(B * world)
     shard = inp.slice(rank * B, (rank + 1) * B)
     dev = torch.device("cuda", local)
@@ -473,10 +473,10 @@ def main():
     q_fl = sum(f for _, f in qkv)
     burst, sustained, src = measured_peaks()
     peak_note = f"{src} bf16_tflops_sustained (kernel timed inside a long step)"
-    if args.precision == "fp8":
-        # no FP8 peak was measured on this pool; e4m3 dense rate is twice bf16
+    if args.precision != "bf16":
+        # no 8-bit peak was measured on this pool; the e4m3 / int8 dense rate is twice bf16
         sustained *= 2.0
-        peak_note = f"2 x {src} bf16_tflops_sustained (e4m3 dense = 2x bf16)"
+        peak_note = f"2 x {src} bf16_tflops_sustained (8-bit dense = 2x bf16)"
     achieved = q_fl / (q_ms / 1e3) / 1e12 if q_ms > 0 else 0.0
     g_achieved = g_fl / (g_ms / 1e3) / 1e12 if g_ms > 0 else 0.0
     traffic, traffic_src = QKV_TRAFFIC.get(args.precision, (None, None)) if B == 1024 else (None, None)
@@ -488,7 +488,7 @@ def main():
             "metric": "BT4-shape positions/sec", "value": value, "unit": "positions/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": ms_max / args.steps, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": args.precision if args.precision == "bf16" else "e4m3",
+            "vs_baseline": None, "dtype": {"bf16": "bf16", "fp8": "e4m3", "int8": "s8"}[args.precision],
             "data": "synthetic (seeded random-playout positions from the reference encoder, "
                     "random-init BT4-shaped weights)",
             "config": {"workload": f"{cfg.name} forward, {args.precision}, batch {B} per GPU",
@@ -503,7 +503,7 @@ def main():
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": sustained,
                          "unit": "TFLOP/s", "frac": achieved / sustained, "traffic": traffic,
                          "kernel": ("gemm_pair_kernel<bf16/fp16>" if args.precision == "bf16"
-                                    else "gemm_sm100_kernel<256, e4m3>")
+                                    else "gemm_pair_kernel<8-bit> (e4m3 or s8)")
                                    + f": QKV+compress projection, M={B * 64} N=3104 K=1024, "
                                      f"{len(qkv)} launches per forward",
                          "traffic_source": traffic_src,
@@ -515,9 +515,9 @@ def main():
             "tensor_roofline": {
                 "per_gpu_encoder_tflops": value * enc["encoder_gemm_flops"] / 1e12 / world,
                 "frac_of_measured_burst": value * enc["encoder_gemm_flops"] / 1e12 / world
-                / (burst * (2.0 if args.precision == "fp8" else 1.0)),
+                / (burst * (2.0 if args.precision != "bf16" else 1.0)),
                 "frac_of_nominal_dense": value * enc["encoder_gemm_flops"] / 1e12 / world
-                / (4500.0 if args.precision == "fp8" else 2250.0),
+                / (4500.0 if args.precision != "bf16" else 2250.0),
                 "note": "encoder QKV/O/FFN FLOPs (14.09 GFLOP per position) per GPU against the "
                         "measured cuBLAS bf16 burst peak (x2 for e4m3) and the nominal dense peak"},
             "latency_batch1_ms": lat,
@@ -769,7 +769,7 @@ def run_sweep(args, batches):
     torch.cuda.set_device(dev)
     net = create_network(cfg, tensors, device=0, max_batch=max(batches), precision=args.precision,
                          fp8_gemms=args.fp8_gemms,
-                         calibration=load_positions(2048).slice(1024, 2048) if args.precision == "fp8" else None)
+                         calibration=load_positions(2048).slice(1024, 2048) if args.precision in ("fp8", "int8") else None)
     stream = torch.cuda.Stream(dev)
     inp = load_positions(max(batches))
     d_m = torch.from_numpy(inp.masks.view(np.int64)).to(dev)

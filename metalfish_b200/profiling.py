@@ -8,9 +8,9 @@
       the same, with the kernel's per-role clock-cycle counters
       (mfb200_debug_gemm_trace): how long the epilogue, MMA and producer
       roles spend waiting and working, per CTA and launch.
-  python -m metalfish_b200.profiling forward [BATCH] [bf16|fp8|bf16-nofold]
+  python -m metalfish_b200.profiling forward [BATCH] [bf16|fp8|int8|bf16-nofold]
       runs two eager forwards (no CUDA graph, so every kernel is a separate
-      launch) of the seeded BT4-shaped network on fixture positions;
+      launch; the second inside the NVTX range "forward2") of the seeded BT4-shaped network on fixture positions;
       bf16-nofold runs the encoder with separate ln1 / ln2 passes instead of
       the deferred LayerNorm.
   python -m metalfish_b200.profiling leaves [BATCH]
@@ -80,10 +80,15 @@ def forward(argv) -> None:
     reps = (batch + 2048 + len(m) - 1) // len(m)
     m, v = np.tile(m, (reps, 1)), np.tile(v, (reps, 1))
     net = create_network(BT4, generate(BT4, 3), max_batch=batch, use_graphs=False, precision=precision,
-                         calibration=PackedInputs(m[1024:2048], v[1024:2048]) if precision == "fp8" else None)
+                         calibration=(PackedInputs(m[1024:2048], v[1024:2048])
+                                      if precision in ("fp8", "int8") else None))
     inp = PackedInputs(m[:batch].copy(), v[:batch].copy())
-    for _ in range(2):
-        net.evaluate_packed(inp)
+    import torch
+    net.evaluate_packed(inp)
+    # the second forward in an NVTX range "forward2", for ncu --nvtx-include "forward2/"
+    torch.cuda.nvtx.range_push("forward2")
+    net.evaluate_packed(inp)
+    torch.cuda.nvtx.range_pop()
     net.close()
     print(f"forward ok: BT4 batch {batch} {precision}")
 
