@@ -534,9 +534,55 @@ __global__ void splitk_act_ln_kernel(const float *__restrict__ part, int splits,
   }
 }
 
+// The same for a few rows (small batches): one CTA per row and one thread
+// per column, so every slice of a column is loaded at once instead of one
+// warp walking the slices of a whole row (the latency of one small batch's
+// smolgen dense1 step).
+__global__ void __launch_bounds__(1024)
+    splitk_act_ln_row_kernel(const float *__restrict__ part, int splits, long long stride,
+                             const float *__restrict__ bias, int act,
+                             const float *__restrict__ gamma, const float *__restrict__ beta,
+                             float eps, __nv_bfloat16 *__restrict__ out) {
+  pdl_wait();
+  pdl_launch();
+  __shared__ float red[32];
+  const int row = blockIdx.x, c = threadIdx.x, lane = c & 31, warp = c >> 5;
+  const int width = blockDim.x, warps = width >> 5;
+  const float *p = part + static_cast<long long>(row) * width + c;
+  float x[16];
+  const int n = splits < 16 ? splits : 16;
+#pragma unroll
+  for (int k = 0; k < 16; ++k) x[k] = k < n ? __ldcg(p + k * stride) : 0.0f;
+  float v = __ldg(bias + c);
+#pragma unroll
+  for (int k = 0; k < 16; ++k) v += x[k];  // slices in order
+  for (int k = 16; k < splits; ++k) v += __ldcg(p + k * stride);
+  v = apply_act(v, act);
+  auto bsum = [&](float t) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+    __syncthreads();
+    if (lane == 0) red[warp] = t;
+    __syncthreads();
+    float r = 0.0f;
+    for (int w = 0; w < warps; ++w) r += red[w];
+    return r;
+  };
+  const float mean = bsum(v) / static_cast<float>(width);
+  const float inv = 1.0f / sqrtf(bsum((v - mean) * (v - mean)) / static_cast<float>(width) + eps);
+  out[static_cast<long long>(row) * width + c] =
+      __float2bfloat16_rn((v - mean) * inv * __ldg(gamma + c) + __ldg(beta + c));
+}
+
 bool launch_splitk_act_ln(const float *part, int splits, long long stride, int rows, int width,
                           const float *bias, int act, const float *gamma, const float *beta,
                           float eps, __nv_bfloat16 *out, cudaStream_t s) {
+  if (rows <= 64 && width % 32 == 0 && width <= 1024) {
+    launch_k(splitk_act_ln_row_kernel, dim3(static_cast<unsigned>(rows)),
+             dim3(static_cast<unsigned>(width)), 0, s, 1, part, splits, stride, bias, act, gamma,
+             beta, eps, out);
+    return true;
+  }
   const int wpb = 8;
   const unsigned grid = static_cast<unsigned>((rows + wpb - 1) / wpb);
   switch (width) {
