@@ -297,12 +297,13 @@ __global__ void __launch_bounds__(256)
   }
 }
 
-// One CTA (256 threads) per row for wide rows (smolgen's H*g = 8192): the row
-// is read once into registers (VPT values per thread in 8-value groups, each
-// warp instruction covering 512 contiguous bytes), then mean, variance and
-// the normalised output come from the registers.
-template <int VPT>
-__global__ void __launch_bounds__(256)
+// One CTA (T threads: 256, or 1024 when there are few rows, so that a small
+// batch's row is spread over more threads) per row for wide rows (smolgen's
+// H*g = 8192): the row is read once into registers (VPT values per thread in
+// 8-value groups, each warp instruction covering 512 contiguous bytes), then
+// mean, variance and the normalised output come from the registers.
+template <int VPT, int T = 256>
+__global__ void __launch_bounds__(T)
     layernorm_block_kernel(const __nv_bfloat16 *__restrict__ in, int width,
                            const float *__restrict__ gamma, const float *__restrict__ beta,
                            float eps, __nv_bfloat16 *__restrict__ out) {
@@ -311,11 +312,11 @@ __global__ void __launch_bounds__(256)
   constexpr int NG = VPT / 8;
   const long long row = blockIdx.x;
   const __nv_bfloat16 *src = in + row * width;
-  __shared__ float red[8];
+  __shared__ float red[T / 32];
   float v[VPT];
 #pragma unroll
   for (int q = 0; q < NG; ++q) {
-    const uint4 u = *reinterpret_cast<const uint4 *>(src + q * 2048 + threadIdx.x * 8);
+    const uint4 u = *reinterpret_cast<const uint4 *>(src + q * (8 * T) + threadIdx.x * 8);
     const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
@@ -332,7 +333,7 @@ __global__ void __launch_bounds__(256)
     __syncthreads();
     float t = 0.0f;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) t += red[i];
+    for (int i = 0; i < T / 32; ++i) t += red[i];
     return t;
   };
   float s = 0.0f;
@@ -348,7 +349,7 @@ __global__ void __launch_bounds__(256)
   const float inv = 1.0f / sqrtf(block_sum(sq) / static_cast<float>(width) + eps);
 #pragma unroll
   for (int q = 0; q < NG; ++q) {
-    const int c = q * 2048 + threadIdx.x * 8;
+    const int c = q * (8 * T) + threadIdx.x * 8;
     float g[8], b[8];
     load_g<Fmt::F32, 8>(gamma, c, g);
     load_g<Fmt::F32, 8>(beta, c, b);
@@ -463,7 +464,12 @@ void launch_layernorm(const void *in, bool in_f32, int rows, int width, const fl
     case 2048: launch_k(layernorm_block_kernel<8>, dim3(rows), dim3(256), 0, s, 1, src, width, gamma, beta, eps, out); return;
     case 4096: launch_k(layernorm_block_kernel<16>, dim3(rows), dim3(256), 0, s, 1, src, width, gamma, beta, eps, out); return;
     case 6144: launch_k(layernorm_block_kernel<24>, dim3(rows), dim3(256), 0, s, 1, src, width, gamma, beta, eps, out); return;
-    case 8192: launch_k(layernorm_block_kernel<32>, dim3(rows), dim3(256), 0, s, 1, src, width, gamma, beta, eps, out); return;
+    case 8192:
+      if (rows <= 64)  // small batch: a row over 1024 threads
+        launch_k(layernorm_block_kernel<8, 1024>, dim3(rows), dim3(1024), 0, s, 1, src, width, gamma, beta, eps, out);
+      else
+        launch_k(layernorm_block_kernel<32>, dim3(rows), dim3(256), 0, s, 1, src, width, gamma, beta, eps, out);
+      return;
     case 12288: launch_k(layernorm_block_kernel<48>, dim3(rows), dim3(256), 0, s, 1, src, width, gamma, beta, eps, out); return;
     case 16384: launch_k(layernorm_block_kernel<64>, dim3(rows), dim3(256), 0, s, 1, src, width, gamma, beta, eps, out); return;
     default: return;
