@@ -612,10 +612,12 @@ bool launch_splitk_act_ln(const float *part, int splits, long long stride, int r
 // and exp(x - max) = 2^(x' - max') with one ex2.approx per element. The bias
 // arrives in "fragment order" (the generator's output columns are permuted
 // when the weights are packed, attention_bias_column()): thread (warp w,
-// lane l) finds the 32 values its score fragments need as 64 contiguous
-// bytes at w*1024 + l*32, loaded with four 16-byte global loads while Q, K
-// and V are still in flight. P stays unnormalised through P V; the 16
-// outputs of each thread are divided by the row sum at the end.
+// lane l) finds the 32 values its score fragments need as four 16-byte
+// pieces at w*1024 + i*256 + l*8 (i = 0..3), so each warp-wide load reads
+// 512 contiguous bytes, issued while Q, K and V are still in flight. P stays
+// unnormalised through P V; the 16 outputs of each thread are divided by the
+// row sum at the end, staged in the warp's own 16 rows of sQ (no other warp
+// reads them) and written back as whole 16-byte pieces of each context row.
 constexpr int kDh = 32;
 constexpr int kQkvStride = 40;   // padded smem row (80 bytes): conflict-free ldmatrix
 
@@ -656,10 +658,10 @@ __global__ void __launch_bounds__(128)
   uint32_t bw[16];
   {
     const uint4 *bp = reinterpret_cast<const uint4 *>(
-        bias + static_cast<long long>(bh) * kSquares * kSquares + warp * 1024 + lane * 32);
+        bias + static_cast<long long>(bh) * kSquares * kSquares + warp * 1024 + lane * 8);
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      const uint4 v = __ldg(bp + i);
+      const uint4 v = __ldg(bp + 32 * i);
       bw[4 * i] = v.x;
       bw[4 * i + 1] = v.y;
       bw[4 * i + 2] = v.z;
@@ -762,39 +764,47 @@ __global__ void __launch_bounds__(128)
     O[j][3] *= inv1;
   }
   const long long base_off = (static_cast<long long>(b) * kSquares + q0) * d + h * kDh;
+  // stage this warp's 16 x 32 outputs in its own rows of sQ (80-byte rows)
+  uint8_t *stage = reinterpret_cast<uint8_t *>(&sQ[q0 * kQkvStride]);
+  constexpr int kRowBytes = kQkvStride * 2;
   if (ctx8) {
     // 8-bit context for an 8-bit output projection: value / *scale8 as e4m3
-    // or (ctx_i8) as a saturated signed integer
+    // or (ctx_i8) as a saturated signed integer; 32-byte rows
     const float inv = 1.0f / __ldg(scale8);
-    if (ctx_i8) {
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int col = 8 * j + 2 * t;
-        const uint16_t lo = pack_s8x2(O[j][0] * inv, O[j][1] * inv);
-        const uint16_t hi = pack_s8x2(O[j][2] * inv, O[j][3] * inv);
-        *reinterpret_cast<uint16_t *>(ctx8 + base_off + static_cast<long long>(g) * d + col) = lo;
-        *reinterpret_cast<uint16_t *>(ctx8 + base_off + static_cast<long long>(g + 8) * d + col) = hi;
-      }
-      return;
-    }
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const int col = 8 * j + 2 * t;
-      const __nv_fp8x2_e4m3 lo(make_float2(O[j][0] * inv, O[j][1] * inv));
-      const __nv_fp8x2_e4m3 hi(make_float2(O[j][2] * inv, O[j][3] * inv));
-      *reinterpret_cast<__nv_fp8x2_storage_t *>(ctx8 + base_off + static_cast<long long>(g) * d + col) = lo.__x;
-      *reinterpret_cast<__nv_fp8x2_storage_t *>(ctx8 + base_off + static_cast<long long>(g + 8) * d + col) = hi.__x;
+      uint16_t lo, hi;
+      if (ctx_i8) {
+        lo = pack_s8x2(O[j][0] * inv, O[j][1] * inv);
+        hi = pack_s8x2(O[j][2] * inv, O[j][3] * inv);
+      } else {
+        lo = __nv_fp8x2_e4m3(make_float2(O[j][0] * inv, O[j][1] * inv)).__x;
+        hi = __nv_fp8x2_e4m3(make_float2(O[j][2] * inv, O[j][3] * inv)).__x;
+      }
+      *reinterpret_cast<uint16_t *>(stage + g * kRowBytes + col) = lo;
+      *reinterpret_cast<uint16_t *>(stage + (g + 8) * kRowBytes + col) = hi;
     }
+    __syncwarp();
+    const int r = lane >> 1, half = lane & 1;
+    *reinterpret_cast<uint4 *>(ctx8 + base_off + static_cast<long long>(r) * d + 16 * half) =
+        *reinterpret_cast<const uint4 *>(stage + r * kRowBytes + 16 * half);
     return;
   }
-  __nv_bfloat16 *out = ctx + base_off;
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
     const int col = 8 * j + 2 * t;
-    *reinterpret_cast<uint32_t *>(out + static_cast<long long>(g) * d + col) =
-        pack_bf16x2(O[j][0], O[j][1]);
-    *reinterpret_cast<uint32_t *>(out + static_cast<long long>(g + 8) * d + col) =
+    *reinterpret_cast<uint32_t *>(stage + g * kRowBytes + 2 * col) = pack_bf16x2(O[j][0], O[j][1]);
+    *reinterpret_cast<uint32_t *>(stage + (g + 8) * kRowBytes + 2 * col) =
         pack_bf16x2(O[j][2], O[j][3]);
+  }
+  __syncwarp();
+  __nv_bfloat16 *out = ctx + base_off;
+#pragma unroll
+  for (int p = 0; p < 2; ++p) {
+    const int piece = lane + 32 * p, r = piece >> 2, c = (piece & 3) * 8;
+    *reinterpret_cast<uint4 *>(out + static_cast<long long>(r) * d + c) =
+        *reinterpret_cast<const uint4 *>(stage + r * kRowBytes + 2 * c);
   }
 }
 

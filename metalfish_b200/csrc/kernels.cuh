@@ -61,11 +61,13 @@ void launch_layernorm_q(const void *in, Fmt in_fmt, int rows, int width, const f
 // Fragment order of the smolgen attention bias: the generator GEMM's output
 // column c (its weight row) holds the reference's bias entry q * 64 + k
 // returned here (query q, key k), so that each attention thread finds its 32
-// values contiguous: c = w * 1024 + lane * 32 + j * 4 + e, with query
-// 16w + lane/4 + 8*(e/2) and key 8j + 2*(lane%4) + e%2 (the accumulator
-// fragment layout of mma.m16n8k16).
+// values as four 16-byte pieces and each warp-wide 16-byte load reads 512
+// contiguous bytes: c = w * 1024 + i * 256 + lane * 8 + jj * 4 + e, with
+// j = 2i + jj, query 16w + lane/4 + 8*(e/2) and key 8j + 2*(lane%4) + e%2
+// (the accumulator fragment layout of mma.m16n8k16).
 inline int attention_bias_column(int c) {
-  const int w = c >> 10, lane = (c >> 5) & 31, j = (c >> 2) & 7, e = c & 3;
+  const int w = c >> 10, i = (c >> 8) & 3, lane = (c >> 3) & 31, jj = (c >> 2) & 1, e = c & 3;
+  const int j = 2 * i + jj;
   const int q = 16 * w + (lane >> 2) + 8 * (e >> 1);
   const int k = 8 * j + 2 * (lane & 3) + (e & 1);
   return q * 64 + k;
