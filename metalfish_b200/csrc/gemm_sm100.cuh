@@ -120,7 +120,11 @@ __device__ __forceinline__ float act_t(float v) {
   else if constexpr (ACT == kActRelu2) { const float r = fmaxf(v, 0.0f); return r * r; }
   else if constexpr (ACT == kActTanh) return tanhf(v);
   else if constexpr (ACT == kActSigmoid) return 1.0f / (1.0f + expf(-v));
-  else if constexpr (ACT == kActSwish) return v / (1.0f + expf(-v));
+  else if constexpr (ACT == kActSwish)
+    // fast exponential and division: relative error ~1e-6, far inside the
+    // bf16 rounding of every consumer; for v < ~-87 the divisor overflows
+    // and the result is 0 (the true value is below 1e-36)
+    return __fdividef(v, 1.0f + __expf(-v));
   else if constexpr (ACT == kActMish) return mish_fast(v);
   else if constexpr (ACT == kActSelu) return 1.05070098f * (v > 0.0f ? v : 1.67326324f * (expf(v) - 1.0f));
   else return v;
