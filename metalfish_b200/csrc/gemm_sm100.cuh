@@ -746,8 +746,25 @@ __global__ void __launch_bounds__(64 + 32 * (LN ? kEpiWarpsLN : kEpiWarpsMax), 1
   tc_fence_after();
   if (ln) cluster_sync();  // peers' barriers are initialised before any remote arrive
   const uint32_t tmem_base = *tmem_slot;
-  // the prologue above overlaps the previous kernel; operands and outputs
-  // are touched only after it has completed
+  // Weight tiles do not depend on the previous kernel: the producer announces
+  // the first stages of its first work unit and loads their W tiles before
+  // the grid-dependency wait, so that their latency overlaps the previous
+  // kernel's tail (small batches, where a GEMM follows a short kernel whose
+  // CTAs leave room for this one's). A tiles, outputs and everything else
+  // are touched only after the wait.
+  int pre = 0;  // stages whose W tile is already in flight
+  if (warp == 0 && lane == 0 && u_begin < u_end &&
+      !(args.debug_withhold && blockIdx.x == 0)) {
+    const int t = ln ? u_begin * tiles_n + static_cast<int>(rank) : u_begin / splits;
+    const int ks = ln ? 0 : u_begin % splits;
+    const int n0 = (t % tiles_n) * BN;
+    const int kb0 = ks * kb_per, kb1 = min(kblocks, (ks + 1) * kb_per);
+    pre = min(STAGES, max(0, kb1 - kb0));
+    for (int i = 0; i < pre; ++i) {
+      mbar_arrive_expect_tx(&full[i], S::A_BYTES + S::B_BYTES);
+      tma_load_2d(smB + i * S::B_BYTES, &tmB, &full[i], (kb0 + i) * S::BK, n0);
+    }
+  }
   pdl_wait();
   pdl_launch();
   const long long t_start = trace_clock(args);
@@ -772,6 +789,12 @@ __global__ void __launch_bounds__(64 + 32 * (LN ? kEpiWarpsLN : kEpiWarpsMax), 1
             for (int x = n0; x < min(n0 + BN, args.N); x += 32) tma_prefetch_l2_2d(&tmRes, x, y);
         }
         for (int kb = ks * kb_per; kb < kb1; ++kb) {
+          if (issued < pre) {  // W already in flight (announced before the wait)
+            tma_load_2d(smA + stage * S::A_BYTES, &tmA, &full[stage], kb * S::BK, m0);
+            ++issued;
+            if (++stage == STAGES) { stage = 0; ++round; }
+            continue;
+          }
           const long long tw = trace_clock(args);
           const bool got = mbar_wait(&empty[stage], (round & 1) ^ 1, args.status, kErrTimeoutProducer,
                          abort_flag, wait_limit(args));
@@ -1031,6 +1054,9 @@ __global__ void __launch_bounds__(64 + 32 * kEpiWarpsMax, 1)
   tc_fence_after();
   cluster_sync();  // both CTAs' barriers exist before any cross-CTA arrive or load
   const uint32_t tmem_base = *tmem_slot;
+  // (no W loads before the wait here, unlike gemm_sm100_kernel: measured
+  // slower at batch 32 and 1024, where a pair kernel follows a kernel whose
+  // CTAs it cannot share an SM with)
   pdl_wait();
   pdl_launch();
   const long long t_start = trace_clock(args);
