@@ -10,7 +10,8 @@ top-1/top-2 logit gap.
 * bf16 (configs 1 and the bench line): max |policy logit diff| <= 5e-2 and
   max |WDL diff| <= 1e-2, evaluated as one batch of 256 (config 1) and as
   one batch of 1024 (the bench's batch; the full-policy check covers the
-  first 256 of them, WDL / moves-left / top-1 all 1024).
+  first 256 of them, WDL / moves-left / top-1 all 1024), and at the small
+  MCTS batches 1, 2 and 16 (split-K GEMMs with their reduction kernels).
 * 8-bit (config 2): top-1 policy agreement >= 99% and max |WDL diff| <= 2e-2
   against the fp32 reference. Top-1 is counted over the positions whose
   reference top-1/top-2 gap exceeds 0.1 logits: the random-init policies
@@ -73,7 +74,7 @@ def stats(out, g, n):
     return dp, dw, dm, top1, msg
 
 
-@pytest.mark.parametrize("batch", [256, 1024])
+@pytest.mark.parametrize("batch", [1, 2, 16, 256, 1024])
 def test_bt4_bf16_matches_reference_at_bench_batch(batch, positions, golden):
     out = bt4_net(positions=positions).evaluate_packed(positions.slice(0, batch))
     dp, dw, dm, top1, msg = stats(out, golden, batch)
