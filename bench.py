@@ -164,6 +164,10 @@ def cpu_baseline(cfg, tensors, sample_positions: int | None = None):
 # when a launch ends, so the write half is an upper estimate.
 QKV_TRAFFIC = {
     "bf16": (4 * (40.235e6 + 53.987e6), "ncu capture at M=16384, scaled x4 to M=65536"),
+    # ncu launch lists of the 8-bit forwards at batch 256 (M=16384): DRAM read + write
+    # bytes of the 15 QKV launches / 15, scaled x4 to M=65536
+    "int8": (4 * (308.8e6 + 1443.5e6) / 15, "ncu launch list at M=16384 (15 launches), scaled x4 to M=65536"),
+    "fp8": (4 * (308.9e6 + 1418.2e6) / 15, "ncu launch list at M=16384 (15 launches), scaled x4 to M=65536"),
 }
 
 
@@ -677,6 +681,8 @@ def eight_bit_line(cfg, tensors, precision, B, local, dev, stream, shard, L, arg
             "roofline": {"bound": "tensor", "kernel": "QKV+compress GEMM", "achieved": achieved,
                          "peak": 2.0 * sustained, "unit": "TFLOP/s",
                          "frac": achieved / (2.0 * sustained),
+                         "traffic": QKV_TRAFFIC[precision][0] if B == 1024 else None,
+                         "traffic_source": QKV_TRAFFIC[precision][1],
                          "peak_source": f"2 x {src} bf16_tflops_sustained (8-bit dense = 2x bf16)"},
             "encoder_tflops_per_gpu": value * enc / 1e12 / world,
             "frac_of_bf16_burst": value * enc / 1e12 / world / burst,
