@@ -67,7 +67,8 @@ def stats(out, g, n):
     dw = float(np.abs(out.wdl - g["wdl"][:n]).max())
     dm = np.abs(out.moves_left - g["moves_left"][:n])
     clear = g["gap"][:n] > GAP
-    top1 = float((out.policy.argmax(1) == g["top1"][:n])[clear].mean())
+    hits = (out.policy.argmax(1) == g["top1"][:n])[clear]
+    top1 = float(hits.mean()) if hits.size else 1.0  # no clear position among the first n
     msg = (f"n={n} policy max {dp:.4g} wdl max {dw:.4g} mlh max {dm.max():.4g} "
            f"top1 {top1:.4f} over {int(clear.sum())} clear positions")
     print(msg)
