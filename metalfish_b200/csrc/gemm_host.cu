@@ -87,7 +87,7 @@ static bool make_tmap(CUtensorMap *tm, const void *base, CUtensorMapDataType dt,
          CUDA_SUCCESS;
 }
 
-template <int BN, bool FP8, bool LN>
+template <int BN, bool FP8, bool LN, int EPI>
 static cudaError_t launch_t(const GemmLaunch &g, cudaStream_t stream) {
   using S = GemmShape<BN, FP8, LN>;
   // the shared-memory opt-in is a per-device function attribute
@@ -96,7 +96,7 @@ static cudaError_t launch_t(const GemmLaunch &g, cudaStream_t stream) {
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   if (!attr_done[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_sm100_kernel<BN, FP8, LN>,
+    cudaError_t e = cudaFuncSetAttribute(gemm_sm100_kernel<BN, FP8, LN, EPI>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          S::SMEM_BYTES);
     if (e != cudaSuccess) return e;
@@ -104,7 +104,7 @@ static cudaError_t launch_t(const GemmLaunch &g, cudaStream_t stream) {
   }
   // the CTAs covering one row block of the LN epilogue form a cluster
   const int cluster = (g.args.mode == kEpiResidLN && g.args.cluster_n > 1) ? g.args.cluster_n : 1;
-  const cudaError_t e = launch_k(gemm_sm100_kernel<BN, FP8, LN>, g.grid, dim3(S::THREADS),
+  const cudaError_t e = launch_k(gemm_sm100_kernel<BN, FP8, LN, EPI>, g.grid, dim3(S::THREADS),
                                  S::SMEM_BYTES, stream, cluster, g.tmA, g.tmB, g.tmOut, g.tmOut2,
                                  g.tmRes, g.args);
   if (e != cudaSuccess) return e;
@@ -121,7 +121,7 @@ static int max_clusters_t(int csize) {
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64 || csize < 1 || csize > 8) return 0;
   if (cache[dev][csize]) return cache[dev][csize];
-  cudaFuncSetAttribute(gemm_sm100_kernel<BN, FP8, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  cudaFuncSetAttribute(gemm_sm100_kernel<BN, FP8, true, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                        S::SMEM_BYTES);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(csize * 64));
@@ -135,7 +135,7 @@ static int max_clusters_t(int csize) {
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   int n = 0;
-  if (cudaOccupancyMaxActiveClusters(&n, gemm_sm100_kernel<BN, FP8, true>, &cfg) != cudaSuccess || n <= 0)
+  if (cudaOccupancyMaxActiveClusters(&n, gemm_sm100_kernel<BN, FP8, true, 0>, &cfg) != cudaSuccess || n <= 0)
     n = num_sms() / csize;
   cudaGetLastError();
   cache[dev][csize] = n;
@@ -151,7 +151,7 @@ static int max_pairs_t() {
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return 0;
   if (cache[dev]) return cache[dev];
-  cudaFuncSetAttribute(gemm_pair_kernel<FP8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  cudaFuncSetAttribute(gemm_pair_kernel<FP8, 0>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                        S::SMEM_BYTES);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * 64);
@@ -165,14 +165,14 @@ static int max_pairs_t() {
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   int n = 0;
-  if (cudaOccupancyMaxActiveClusters(&n, gemm_pair_kernel<FP8>, &cfg) != cudaSuccess || n <= 0)
+  if (cudaOccupancyMaxActiveClusters(&n, gemm_pair_kernel<FP8, 0>, &cfg) != cudaSuccess || n <= 0)
     n = num_sms() / 2;
   cudaGetLastError();
   cache[dev] = n;
   return n;
 }
 
-template <bool FP8>
+template <bool FP8, int EPI>
 static cudaError_t launch_pair_t(const GemmLaunch &g, cudaStream_t stream) {
   using S = PairShape<FP8>;
   static bool attr_done[64] = {};
@@ -180,12 +180,12 @@ static cudaError_t launch_pair_t(const GemmLaunch &g, cudaStream_t stream) {
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
   if (!attr_done[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(gemm_pair_kernel<FP8>,
+    cudaError_t e = cudaFuncSetAttribute(gemm_pair_kernel<FP8, EPI>,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM_BYTES);
     if (e != cudaSuccess) return e;
     attr_done[dev] = true;
   }
-  return launch_k(gemm_pair_kernel<FP8>, g.grid, dim3(S::THREADS), S::SMEM_BYTES, stream, 2, g.tmA,
+  return launch_k(gemm_pair_kernel<FP8, EPI>, g.grid, dim3(S::THREADS), S::SMEM_BYTES, stream, 2, g.tmA,
                   g.tmB, g.tmOut, g.tmOut2, g.tmRes, g.args);
 }
 
@@ -196,26 +196,46 @@ static int max_clusters(int bn, bool fp8, int csize) {
                    : (bn == 128 ? max_clusters_t<128, false>(csize) : max_clusters_t<64, false>(csize));
 }
 
-cudaError_t launch_gemm(const GemmLaunch &g, cudaStream_t stream) {
-  if (g.pair) return g.fp8 ? launch_pair_t<true>(g, stream) : launch_pair_t<false>(g, stream);
-  const bool ln = g.args.mode == kEpiResidLN;
-#define MFB_LAUNCH(BN, F8) \
-  return ln ? launch_t<BN, F8, true>(g, stream) : launch_t<BN, F8, false>(g, stream)
-  if (g.fp8) {
-    switch (g.bn) {
-    case 256: MFB_LAUNCH(256, true);
-    case 128: MFB_LAUNCH(128, true);
-    case 64: MFB_LAUNCH(64, true);
-    }
-  } else {
-    switch (g.bn) {
-    case 256: MFB_LAUNCH(256, false);
-    case 128: MFB_LAUNCH(128, false);
-    case 64: MFB_LAUNCH(64, false);
-    }
+// One kernel instance per (tile width, operand width, epilogue selector).
+template <bool FP8, int EPI>
+static cudaError_t launch_sel(const GemmLaunch &g, cudaStream_t stream) {
+  if (g.pair) return launch_pair_t<FP8, EPI>(g, stream);
+  switch (g.bn) {
+  case 256: return launch_t<256, FP8, false, EPI>(g, stream);
+  case 128: return launch_t<128, FP8, false, EPI>(g, stream);
+  case 64: return launch_t<64, FP8, false, EPI>(g, stream);
   }
-#undef MFB_LAUNCH
   return cudaErrorInvalidValue;
+}
+
+template <bool FP8>
+static cudaError_t launch_fmt(const GemmLaunch &g, cudaStream_t stream) {
+  if (g.args.mode == kEpiResidLN) {  // the cluster LayerNorm epilogue has its own kernel
+    switch (g.bn) {
+    case 256: return launch_t<256, FP8, true, 0>(g, stream);
+    case 128: return launch_t<128, FP8, true, 0>(g, stream);
+    case 64: return launch_t<64, FP8, true, 0>(g, stream);
+    }
+    return cudaErrorInvalidValue;
+  }
+  switch (epi_select(g.args.mode, g.args.act, g.args.k_splits)) {
+  case kActNone: return launch_sel<FP8, kActNone>(g, stream);
+  case kActRelu: return launch_sel<FP8, kActRelu>(g, stream);
+  case kActRelu2: return launch_sel<FP8, kActRelu2>(g, stream);
+  case kActTanh: return launch_sel<FP8, kActTanh>(g, stream);
+  case kActSigmoid: return launch_sel<FP8, kActSigmoid>(g, stream);
+  case kActSwish: return launch_sel<FP8, kActSwish>(g, stream);
+  case kActMish: return launch_sel<FP8, kActMish>(g, stream);
+  case kActSelu: return launch_sel<FP8, kActSelu>(g, stream);
+  case kSelResid: return launch_sel<FP8, kSelResid>(g, stream);
+  case kSelAccum: return launch_sel<FP8, kSelAccum>(g, stream);
+  case kSelResidNorm: return launch_sel<FP8, kSelResidNorm>(g, stream);
+  }
+  return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_gemm(const GemmLaunch &g, cudaStream_t stream) {
+  return g.fp8 ? launch_fmt<true>(g, stream) : launch_fmt<false>(g, stream);
 }
 
 // Second half of a split-K GEMM: one warp per (row, 32-column chunk), lane =
