@@ -312,7 +312,7 @@ __device__ __forceinline__ void stage_row(const GemmArgs &args, uint8_t *st, int
 // The chunks of one tile owned by this warp (every other 32-column chunk,
 // starting at `group`*32), with the TMEM load of the next chunk in flight
 // while the current one is processed. Returns false on a barrier timeout.
-template <int BN, int MODE, int ACT, int EW>
+template <int BN, int MODE, int ACT, int EW, bool OP8>
 __device__ __forceinline__ bool epilogue_tile(const GemmArgs &args, EpiCtx &e, uint32_t taddr,
                                               int row0, int n0, int group, int ks) {
   constexpr int STEP = 32 * (EW / 4);  // columns between this warp's chunks
@@ -352,7 +352,7 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs &args, EpiCtx &e, u
     if (!PREFETCH) tmem_ld32(taddr + c, raw);
     tmem_wait_ld();
     float v[32];
-    if (args.ab_i8) {
+    if (OP8 && args.ab_i8) {
 #pragma unroll
       for (int j = 0; j < 32; ++j) v[j] = static_cast<float>(static_cast<int>(raw[j]));
     } else {
@@ -376,7 +376,7 @@ __device__ __forceinline__ bool epilogue_tile(const GemmArgs &args, EpiCtx &e, u
       __syncwarp();
     }
     if (ks < 0) {
-      const float as = args.a_row_scale ? a_scale * e.arow : a_scale;
+      const float as = (OP8 && args.a_row_scale) ? a_scale * e.arow : a_scale;
       if (as != 1.0f) {
 #pragma unroll
         for (int j = 0; j < 32; ++j) v[j] *= as;
@@ -648,20 +648,20 @@ __host__ __device__ constexpr int epi_select(int mode, int act, int k_splits) {
                                                                 : (mode == kEpiResidNorm ? kSelResidNorm : act)));
 }
 
-template <int BN, bool LN, int EW, int EPI>
+template <int BN, bool LN, int EW, int EPI, bool OP8>
 __device__ __forceinline__ bool epilogue_dispatch(const GemmArgs &args, EpiCtx &e, uint32_t taddr,
                                                   int row0, int n0, int group, int ks) {
   if constexpr (LN) {
     return epilogue_tile_ln<BN>(args, e, taddr, row0, n0);
   } else if constexpr (EPI == kSelResid) {
-    return epilogue_tile<BN, kEpiResid, kActNone, EW>(args, e, taddr, row0, n0, group, ks);
+    return epilogue_tile<BN, kEpiResid, kActNone, EW, OP8>(args, e, taddr, row0, n0, group, ks);
   } else if constexpr (EPI == kSelAccum) {
-    return epilogue_tile<BN, kEpiAccum, kActNone, EW>(args, e, taddr, row0, n0, group, ks);
+    return epilogue_tile<BN, kEpiAccum, kActNone, EW, OP8>(args, e, taddr, row0, n0, group, ks);
   } else if constexpr (EPI == kSelResidNorm) {
     static_assert(EW == kEpiWarpsMax, "the residual-norm epilogue needs 16 epilogue warps");
-    return epilogue_tile<BN, kEpiResidNorm, kActNone, EW>(args, e, taddr, row0, n0, group, ks);
+    return epilogue_tile<BN, kEpiResidNorm, kActNone, EW, OP8>(args, e, taddr, row0, n0, group, ks);
   } else {
-    return epilogue_tile<BN, kEpiStore, EPI, EW>(args, e, taddr, row0, n0, group, ks);
+    return epilogue_tile<BN, kEpiStore, EPI, EW, OP8>(args, e, taddr, row0, n0, group, ks);
   }
 }
 
@@ -939,7 +939,7 @@ __global__ void __launch_bounds__(64 + 32 * (LN ? kEpiWarpsLN : kEpiWarpsMax), 1
       const uint32_t taddr =
           tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
       const long long te = trace_clock(args);
-      const bool ok = epilogue_dispatch<BN, LN, S::EW, EPI>(args, e, taddr, m0 + quarter * 32, n0, group, ks);
+      const bool ok = epilogue_dispatch<BN, LN, S::EW, EPI, FP8>(args, e, taddr, m0 + quarter * 32, n0, group, ks);
       tr_b += trace_clock(args) - te;
       tr_c += 1;
       tc_fence_before();
@@ -1211,7 +1211,7 @@ __global__ void __launch_bounds__(64 + 32 * kEpiWarpsMax, 1)
       const uint32_t taddr =
           tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
       const long long te = trace_clock(args);
-      const bool ok = epilogue_dispatch<BN, false, S::EW, EPI>(args, e, taddr, m0 + quarter * 32, n0, group, -1);
+      const bool ok = epilogue_dispatch<BN, false, S::EW, EPI, FP8>(args, e, taddr, m0 + quarter * 32, n0, group, -1);
       tr_b += trace_clock(args) - te;
       tr_c += 1;
       tc_fence_before();
