@@ -12,12 +12,17 @@
 //              accumulators, so the epilogue of tile i overlaps the MMAs of
 //              tile i+1) and issues tcgen05.mma (M=128, N=BN, K=16 bf16 or
 //              K=32 fp8 per instruction) from one lane;
-//   warps 2-9  epilogue: two warps per TMEM lane quarter (TMEM lane = tile
-//              row), alternating 32-column chunks; tcgen05.ld the
+//   warps 2-17 epilogue (warps 2-9 in the cluster-LayerNorm variant): four
+//              (two) warps per TMEM lane quarter (TMEM lane = tile row), each
+//              taking every fourth (second) 32-column chunk; tcgen05.ld the
 //              accumulator, apply scale / bias / activation / residual
 //              (residual tiles fetched by TMA), write each 32 x 32 chunk into
 //              a per-warp swizzled shared-memory tile in the output format
-//              (bf16, e4m3 or fp32) and TMA-store it asynchronously.
+//              (bf16, fp16, e4m3, int8 or fp32) and TMA-store it
+//              asynchronously.
+// Each kernel instance carries one epilogue (template parameter EPI), and
+// gemm_pair_kernel runs the same roles over a cluster of two CTAs
+// (tcgen05 cta_group::2, 256-row tiles).
 // All barrier waits are bounded (sm100_ptx.cuh).
 #pragma once
 #include <cuda_fp16.h>
