@@ -12,9 +12,11 @@
 //              accumulators, so the epilogue of tile i overlaps the MMAs of
 //              tile i+1) and issues tcgen05.mma (M=128, N=BN, K=16 bf16 or
 //              K=32 fp8 per instruction) from one lane;
-//   warps 2-17 epilogue (warps 2-9 in the cluster-LayerNorm variant): four
-//              (two) warps per TMEM lane quarter (TMEM lane = tile row), each
-//              taking every fourth (second) 32-column chunk; tcgen05.ld the
+//   warps 2-17 epilogue: four warps per TMEM lane quarter (TMEM lane =
+//              tile row), each taking every fourth 32-column chunk (in the
+//              cluster-LayerNorm variant warps 2-9, two teams of four that
+//              alternate tiles, each warp covering all columns of its 32
+//              rows); tcgen05.ld the
 //              accumulator, apply scale / bias / activation / residual
 //              (residual tiles fetched by TMA), write each 32 x 32 chunk into
 //              a per-warp swizzled shared-memory tile in the output format
