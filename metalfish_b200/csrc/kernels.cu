@@ -627,11 +627,14 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
+// OUT: the context format, 0 bf16, 1 e4m3, 2 signed 8-bit integers (one
+// kernel instance each).
+template <int OUT>
 __global__ void __launch_bounds__(128)
     attention_kernel(const __nv_bfloat16 *__restrict__ qkv, long long ldq,
                      const __nv_bfloat16 *__restrict__ bias, int heads, int d,
                      __nv_bfloat16 *__restrict__ ctx, uint8_t *__restrict__ ctx8,
-                     const float *__restrict__ scale8, int ctx_i8) {
+                     const float *__restrict__ scale8) {
   pdl_wait();
   pdl_launch();
   __shared__ __align__(16) __nv_bfloat16 sQ[kSquares * kQkvStride];
@@ -767,15 +770,15 @@ __global__ void __launch_bounds__(128)
   // stage this warp's 16 x 32 outputs in its own rows of sQ (80-byte rows)
   uint8_t *stage = reinterpret_cast<uint8_t *>(&sQ[q0 * kQkvStride]);
   constexpr int kRowBytes = kQkvStride * 2;
-  if (ctx8) {
+  if constexpr (OUT != 0) {
     // 8-bit context for an 8-bit output projection: value / *scale8 as e4m3
-    // or (ctx_i8) as a saturated signed integer; 32-byte rows
+    // or (OUT 2) as a saturated signed integer; 32-byte rows
     const float inv = 1.0f / __ldg(scale8);
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const int col = 8 * j + 2 * t;
       uint16_t lo, hi;
-      if (ctx_i8) {
+      if constexpr (OUT == 2) {
         lo = pack_s8x2(O[j][0] * inv, O[j][1] * inv);
         hi = pack_s8x2(O[j][2] * inv, O[j][3] * inv);
       } else {
@@ -811,7 +814,13 @@ __global__ void __launch_bounds__(128)
 void launch_attention(const __nv_bfloat16 *qkv, long long ldq, const __nv_bfloat16 *bias,
                       int batch, int heads, int d, __nv_bfloat16 *ctx, cudaStream_t s,
                       uint8_t *ctx8, const float *scale8, int ctx_i8) {
-  launch_k(attention_kernel, dim3(batch * heads), dim3(128), 0, s, 1, qkv, ldq, bias, heads, d, ctx, ctx8, scale8, ctx_i8);
+  const dim3 grid(batch * heads);
+  if (!ctx8)
+    launch_k(attention_kernel<0>, grid, dim3(128), 0, s, 1, qkv, ldq, bias, heads, d, ctx, ctx8, scale8);
+  else if (ctx_i8)
+    launch_k(attention_kernel<2>, grid, dim3(128), 0, s, 1, qkv, ldq, bias, heads, d, ctx, ctx8, scale8);
+  else
+    launch_k(attention_kernel<1>, grid, dim3(128), 0, s, 1, qkv, ldq, bias, heads, d, ctx, ctx8, scale8);
 }
 
 // ------------------------------------------------------------------ legal-move priors
